@@ -1,0 +1,221 @@
+"""ctypes binding of the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+arm import this module; the product path never does. The arithmetic lives in
+oracle/mpp41_oracle.c, a C restatement of the reference's Metal kernels and
+Swift data generators (each C function cites its reference file:line).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+# weight formats (match include/mpp41.h enum mpp41_wfmt)
+W_F16, W_I8, W_I4, W_I2, W_FP4, W_E4M3, W_E5M2, W_MXFP4 = range(8)
+
+# reference seeds, main.swift:611-638 (MLP) and 409-413 (big matmul)
+MLP_SEEDS = {
+    "x_half": 0x11112222, "x_int8": 0x22223333,
+    "wg_half": 0x55556666, "wu_half": 0x77778888, "wd_half": 0x9999AAAA,
+    "wg_i8": 0x33334444, "wu_i8": 0x44445555, "wd_i8": 0x55557777,
+    "wg_i4": 0x13572468, "wu_i4": 0xACE01357, "wd_i4": 0xC001D00D,
+    "wg_i2": 0x24681357, "wu_i2": 0xBAD0CAFE, "wd_i2": 0xD00DC001,
+    "wg_fp4": 0xABCD1357, "wu_fp4": 0x2468BDF0, "wd_fp4": 0x0BADCAFE,
+    "wg_e4m3": 0x11117777, "wu_e4m3": 0x22228888, "wd_e4m3": 0x33339999,
+    "wg_e5m2": 0x4444AAAA, "wu_e5m2": 0x5555BBBB, "wd_e5m2": 0x6666CCCC,
+    "sg": 0x7777DDDD, "su": 0x8888EEEE, "sd": 0x9999FFFF,
+}
+MXFP4_SCALE_PATTERN = bytes([124, 125, 126, 127, 127, 128, 128, 129, 130])
+MATMUL_SEEDS = {"a_packed": 0x12345678, "b_packed": 0x87654321, "a_half": 0x2468ACE0,
+                "a_int8": 0x13579BDF, "b_half": 0xFDB97531}
+
+_lib = None
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        vp, u32, sz = C.c_void_p, C.c_uint32, C.c_size_t
+        L.orc_make_packed_bytes.argtypes = [vp, sz, u32]
+        L.orc_make_pattern_bytes.argtypes = [vp, sz, u32, vp, sz]
+        L.orc_make_fp8_e4m3_bytes.argtypes = [vp, sz, u32]
+        L.orc_make_fp8_e5m2_bytes.argtypes = [vp, sz, u32]
+        L.orc_make_half_values.argtypes = [vp, sz, u32, C.c_float]
+        L.orc_make_int8_values.argtypes = [vp, sz, u32]
+        L.orc_pack.argtypes = [C.c_int, vp, sz, vp]
+        L.orc_unpack.argtypes = [C.c_int, vp, sz, vp]
+        L.orc_decode_weights.argtypes = [C.c_int, vp, vp, u32, u32, vp]
+        L.orc_mxfp4_dequant_half.argtypes = [vp, vp, vp, u32, u32]
+        L.orc_gemm_f64.argtypes = [vp, vp, vp, u32, u32, u32]
+        L.orc_mlp.argtypes = [C.c_int] * 4 + [u32] * 3 + [vp] * 9
+        L.orc_mlp_mxfp4_cpu.argtypes = [u32] * 3 + [vp] * 8 + [C.c_int, u32, u32]
+        L.orc_mlp_mxfp4_cpu.restype = C.c_int
+        L.orc_scalar_mlp_gate_up.argtypes = [C.c_int, u32, u32, u32, vp, vp, vp, vp]
+        L.orc_scalar_mlp_down.argtypes = [C.c_int, u32, u32, u32, vp, vp, vp]
+        L.orc_scalar_matmul.argtypes = [C.c_int, u32, u32, u32, vp, vp, vp]
+        L.orc_half_fma.argtypes = [C.c_uint16] * 3
+        L.orc_half_fma.restype = C.c_uint16
+        L.orc_swiglu_i8.argtypes = [C.c_int32, C.c_int32]
+        L.orc_swiglu_i8.restype = C.c_int8
+        L.orc_e2m1_encode.argtypes = [C.c_float]
+        L.orc_e2m1_encode.restype = C.c_uint8
+        L.orc_e8m0_decode.argtypes = [C.c_uint8]
+        L.orc_e8m0_decode.restype = C.c_float
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(C.c_void_p)
+
+
+# ---------------------------------------------------------------- generators
+def packed_bytes(n: int, seed: int) -> np.ndarray:
+    out = np.empty(n, np.uint8)
+    lib().orc_make_packed_bytes(_p(out), n, seed)
+    return out
+
+
+def pattern_bytes(n: int, seed: int, pattern: bytes) -> np.ndarray:
+    out = np.empty(n, np.uint8)
+    pat = np.frombuffer(pattern, np.uint8).copy()
+    lib().orc_make_pattern_bytes(_p(out), n, seed, _p(pat), len(pat))
+    return out
+
+
+def fp8_bytes(n: int, seed: int, e5m2: bool) -> np.ndarray:
+    out = np.empty(n, np.uint8)
+    (lib().orc_make_fp8_e5m2_bytes if e5m2 else lib().orc_make_fp8_e4m3_bytes)(_p(out), n, seed)
+    return out
+
+
+def half_values(n: int, seed: int, scale: float = 0.25) -> np.ndarray:
+    out = np.empty(n, np.uint16)
+    lib().orc_make_half_values(_p(out), n, seed, scale)
+    return out.view(np.float16)
+
+
+def int8_values(n: int, seed: int) -> np.ndarray:
+    out = np.empty(n, np.int8)
+    lib().orc_make_int8_values(_p(out), n, seed)
+    return out
+
+
+# ---------------------------------------------------------------- codecs
+def pack(fmt: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    n = x.size
+    out = np.zeros((n + 1) // 2 if fmt == 0 else n, np.uint8)
+    lib().orc_pack(fmt, _p(x), n, _p(out))
+    return out
+
+
+def unpack(fmt: int, packed: np.ndarray, n: int) -> np.ndarray:
+    packed = np.ascontiguousarray(packed, np.uint8)
+    out = np.empty(n, np.float32)
+    lib().orc_unpack(fmt, _p(packed), n, _p(out))
+    return out
+
+
+def decode_weights(wfmt: int, w: np.ndarray, scales, rows: int, depth: int) -> np.ndarray:
+    out = np.empty((rows, depth), np.float64)
+    s = _p(scales) if scales is not None else None
+    lib().orc_decode_weights(wfmt, _p(np.ascontiguousarray(w)), s, rows, depth, _p(out))
+    return out
+
+
+def mxfp4_dequant_half(packed, scales, rows, depth) -> np.ndarray:
+    out = np.empty((rows, depth), np.uint16)
+    lib().orc_mxfp4_dequant_half(_p(packed), _p(scales), _p(out), rows, depth)
+    return out.view(np.float16)
+
+
+def mlp(act, wfmt, epi, out_kind, T, H, I, x, wg, wu, wd, sg=None, su=None, sd=None):
+    """Returns (mid, out) of one MLP row, fp64-exact GEMMs (see mpp41_oracle.h)."""
+    mid_dt = {0: np.float32, 1: np.float16, 2: np.float16, 3: np.int8}[epi]
+    out_dt = {0: np.float32, 1: np.float16, 2: np.int32}[out_kind]
+    mid = np.empty((T, I), mid_dt)
+    out = np.empty((T, H), out_dt)
+    ps = [(_p(np.ascontiguousarray(a)) if a is not None else None) for a in (sg, su, sd)]
+    lib().orc_mlp(act, wfmt, epi, out_kind, T, H, I, _p(np.ascontiguousarray(x)),
+                  _p(np.ascontiguousarray(wg)), _p(np.ascontiguousarray(wu)),
+                  _p(np.ascontiguousarray(wd)), *ps, _p(mid), _p(out))
+    return mid, out
+
+
+def mlp_mxfp4_cpu(T, H, I, x, wg, wu, wd, sg, su, sd, nthreads=0, t0=0, t1=None):
+    out = np.zeros((T, H), np.float32)
+    t1 = T if t1 is None else t1
+    n = lib().orc_mlp_mxfp4_cpu(T, H, I, _p(x), _p(wg), _p(wu), _p(wd), _p(sg), _p(su), _p(sd),
+                                _p(out), nthreads, t0, t1)
+    return out, n
+
+
+def scalar_mlp(wfmt, T, H, I, x, wg, wu, wd):
+    mid = np.empty((T, I), np.uint16)
+    out = np.empty((T, H), np.uint16)
+    lib().orc_scalar_mlp_gate_up(wfmt, T, H, I, _p(x), _p(wg), _p(wu), _p(mid))
+    lib().orc_scalar_mlp_down(wfmt, T, H, I, _p(mid), _p(wd), _p(out))
+    return mid.view(np.float16), out.view(np.float16)
+
+
+def scalar_matmul(kind, M, N, K, a, b):
+    dt = {0: np.float32, 4: np.int32}.get(kind, np.uint16)
+    out = np.empty((M, N), dt)
+    lib().orc_scalar_matmul(kind, M, N, K, _p(np.ascontiguousarray(a)), _p(np.ascontiguousarray(b)), _p(out))
+    return out.view(np.float16) if dt is np.uint16 else out
+
+
+# ---------------------------------------------------------------- checksums
+def sample_indices(count: int) -> np.ndarray:
+    step = max(1, count // 32)
+    return np.arange(0, count, step)
+
+
+def float_checksum(a: np.ndarray) -> str:
+    flat = np.ascontiguousarray(a, np.float32).ravel()
+    idx = sample_indices(flat.size)
+    s = float(np.sum(flat[idx].astype(np.float64)))
+    return f"{s:.6g} over {idx.size} samples"
+
+
+def int_checksum(a: np.ndarray) -> str:
+    flat = np.ascontiguousarray(a, np.int32).ravel()
+    idx = sample_indices(flat.size)
+    return f"{int(np.sum(flat[idx].astype(np.int64)))} over {idx.size} samples"
+
+
+def half_raw_checksum(a: np.ndarray) -> str:
+    flat = np.ascontiguousarray(a).view(np.uint16).ravel()
+    idx = sample_indices(flat.size)
+    return f"raw16 sum {int(np.sum(flat[idx].astype(np.uint64)))} over {idx.size} samples"
+
+
+# ---------------------------------------------------------------- mode-R data
+def reference_mlp_inputs(T=128, H=1024, I=4096):
+    """The MXFP4 MLP inputs of runMLPBenchmark (main.swift:611-638)."""
+    s = MLP_SEEDS
+    return {
+        "x": half_values(T * H, s["x_half"], 0.125).reshape(T, H),
+        "wg": packed_bytes(I * H // 2, s["wg_fp4"]).reshape(I, H // 2),
+        "wu": packed_bytes(I * H // 2, s["wu_fp4"]).reshape(I, H // 2),
+        "wd": packed_bytes(H * I // 2, s["wd_fp4"]).reshape(H, I // 2),
+        "sg": pattern_bytes(I * (H // 32), s["sg"], MXFP4_SCALE_PATTERN).reshape(I, H // 32),
+        "su": pattern_bytes(I * (H // 32), s["su"], MXFP4_SCALE_PATTERN).reshape(I, H // 32),
+        "sd": pattern_bytes(H * (I // 32), s["sd"], MXFP4_SCALE_PATTERN).reshape(H, I // 32),
+    }
