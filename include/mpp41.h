@@ -1,0 +1,188 @@
+/*
+ * libmpp41 -- C ABI of the B200 (sm_100a) quantized-weight MLP hot path.
+ *
+ * Drop-in boundary for the reference probe's Metal kernel ABI
+ * (Sources/MetalFP41Probe/main.swift). The reference binds kernels by name
+ * (library.makeFunction(name:), main.swift:208-212, 1730-1733, 1981-1989),
+ * binds buffers by index (a=0, b=1, c=2, m=3, n=4, k=5, scales=6 for the
+ * matmul2d kernels, main.swift:2151-2161 and 2734-2743) and runs every
+ * iteration of a row in one command buffer (main.swift:2062-2121). Each entry
+ * point below names the reference interface it replaces.
+ *
+ * Plain C: pointers and sizes only, no exceptions across the ABI. Device
+ * pointers are CUDA global-memory addresses owned by the caller. Launches are
+ * asynchronous on the context's stream; mpp41_synchronize() waits and turns
+ * a device-side error word (bounded-wait timeout, bounds check) into a status.
+ * Threading: one context per host thread (or per stream).
+ */
+#ifndef MPP41_H
+#define MPP41_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MPP41_ABI_VERSION 1
+
+/* Replaces the ProbeError cases of main.swift:5-38. */
+typedef enum mpp41_status {
+    MPP41_OK = 0,
+    MPP41_ERR_INVALID_ARGUMENT = 1,  /* .invalidArgument */
+    MPP41_ERR_UNSUPPORTED_SHAPE = 2, /* size gates of main.swift:390-392, 595-597, 946, 1043 */
+    MPP41_ERR_NO_DEVICE = 3,         /* .missingDevice */
+    MPP41_ERR_MISSING_KERNEL = 4,    /* .missingFunction: makeFunction(name:) == nil */
+    MPP41_ERR_OUT_OF_MEMORY = 5,     /* .missingBuffer */
+    MPP41_ERR_CUDA = 6,              /* .gpuExecutionFailed */
+    MPP41_ERR_TIMEOUT = 7,           /* a bounded device-side wait ran out */
+    MPP41_ERR_BOUNDS = 8,            /* device-side bounds check tripped */
+    MPP41_ERR_COMM = 9               /* multi-GPU communication failure */
+} mpp41_status;
+
+/* Weight formats (the B operand of the reference's kernels). */
+typedef enum mpp41_wfmt {
+    MPP41_W_F16 = 0,    /* half [n][k] */
+    MPP41_W_I8 = 1,     /* int8 [n][k] */
+    MPP41_W_I4 = 2,     /* int4 [n][k/2], low nibble = even k, (n^8)-8 */
+    MPP41_W_I2 = 3,     /* int2 [n][k/4], LSB pair first, ((b&3)^2)-2 */
+    MPP41_W_FP4 = 4,    /* E2M1 [n][k/2], unscaled */
+    MPP41_W_E4M3 = 5,   /* FP8 E4M3 [n][k] */
+    MPP41_W_E5M2 = 6,   /* FP8 E5M2 [n][k] */
+    MPP41_W_MXFP4 = 7   /* E2M1 [n][k/2] + E8M0 scales [n][k/32] */
+} mpp41_wfmt;
+
+/* Activation (A operand) formats. */
+typedef enum mpp41_afmt { MPP41_A_F16 = 0, MPP41_A_S8 = 1 } mpp41_afmt;
+
+/* SwiGLU variants, MPPMLPKernels.metal:186-257. */
+typedef enum mpp41_epilogue {
+    MPP41_SWIGLU_FLOAT = 0,          /* mpp_mlp_swiglu_float: fp32 mid */
+    MPP41_SWIGLU_HALF = 1,           /* mpp_mlp_swiglu_half: /16, clamp 20, fp16 mid */
+    MPP41_SWIGLU_HALF_FROM_HALF = 2, /* mpp_mlp_swiglu_half_from_half: fp16 gate/up */
+    MPP41_SWIGLU_I8 = 3              /* mpp_mlp_swiglu_i8: int8 mid */
+} mpp41_epilogue;
+
+typedef enum mpp41_dtype { MPP41_F32 = 0, MPP41_F16 = 1, MPP41_S32 = 2, MPP41_S8 = 3 } mpp41_dtype;
+
+/* MatmulConfig, main.swift:55-60 (PackedNumericKernels.metal:6-11). */
+typedef struct mpp41_matmul_config {
+    uint32_t rows, columns, depth, packed_depth_bytes;
+} mpp41_matmul_config;
+
+/* MLPConfig, main.swift:62-66 (PackedNumericKernels.metal:13-17). */
+typedef struct mpp41_mlp_config {
+    uint32_t tokens, hidden, intermediate;
+} mpp41_mlp_config;
+
+/* One MLP row: down(swiglu(gate(x), up(x))). */
+typedef struct mpp41_mlp_desc {
+    uint32_t tokens, hidden, intermediate;
+    int32_t wfmt;      /* mpp41_wfmt of gate, up and down weights */
+    int32_t afmt;      /* mpp41_afmt of x */
+    int32_t epilogue;  /* mpp41_epilogue */
+    int32_t out_dtype; /* mpp41_dtype of out: F32, F16 or S32 */
+    uint32_t flags;    /* MPP41_MLP_* below */
+} mpp41_mlp_desc;
+
+/* Run the reference's four-dispatch structure (gate GEMM, up GEMM, SwiGLU
+ * kernel, down GEMM) instead of the fused path; scratch then also holds
+ * gate and up. */
+#define MPP41_MLP_UNFUSED 0x1u
+
+typedef struct mpp41_ctx mpp41_ctx;
+
+/* ---- context: replaces MTLCreateSystemDefaultDevice + makeLibrary +
+ *      makeCommandQueue (main.swift:90-105, 164-200) ---- */
+mpp41_status mpp41_create(int device, mpp41_ctx **out);
+void mpp41_destroy(mpp41_ctx *ctx);
+/* Message of the last failing call on this host thread. */
+const char *mpp41_last_error(void);
+const char *mpp41_status_string(mpp41_status s);
+/* "Device:" line of main.swift:95. */
+mpp41_status mpp41_device_name(mpp41_ctx *ctx, char *buf, size_t len);
+/* Launch on this cudaStream_t from now on (NULL = the context's own stream). */
+mpp41_status mpp41_set_stream(mpp41_ctx *ctx, void *cuda_stream);
+void *mpp41_get_stream(mpp41_ctx *ctx);
+/* Waits for the stream, then reports CUDA and device-side errors. */
+mpp41_status mpp41_synchronize(mpp41_ctx *ctx);
+/* Device address of the context's 32-bit device error word. */
+uint32_t *mpp41_device_error_word(mpp41_ctx *ctx);
+
+/* ---- buffers: replace device.makeBuffer / contents() ---- */
+mpp41_status mpp41_alloc(mpp41_ctx *ctx, size_t bytes, void **dev);
+mpp41_status mpp41_free(mpp41_ctx *ctx, void *dev);
+mpp41_status mpp41_upload(mpp41_ctx *ctx, void *dev, const void *host, size_t bytes);
+mpp41_status mpp41_download(mpp41_ctx *ctx, void *host, const void *dev, size_t bytes);
+mpp41_status mpp41_memset(mpp41_ctx *ctx, void *dev, int value, size_t bytes);
+
+/* ---- kernel registry: makeFunction(name:) != nil (main.swift:949-950).
+ *      Returns 1 if `name` (a reference kernel name) is implemented. ---- */
+int mpp41_has_kernel(const char *name);
+
+/* ---- packed formats: fp4_e2m1_roundtrip / fp8_e4m3_roundtrip /
+ *      fp8_e5m2_roundtrip (PackedNumericKernels.metal:35-96; host driver
+ *      run(testCase:) main.swift:202-262). in: 16 (E2M1) or 8 (FP8) floats;
+ *      packed: 8 bytes; out: unpacked floats. ---- */
+mpp41_status mpp41_roundtrip(mpp41_ctx *ctx, const char *kernel_name, const float *in, uint8_t *packed, float *out);
+/* Bulk pack / unpack. fmt: 0 = E2M1 (2 per byte, low nibble first),
+ * 1 = E4M3, 2 = E5M2. Round to nearest even, saturating. */
+mpp41_status mpp41_pack(mpp41_ctx *ctx, int fmt, const float *in, size_t n, uint8_t *packed);
+mpp41_status mpp41_unpack(mpp41_ctx *ctx, int fmt, const uint8_t *packed, size_t n, float *out);
+
+/* ---- MXFP4 dequant: mxfp4_dequant_native_half / mxfp4_dequant_lut_half
+ *      (MXFP4Kernels.metal:509-564; encodeMXFP4DequantMLP main.swift:2426-2469).
+ *      out: fp16 [rows][depth]. ---- */
+mpp41_status mpp41_dequant(mpp41_ctx *ctx, const char *kernel_name, const uint8_t *packed, const uint8_t *scales,
+                           void *out_half, uint32_t rows, uint32_t depth);
+
+/* ---- GEMM by reference kernel name: the matmul2d kernels of
+ *      MPPMLPKernels.metal:39-184 and MXFP4Kernels.metal:108-296 with the
+ *      encodeMPPMatmulDispatch / encodeMXFP4MatmulDispatch binding
+ *      (main.swift:2137-2170, 2724-2752): c[m][n] = a[m][k] * b[n][k]^T.
+ *      scales: [n][k/32] E8M0 for MXFP4 kernels, else NULL. ---- */
+mpp41_status mpp41_gemm(mpp41_ctx *ctx, const char *kernel_name, const void *a, const void *b, void *c, uint32_t m,
+                        uint32_t n, uint32_t k, const uint8_t *scales);
+
+/* ---- SwiGLU by reference kernel name (mpp_mlp_swiglu_*,
+ *      MPPMLPKernels.metal:186-257; encoder main.swift:2092-2100). ---- */
+mpp41_status mpp41_swiglu(mpp41_ctx *ctx, const char *kernel_name, const void *gate, const void *up, void *mid,
+                          const mpp41_mlp_config *cfg);
+
+/* ---- scalar rows of PackedNumericKernels.metal (half serial accumulate):
+ *      big matmul (runMatmulBenchmarkKernel main.swift:1715-1793) and the
+ *      scalar MLP (encodeMLP main.swift:2575-2634). ---- */
+mpp41_status mpp41_matmul_scalar(mpp41_ctx *ctx, const char *kernel_name, const void *a, const void *b, void *c,
+                                 const mpp41_matmul_config *cfg);
+mpp41_status mpp41_mlp_scalar(mpp41_ctx *ctx, const char *gate_kernel_name, const char *down_kernel_name,
+                              const void *x, const void *wg, const void *wu, void *mid, const void *wd, void *out,
+                              const mpp41_mlp_config *cfg);
+
+/* ---- the hot path: one MLP layer down(swiglu(gate(x), up(x))).
+ *      Replaces encodeMPPMLP (main.swift:2636-2722) and encodeMXFP4FusedMLP
+ *      (main.swift:2033-2135). Weights use the reference layouts ([n][k],
+ *      scales [n][k/32]); sg/su/sd are only read for MXFP4. scratch must hold
+ *      mpp41_mlp_scratch_bytes(desc) bytes (the fp16/fp32/int8 mid). ---- */
+size_t mpp41_mlp_scratch_bytes(const mpp41_mlp_desc *desc);
+mpp41_status mpp41_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const void *wg, const void *wu,
+                       const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *scratch,
+                       void *out);
+/* Fill a descriptor from a reference gate/up kernel name (e.g.
+ * "mxfp4_native_sp_h_f_n64", "mpp_mlp_h_i4_f_n128", "mpp_mlp_i8_i8_i32_n128")
+ * with the SwiGLU and output type the reference pairs with it in
+ * runMLPBenchmark (main.swift:945-1416). */
+mpp41_status mpp41_mlp_describe(const char *gate_kernel_name, uint32_t tokens, uint32_t hidden,
+                                uint32_t intermediate, mpp41_mlp_desc *desc);
+
+/* Timed run: `iterations` back-to-back layers captured in one CUDA graph
+ * (the analogue of one command buffer, main.swift:2062-2134); writes the GPU
+ * seconds of the timed replay (CUDA events) after one untimed warm-up. */
+mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const void *wg,
+                                 const void *wu, const void *wd, const uint8_t *sg, const uint8_t *su,
+                                 const uint8_t *sd, void *scratch, void *out, int iterations, double *gpu_seconds);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MPP41_H */

@@ -1,0 +1,42 @@
+// Internal launch interface shared by the .cu files of libmpp41.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace mpp41 {
+
+// Weight formats; values match enum mpp41_wfmt of include/mpp41.h.
+enum WFmt : int { W_F16 = 0, W_I8 = 1, W_I4 = 2, W_I2 = 3, W_FP4 = 4, W_E4M3 = 5, W_E5M2 = 6, W_MXFP4 = 7 };
+
+cudaError_t launch_pack(int fmt, const float *in, size_t n, uint8_t *out, cudaStream_t st);
+cudaError_t launch_unpack(int fmt, const uint8_t *in, size_t n, float *out, cudaStream_t st);
+cudaError_t launch_roundtrip(int fmt, const float *in, uint8_t *packed, float *out, cudaStream_t st);
+cudaError_t launch_dequant(int lut, const uint8_t *packed, const uint8_t *scales, void *out, uint32_t rows,
+                           uint32_t depth, cudaStream_t st);
+cudaError_t launch_swiglu(int kind, const void *gate, const void *up, void *mid, size_t n, cudaStream_t st);
+cudaError_t launch_scalar_mlp(int wfmt, uint32_t T, uint32_t H, uint32_t I, const void *x, const void *wg,
+                              const void *wu, void *mid, const void *wd, void *out, cudaStream_t st);
+cudaError_t launch_scalar_matmul(int kind, uint32_t M, uint32_t N, uint32_t K, const void *a, const void *b, void *c,
+                                 cudaStream_t st);
+
+// Quantized-weight tensor-core GEMM (mpp41_wq_gemm.cuh). epi is an Epi
+// value; b1/s1 are the up-projection operands of the SwiGLU pair epilogues.
+struct WqLaunch {
+    int wfmt;
+    int epi;
+    const void *a;          // fp16 [M][K]
+    const void *b0;
+    const void *b1;
+    const uint8_t *s0;
+    const uint8_t *s1;
+    void *out;
+    uint32_t M, N, K, ldc;
+    uint32_t splits;        // split-K factor (EPI_ATOMIC_F32 only)
+    uint32_t *err;
+};
+// Returns 0 on success, 1 for an unsupported combination/shape, 2 for a CUDA error.
+int launch_wq_gemm(const WqLaunch &L, cudaStream_t st, const char **why);
+
+}  // namespace mpp41

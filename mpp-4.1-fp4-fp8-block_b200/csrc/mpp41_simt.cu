@@ -1,0 +1,371 @@
+// SIMT kernels of libmpp41 (sm_100a): packed-format pack/unpack, the
+// materialised MXFP4 dequant kernels, the standalone SwiGLU kernels and the
+// reference's scalar half-accumulate rows. These are byte/elementwise work
+// bound by HBM (or, for the scalar rows, deliberately serial to reproduce the
+// reference bit for bit), so they use wide coalesced loads, not tensor cores.
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "mpp41_device.cuh"
+#include "mpp41_internal.h"
+
+namespace mpp41 {
+
+// ------------------------------------------------------------------ codecs
+// Hardware conversions: cvt.rn.satfinite.{e2m1x2,e4m3x2,e5m2x2}.f32 round to
+// nearest even and saturate to the largest finite value, which is the
+// behaviour the reference's pack<> shows (main.swift:112-130).
+__device__ __forceinline__ uint32_t enc_e2m1x2(float lo, float hi)
+{
+    uint16_t r;
+    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}" : "=h"(r) : "f"(hi), "f"(lo));
+    return r & 0xFFu;
+}
+__device__ __forceinline__ uint32_t enc_e4m3x2(float lo, float hi)
+{
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ uint32_t enc_e5m2x2(float lo, float hi)
+{
+    uint16_t r;
+    asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ float2 dec_e2m1x2(uint32_t byte)
+{
+    uint32_t h2;
+    asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "r"(byte));
+    __half2 h = *reinterpret_cast<__half2 *>(&h2);
+    return __half22float2(h);
+}
+__device__ __forceinline__ float2 dec_e4m3x2(uint32_t two)
+{
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"((uint16_t)two));
+    __half2 h = *reinterpret_cast<__half2 *>(&h2);
+    return __half22float2(h);
+}
+__device__ __forceinline__ float2 dec_e5m2x2(uint32_t two)
+{
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h2) : "h"((uint16_t)two));
+    __half2 h = *reinterpret_cast<__half2 *>(&h2);
+    return __half22float2(h);
+}
+
+// Bulk pack: fmt 0 = E2M1 (2 per byte, low nibble = even index),
+// 1 = E4M3, 2 = E5M2. Each thread handles 8 inputs (two float4 loads).
+__global__ void pack_kernel(int fmt, const float *__restrict__ in, size_t n, uint8_t *__restrict__ out)
+{
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g * 8 < n; g += stride) {
+        const size_t base = g * 8;
+        float v[8];
+        if (base + 8 <= n && (reinterpret_cast<uintptr_t>(in) & 15u) == 0) {
+            const float4 a = reinterpret_cast<const float4 *>(in + base)[0];
+            const float4 b = reinterpret_cast<const float4 *>(in + base)[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+            for (int i = 0; i < 8; ++i) v[i] = (base + i < n) ? in[base + i] : 0.0f;
+        }
+        if (fmt == 0) {
+            uint32_t w = 0;
+            for (int i = 0; i < 4; ++i) w |= enc_e2m1x2(v[2 * i], v[2 * i + 1]) << (8 * i);
+            const size_t nb = (n + 1) / 2, ob = base / 2;
+            if (ob + 4 <= nb && (ob & 3) == 0) *reinterpret_cast<uint32_t *>(out + ob) = w;
+            else for (int i = 0; i < 4 && ob + i < nb; ++i) out[ob + i] = (uint8_t)(w >> (8 * i));
+        } else {
+            uint32_t w0 = 0, w1 = 0;
+            for (int i = 0; i < 2; ++i) {
+                const uint32_t a = fmt == 1 ? enc_e4m3x2(v[2 * i], v[2 * i + 1]) : enc_e5m2x2(v[2 * i], v[2 * i + 1]);
+                const uint32_t b = fmt == 1 ? enc_e4m3x2(v[4 + 2 * i], v[5 + 2 * i]) : enc_e5m2x2(v[4 + 2 * i], v[5 + 2 * i]);
+                w0 |= a << (16 * i);
+                w1 |= b << (16 * i);
+            }
+            if (base + 8 <= n && (reinterpret_cast<uintptr_t>(out) & 7u) == 0) {
+                *reinterpret_cast<uint2 *>(out + base) = make_uint2(w0, w1);
+            } else {
+                for (int i = 0; i < 8 && base + i < n; ++i) out[base + i] = (uint8_t)((i < 4 ? w0 : w1) >> (8 * (i & 3)));
+            }
+        }
+    }
+}
+
+__global__ void unpack_kernel(int fmt, const uint8_t *__restrict__ in, size_t n, float *__restrict__ out)
+{
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g * 8 < n; g += stride) {
+        const size_t base = g * 8;
+        float v[8];
+        if (fmt == 0) {
+            for (int i = 0; i < 4; ++i) {
+                const size_t bi = base / 2 + i;
+                const float2 f = (2 * bi < n) ? dec_e2m1x2(in[bi]) : make_float2(0.f, 0.f);
+                v[2 * i] = f.x; v[2 * i + 1] = f.y;
+            }
+        } else {
+            for (int i = 0; i < 4; ++i) {
+                const size_t bi = base + 2 * i;
+                const uint32_t two = (bi < n ? in[bi] : 0u) | ((bi + 1 < n ? in[bi + 1] : 0u) << 8);
+                const float2 f = fmt == 1 ? dec_e4m3x2(two) : dec_e5m2x2(two);
+                v[2 * i] = f.x; v[2 * i + 1] = f.y;
+            }
+        }
+        if (base + 8 <= n && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+            reinterpret_cast<float4 *>(out + base)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4 *>(out + base)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+            for (int i = 0; i < 8 && base + i < n; ++i) out[base + i] = v[i];
+        }
+    }
+}
+
+// fp4_e2m1_roundtrip / fp8_e4m3_roundtrip / fp8_e5m2_roundtrip
+// (PackedNumericKernels.metal:35-96): one thread, a vector of 16 (E2M1) or
+// 8 (FP8) values packed, stored, unpacked.
+__global__ void roundtrip_kernel(int fmt, const float *in, uint8_t *packed, float *out)
+{
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const int n = fmt == 0 ? 16 : 8;
+    for (int i = 0; i < n; i += 2) {
+        if (fmt == 0) {
+            const uint32_t b = enc_e2m1x2(in[i], in[i + 1]);
+            packed[i / 2] = (uint8_t)b;
+            const float2 f = dec_e2m1x2(b);
+            out[i] = f.x; out[i + 1] = f.y;
+        } else {
+            const uint32_t two = fmt == 1 ? enc_e4m3x2(in[i], in[i + 1]) : enc_e5m2x2(in[i], in[i + 1]);
+            packed[i] = (uint8_t)two;
+            packed[i + 1] = (uint8_t)(two >> 8);
+            const float2 f = fmt == 1 ? dec_e4m3x2(two) : dec_e5m2x2(two);
+            out[i] = f.x; out[i + 1] = f.y;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ dequant
+// mxfp4_dequant_native_half (MXFP4Kernels.metal:509-538): hardware E2M1
+// unpack of 16 nibbles per thread, times the E8M0 block scale, to fp16.
+// One 8-byte load in, one 32-byte store out per thread.
+__global__ void mxfp4_dequant_native_kernel(const uint8_t *__restrict__ packed, const uint8_t *__restrict__ scales,
+                                            __half *__restrict__ out, uint32_t rows, uint32_t depth)
+{
+    const uint32_t chunks = depth / 16;
+    const size_t total = (size_t)rows * chunks;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t row = (uint32_t)(i / chunks), chunk = (uint32_t)(i % chunks);
+        const uint2 w = *reinterpret_cast<const uint2 *>(packed + (size_t)row * (depth / 2) + chunk * 8);
+        const float s = e8m0_to_float(scales[(size_t)row * (depth / 32) + chunk / 2]);
+        uint32_t h[8];
+        for (int b = 0; b < 8; ++b) {
+            const float2 f = dec_e2m1x2(((b < 4 ? w.x : w.y) >> (8 * (b & 3))) & 0xFFu);
+            h[b] = half2_bits(f.x * s, f.y * s);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)row * depth + chunk * 16);
+        dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+        dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+    }
+}
+
+// mxfp4_dequant_lut_half (MXFP4Kernels.metal:543-564): nibble table lookup,
+// two values per thread as in the reference.
+__constant__ float kE2M1Lut[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+                                   -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+
+__global__ void mxfp4_dequant_lut_kernel(const uint8_t *__restrict__ packed, const uint8_t *__restrict__ scales,
+                                         __half *__restrict__ out, uint32_t rows, uint32_t depth)
+{
+    const uint32_t bpr = depth / 2;
+    const size_t total = (size_t)rows * bpr;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t row = (uint32_t)(i / bpr), bi = (uint32_t)(i % bpr), k = bi * 2;
+        const float s = e8m0_to_float(scales[(size_t)row * (depth / 32) + k / 32]);
+        const uint8_t b = packed[i];
+        *reinterpret_cast<uint32_t *>(out + (size_t)row * depth + k) = half2_bits(kE2M1Lut[b & 0xF] * s, kE2M1Lut[b >> 4] * s);
+    }
+}
+
+// ------------------------------------------------------------------ SwiGLU
+// mpp_mlp_swiglu_{float,half,half_from_half,i8}, MPPMLPKernels.metal:186-257.
+// Elementwise over [tokens][intermediate]. exp() is evaluated in double and
+// rounded to float, exactly as the CPU oracle does, so these kernels are
+// reproducible bit for bit from the same gate/up inputs.
+__device__ __forceinline__ float clamp20(float v) { return fminf(fmaxf(v, -20.0f), 20.0f); }
+
+__global__ void swiglu_kernel(int kind, const void *__restrict__ gate, const void *__restrict__ up,
+                              void *__restrict__ mid, size_t n)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        if (kind == 0) {
+            const float g = static_cast<const float *>(gate)[i], u = static_cast<const float *>(up)[i];
+            static_cast<float *>(mid)[i] = (g / (1.0f + (float)exp(-(double)g))) * u;
+        } else if (kind == 1 || kind == 2) {
+            float g, u;
+            if (kind == 1) { g = static_cast<const float *>(gate)[i]; u = static_cast<const float *>(up)[i]; }
+            else { g = __half2float(static_cast<const __half *>(gate)[i]); u = __half2float(static_cast<const __half *>(up)[i]); }
+            const float gs = clamp20(g * 0.0625f), us = u * 0.0625f;
+            static_cast<__half *>(mid)[i] = __float2half_rn((gs / (1.0f + (float)exp(-(double)gs))) * us);
+        } else {
+            const float gs = clamp20((float)static_cast<const int32_t *>(gate)[i] * 0.000244140625f);
+            const float us = (float)static_cast<const int32_t *>(up)[i] * 0.000244140625f;
+            // exp in double, rounded to float: reproducible bit for bit on the CPU side
+            const float value = (gs / (1.0f + (float)exp(-(double)gs))) * us * 32.0f;
+            static_cast<int8_t *>(mid)[i] = (int8_t)(int)rintf(fminf(fmaxf(value, -128.0f), 127.0f));
+        }
+    }
+}
+
+// ------------------------------------------------------------------ scalar rows
+// The reference's scalar kernels accumulate serially in half with fused
+// multiply-add (PackedNumericKernels.metal:98-832). They are format-validation
+// rows; reproducing them bit for bit needs the same serial order, so one
+// thread computes one output exactly as the reference does.
+__device__ __forceinline__ __half w_half(int wfmt, const void *w, uint32_t r, uint32_t depth, uint32_t k)
+{
+    const uint8_t *b = static_cast<const uint8_t *>(w);
+    switch (wfmt) {
+    case W_F16: return static_cast<const __half *>(w)[(size_t)r * depth + k];
+    case W_I8: return __int2half_rn((int)static_cast<const int8_t *>(w)[(size_t)r * depth + k]);
+    case W_I4: return __int2half_rn(((int)((b[(size_t)r * (depth / 2) + k / 2] >> ((k & 1) * 4)) & 0xF) ^ 8) - 8);
+    case W_I2: return __int2half_rn(((int)((b[(size_t)r * (depth / 4) + k / 4] >> ((k & 3) * 2)) & 0x3) ^ 2) - 2);
+    default: return __float2half_rn(kE2M1Lut[(b[(size_t)r * (depth / 2) + k / 2] >> ((k & 1) * 4)) & 0xF]);
+    }
+}
+
+__device__ __forceinline__ __half silu_half(__half v)
+{
+    const float x = __half2float(v);
+    return __float2half_rn(x / (1.0f + (float)exp(-(double)x)));
+}
+
+// half_*_mlp_gate_up_benchmark, PackedNumericKernels.metal:425-664
+__global__ void scalar_mlp_gate_up_kernel(int wfmt, uint32_t T, uint32_t H, uint32_t I, const __half *__restrict__ x,
+                                          const void *wg, const void *wu, __half *__restrict__ mid)
+{
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y * blockDim.y + threadIdx.y;
+    if (t >= T || c >= I) return;
+    __half gate = __float2half(0.0f), up = __float2half(0.0f);
+    for (uint32_t i = 0; i < H; ++i) {
+        const __half xv = x[(size_t)t * H + i];
+        gate = __hfma(xv, w_half(wfmt, wg, c, H, i), gate);
+        up = __hfma(xv, w_half(wfmt, wu, c, H, i), up);
+    }
+    mid[(size_t)t * I + c] = __hmul(silu_half(gate), up);
+}
+
+// half_*_mlp_down_benchmark, PackedNumericKernels.metal:666-832
+__global__ void scalar_mlp_down_kernel(int wfmt, uint32_t T, uint32_t H, uint32_t I, const __half *__restrict__ mid,
+                                       const void *wd, __half *__restrict__ out)
+{
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y * blockDim.y + threadIdx.y;
+    if (t >= T || c >= H) return;
+    __half acc = __float2half(0.0f);
+    for (uint32_t i = 0; i < I; ++i) acc = __hfma(mid[(size_t)t * I + i], w_half(wfmt, wd, c, I, i), acc);
+    out[(size_t)t * H + c] = acc;
+}
+
+// Big-matmul scalar rows, PackedNumericKernels.metal:98-423.
+// kind 0 fp4 x fp4 -> f32, 1 half x fp4 -> half, 2 half x int4 -> half,
+// 3 int8 x half -> half, 4 int4 x int4 -> int32.
+__global__ void scalar_matmul_kernel(int kind, uint32_t M, uint32_t N, uint32_t K, const void *a, const void *b, void *c)
+{
+    const uint32_t col = blockIdx.x * blockDim.x + threadIdx.x, row = blockIdx.y * blockDim.y + threadIdx.y;
+    if (row >= M || col >= N) return;
+    const uint8_t *ab = static_cast<const uint8_t *>(a), *bb = static_cast<const uint8_t *>(b);
+    const size_t idx = (size_t)row * N + col;
+    if (kind == 0) {
+        float acc = 0.0f;
+        for (uint32_t k = 0; k < K; ++k) {
+            const float av = kE2M1Lut[(ab[(size_t)row * (K / 2) + k / 2] >> ((k & 1) * 4)) & 0xF];
+            const float bv = kE2M1Lut[(bb[(size_t)col * (K / 2) + k / 2] >> ((k & 1) * 4)) & 0xF];
+            acc = fmaf(av, bv, acc);
+        }
+        static_cast<float *>(c)[idx] = acc;
+    } else if (kind == 1 || kind == 2) {
+        const __half *ah = static_cast<const __half *>(a);
+        __half acc = __float2half(0.0f);
+        for (uint32_t k = 0; k < K; ++k)
+            acc = __hfma(ah[(size_t)row * K + k], w_half(kind == 1 ? W_FP4 : W_I4, b, col, K, k), acc);
+        static_cast<__half *>(c)[idx] = acc;
+    } else if (kind == 3) {
+        const int8_t *ai = static_cast<const int8_t *>(a);
+        const __half *bh = static_cast<const __half *>(b);
+        __half acc = __float2half(0.0f);
+        for (uint32_t k = 0; k < K; ++k) acc = __hfma(__int2half_rn((int)ai[(size_t)row * K + k]), bh[(size_t)col * K + k], acc);
+        static_cast<__half *>(c)[idx] = acc;
+    } else {
+        int32_t acc = 0;
+        for (uint32_t k = 0; k < K; ++k) {
+            const int av = ((int)((ab[(size_t)row * (K / 2) + k / 2] >> ((k & 1) * 4)) & 0xF) ^ 8) - 8;
+            const int bv = ((int)((bb[(size_t)col * (K / 2) + k / 2] >> ((k & 1) * 4)) & 0xF) ^ 8) - 8;
+            acc += av * bv;
+        }
+        static_cast<int32_t *>(c)[idx] = acc;
+    }
+}
+
+// ------------------------------------------------------------------ launchers
+static unsigned grid_for(size_t work, int block)
+{
+    size_t g = (work + block - 1) / block;
+    const size_t cap = 148ull * 16;   // grid-stride beyond 16 CTAs per SM
+    return (unsigned)(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+cudaError_t launch_pack(int fmt, const float *in, size_t n, uint8_t *out, cudaStream_t st)
+{
+    pack_kernel<<<grid_for((n + 7) / 8, 256), 256, 0, st>>>(fmt, in, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_unpack(int fmt, const uint8_t *in, size_t n, float *out, cudaStream_t st)
+{
+    unpack_kernel<<<grid_for((n + 7) / 8, 256), 256, 0, st>>>(fmt, in, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_roundtrip(int fmt, const float *in, uint8_t *packed, float *out, cudaStream_t st)
+{
+    roundtrip_kernel<<<1, 32, 0, st>>>(fmt, in, packed, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequant(int lut, const uint8_t *packed, const uint8_t *scales, void *out, uint32_t rows,
+                           uint32_t depth, cudaStream_t st)
+{
+    if (lut)
+        mxfp4_dequant_lut_kernel<<<grid_for((size_t)rows * depth / 2, 256), 256, 0, st>>>(packed, scales,
+                                                                                      static_cast<__half *>(out), rows, depth);
+    else
+        mxfp4_dequant_native_kernel<<<grid_for((size_t)rows * depth / 16, 256), 256, 0, st>>>(packed, scales,
+                                                                                          static_cast<__half *>(out), rows, depth);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(int kind, const void *gate, const void *up, void *mid, size_t n, cudaStream_t st)
+{
+    swiglu_kernel<<<grid_for(n, 256), 256, 0, st>>>(kind, gate, up, mid, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scalar_mlp(int wfmt, uint32_t T, uint32_t H, uint32_t I, const void *x, const void *wg,
+                              const void *wu, void *mid, const void *wd, void *out, cudaStream_t st)
+{
+    const dim3 blk(16, 16);
+    scalar_mlp_gate_up_kernel<<<dim3((I + 15) / 16, (T + 15) / 16), blk, 0, st>>>(
+        wfmt, T, H, I, static_cast<const __half *>(x), wg, wu, static_cast<__half *>(mid));
+    scalar_mlp_down_kernel<<<dim3((H + 15) / 16, (T + 15) / 16), blk, 0, st>>>(
+        wfmt, T, H, I, static_cast<const __half *>(mid), wd, static_cast<__half *>(out));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scalar_matmul(int kind, uint32_t M, uint32_t N, uint32_t K, const void *a, const void *b, void *c,
+                                 cudaStream_t st)
+{
+    scalar_matmul_kernel<<<dim3((N + 15) / 16, (M + 15) / 16), dim3(16, 16), 0, st>>>(kind, M, N, K, a, b, c);
+    return cudaGetLastError();
+}
+
+}  // namespace mpp41

@@ -1,0 +1,129 @@
+// Host side of the quantized-weight tensor-core GEMM: TMA descriptor
+// encoding, template dispatch over (weight format, epilogue) and launch.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "mpp41_internal.h"
+#include "mpp41_wq_gemm.cuh"
+
+namespace mpp41 {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2D row-major tensor [rows][cols] of `elem`-byte elements, tile box {bc, br}.
+static bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols,
+                     uint64_t rows, uint32_t bc, uint32_t br, CUtensorMapSwizzle sw)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+    if ((cols * elem) % 16 != 0) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * elem};
+    const cuuint32_t box[2] = {bc, br};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int W, int BN, int E>
+static int launch_t(const WqLaunch &L, cudaStream_t st, const char **why)
+{
+    using Cfg = WqCfg<W, BN, E>;
+    WqGemmParams p;
+    memset(&p, 0, sizeof(p));
+    const uint32_t splits = (E == EPI_ATOMIC_F32) ? (L.splits ? L.splits : 1) : 1;
+    if (L.K % (kBK * splits) != 0) { *why = "K must be a multiple of 64 * split"; return 1; }
+    if (L.N % Cfg::kCols != 0) { *why = "N must be a multiple of the CTA column tile"; return 1; }
+    const uint32_t kps = L.K / splits;
+    if (!make_map(&p.tmap_a, L.a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.K, L.M, kBK, kBM,
+                  CU_TENSOR_MAP_SWIZZLE_128B)) {
+        *why = "activation tensor map (needs 16-byte aligned base, K % 8 == 0)";
+        return 1;
+    }
+    const uint32_t rows_box = Cfg::kPair ? BN / 2 : BN;
+    const void *bs[2] = {L.b0, L.b1};
+    CUtensorMap *maps[2] = {&p.tmap_b0, &p.tmap_b1};
+    for (int i = 0; i < (Cfg::kPair ? 2 : 1); ++i) {
+        bool ok;
+        if (Cfg::kDirect)
+            ok = make_map(maps[i], bs[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.K, L.N, kBK, rows_box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+        else
+            ok = make_map(maps[i], bs[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)L.K * wfmt_bits(W) / 8, L.N,
+                          Cfg::kRawRow, rows_box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!ok) { *why = "weight tensor map (needs 16-byte aligned base and row pitch)"; return 1; }
+    }
+    p.scales0 = L.s0;
+    p.scales1 = L.s1;
+    p.out = L.out;
+    p.M = L.M; p.N = L.N; p.K = L.K;
+    p.k_per_split = kps;
+    p.ldc = L.ldc;
+    p.err = L.err;
+    const uint32_t smem = Cfg::smem_bytes(kps);
+    if (smem > 227u * 1024u) { *why = "K range per CTA too large for shared memory"; return 1; }
+    static bool attr_set = false;   // per instantiation
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(wq_gemm_kernel<W, BN, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+            cudaSuccess) {
+            *why = "cudaFuncSetAttribute";
+            return 2;
+        }
+        attr_set = true;
+    }
+    const dim3 grid(L.N / Cfg::kCols, (L.M + kBM - 1) / kBM, splits);
+    wq_gemm_kernel<W, BN, E><<<grid, kThreads, smem, st>>>(p);
+    if (cudaGetLastError() != cudaSuccess) { *why = "kernel launch"; return 2; }
+    return 0;
+}
+
+template <int W>
+static int launch_w(const WqLaunch &L, cudaStream_t st, const char **why)
+{
+    switch (L.epi) {
+    case EPI_STORE_F32: return launch_t<W, 64, EPI_STORE_F32>(L, st, why);
+    case EPI_STORE_F16: return launch_t<W, 64, EPI_STORE_F16>(L, st, why);
+    case EPI_ATOMIC_F32: return launch_t<W, 64, EPI_ATOMIC_F32>(L, st, why);
+    case EPI_SWIGLU_FLOAT: return launch_t<W, 64, EPI_SWIGLU_FLOAT>(L, st, why);
+    case EPI_SWIGLU_HALF: return launch_t<W, 64, EPI_SWIGLU_HALF>(L, st, why);
+    case EPI_SWIGLU_HALF_H: return launch_t<W, 64, EPI_SWIGLU_HALF_H>(L, st, why);
+    default: *why = "unknown epilogue"; return 1;
+    }
+}
+
+int launch_wq_gemm(const WqLaunch &L, cudaStream_t st, const char **why)
+{
+    switch (L.wfmt) {
+    case W_F16: return launch_w<W_F16>(L, st, why);
+    case W_I8: return launch_w<W_I8>(L, st, why);
+    case W_I4: return launch_w<W_I4>(L, st, why);
+    case W_I2: return launch_w<W_I2>(L, st, why);
+    case W_FP4: return launch_w<W_FP4>(L, st, why);
+    case W_E4M3: return launch_w<W_E4M3>(L, st, why);
+    case W_E5M2: return launch_w<W_E5M2>(L, st, why);
+    case W_MXFP4: return launch_w<W_MXFP4>(L, st, why);
+    default: *why = "unknown weight format"; return 1;
+    }
+}
+
+}  // namespace mpp41

@@ -1,0 +1,230 @@
+"""Python binding of libmpp41 (the C ABI in include/mpp41.h).
+
+A thin ctypes layer that mirrors the reference probe's kernel interface:
+kernels are addressed by the reference's own names ("mxfp4_native_sp_h_f_n64",
+"mpp_mlp_h_i4_f_n128", "fp4_e2m1_roundtrip", ...), buffers are device
+pointers, and every failing call raises MPP41Error carrying the status code
+(the analogue of the reference's ProbeError, main.swift:5-38).
+
+Device memory is any object with a ``data_ptr()`` (a torch CUDA tensor) or an
+integer address. There is no CPU fallback: without the built library or a
+B200 every call fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+ROOT = os.path.dirname(PKG)
+LIB_PATH = os.path.join(PKG, "lib", "libmpp41.so")
+HEADER = os.path.join(ROOT, "include", "mpp41.h")
+
+OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED_SHAPE, ERR_NO_DEVICE, ERR_MISSING_KERNEL, ERR_OUT_OF_MEMORY, \
+    ERR_CUDA, ERR_TIMEOUT, ERR_BOUNDS, ERR_COMM = range(10)
+W_F16, W_I8, W_I4, W_I2, W_FP4, W_E4M3, W_E5M2, W_MXFP4 = range(8)
+A_F16, A_S8 = 0, 1
+SWIGLU_FLOAT, SWIGLU_HALF, SWIGLU_HALF_FROM_HALF, SWIGLU_I8 = range(4)
+F32, F16, S32, S8 = range(4)
+MLP_UNFUSED = 0x1
+FMT_E2M1, FMT_E4M3, FMT_E5M2 = 0, 1, 2
+
+
+class MPP41Error(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"mpp41 status {status}: {message}")
+        self.status = status
+
+
+class MatmulConfig(C.Structure):
+    _fields_ = [("rows", C.c_uint32), ("columns", C.c_uint32), ("depth", C.c_uint32),
+                ("packed_depth_bytes", C.c_uint32)]
+
+
+class MLPConfig(C.Structure):
+    _fields_ = [("tokens", C.c_uint32), ("hidden", C.c_uint32), ("intermediate", C.c_uint32)]
+
+
+class MLPDesc(C.Structure):
+    _fields_ = [("tokens", C.c_uint32), ("hidden", C.c_uint32), ("intermediate", C.c_uint32),
+                ("wfmt", C.c_int32), ("afmt", C.c_int32), ("epilogue", C.c_int32), ("out_dtype", C.c_int32),
+                ("flags", C.c_uint32)]
+
+
+_lib = None
+
+
+def build() -> str:
+    """Compile libmpp41.so in-tree (nvcc, sm_100a)."""
+    subprocess.run(["make", "-s", "-C", PKG, "-j8"], check=True)
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise MPP41Error(ERR_MISSING_KERNEL, f"{LIB_PATH} is not built; run make -C {PKG}")
+    L = C.CDLL(LIB_PATH)
+    vp, u32, st, sz = C.c_void_p, C.c_uint32, C.c_int, C.c_size_t
+    sigs = {
+        "mpp41_create": ([C.c_int, C.POINTER(vp)], st),
+        "mpp41_destroy": ([vp], None),
+        "mpp41_last_error": ([], C.c_char_p),
+        "mpp41_status_string": ([st], C.c_char_p),
+        "mpp41_device_name": ([vp, C.c_char_p, sz], st),
+        "mpp41_set_stream": ([vp, vp], st),
+        "mpp41_get_stream": ([vp], vp),
+        "mpp41_synchronize": ([vp], st),
+        "mpp41_device_error_word": ([vp], vp),
+        "mpp41_alloc": ([vp, sz, C.POINTER(vp)], st),
+        "mpp41_free": ([vp, vp], st),
+        "mpp41_upload": ([vp, vp, vp, sz], st),
+        "mpp41_download": ([vp, vp, vp, sz], st),
+        "mpp41_memset": ([vp, vp, C.c_int, sz], st),
+        "mpp41_has_kernel": ([C.c_char_p], C.c_int),
+        "mpp41_roundtrip": ([vp, C.c_char_p, vp, vp, vp], st),
+        "mpp41_pack": ([vp, C.c_int, vp, sz, vp], st),
+        "mpp41_unpack": ([vp, C.c_int, vp, sz, vp], st),
+        "mpp41_dequant": ([vp, C.c_char_p, vp, vp, vp, u32, u32], st),
+        "mpp41_gemm": ([vp, C.c_char_p, vp, vp, vp, u32, u32, u32, vp], st),
+        "mpp41_swiglu": ([vp, C.c_char_p, vp, vp, vp, C.POINTER(MLPConfig)], st),
+        "mpp41_matmul_scalar": ([vp, C.c_char_p, vp, vp, vp, C.POINTER(MatmulConfig)], st),
+        "mpp41_mlp_scalar": ([vp, C.c_char_p, C.c_char_p, vp, vp, vp, vp, vp, vp, C.POINTER(MLPConfig)], st),
+        "mpp41_mlp_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
+        "mpp41_mlp": ([vp, C.POINTER(MLPDesc)] + [vp] * 9, st),
+        "mpp41_mlp_describe": ([C.c_char_p, u32, u32, u32, C.POINTER(MLPDesc)], st),
+        "mpp41_mlp_benchmark": ([vp, C.POINTER(MLPDesc)] + [vp] * 9 + [C.c_int, C.POINTER(C.c_double)], st),
+    }
+    for name, (args, res) in sigs.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = L
+    return L
+
+
+def declared_symbols() -> list[str]:
+    """Every function the public header declares."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(mpp41_[a-z0-9_]+)\s*\(", text)))
+
+
+def _ptr(x):
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _check(status: int):
+    if status != OK:
+        msg = lib().mpp41_last_error()
+        raise MPP41Error(status, msg.decode() if msg else "")
+
+
+def has_kernel(name: str) -> bool:
+    return bool(lib().mpp41_has_kernel(name.encode()))
+
+
+def describe(gate_kernel: str, tokens: int, hidden: int, intermediate: int) -> MLPDesc:
+    d = MLPDesc()
+    _check(lib().mpp41_mlp_describe(gate_kernel.encode(), tokens, hidden, intermediate, C.byref(d)))
+    return d
+
+
+def mlp_desc(tokens, hidden, intermediate, wfmt=W_MXFP4, afmt=A_F16, epilogue=SWIGLU_HALF, out_dtype=F32,
+             flags=0) -> MLPDesc:
+    return MLPDesc(tokens, hidden, intermediate, wfmt, afmt, epilogue, out_dtype, flags)
+
+
+def scratch_bytes(desc: MLPDesc) -> int:
+    return lib().mpp41_mlp_scratch_bytes(C.byref(desc))
+
+
+class Context:
+    """One libmpp41 context (device + stream + device error word)."""
+
+    def __init__(self, device: int = 0):
+        L = lib()
+        h = C.c_void_p()
+        _check(L.mpp41_create(device, C.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if self.h:
+            lib().mpp41_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- plumbing
+    def device_name(self) -> str:
+        buf = C.create_string_buffer(256)
+        _check(lib().mpp41_device_name(self.h, buf, 256))
+        return buf.value.decode()
+
+    def set_stream(self, stream_handle: int | None):
+        _check(lib().mpp41_set_stream(self.h, stream_handle))
+
+    def synchronize(self):
+        _check(lib().mpp41_synchronize(self.h))
+
+    def error_word_ptr(self) -> int:
+        return lib().mpp41_device_error_word(self.h)
+
+    # -- kernels
+    def roundtrip(self, kernel: str, inp, packed, out):
+        _check(lib().mpp41_roundtrip(self.h, kernel.encode(), _ptr(inp), _ptr(packed), _ptr(out)))
+
+    def pack(self, fmt: int, inp, n: int, packed):
+        _check(lib().mpp41_pack(self.h, fmt, _ptr(inp), n, _ptr(packed)))
+
+    def unpack(self, fmt: int, packed, n: int, out):
+        _check(lib().mpp41_unpack(self.h, fmt, _ptr(packed), n, _ptr(out)))
+
+    def dequant(self, kernel: str, packed, scales, out, rows: int, depth: int):
+        _check(lib().mpp41_dequant(self.h, kernel.encode(), _ptr(packed), _ptr(scales), _ptr(out), rows, depth))
+
+    def gemm(self, kernel: str, a, b, c, m: int, n: int, k: int, scales=None):
+        _check(lib().mpp41_gemm(self.h, kernel.encode(), _ptr(a), _ptr(b), _ptr(c), m, n, k, _ptr(scales)))
+
+    def swiglu(self, kernel: str, gate, up, mid, tokens: int, hidden: int, intermediate: int):
+        cfg = MLPConfig(tokens, hidden, intermediate)
+        _check(lib().mpp41_swiglu(self.h, kernel.encode(), _ptr(gate), _ptr(up), _ptr(mid), C.byref(cfg)))
+
+    def matmul_scalar(self, kernel: str, a, b, c, rows: int, columns: int, depth: int):
+        cfg = MatmulConfig(rows, columns, depth, depth // 2)
+        _check(lib().mpp41_matmul_scalar(self.h, kernel.encode(), _ptr(a), _ptr(b), _ptr(c), C.byref(cfg)))
+
+    def mlp_scalar(self, gate_kernel: str, down_kernel: str, x, wg, wu, mid, wd, out, tokens, hidden, intermediate):
+        cfg = MLPConfig(tokens, hidden, intermediate)
+        _check(lib().mpp41_mlp_scalar(self.h, gate_kernel.encode(), down_kernel.encode(), _ptr(x), _ptr(wg),
+                                      _ptr(wu), _ptr(mid), _ptr(wd), _ptr(out), C.byref(cfg)))
+
+    def mlp(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out):
+        _check(lib().mpp41_mlp(self.h, C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(wd), _ptr(sg), _ptr(su),
+                               _ptr(sd), _ptr(scratch), _ptr(out)))
+
+    def mlp_benchmark(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out, iterations: int) -> float:
+        secs = C.c_double()
+        _check(lib().mpp41_mlp_benchmark(self.h, C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(wd), _ptr(sg),
+                                         _ptr(su), _ptr(sd), _ptr(scratch), _ptr(out), iterations,
+                                         C.byref(secs)))
+        return secs.value

@@ -600,3 +600,17 @@ uint64_t orc_sample_half_raw_sum(const uint16_t *p, size_t count, int *samples)
     if (samples) *samples = n;
     return sum;
 }
+
+/* Elementwise SwiGLU over n elements; kind as the standalone kernels:
+ * 0 float->float, 1 float->half, 2 half->half, 3 int32->int8. */
+void orc_swiglu_array(int kind, const void *gate, const void *up, void *mid, size_t n)
+{
+    for (size_t i = 0; i < n; ++i) {
+        switch (kind) {
+        case 0: ((float *)mid)[i] = orc_swiglu_float(((const float *)gate)[i], ((const float *)up)[i]); break;
+        case 1: ((uint16_t *)mid)[i] = orc_swiglu_half(((const float *)gate)[i], ((const float *)up)[i]); break;
+        case 2: ((uint16_t *)mid)[i] = orc_swiglu_half_from_half(((const uint16_t *)gate)[i], ((const uint16_t *)up)[i]); break;
+        default: ((int8_t *)mid)[i] = orc_swiglu_i8(((const int32_t *)gate)[i], ((const int32_t *)up)[i]); break;
+        }
+    }
+}

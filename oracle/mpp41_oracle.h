@@ -70,6 +70,8 @@ float orc_swiglu_float(float g, float u);
 uint16_t orc_swiglu_half(float g, float u);
 uint16_t orc_swiglu_half_from_half(uint16_t g, uint16_t u);
 int8_t orc_swiglu_i8(int32_t g, int32_t u);
+/* elementwise: kind 0 float->float, 1 float->half, 2 half->half, 3 int32->int8 */
+void orc_swiglu_array(int kind, const void *gate, const void *up, void *mid, size_t n);
 
 /* ---- whole MLP rows ----
  * act: 0 = fp16 x, 1 = int8 x. epi: 0 = swiglu_float (fp32 mid),

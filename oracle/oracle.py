@@ -69,6 +69,7 @@ def lib() -> C.CDLL:
         L.orc_scalar_matmul.argtypes = [C.c_int, u32, u32, u32, vp, vp, vp]
         L.orc_half_fma.argtypes = [C.c_uint16] * 3
         L.orc_half_fma.restype = C.c_uint16
+        L.orc_swiglu_array.argtypes = [C.c_int, vp, vp, vp, sz]
         L.orc_swiglu_i8.argtypes = [C.c_int32, C.c_int32]
         L.orc_swiglu_i8.restype = C.c_int8
         L.orc_e2m1_encode.argtypes = [C.c_float]
@@ -156,6 +157,14 @@ def mlp(act, wfmt, epi, out_kind, T, H, I, x, wg, wu, wd, sg=None, su=None, sd=N
                   _p(np.ascontiguousarray(wg)), _p(np.ascontiguousarray(wu)),
                   _p(np.ascontiguousarray(wd)), *ps, _p(mid), _p(out))
     return mid, out
+
+
+def swiglu(kind: int, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """Standalone SwiGLU kernels (MPPMLPKernels.metal:186-257), elementwise."""
+    gate, up = np.ascontiguousarray(gate), np.ascontiguousarray(up)
+    out = np.empty(gate.shape, {0: np.float32, 1: np.float16, 2: np.float16, 3: np.int8}[kind])
+    lib().orc_swiglu_array(kind, _p(gate), _p(up), _p(out), gate.size)
+    return out
 
 
 def mlp_mxfp4_cpu(T, H, I, x, wg, wu, wd, sg, su, sd, nthreads=0, t0=0, t1=None):

@@ -20,3 +20,37 @@ def golden():
     import json
     with open(os.path.join(ROOT, "tests", "golden", "reference_kats.json")) as f:
         return json.load(f)
+
+
+@pytest.fixture(scope="session")
+def ctx():
+    """libmpp41 context on cuda:0, launching on torch's current stream."""
+    import torch
+    import mpp41
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test collected without a CUDA device")
+    c = mpp41.Context(0)
+    c.set_stream(torch.cuda.current_stream().cuda_stream)
+    yield c
+    c.close()
+
+
+def to_dev(a):
+    """numpy -> CUDA tensor with the same bytes."""
+    import numpy as np
+    import torch
+    a = np.ascontiguousarray(a)
+    t = torch.from_numpy(a.view(np.uint8).reshape(-1).copy()).cuda()
+    return t
+
+
+def from_dev(t, dtype, shape):
+    import numpy as np
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy().view(dtype).reshape(shape)
+
+
+def empty_dev(nbytes):
+    import torch
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device="cuda")
