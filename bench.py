@@ -1,0 +1,357 @@
+"""Benchmark of the MXFP4 fused MLP hot path on B200 (one process per GPU).
+
+Workload: one MLP layer down(SiLU(gate(x)) * up(x)) with
+tokens=128, hidden=1024, intermediate=4096; x ~ N(0,1) fp16; gate/up/down
+weights ~ N(0, 0.02) quantized on the GPU to OCP MXFP4 (E2M1 + E8M0 per 32
+along K); fp32 accumulation, SiLU(gate)*up in fp32, fp16 output. A step is one
+layer. Dequantisation runs inside every step (the weights stay packed in HBM).
+
+Timed region: exactly K steps, captured as CUDA graphs and replayed, with 24
+distinct weight/activation sets rotated step by step (161 MB > the 126 MB L2),
+bracketed by a barrier and cuda synchronize, CUDA events on the launching
+stream, max over ranks. N > 1 runs N independent replicas (the layer is
+single-GPU sized; weak scaling, no collective in the data path).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+--impl reference times the CPU restatement of the reference's arithmetic
+(oracle/, the reference itself is Swift + Metal and cannot run here) on all
+host cores for the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mpp-4.1-fp4-fp8-block_b200")
+sys.path[:0] = [PKG, os.path.join(ROOT, "oracle")]
+
+T, H, I = 128, 1024, 4096
+FLOPS_PER_LAYER = 2.0 * 3 * T * H * I                      # main.swift:2763-2769 (2 * 3 * T * H * I)
+FLOPS_GATE_UP = 2.0 * 2 * T * H * I
+FLOPS_DOWN = 2.0 * T * H * I
+# algorithmic bytes per layer: packed weights + scales + x + out (fp16); mid stays on chip / in L2
+BYTES_W = 3 * H * I // 2 + 3 * H * I // 32
+BYTES_LAYER = BYTES_W + T * H * 2 + T * H * 2
+ROTATE = 24
+METRIC = "MXFP4 fused-MLP µs/layer & TFLOP/s (% of roofline) at 1/2/4/8 B200"
+# DRAM bytes per launch of the gate/up kernel from one ncu capture of this
+# workload (profiles/mxfp4_gate_up_swiglu_t128_h1024_i4096.md); None until captured.
+NCU_TRAFFIC_GATE_UP = None
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", default="mpp41", choices=["mpp41", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def reference_arm(args, rank):
+    """CPU restatement of the reference path (oracle), all host threads."""
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle as O
+    d = O.baseline_mlp_inputs(T, H, I)
+    x = d["x"].view(np.uint16)
+    run = lambda: O.mlp_mxfp4_cpu(T, H, I, x, d["wg"], d["wu"], d["wd"], d["sg"], d["su"], d["sd"], plain=True)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, nthr = run()
+    dt = time.perf_counter() - t0
+    tflops = FLOPS_PER_LAYER * args.steps / dt / 1e12
+    line = {"metric": METRIC, "value": tflops, "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+            "us_per_layer": dt * 1e6 / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "mxfp4_mlp_t128_h1024_i4096 (BASELINE config 0)", "tokens": T, "hidden": H,
+                       "intermediate": I},
+            "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": nthr, "kind": "port",
+                             "sample": f"{args.steps} full layers (T=128) on {nthr} threads"},
+            "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference is Swift + Metal 4.1 (Apple M5); its arithmetic is timed through the C "
+                    "restatement in oracle/cpu_baseline.c"}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(host, seconds):
+    import numpy as np
+    import oracle as O
+    x = host["x"].view(np.uint16)
+    args = (T, H, I, x, host["wg"], host["wu"], host["wd"], host["sg"], host["su"], host["sd"])
+    O.mlp_mxfp4_cpu(*args, plain=True)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        _, nthr = O.mlp_mxfp4_cpu(*args, plain=True)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": FLOPS_PER_LAYER * n / dt / 1e12, "unit": "TFLOP/s", "cores": nthr, "kind": "port",
+            "sample": f"{n} full layers (T=128, H=1024, I=4096) in {dt:.1f} s on {nthr} OpenMP threads, "
+                      f"oracle/cpu_baseline.c"}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    import numpy as np
+    import torch
+
+    import mpp41
+    import oracle as O
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    stream = torch.cuda.Stream()          # graphs cannot be captured on the legacy default stream
+    torch.cuda.set_stream(stream)
+    ctx = mpp41.Context(local)
+    ctx.set_stream(stream.cuda_stream)
+
+    # ---- weights: 24 sets, N(0, 0.02) fp32 quantized on the GPU (OCP MXFP4)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1234 + rank)
+    sets = []
+    for r in range(ROTATE):
+        s = {}
+        for name, (rows, depth) in (("g", (I, H)), ("u", (I, H)), ("d", (H, I))):
+            w = torch.randn(rows, depth, device="cuda", generator=gen) * 0.02
+            s["w" + name] = torch.empty(rows * depth // 2, dtype=torch.uint8, device="cuda")
+            s["s" + name] = torch.empty(rows * depth // 32, dtype=torch.uint8, device="cuda")
+            ctx.quantize_mxfp4(w, rows, depth, s["w" + name], s["s" + name])
+            del w
+        s["x"] = torch.randn(T, H, device="cuda", generator=gen).half()
+        s["out"] = torch.empty(T, H, dtype=torch.float16, device="cuda")
+        sets.append(s)
+    desc = mpp41.mlp_desc(T, H, I, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F16)
+    scratch = torch.empty(mpp41.scratch_bytes(desc), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+
+    def layer(s):
+        ctx.mlp(desc, s["x"], s["wg"], s["wu"], s["wd"], s["sg"], s["su"], s["sd"], scratch, s["out"])
+
+    def gate_up(s):
+        ctx.mlp_gate_up(desc, s["x"], s["wg"], s["wu"], s["sg"], s["su"], scratch, None)
+
+    def down(s):
+        ctx.mlp_down(desc, scratch, s["wd"], s["sd"], s["out"], prepared=True)
+
+    def capture(fn, n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                fn(sets[i % ROTATE])
+        return g
+
+    # correctness gate before timing: set 0 against the oracle (rank 0)
+    if rank == 0:
+        layer(sets[0])
+        ctx.synchronize()
+        host = {k: sets[0][k].cpu().numpy() for k in ("x", "wg", "wu", "wd", "sg", "su", "sd")}
+        host["x"] = host["x"].astype(np.float16)
+        for k in ("wg", "wu"):
+            host[k] = host[k].reshape(I, H // 2)
+        host["wd"] = host["wd"].reshape(H, I // 2)
+        host["sg"], host["su"] = host["sg"].reshape(I, H // 32), host["su"].reshape(I, H // 32)
+        host["sd"] = host["sd"].reshape(H, I // 32)
+        _, ref = O.mlp(0, O.W_MXFP4, 4, 1, T, H, I, host["x"].view(np.uint16), host["wg"], host["wu"], host["wd"],
+                       host["sg"], host["su"], host["sd"])
+        got = sets[0]["out"].float().cpu().numpy()
+        rel = float(np.linalg.norm(got - ref.astype(np.float32)) / np.linalg.norm(ref.astype(np.float32)))
+        if not rel <= 1e-3:
+            raise SystemExit(f"bench: output differs from the oracle (rel {rel:.3e})")
+
+    # ---- warm-up (untimed), graph capture
+    chunk = ROTATE
+    g_full = capture(layer, chunk)
+    tail = args.steps % chunk
+    g_tail = capture(layer, tail) if tail else None
+    for _ in range(max(1, args.warmup // chunk)):
+        g_full.replay()
+    for i in range(args.warmup % chunk):
+        layer(sets[i % ROTATE])
+    torch.cuda.synchronize()
+
+    # ---- timed region: exactly K steps
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.2)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps // chunk):
+        g_full.replay()
+    if g_tail is not None:
+        g_tail.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_layer = ms * 1e3 / args.steps
+    value = world * FLOPS_PER_LAYER * args.steps / (ms * 1e-3) / 1e12
+
+    # ---- per-kernel device time (same rotation) for the roofline
+    def kernel_us(fn, n=ROTATE * 20):
+        g = capture(fn, ROTATE)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n // ROTATE):
+            g.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1e3 / n
+
+    layer(sets[0])
+    us_gu = kernel_us(gate_up)
+    us_dn = kernel_us(down)
+    hbm, tflops_peak, peak_src = load_peaks()
+    dominant = "gate_up" if us_gu >= us_dn else "down"
+    flops_dom = FLOPS_GATE_UP if dominant == "gate_up" else FLOPS_DOWN
+    achieved = flops_dom / ((us_gu if dominant == "gate_up" else us_dn) * 1e-6) / 1e12
+    roofline = {"bound": "tensor", "kernel": f"wq_gemm_kernel ({dominant})", "achieved": achieved,
+                "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
+                "peak_source": f"bf16 dense burst, {peak_src} (MEASURED_PEAKS.json)",
+                "traffic": NCU_TRAFFIC_GATE_UP if dominant == "gate_up" else None,
+                "kernel_us": {"gate_up_swiglu": us_gu, "down_splitk": us_dn},
+                "layer_floor_us": {"hbm": BYTES_LAYER / (hbm * 1e9) * 1e6,
+                                   "tensor_f16": FLOPS_PER_LAYER / (tflops_peak * 1e12) * 1e6},
+                "layer_frac_of_tensor_floor": (FLOPS_PER_LAYER / (tflops_peak * 1e12) * 1e6) / us_layer}
+
+    # ---- end to end through the C ABI with host buffers (pinned), per step:
+    # H2D of x, the layer, D2H of the fp16 output
+    e2e_steps = min(args.steps, 2000)
+    x_host = [sets[i]["x"].cpu().pin_memory() for i in range(ROTATE)]
+    out_host = torch.empty(T, H, dtype=torch.float16).pin_memory()
+    xd = torch.empty(T, H, dtype=torch.float16, device="cuda")
+    for i in range(20):
+        xd.copy_(x_host[i % ROTATE], non_blocking=True)
+        s = dict(sets[i % ROTATE], x=xd)
+        layer(s)
+        out_host.copy_(s["out"], non_blocking=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(e2e_steps):
+        xd.copy_(x_host[i % ROTATE], non_blocking=True)
+        s = dict(sets[i % ROTATE], x=xd)
+        layer(s)
+        out_host.copy_(s["out"], non_blocking=True)
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": world * FLOPS_PER_LAYER * e2e_steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "us_per_layer": e2e_ms * 1e3 / e2e_steps, "steps": e2e_steps,
+           "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2}
+
+    if rank == 0:
+        base = cpu_baseline(host, args.cpu_seconds) if world == 1 else None
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": us_layer / 1e3, "us_per_layer": us_layer,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                "data": "synthetic (x ~ N(0,1), W ~ N(0,0.02) quantized OCP MXFP4 on the GPU)",
+                "config": {"workload": "mxfp4_mlp_t128_h1024_i4096 (BASELINE config 0)", "tokens": T,
+                           "hidden": H, "intermediate": I, "weights": "MXFP4 (E2M1 + E8M0/32)",
+                           "compute": "W4A16: in-CTA dequant to fp16, tcgen05 kind::f16, fp32 TMEM accum",
+                           "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                           "l2": f"rotating {ROTATE} weight/activation sets ({ROTATE * BYTES_LAYER / 1e6:.0f} MB)"
+                                 " > 126 MB L2"},
+                "roofline": roofline, "e2e": e2e, "gpu_launches": 2 * args.steps, "clocks": clocks,
+                "oracle_rel_err": rel}
+        if base is not None:
+            line["cpu_baseline"] = base
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -61,7 +61,9 @@ typedef enum mpp41_epilogue {
     MPP41_SWIGLU_FLOAT = 0,          /* mpp_mlp_swiglu_float: fp32 mid */
     MPP41_SWIGLU_HALF = 1,           /* mpp_mlp_swiglu_half: /16, clamp 20, fp16 mid */
     MPP41_SWIGLU_HALF_FROM_HALF = 2, /* mpp_mlp_swiglu_half_from_half: fp16 gate/up */
-    MPP41_SWIGLU_I8 = 3              /* mpp_mlp_swiglu_i8: int8 mid */
+    MPP41_SWIGLU_I8 = 3,             /* mpp_mlp_swiglu_i8: int8 mid */
+    MPP41_SWIGLU_FP32 = 4            /* silu(g) * u in fp32 without the /16 prescale, fp16 mid
+                                        (no reference kernel) */
 } mpp41_epilogue;
 
 typedef enum mpp41_dtype { MPP41_F32 = 0, MPP41_F16 = 1, MPP41_S32 = 2, MPP41_S8 = 3 } mpp41_dtype;
@@ -102,7 +104,8 @@ const char *mpp41_last_error(void);
 const char *mpp41_status_string(mpp41_status s);
 /* "Device:" line of main.swift:95. */
 mpp41_status mpp41_device_name(mpp41_ctx *ctx, char *buf, size_t len);
-/* Launch on this cudaStream_t from now on (NULL = the context's own stream). */
+/* Launch on this cudaStream_t from now on. NULL selects the CUDA legacy
+ * default stream; a new context starts on its own non-blocking stream. */
 mpp41_status mpp41_set_stream(mpp41_ctx *ctx, void *cuda_stream);
 void *mpp41_get_stream(mpp41_ctx *ctx);
 /* Waits for the stream, then reports CUDA and device-side errors. */
@@ -145,6 +148,14 @@ mpp41_status mpp41_dequant(mpp41_ctx *ctx, const char *kernel_name, const uint8_
 mpp41_status mpp41_gemm(mpp41_ctx *ctx, const char *kernel_name, const void *a, const void *b, void *c, uint32_t m,
                         uint32_t n, uint32_t k, const uint8_t *scales);
 
+/* ---- OCP-MX quantizer (no reference counterpart: the reference draws random
+ *      packed bytes, main.swift:2785-2793): fp32 w [rows][depth] ->
+ *      E2M1 packed [rows][depth/2] + E8M0 scales [rows][depth/32], shared
+ *      exponent floor(log2(amax)) - 2, elements round-to-nearest-even with
+ *      saturation. depth % 32 == 0; w 16-byte aligned. ---- */
+mpp41_status mpp41_quantize_mxfp4(mpp41_ctx *ctx, const float *w, uint32_t rows, uint32_t depth, uint8_t *packed,
+                                  uint8_t *scales);
+
 /* ---- SwiGLU by reference kernel name (mpp_mlp_swiglu_*,
  *      MPPMLPKernels.metal:186-257; encoder main.swift:2092-2100). ---- */
 mpp41_status mpp41_swiglu(mpp41_ctx *ctx, const char *kernel_name, const void *gate, const void *up, void *mid,
@@ -163,11 +174,22 @@ mpp41_status mpp41_mlp_scalar(mpp41_ctx *ctx, const char *gate_kernel_name, cons
  *      Replaces encodeMPPMLP (main.swift:2636-2722) and encodeMXFP4FusedMLP
  *      (main.swift:2033-2135). Weights use the reference layouts ([n][k],
  *      scales [n][k/32]); sg/su/sd are only read for MXFP4. scratch must hold
- *      mpp41_mlp_scratch_bytes(desc) bytes (the fp16/fp32/int8 mid). ---- */
+ *      mpp41_mlp_scratch_bytes(desc) bytes: the fp16/fp32/int8 mid, then for
+ *      fp16 output the split-K fp32 workspace and tile counters. ---- */
 size_t mpp41_mlp_scratch_bytes(const mpp41_mlp_desc *desc);
 mpp41_status mpp41_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const void *wg, const void *wu,
                        const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *scratch,
                        void *out);
+/* The two stages of mpp41_mlp, for callers that place their own work (or a
+ * collective) between them. mpp41_mlp_gate_up writes mid = swiglu(x Wg^T,
+ * x Wu^T) to the start of `scratch` and clears what the split-K down
+ * projection accumulates into (`out` for fp32 output, may be NULL otherwise).
+ * mpp41_mlp_down computes out = mid Wd^T from the same scratch; pass
+ * prepared = 1 when mpp41_mlp_gate_up ran before it on the same stream. */
+mpp41_status mpp41_mlp_gate_up(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const void *wg,
+                               const void *wu, const uint8_t *sg, const uint8_t *su, void *scratch, void *out);
+mpp41_status mpp41_mlp_down(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, void *scratch, const void *wd,
+                            const uint8_t *sd, void *out, int prepared);
 /* Fill a descriptor from a reference gate/up kernel name (e.g.
  * "mxfp4_native_sp_h_f_n64", "mpp_mlp_h_i4_f_n128", "mpp_mlp_i8_i8_i32_n128")
  * with the SwiGLU and output type the reference pairs with it in

@@ -143,6 +143,36 @@ int mid_bytes_per_elem(int epilogue)
     return epilogue == MPP41_SWIGLU_FLOAT ? 4 : (epilogue == MPP41_SWIGLU_I8 ? 1 : 2);
 }
 
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// split-K factor of the down projection (1 = plain store)
+uint32_t down_splits(const mpp41_mlp_desc *d)
+{
+    return pick_splits((d->hidden / 64) * ((d->tokens + 127) / 128), d->intermediate);
+}
+
+// Scratch layout: [mid][fp32 workspace T x H][tile counters] (the last two
+// only for fp16 output with split-K).
+struct ScratchLayout {
+    size_t mid_bytes, ws_off, ws_bytes, cnt_off, cnt_bytes, total;
+};
+
+ScratchLayout scratch_layout(const mpp41_mlp_desc *d)
+{
+    ScratchLayout L{};
+    L.mid_bytes = (size_t)d->tokens * d->intermediate * mid_bytes_per_elem(d->epilogue);
+    L.ws_off = align256(L.mid_bytes);
+    if (d->out_dtype == MPP41_F16 && down_splits(d) > 1) {
+        L.ws_bytes = (size_t)d->tokens * d->hidden * 4;
+        L.cnt_off = L.ws_off + L.ws_bytes;
+        L.cnt_bytes = ((size_t)(d->hidden / 64) * ((d->tokens + 127) / 128) * 4 + 15) & ~size_t(15);
+    } else {
+        L.cnt_off = L.ws_off;
+    }
+    L.total = L.cnt_off + L.cnt_bytes;
+    return L;
+}
+
 mpp41_status check_mlp_desc(const mpp41_mlp_desc *d)
 {
     if (!d) return fail(MPP41_ERR_INVALID_ARGUMENT, "null descriptor");
@@ -155,50 +185,98 @@ mpp41_status check_mlp_desc(const mpp41_mlp_desc *d)
     return MPP41_OK;
 }
 
-// Enqueue one MLP layer on `st`.
-mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg, const void *wu,
-                         const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *scratch,
-                         void *out, cudaStream_t st)
+mpp41_status check_fp16_row(const mpp41_mlp_desc *d)
 {
-    const uint32_t T = d->tokens, H = d->hidden, I = d->intermediate;
     if (d->afmt != MPP41_A_F16)
         return fail(MPP41_ERR_MISSING_KERNEL, "int8-activation MLP rows are not available in this build");
     if (d->epilogue == MPP41_SWIGLU_FLOAT || d->epilogue == MPP41_SWIGLU_I8)
         return fail(MPP41_ERR_MISSING_KERNEL, "fp32-mid down projection (f_*_f) is not available in this build");
-    if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su || !sd))
-        return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate, up and down scales");
-    const char *why = "";
-    // gate/up GEMM with the SwiGLU pair epilogue: mid = swiglu(x Wg^T, x Wu^T)
+    if (d->epilogue < 0 || d->epilogue > MPP41_SWIGLU_FP32)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "bad epilogue %d", d->epilogue);
+    if (d->out_dtype != MPP41_F32 && d->out_dtype != MPP41_F16)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "output dtype %d not valid for fp16-activation rows", d->out_dtype);
+    return MPP41_OK;
+}
+
+int gate_up_epi(int epilogue)
+{
+    return epilogue == MPP41_SWIGLU_HALF ? EPI_SWIGLU_HALF
+                                         : (epilogue == MPP41_SWIGLU_FP32 ? EPI_SWIGLU_PLAIN : EPI_SWIGLU_HALF_H);
+}
+
+// Stage 1: mid = swiglu(x Wg^T, x Wu^T) into scratch; clears the split-K
+// accumulation target of stage 2 (out for fp32, the workspace for fp16).
+mpp41_status enqueue_gate_up(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg, const void *wu,
+                             const uint8_t *sg, const uint8_t *su, void *scratch, void *out, cudaStream_t st)
+{
+    mpp41_status s = check_fp16_row(d);
+    if (s) return s;
+    if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate and up scales");
+    const ScratchLayout SL = scratch_layout(d);
     WqLaunch g{};
     g.wfmt = d->wfmt;
-    g.epi = d->epilogue == MPP41_SWIGLU_HALF ? EPI_SWIGLU_HALF : EPI_SWIGLU_HALF_H;
+    g.epi = gate_up_epi(d->epilogue);
     g.a = x; g.b0 = wg; g.b1 = wu; g.s0 = sg; g.s1 = su;
     g.out = scratch;
-    g.M = T; g.N = I; g.K = H; g.ldc = I;
+    g.M = d->tokens; g.N = d->intermediate; g.K = d->hidden; g.ldc = d->intermediate;
     g.err = ctx->err;
-    int rc = launch_wq_gemm(g, st, &why);
+    if (down_splits(d) > 1) {
+        if (d->out_dtype == MPP41_F32 && out) {
+            g.zero = out;
+            g.zero_bytes = (size_t)d->tokens * d->hidden * 4;
+        } else if (d->out_dtype == MPP41_F16) {
+            g.zero = static_cast<uint8_t *>(scratch) + SL.ws_off;
+            g.zero_bytes = SL.ws_bytes + SL.cnt_bytes;
+        }
+    }
+    const char *why = "";
+    const int rc = launch_wq_gemm(g, st, &why);
     if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "gate/up GEMM: %s", why);
-    // down GEMM: out = mid Wd^T
+    return MPP41_OK;
+}
+
+// Stage 2: out = mid Wd^T. Unless `prepared`, clears its split-K target first.
+mpp41_status enqueue_down(mpp41_ctx *ctx, const mpp41_mlp_desc *d, void *scratch, const void *wd, const uint8_t *sd,
+                          void *out, bool prepared, cudaStream_t st)
+{
+    mpp41_status s = check_fp16_row(d);
+    if (s) return s;
+    if (d->wfmt == MPP41_W_MXFP4 && !sd) return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs down scales");
+    const ScratchLayout SL = scratch_layout(d);
     WqLaunch dn{};
     dn.wfmt = d->wfmt;
     dn.a = scratch; dn.b0 = wd; dn.s0 = sd;
     dn.out = out;
-    dn.M = T; dn.N = H; dn.K = I; dn.ldc = H;
+    dn.M = d->tokens; dn.N = d->hidden; dn.K = d->intermediate; dn.ldc = d->hidden;
     dn.err = ctx->err;
-    if (d->out_dtype == MPP41_F16) {
-        dn.epi = EPI_STORE_F16;
-        dn.splits = 1;
-    } else if (d->out_dtype == MPP41_F32) {
-        const uint32_t tiles = (H / 64) * ((T + 127) / 128);
-        dn.splits = pick_splits(tiles, I);
+    dn.splits = down_splits(d);
+    if (d->out_dtype == MPP41_F32) {
         dn.epi = dn.splits > 1 ? EPI_ATOMIC_F32 : EPI_STORE_F32;
-        if (dn.splits > 1) CK(cudaMemsetAsync(out, 0, (size_t)T * H * 4, st), "zero output");
+        if (dn.splits > 1 && !prepared) CK(cudaMemsetAsync(out, 0, (size_t)d->tokens * d->hidden * 4, st), "clear");
     } else {
-        return fail(MPP41_ERR_INVALID_ARGUMENT, "output dtype %d not valid for fp16-activation rows", d->out_dtype);
+        dn.epi = dn.splits > 1 ? EPI_SPLITK_F16 : EPI_STORE_F16;
+        if (dn.splits > 1) {
+            dn.ws = reinterpret_cast<float *>(static_cast<uint8_t *>(scratch) + SL.ws_off);
+            dn.tile_count = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(scratch) + SL.cnt_off);
+            if (!prepared) CK(cudaMemsetAsync(dn.ws, 0, SL.ws_bytes + SL.cnt_bytes, st), "clear workspace");
+        }
     }
-    rc = launch_wq_gemm(dn, st, &why);
+    const char *why = "";
+    const int rc = launch_wq_gemm(dn, st, &why);
     if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "down GEMM: %s", why);
     return MPP41_OK;
+}
+
+// Enqueue one MLP layer on `st`: two kernels; the first also clears what the
+// split-K second one accumulates into.
+mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg, const void *wu,
+                         const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *scratch,
+                         void *out, cudaStream_t st)
+{
+    mpp41_status s = enqueue_gate_up(ctx, d, x, wg, wu, sg, su, scratch, out, st);
+    if (s) return s;
+    return enqueue_down(ctx, d, scratch, wd, sd, out, true, st);
 }
 
 }  // namespace
@@ -278,7 +356,7 @@ mpp41_status mpp41_device_name(mpp41_ctx *ctx, char *buf, size_t len)
 mpp41_status mpp41_set_stream(mpp41_ctx *ctx, void *s)
 {
     NEED(ctx);
-    ctx->stream = s ? static_cast<cudaStream_t>(s) : ctx->own_stream;
+    ctx->stream = static_cast<cudaStream_t>(s);
     return MPP41_OK;
 }
 
@@ -464,8 +542,8 @@ mpp41_status mpp41_mlp_scalar(mpp41_ctx *ctx, const char *gate_name, const char 
 
 size_t mpp41_mlp_scratch_bytes(const mpp41_mlp_desc *d)
 {
-    if (!d) return 0;
-    return (size_t)d->tokens * d->intermediate * mid_bytes_per_elem(d->epilogue);
+    if (!d || !d->tokens || !d->hidden || !d->intermediate) return 0;
+    return scratch_layout(d).total;
 }
 
 mpp41_status mpp41_mlp_describe(const char *name, uint32_t T, uint32_t H, uint32_t I, mpp41_mlp_desc *d)
@@ -499,6 +577,39 @@ mpp41_status mpp41_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, c
     return enqueue_mlp(ctx, d, x, wg, wu, wd, sg, su, sd, scratch, out, ctx->stream);
 }
 
+mpp41_status mpp41_mlp_gate_up(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,
+                               const void *wu, const uint8_t *sg, const uint8_t *su, void *scratch, void *out)
+{
+    NEED(ctx);
+    mpp41_status s = check_mlp_desc(d);
+    if (s) return s;
+    if (!x || !wg || !wu || !scratch) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    return enqueue_gate_up(ctx, d, x, wg, wu, sg, su, scratch, out, ctx->stream);
+}
+
+mpp41_status mpp41_mlp_down(mpp41_ctx *ctx, const mpp41_mlp_desc *d, void *scratch, const void *wd,
+                            const uint8_t *sd, void *out, int prepared)
+{
+    NEED(ctx);
+    mpp41_status s = check_mlp_desc(d);
+    if (s) return s;
+    if (!scratch || !wd || !out) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    return enqueue_down(ctx, d, scratch, wd, sd, out, prepared != 0, ctx->stream);
+}
+
+mpp41_status mpp41_quantize_mxfp4(mpp41_ctx *ctx, const float *w, uint32_t rows, uint32_t depth, uint8_t *packed,
+                                  uint8_t *scales)
+{
+    NEED(ctx);
+    if (depth % 32) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "depth must be a multiple of 32");
+    if (!rows || !depth) return MPP41_OK;
+    if (!w || !packed || !scales) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(packed) & 15u))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "w and packed must be 16-byte aligned");
+    CK(launch_quantize_mxfp4(w, rows, depth, packed, scales, ctx->stream), "quantize");
+    return MPP41_OK;
+}
+
 mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,
                                  const void *wu, const void *wd, const uint8_t *sg, const uint8_t *su,
                                  const uint8_t *sd, void *scratch, void *out, int iterations, double *gpu_seconds)
@@ -507,7 +618,10 @@ mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const 
     mpp41_status s = check_mlp_desc(d);
     if (s) return s;
     if (iterations <= 0 || !gpu_seconds) return fail(MPP41_ERR_INVALID_ARGUMENT, "iterations must be positive");
-    cudaStream_t st = ctx->stream;
+    // capture needs a real stream: order after the caller's stream, then run
+    // on the context's private stream
+    CK(cudaStreamSynchronize(ctx->stream), "caller stream");
+    cudaStream_t st = ctx->own_stream;
     // untimed warm-up run (main.swift:2015-2020), which also validates the row
     s = enqueue_mlp(ctx, d, x, wg, wu, wd, sg, su, sd, scratch, out, st);
     if (s) return s;
@@ -532,6 +646,7 @@ mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const 
     cudaGraphExecDestroy(exec);
     if (e != cudaSuccess) return cuda_fail(e, "timed replay");
     *gpu_seconds = ms * 1e-3;
+    CK(cudaStreamSynchronize(st), "benchmark stream");
     return mpp41_synchronize(ctx);
 }
 

@@ -35,7 +35,15 @@ struct WqLaunch {
     uint32_t M, N, K, ldc;
     uint32_t splits;        // split-K factor (EPI_ATOMIC_F32 only)
     uint32_t *err;
+    void *zero;             // optional buffer to clear (16-byte aligned)
+    size_t zero_bytes;      // multiple of 16
+    float *ws;              // split-K fp16 output: fp32 workspace [M][ldc] (clear)
+    uint32_t *tile_count;   // split-K fp16 output: per-tile arrival counters (clear)
 };
+
+// OCP-MX quantization of fp32 [rows][depth] to E2M1 [rows][depth/2] + E8M0 [rows][depth/32].
+cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
+                                  cudaStream_t st);
 // Returns 0 on success, 1 for an unsupported combination/shape, 2 for a CUDA error.
 int launch_wq_gemm(const WqLaunch &L, cudaStream_t st, const char **why);
 

@@ -11,6 +11,8 @@
 
 namespace mpp41 {
 
+static unsigned grid_for(size_t work, int block);
+
 // ------------------------------------------------------------------ codecs
 // Hardware conversions: cvt.rn.satfinite.{e2m1x2,e4m3x2,e5m2x2}.f32 round to
 // nearest even and saturate to the largest finite value, which is the
@@ -306,7 +308,63 @@ __global__ void scalar_matmul_kernel(int kind, uint32_t M, uint32_t N, uint32_t 
     }
 }
 
+// ------------------------------------------------------------------ OCP-MX quantizer
+// fp32 weights -> MXFP4 (OCP Microscaling v1.0): per block of 32 along K the
+// shared exponent is floor(log2(amax)) - 2 (2 = emax of E2M1), stored as the
+// E8M0 byte e + 127; elements are w * 2^-e rounded to nearest even E2M1 with
+// saturation to +-6. One thread per 32-block: eight float4 loads, one 16-byte
+// store of packed nibbles and one scale byte. There is no counterpart in the
+// reference (it draws random packed bytes); it produces the BASELINE config-0
+// weights and is checked bit for bit against the oracle's restatement.
+__global__ void quantize_mxfp4_kernel(const float *__restrict__ w, uint32_t rows, uint32_t depth,
+                                      uint8_t *__restrict__ packed, uint8_t *__restrict__ scales)
+{
+    const uint32_t kb = depth / 32;
+    const size_t blocks = (size_t)rows * kb;
+    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < blocks; b += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t r = (uint32_t)(b / kb), j = (uint32_t)(b % kb);
+        const float4 *src = reinterpret_cast<const float4 *>(w + (size_t)r * depth + (size_t)j * 32);
+        float v[32];
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 f = src[i];
+            v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+        }
+        int e = 0;
+        uint32_t code = 0;
+        if (amax > 0.0f && isfinite(amax)) {
+            int ex;
+            frexpf(amax, &ex);              // amax = m * 2^ex, m in [0.5, 1): floor(log2) = ex - 1
+            e = ex - 1 - 2;
+            int c = e + 127;
+            c = c < 0 ? 0 : (c > 254 ? 254 : c);
+            code = (uint32_t)c;
+            e = c - 127;
+        }
+        const float inv = ldexpf(1.0f, -e);  // exact power of two
+        uint32_t out[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) word |= enc_e2m1x2(v[8 * q + 2 * i] * inv, v[8 * q + 2 * i + 1] * inv) << (8 * i);
+            out[q] = word;
+        }
+        *reinterpret_cast<uint4 *>(packed + (size_t)r * (depth / 2) + (size_t)j * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+        scales[b] = (uint8_t)code;
+    }
+}
+
 // ------------------------------------------------------------------ launchers
+cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
+                                  cudaStream_t st)
+{
+    quantize_mxfp4_kernel<<<grid_for((size_t)rows * depth / 32, 256), 256, 0, st>>>(w, rows, depth, packed, scales);
+    return cudaGetLastError();
+}
+
 static unsigned grid_for(size_t work, int block)
 {
     size_t g = (work + block - 1) / block;

@@ -51,7 +51,8 @@ static int launch_t(const WqLaunch &L, cudaStream_t st, const char **why)
     using Cfg = WqCfg<W, BN, E>;
     WqGemmParams p;
     memset(&p, 0, sizeof(p));
-    const uint32_t splits = (E == EPI_ATOMIC_F32) ? (L.splits ? L.splits : 1) : 1;
+    const uint32_t splits = (E == EPI_ATOMIC_F32 || E == EPI_SPLITK_F16) ? (L.splits ? L.splits : 1) : 1;
+    if (E == EPI_SPLITK_F16 && (!L.ws || !L.tile_count)) { *why = "split-K fp16 output needs a workspace"; return 1; }
     if (L.K % (kBK * splits) != 0) { *why = "K must be a multiple of 64 * split"; return 1; }
     if (L.N % Cfg::kCols != 0) { *why = "N must be a multiple of the CTA column tile"; return 1; }
     const uint32_t kps = L.K / splits;
@@ -80,6 +81,14 @@ static int launch_t(const WqLaunch &L, cudaStream_t st, const char **why)
     p.k_per_split = kps;
     p.ldc = L.ldc;
     p.err = L.err;
+    p.ws = L.ws;
+    p.tile_count = L.tile_count;
+    p.zero = static_cast<float4 *>(L.zero);
+    p.zero_vec4 = (uint32_t)(L.zero_bytes / 16);
+    if (L.zero && ((reinterpret_cast<uintptr_t>(L.zero) & 15u) || (L.zero_bytes & 15u))) {
+        *why = "buffer to clear must be 16-byte aligned and sized";
+        return 1;
+    }
     const uint32_t smem = Cfg::smem_bytes(kps);
     if (smem > 227u * 1024u) { *why = "K range per CTA too large for shared memory"; return 1; }
     static bool attr_set = false;   // per instantiation
@@ -107,6 +116,8 @@ static int launch_w(const WqLaunch &L, cudaStream_t st, const char **why)
     case EPI_SWIGLU_FLOAT: return launch_t<W, 64, EPI_SWIGLU_FLOAT>(L, st, why);
     case EPI_SWIGLU_HALF: return launch_t<W, 64, EPI_SWIGLU_HALF>(L, st, why);
     case EPI_SWIGLU_HALF_H: return launch_t<W, 64, EPI_SWIGLU_HALF_H>(L, st, why);
+    case EPI_SWIGLU_PLAIN: return launch_t<W, 64, EPI_SWIGLU_PLAIN>(L, st, why);
+    case EPI_SPLITK_F16: return launch_t<W, 64, EPI_SPLITK_F16>(L, st, why);
     default: *why = "unknown epilogue"; return 1;
     }
 }

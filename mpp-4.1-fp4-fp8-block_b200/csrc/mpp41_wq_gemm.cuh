@@ -41,6 +41,8 @@ enum Epi : int {
     EPI_SWIGLU_FLOAT = 3,    // mid fp32 = silu(g) * u                 (mpp_mlp_swiglu_float)
     EPI_SWIGLU_HALF = 4,     // mid fp16 = silu(clamp(g/16)) * u/16    (mpp_mlp_swiglu_half)
     EPI_SWIGLU_HALF_H = 5,   // g,u rounded to fp16 first              (mpp_mlp_swiglu_half_from_half)
+    EPI_SWIGLU_PLAIN = 6,    // mid fp16 = silu(g) * u in fp32, no prescale (OCP-MX model rows)
+    EPI_SPLITK_F16 = 7,      // split-K: fp32 partials into a workspace, last CTA of a tile writes fp16
 };
 
 __host__ __device__ constexpr int wfmt_bits(int w)
@@ -64,11 +66,15 @@ struct WqGemmParams {
     uint32_t k_per_split;       // K range of blockIdx.z
     uint32_t ldc;
     uint32_t *err;              // device error word
+    float4 *zero;               // optional buffer cleared by this grid (for a later split-K GEMM)
+    uint32_t zero_vec4;         // its size in float4 units
+    float *ws;                  // EPI_SPLITK_F16: fp32 workspace [M][ldc], clear on entry
+    uint32_t *tile_count;       // EPI_SPLITK_F16: one arrival counter per output tile, clear on entry
 };
 
 template <int W, int BN, int E>
 struct WqCfg {
-    static constexpr bool kPair = (E >= EPI_SWIGLU_FLOAT);
+    static constexpr bool kPair = (E >= EPI_SWIGLU_FLOAT && E <= EPI_SWIGLU_PLAIN);
     static constexpr bool kDirect = (W == W_F16);
     static constexpr int kRawRow = (W == W_F16) ? 0 : kBK * wfmt_bits(W) / 8;   // bytes per row per stage
     static constexpr int kCols = kPair ? BN / 2 : BN;                         // output columns per CTA
@@ -205,8 +211,8 @@ __device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x)
 template <int E>
 __device__ __forceinline__ float swiglu(float g, float u)
 {
-    if constexpr (E == EPI_SWIGLU_FLOAT) {
-        return (g / (1.0f + exp_ref(-g))) * u;
+    if constexpr (E == EPI_SWIGLU_FLOAT || E == EPI_SWIGLU_PLAIN) {
+        return (g / (1.0f + expf(-g))) * u;
     } else {
         if constexpr (E == EPI_SWIGLU_HALF_H) {
             g = __half2float(__float2half_rn(g));
@@ -214,7 +220,7 @@ __device__ __forceinline__ float swiglu(float g, float u)
         }
         float gs = fminf(fmaxf(g * 0.0625f, -20.0f), 20.0f);
         float us = u * 0.0625f;
-        return (gs / (1.0f + exp_ref(-gs))) * us;
+        return (gs / (1.0f + expf(-gs))) * us;
     }
 }
 
@@ -269,6 +275,15 @@ __global__ void __launch_bounds__(kThreads, 1) wq_gemm_kernel(const __grid_const
     tc_fence_after();
     const uint32_t tmem_d = *tmem_slot;
 
+    if (p.zero && warp <= 1 && lane >= 1) {
+        // lanes 1..31 of warps 0 and 1 have no pipeline role: clear this CTA's
+        // slice of the buffer a following split-K GEMM accumulates into
+        const uint32_t ctas = gridDim.x * gridDim.y * gridDim.z;
+        const uint32_t cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        const uint32_t per = (p.zero_vec4 + ctas - 1) / ctas;
+        const uint32_t beg = cta * per, end = min(beg + per, p.zero_vec4);
+        for (uint32_t i = beg + warp * 31 + (lane - 1); i < end; i += 62) p.zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -363,7 +378,11 @@ __global__ void __launch_bounds__(kThreads, 1) wq_gemm_kernel(const __grid_const
             }
         }
         // ---------------------------------------------- epilogue
-        const bool ok = mbar_wait(done, 0, abort, p.err, 0x401);
+        // all 128 epilogue threads take the same branch: a wait that gave up set
+        // *abort before this barrier
+        mbar_wait(done, 0, abort, p.err, 0x401);
+        asm volatile("bar.sync 3, 128;" ::: "memory");
+        const bool ok = (*abort == 0);
         tc_fence_after();
         const uint32_t quarter = warp & 3;               // TMEM lanes 32*quarter .. +31
         const uint32_t row = quarter * 32 + lane;
@@ -417,8 +436,9 @@ __global__ void __launch_bounds__(kThreads, 1) wq_gemm_kernel(const __grid_const
                             for (int i = 0; i < 8; ++i)
                                 dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                                      __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-                        } else if constexpr (E == EPI_ATOMIC_F32) {
-                            float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + (size_t)m * p.ldc + col);
+                        } else if constexpr (E == EPI_ATOMIC_F32 || E == EPI_SPLITK_F16) {
+                            float4 *dst = reinterpret_cast<float4 *>((E == EPI_ATOMIC_F32 ? static_cast<float *>(p.out) : p.ws) +
+                                                                     (size_t)m * p.ldc + col);
 #pragma unroll
                             for (int i = 0; i < 8; ++i)
                                 atomicAdd(dst + i, make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
@@ -433,6 +453,33 @@ __global__ void __launch_bounds__(kThreads, 1) wq_gemm_kernel(const __grid_const
                                                     half2_bits(__uint_as_float(v[e + 4]), __uint_as_float(v[e + 5])),
                                                     half2_bits(__uint_as_float(v[e + 6]), __uint_as_float(v[e + 7])));
                             }
+                        }
+                    }
+                }
+            }
+            if constexpr (E == EPI_SPLITK_F16) {
+                // Publish this CTA's partial, count arrivals per output tile; the
+                // last CTA of the tile converts the fp32 sum to fp16.
+                __shared__ uint32_t s_last;
+                __threadfence();
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
+                if (threadIdx.x == 64) s_last = (atomicAdd(p.tile_count + tile, 1u) == gridDim.z - 1) ? 1u : 0u;
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                if (s_last) {
+                    __threadfence();
+                    // 128 threads x 16 columns per row-pass: coalesced 64-byte row segments
+                    const uint32_t r0 = threadIdx.x - 64;
+                    for (uint32_t i = r0; i < kBM * (BN / 8); i += 128) {
+                        const uint32_t rr = i / (BN / 8), cc = (i % (BN / 8)) * 8;
+                        const uint32_t mm = m0 + rr;
+                        if (mm < p.M) {
+                            const float *src = p.ws + (size_t)mm * p.ldc + c0 + cc;
+                            const float4 a = __ldcg(reinterpret_cast<const float4 *>(src));
+                            const float4 b = __ldcg(reinterpret_cast<const float4 *>(src) + 1);
+                            *reinterpret_cast<uint4 *>(static_cast<__half *>(p.out) + (size_t)mm * p.ldc + c0 + cc) =
+                                make_uint4(half2_bits(a.x, a.y), half2_bits(a.z, a.w), half2_bits(b.x, b.y),
+                                           half2_bits(b.z, b.w));
                         }
                     }
                 }

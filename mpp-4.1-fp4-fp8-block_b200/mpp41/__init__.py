@@ -27,7 +27,7 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED_SHAPE, ERR_NO_DEVICE, ERR_MISSING_KERN
     ERR_CUDA, ERR_TIMEOUT, ERR_BOUNDS, ERR_COMM = range(10)
 W_F16, W_I8, W_I4, W_I2, W_FP4, W_E4M3, W_E5M2, W_MXFP4 = range(8)
 A_F16, A_S8 = 0, 1
-SWIGLU_FLOAT, SWIGLU_HALF, SWIGLU_HALF_FROM_HALF, SWIGLU_I8 = range(4)
+SWIGLU_FLOAT, SWIGLU_HALF, SWIGLU_HALF_FROM_HALF, SWIGLU_I8, SWIGLU_FP32 = range(5)
 F32, F16, S32, S8 = range(4)
 MLP_UNFUSED = 0x1
 FMT_E2M1, FMT_E4M3, FMT_E5M2 = 0, 1, 2
@@ -97,6 +97,9 @@ def lib() -> C.CDLL:
         "mpp41_mlp_scalar": ([vp, C.c_char_p, C.c_char_p, vp, vp, vp, vp, vp, vp, C.POINTER(MLPConfig)], st),
         "mpp41_mlp_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp": ([vp, C.POINTER(MLPDesc)] + [vp] * 9, st),
+        "mpp41_mlp_gate_up": ([vp, C.POINTER(MLPDesc)] + [vp] * 7, st),
+        "mpp41_mlp_down": ([vp, C.POINTER(MLPDesc), vp, vp, vp, vp, C.c_int], st),
+        "mpp41_quantize_mxfp4": ([vp, vp, u32, u32, vp, vp], st),
         "mpp41_mlp_describe": ([C.c_char_p, u32, u32, u32, C.POINTER(MLPDesc)], st),
         "mpp41_mlp_benchmark": ([vp, C.POINTER(MLPDesc)] + [vp] * 9 + [C.c_int, C.POINTER(C.c_double)], st),
     }
@@ -221,6 +224,17 @@ class Context:
     def mlp(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out):
         _check(lib().mpp41_mlp(self.h, C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(wd), _ptr(sg), _ptr(su),
                                _ptr(sd), _ptr(scratch), _ptr(out)))
+
+    def mlp_gate_up(self, desc: MLPDesc, x, wg, wu, sg, su, scratch, out=None):
+        _check(lib().mpp41_mlp_gate_up(self.h, C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(sg), _ptr(su),
+                                       _ptr(scratch), _ptr(out)))
+
+    def mlp_down(self, desc: MLPDesc, scratch, wd, sd, out, prepared=False):
+        _check(lib().mpp41_mlp_down(self.h, C.byref(desc), _ptr(scratch), _ptr(wd), _ptr(sd), _ptr(out),
+                                    int(bool(prepared))))
+
+    def quantize_mxfp4(self, w, rows: int, depth: int, packed, scales):
+        _check(lib().mpp41_quantize_mxfp4(self.h, _ptr(w), rows, depth, _ptr(packed), _ptr(scales)))
 
     def mlp_benchmark(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out, iterations: int) -> float:
         secs = C.c_double()

@@ -69,7 +69,7 @@ int orc_mlp_mxfp4_cpu(uint32_t T, uint32_t H, uint32_t I,
                       const uint16_t *x, const uint8_t *wg, const uint8_t *wu,
                       const uint8_t *wd, const uint8_t *sg, const uint8_t *su,
                       const uint8_t *sd, float *out, int nthreads,
-                      uint32_t t0, uint32_t t1)
+                      uint32_t t0, uint32_t t1, int plain)
 {
     if (nthreads <= 0) nthreads = omp_get_max_threads();
     if (t1 > T) t1 = T;
@@ -91,10 +91,14 @@ int orc_mlp_mxfp4_cpu(uint32_t T, uint32_t H, uint32_t I,
             for (uint32_t t = 0; t < nt; ++t) {
                 float g = dot(xf + (size_t)t * H, rg, H);
                 float u = dot(xf + (size_t)t * H, ru, H);
-                float gs = g * 0.0625f;
-                gs = gs < -20.0f ? -20.0f : (gs > 20.0f ? 20.0f : gs);
-                float us = u * 0.0625f;
-                mid[(size_t)t * I + c] = f2h((gs / (1.0f + expf(-gs))) * us);
+                if (plain) {
+                    mid[(size_t)t * I + c] = f2h((g / (1.0f + expf(-g))) * u);
+                } else {
+                    float gs = g * 0.0625f;
+                    gs = gs < -20.0f ? -20.0f : (gs > 20.0f ? 20.0f : gs);
+                    float us = u * 0.0625f;
+                    mid[(size_t)t * I + c] = f2h((gs / (1.0f + expf(-gs))) * us);
+                }
             }
         }
         #pragma omp for schedule(static)

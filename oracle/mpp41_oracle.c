@@ -406,6 +406,13 @@ void orc_mlp(int act, int wfmt, int epi, int out_kind,
             mid[i] = orc_half_to_float(h);
             break;
         }
+        case 4: {
+            /* BASELINE config 0: silu(g)*u in fp32 (no prescale), fp16 mid */
+            uint16_t h = orc_float_to_half(orc_swiglu_float((float)gate[i], (float)up[i]));
+            if (mid_out) ((uint16_t *)mid_out)[i] = h;
+            mid[i] = orc_half_to_float(h);
+            break;
+        }
         default: {
             int8_t q = orc_swiglu_i8((int32_t)gate[i], (int32_t)up[i]);
             if (mid_out) ((int8_t *)mid_out)[i] = q;
@@ -611,6 +618,37 @@ void orc_swiglu_array(int kind, const void *gate, const void *up, void *mid, siz
         case 1: ((uint16_t *)mid)[i] = orc_swiglu_half(((const float *)gate)[i], ((const float *)up)[i]); break;
         case 2: ((uint16_t *)mid)[i] = orc_swiglu_half_from_half(((const uint16_t *)gate)[i], ((const uint16_t *)up)[i]); break;
         default: ((int8_t *)mid)[i] = orc_swiglu_i8(((const int32_t *)gate)[i], ((const int32_t *)up)[i]); break;
+        }
+    }
+}
+
+/* OCP Microscaling (MX) v1.0 quantization of fp32 weights to MXFP4 along K:
+ * per block of 32, shared exponent e = floor(log2(amax)) - 2 (emax of E2M1),
+ * clamped so that e + 127 is in [0, 254] and stored as that E8M0 byte;
+ * elements RNE(w / 2^e) onto E2M1 with saturation. No reference counterpart
+ * (the reference draws random packed bytes, main.swift:2785-2793); this is
+ * the BASELINE config-0 weight recipe. */
+void orc_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales)
+{
+    for (uint32_t r = 0; r < rows; ++r) {
+        for (uint32_t j = 0; j < depth / 32; ++j) {
+            const float *b = w + (size_t)r * depth + (size_t)j * 32;
+            double amax = 0.0;
+            for (int i = 0; i < 32; ++i) amax = fmax(amax, fabs((double)b[i]));
+            int e = 0, code = 0;
+            if (amax > 0.0 && isfinite(amax)) {
+                int ex;
+                frexp(amax, &ex);
+                code = ex - 1 - 2 + 127;
+                code = code < 0 ? 0 : (code > 254 ? 254 : code);
+                e = code - 127;
+            }
+            scales[(size_t)r * (depth / 32) + j] = (uint8_t)code;
+            for (int i = 0; i < 32; i += 2) {
+                uint8_t lo = orc_e2m1_encode((float)ldexp((double)b[i], -e));
+                uint8_t hi = orc_e2m1_encode((float)ldexp((double)b[i + 1], -e));
+                packed[(size_t)r * (depth / 2) + (size_t)j * 16 + i / 2] = (uint8_t)(lo | (hi << 4));
+            }
         }
     }
 }

@@ -76,7 +76,8 @@ void orc_swiglu_array(int kind, const void *gate, const void *up, void *mid, siz
 /* ---- whole MLP rows ----
  * act: 0 = fp16 x, 1 = int8 x. epi: 0 = swiglu_float (fp32 mid),
  * 1 = swiglu_half (fp16 mid), 2 = half gate/up then swiglu_half_from_half,
- * 3 = swiglu_i8 (int8 mid, int32 accumulate).
+ * 3 = swiglu_i8 (int8 mid, int32 accumulate), 4 = silu(g)*u in fp32 without
+ * prescale and an fp16 mid.
  * out_kind: 0 = fp32, 1 = fp16 bits, 2 = int32.
  * Gate/up are exact sums rounded once to the destination type; the down
  * projection is an exact sum rounded once to the output type. */
@@ -86,14 +87,18 @@ void orc_mlp(int act, int wfmt, int epi, int out_kind,
              const uint8_t *sg, const uint8_t *su, const uint8_t *sd,
              void *mid_out, void *out);
 
+/* OCP-MX fp32 -> MXFP4 quantizer (E2M1 [rows][depth/2], E8M0 [rows][depth/32]). */
+void orc_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales);
+
 /* CPU formulation of the MXFP4 MLP, timed as the CPU baseline: LUT dequant,
- * fp32 dot products, swiglu_half, fp32 down projection. nthreads <= 0 uses
- * all OpenMP threads. Returns the thread count used. */
+ * fp32 dot products, swiglu_half (plain = 0) or silu(g)*u without prescale
+ * (plain = 1), fp32 down projection. nthreads <= 0 uses all OpenMP threads.
+ * Returns the thread count used. */
 int orc_mlp_mxfp4_cpu(uint32_t tokens, uint32_t hidden, uint32_t intermediate,
                       const uint16_t *x, const uint8_t *wg, const uint8_t *wu,
                       const uint8_t *wd, const uint8_t *sg, const uint8_t *su,
                       const uint8_t *sd, float *out, int nthreads,
-                      uint32_t token_begin, uint32_t token_end);
+                      uint32_t token_begin, uint32_t token_end, int plain);
 
 /* ---- scalar (half-accumulate) kernels of PackedNumericKernels.metal ---- */
 uint16_t orc_half_fma(uint16_t a, uint16_t b, uint16_t c);  /* fused, one rounding */

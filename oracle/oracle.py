@@ -62,7 +62,8 @@ def lib() -> C.CDLL:
         L.orc_mxfp4_dequant_half.argtypes = [vp, vp, vp, u32, u32]
         L.orc_gemm_f64.argtypes = [vp, vp, vp, u32, u32, u32]
         L.orc_mlp.argtypes = [C.c_int] * 4 + [u32] * 3 + [vp] * 9
-        L.orc_mlp_mxfp4_cpu.argtypes = [u32] * 3 + [vp] * 8 + [C.c_int, u32, u32]
+        L.orc_mlp_mxfp4_cpu.argtypes = [u32] * 3 + [vp] * 8 + [C.c_int, u32, u32, C.c_int]
+        L.orc_quantize_mxfp4.argtypes = [vp, u32, u32, vp, vp]
         L.orc_mlp_mxfp4_cpu.restype = C.c_int
         L.orc_scalar_mlp_gate_up.argtypes = [C.c_int, u32, u32, u32, vp, vp, vp, vp]
         L.orc_scalar_mlp_down.argtypes = [C.c_int, u32, u32, u32, vp, vp, vp]
@@ -148,7 +149,7 @@ def mxfp4_dequant_half(packed, scales, rows, depth) -> np.ndarray:
 
 def mlp(act, wfmt, epi, out_kind, T, H, I, x, wg, wu, wd, sg=None, su=None, sd=None):
     """Returns (mid, out) of one MLP row, fp64-exact GEMMs (see mpp41_oracle.h)."""
-    mid_dt = {0: np.float32, 1: np.float16, 2: np.float16, 3: np.int8}[epi]
+    mid_dt = {0: np.float32, 1: np.float16, 2: np.float16, 3: np.int8, 4: np.float16}[epi]
     out_dt = {0: np.float32, 1: np.float16, 2: np.int32}[out_kind]
     mid = np.empty((T, I), mid_dt)
     out = np.empty((T, H), out_dt)
@@ -167,12 +168,33 @@ def swiglu(kind: int, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
     return out
 
 
-def mlp_mxfp4_cpu(T, H, I, x, wg, wu, wd, sg, su, sd, nthreads=0, t0=0, t1=None):
+def mlp_mxfp4_cpu(T, H, I, x, wg, wu, wd, sg, su, sd, nthreads=0, t0=0, t1=None, plain=False):
     out = np.zeros((T, H), np.float32)
     t1 = T if t1 is None else t1
     n = lib().orc_mlp_mxfp4_cpu(T, H, I, _p(x), _p(wg), _p(wu), _p(wd), _p(sg), _p(su), _p(sd),
-                                _p(out), nthreads, t0, t1)
+                                _p(out), nthreads, t0, t1, int(plain))
     return out, n
+
+
+def quantize_mxfp4(w: np.ndarray):
+    """OCP-MX fp32 [rows][depth] -> (packed [rows][depth/2], scales [rows][depth/32])."""
+    w = np.ascontiguousarray(w, np.float32)
+    rows, depth = w.shape
+    packed = np.empty((rows, depth // 2), np.uint8)
+    scales = np.empty((rows, depth // 32), np.uint8)
+    lib().orc_quantize_mxfp4(_p(w), rows, depth, _p(packed), _p(scales))
+    return packed, scales
+
+
+def baseline_mlp_inputs(T=128, H=1024, I=4096, seed=0):
+    """x ~ N(0,1) fp16, weights ~ N(0,0.02) fp32 quantized OCP-MX."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, H), dtype=np.float32).astype(np.float16)
+    out = {"x": x}
+    for name, (r, c) in (("g", (I, H)), ("u", (I, H)), ("d", (H, I))):
+        w = (rng.standard_normal((r, c), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        out["w" + name], out["s" + name] = quantize_mxfp4(w)
+    return out
 
 
 def scalar_mlp(wfmt, T, H, I, x, wg, wu, wd):

@@ -48,10 +48,19 @@ def test_mxfp4_reference_checksum_403573(ctx, golden):
             to_dev(d["su"]), to_dev(d["sd"]), d_scr, d_out)
     ctx.synchronize()
     got = from_dev(d_out, np.float32, (T, H))
-    assert O.float_checksum(got) == g["value"]
     _, ref = O.mlp(0, O.W_MXFP4, 1, 0, T, H, I, d["x"].view(np.uint16), d["wg"], d["wu"], d["wd"],
                    d["sg"], d["su"], d["sd"])
-    assert rel_fro(got, ref) <= TOL
+    # The oracle (FP64 sums) reproduces the published checksum exactly: its
+    # 32-sample sum is 403572.549, printed "%.6g" -> 403573. That is 0.049
+    # above the rounding boundary, i.e. 1.2e-7 relative, below the noise of any
+    # fp32 accumulation over K=4096 (about +-0.3 on this sum). So the GPU sum
+    # must sit within one unit of the published last digit and the output
+    # within 1e-6 relative Frobenius of FP64.
+    assert O.float_checksum(ref) == g["value"]
+    idx = O.sample_indices(got.size)
+    gpu_sum = float(np.sum(got.ravel()[idx].astype(np.float64)))
+    assert abs(gpu_sum - float(g["value"].split()[0])) <= 1.0
+    assert rel_fro(got, ref) <= 1e-6
 
 
 @pytest.mark.parametrize("gate_kernel", [
@@ -89,4 +98,54 @@ def test_benchmark_entry_point(ctx):
     secs = ctx.mlp_benchmark(desc, to_dev(d["x"]), to_dev(d["wg"]), to_dev(d["wu"]), to_dev(d["wd"]),
                              to_dev(d["sg"]), to_dev(d["su"]), to_dev(d["sd"]), d_scr, d_out, 20)
     assert 0 < secs < 1.0
-    assert O.float_checksum(from_dev(d_out, np.float32, (T, H))) == "403573 over 32 samples"
+    got = from_dev(d_out, np.float32, (T, H))
+    idx = O.sample_indices(got.size)
+    assert abs(float(np.sum(got.ravel()[idx].astype(np.float64))) - 403573.0) <= 1.0
+
+
+def test_quantizer_bit_exact(ctx):
+    rng = np.random.default_rng(5)
+    rows, depth = 1024, 2048
+    w = (rng.standard_normal((rows, depth)) * 0.02).astype(np.float32)
+    w[3, :32] = 0.0
+    w[7, 64:96] *= 1e6
+    w[9, 32:64] *= 1e-30
+    p_ref, s_ref = O.quantize_mxfp4(w)
+    d_p, d_s = empty_dev(rows * depth // 2), empty_dev(rows * depth // 32)
+    ctx.quantize_mxfp4(to_dev(w), rows, depth, d_p, d_s)
+    assert np.array_equal(from_dev(d_p, np.uint8, p_ref.shape), p_ref)
+    assert np.array_equal(from_dev(d_s, np.uint8, s_ref.shape), s_ref)
+
+
+@pytest.mark.parametrize("T", [1, 128, 333, 1024])
+def test_baseline_config0_mode_b(ctx, T):
+    """x ~ N(0,1) fp16, OCP-MX quantized N(0, 0.02) weights,
+    SiLU(gate)*up in fp32, fp16 output (split-K through the fp32 workspace)."""
+    H, I = 1024, 4096
+    d = O.baseline_mlp_inputs(T, H, I, seed=T)
+    desc = mpp41.mlp_desc(T, H, I, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F16)
+    d_out, d_scr = empty_dev(T * H * 2), empty_dev(mpp41.scratch_bytes(desc))
+    dv = {k: to_dev(v) for k, v in d.items()}
+    for _ in range(2):   # the second call checks the workspace is re-cleared
+        ctx.mlp(desc, dv["x"], dv["wg"], dv["wu"], dv["wd"], dv["sg"], dv["su"], dv["sd"], d_scr, d_out)
+    ctx.synchronize()
+    got = from_dev(d_out, np.float16, (T, H))
+    _, ref = O.mlp(0, O.W_MXFP4, 4, 1, T, H, I, d["x"].view(np.uint16), d["wg"], d["wu"], d["wd"],
+                   d["sg"], d["su"], d["sd"])
+    assert rel_fro(got, ref) <= TOL
+
+
+def test_two_stage_api_matches_fused_call(ctx):
+    T, H, I = 128, 1024, 4096
+    d = O.baseline_mlp_inputs(T, H, I, seed=9)
+    dv = {k: to_dev(v) for k, v in d.items()}
+    for out_dtype, dt in ((mpp41.F16, np.float16), (mpp41.F32, np.float32)):
+        desc = mpp41.mlp_desc(T, H, I, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, out_dtype)
+        a, b = empty_dev(T * H * 4), empty_dev(T * H * 4)
+        s1, s2 = empty_dev(mpp41.scratch_bytes(desc)), empty_dev(mpp41.scratch_bytes(desc))
+        ctx.mlp(desc, dv["x"], dv["wg"], dv["wu"], dv["wd"], dv["sg"], dv["su"], dv["sd"], s1, a)
+        ctx.mlp_gate_up(desc, dv["x"], dv["wg"], dv["wu"], dv["sg"], dv["su"], s2, b)
+        ctx.mlp_down(desc, s2, dv["wd"], dv["sd"], b, prepared=True)
+        ctx.synchronize()
+        ga, gb = from_dev(a, dt, (T, H)), from_dev(b, dt, (T, H))
+        assert rel_fro(ga, gb) <= 1e-6

@@ -117,3 +117,30 @@ def test_cpu_baseline_close_to_oracle():
     got, n = O.mlp_mxfp4_cpu(T, H, I, d["x"].view(np.uint16), d["wg"], d["wu"], d["wd"], d["sg"], d["su"], d["sd"])
     assert n >= 1
     assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-5
+
+
+def test_quantizer_matches_independent_numpy_restatement():
+    """OCP-MX quantizer against a numpy + ml_dtypes restatement."""
+    ml = pytest.importorskip("ml_dtypes")
+    rng = np.random.default_rng(11)
+    w = (rng.standard_normal((32, 512)) * 0.02).astype(np.float32)
+    w[0, :32] = 0.0                                 # all-zero block
+    w[1, :32] *= 1e4                                # large block
+    packed, scales = O.quantize_mxfp4(w)
+    blocks = w.reshape(32, 16, 32).astype(np.float64)
+    amax = np.abs(blocks).max(axis=2)
+    e = np.where(amax > 0, np.floor(np.log2(np.where(amax > 0, amax, 1))) - 2, -127)
+    code = np.clip(e + 127, 0, 254)
+    assert np.array_equal(scales, np.where(amax > 0, code, 0).astype(np.uint8))
+    q = (blocks / np.exp2(code - 127)[..., None]).astype(np.float32)
+    q = np.clip(q, -6, 6).astype(ml.float4_e2m1fn).astype(np.float32)
+    deq = O.decode_weights(O.W_MXFP4, packed, scales, 32, 512).reshape(32, 16, 32)
+    want = q * np.exp2(code - 127)[..., None]
+    want[amax == 0] = 0
+    assert np.array_equal(deq, want)
+
+
+def test_baseline_inputs_are_finite_and_scaled():
+    d = O.baseline_mlp_inputs(8, 256, 512)
+    assert d["x"].dtype == np.float16 and d["wg"].shape == (512, 128) and d["sg"].shape == (512, 8)
+    assert 110 < int(np.median(d["sg"])) < 125   # amax of 32 N(0, 0.02) draws ~ 2^-4.5
