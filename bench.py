@@ -42,9 +42,9 @@ BYTES_W = 3 * H * I // 2 + 3 * H * I // 32
 BYTES_LAYER = BYTES_W + T * H * 2 + T * H * 2
 ROTATE = 24
 METRIC = "MXFP4 fused-MLP µs/layer & TFLOP/s (% of roofline) at 1/2/4/8 B200"
-# DRAM bytes per launch of the gate/up kernel from one ncu capture of this
-# workload (profiles/mxfp4_gate_up_swiglu_t128_h1024_i4096.md); None until captured.
-NCU_TRAFFIC_GATE_UP = None
+# DRAM bytes per launch of mlp_fused_kernel from one ncu capture of this
+# workload (profiles/mlp_fused_mxfp4_t128_h1024_i4096.md); None until captured.
+NCU_TRAFFIC_LAYER = None
 
 
 def load_peaks():
@@ -139,6 +139,8 @@ def reference_arm(args, rank):
 
 
 def cpu_baseline(host, seconds):
+    if seconds <= 0:
+        return None
     import numpy as np
     import oracle as O
     x = host["x"].view(np.uint16)
@@ -203,12 +205,6 @@ def main():
     def layer(s):
         ctx.mlp(desc, s["x"], s["wg"], s["wu"], s["wd"], s["sg"], s["su"], s["sd"], scratch, s["out"])
 
-    def gate_up(s):
-        ctx.mlp_gate_up(desc, s["x"], s["wg"], s["wu"], s["sg"], s["su"], scratch, None)
-
-    def down(s):
-        ctx.mlp_down(desc, scratch, s["wd"], s["sd"], s["out"], prepared=True)
-
     def capture(fn, n):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
@@ -269,34 +265,18 @@ def main():
     us_layer = ms * 1e3 / args.steps
     value = world * FLOPS_PER_LAYER * args.steps / (ms * 1e-3) / 1e12
 
-    # ---- per-kernel device time (same rotation) for the roofline
-    def kernel_us(fn, n=ROTATE * 20):
-        g = capture(fn, ROTATE)
-        g.replay()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(n // ROTATE):
-            g.replay()
-        b.record(stream)
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) * 1e3 / n
-
-    layer(sets[0])
-    us_gu = kernel_us(gate_up)
-    us_dn = kernel_us(down)
+    # ---- roofline of the one kernel per step (mlp_fused_kernel): its average
+    # launch duration is the timed region divided by the K launches
     hbm, tflops_peak, peak_src = load_peaks()
-    dominant = "gate_up" if us_gu >= us_dn else "down"
-    flops_dom = FLOPS_GATE_UP if dominant == "gate_up" else FLOPS_DOWN
-    achieved = flops_dom / ((us_gu if dominant == "gate_up" else us_dn) * 1e-6) / 1e12
-    roofline = {"bound": "tensor", "kernel": f"wq_gemm_kernel ({dominant})", "achieved": achieved,
-                "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
-                "peak_source": f"bf16 dense burst, {peak_src} (MEASURED_PEAKS.json)",
-                "traffic": NCU_TRAFFIC_GATE_UP if dominant == "gate_up" else None,
-                "kernel_us": {"gate_up_swiglu": us_gu, "down_splitk": us_dn},
+    achieved = FLOPS_PER_LAYER / (us_layer * 1e-6) / 1e12
+    roofline = {"bound": "tensor", "kernel": "mlp_fused_kernel (gate/up + SwiGLU + down, one launch per layer)",
+                "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
+                "peak_source": f"bf16/f16 dense burst, {peak_src} (MEASURED_PEAKS.json)",
+                "traffic": NCU_TRAFFIC_LAYER,
+                "algorithmic_bytes": BYTES_LAYER, "algorithmic_flops": FLOPS_PER_LAYER,
+                "achieved_gbs": BYTES_LAYER / (us_layer * 1e-6) / 1e9,
                 "layer_floor_us": {"hbm": BYTES_LAYER / (hbm * 1e9) * 1e6,
-                                   "tensor_f16": FLOPS_PER_LAYER / (tflops_peak * 1e12) * 1e6},
-                "layer_frac_of_tensor_floor": (FLOPS_PER_LAYER / (tflops_peak * 1e12) * 1e6) / us_layer}
+                                   "tensor_f16": FLOPS_PER_LAYER / (tflops_peak * 1e12) * 1e6}}
 
     # ---- end to end through the C ABI with host buffers (pinned), per step:
     # H2D of x, the layer, D2H of the fp16 output
@@ -342,7 +322,7 @@ def main():
                            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                            "l2": f"rotating {ROTATE} weight/activation sets ({ROTATE * BYTES_LAYER / 1e6:.0f} MB)"
                                  " > 126 MB L2"},
-                "roofline": roofline, "e2e": e2e, "gpu_launches": 2 * args.steps, "clocks": clocks,
+                "roofline": roofline, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
                 "oracle_rel_err": rel}
         if base is not None:
             line["cpu_baseline"] = base

@@ -16,6 +16,8 @@ struct mpp41_ctx {
     cudaStream_t own_stream;
     cudaStream_t stream;
     uint32_t *err;          // device error word
+    uint32_t *sync;         // grid-wide counters of the fused layer kernel (kept zero between launches)
+    size_t sync_words;
     cudaEvent_t ev0, ev1;
 };
 
@@ -152,7 +154,7 @@ uint32_t down_splits(const mpp41_mlp_desc *d)
 }
 
 // Scratch layout: [mid][fp32 workspace T x H][tile counters] (the last two
-// only for fp16 output with split-K).
+// only for fp16 output).
 struct ScratchLayout {
     size_t mid_bytes, ws_off, ws_bytes, cnt_off, cnt_bytes, total;
 };
@@ -162,7 +164,7 @@ ScratchLayout scratch_layout(const mpp41_mlp_desc *d)
     ScratchLayout L{};
     L.mid_bytes = (size_t)d->tokens * d->intermediate * mid_bytes_per_elem(d->epilogue);
     L.ws_off = align256(L.mid_bytes);
-    if (d->out_dtype == MPP41_F16 && down_splits(d) > 1) {
+    if (d->out_dtype == MPP41_F16) {
         L.ws_bytes = (size_t)d->tokens * d->hidden * 4;
         L.cnt_off = L.ws_off + L.ws_bytes;
         L.cnt_bytes = ((size_t)(d->hidden / 64) * ((d->tokens + 127) / 128) * 4 + 15) & ~size_t(15);
@@ -268,13 +270,39 @@ mpp41_status enqueue_down(mpp41_ctx *ctx, const mpp41_mlp_desc *d, void *scratch
     return MPP41_OK;
 }
 
-// Enqueue one MLP layer on `st`: two kernels; the first also clears what the
-// split-K second one accumulates into.
+// Enqueue one MLP layer on `st`. Preferred: the single persistent kernel
+// (mpp41_mlp_fused.cuh). Otherwise, or with MPP41_MLP_UNFUSED: two kernels,
+// the first also clearing what the split-K second one accumulates into.
 mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg, const void *wu,
                          const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *scratch,
                          void *out, cudaStream_t st)
 {
-    mpp41_status s = enqueue_gate_up(ctx, d, x, wg, wu, sg, su, scratch, out, st);
+    mpp41_status s = check_fp16_row(d);
+    if (s) return s;
+    if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su || !sd))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate, up and down scales");
+    if (!(d->flags & MPP41_MLP_UNFUSED) && d->wfmt != MPP41_W_F16 &&
+        fused_sync_words(d->tokens, d->hidden) <= ctx->sync_words) {
+        const ScratchLayout SL = scratch_layout(d);
+        FusedLaunch L{};
+        L.wfmt = d->wfmt;
+        L.gate_epi = gate_up_epi(d->epilogue);
+        L.out_f16 = d->out_dtype == MPP41_F16;
+        L.x = x; L.wg = wg; L.wu = wu; L.wd = wd; L.sg = sg; L.su = su; L.sd = sd;
+        L.mid = scratch;
+        L.out = out;
+        L.ws = L.out_f16 ? reinterpret_cast<float *>(static_cast<uint8_t *>(scratch) + SL.ws_off) : nullptr;
+        L.sync = ctx->sync;
+        L.err = ctx->err;
+        L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
+        L.splits = down_splits(d);
+        if (L.out_f16 && L.splits == 1) L.splits = 2;   // the fp16 path always reduces through the workspace
+        const char *why = "";
+        const int rc = launch_mlp_fused(L, st, &why);
+        if (rc == 0) return MPP41_OK;
+        if (rc == 2) return fail(MPP41_ERR_CUDA, "fused MLP kernel: %s", why);
+    }
+    s = enqueue_gate_up(ctx, d, x, wg, wu, sg, su, scratch, out, st);
     if (s) return s;
     return enqueue_down(ctx, d, scratch, wd, sd, out, true, st);
 }
@@ -320,6 +348,9 @@ mpp41_status mpp41_create(int device, mpp41_ctx **out)
     cudaError_t e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&c->err, sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof(uint32_t));
+    c->sync_words = 1u << 16;
+    if (e == cudaSuccess) e = cudaMalloc(&c->sync, c->sync_words * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(c->sync, 0, c->sync_words * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaEventCreate(&c->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&c->ev1);
     if (e != cudaSuccess) {
@@ -337,6 +368,7 @@ void mpp41_destroy(mpp41_ctx *ctx)
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->err);
+    cudaFree(ctx->sync);
     cudaEventDestroy(ctx->ev0);
     cudaEventDestroy(ctx->ev1);
     cudaStreamDestroy(ctx->own_stream);
@@ -372,6 +404,8 @@ mpp41_status mpp41_synchronize(mpp41_ctx *ctx)
     CK(cudaMemcpy(&w, ctx->err, sizeof(w), cudaMemcpyDeviceToHost), "read device error word");
     if (w) {
         cudaMemset(ctx->err, 0, sizeof(uint32_t));
+        // a kernel that gave up may have left grid counters mid-count
+        cudaMemset(ctx->sync, 0, ctx->sync_words * sizeof(uint32_t));
         const uint32_t code = w & 0xFFFFu, site = w >> 16;
         return fail(code == 7 ? MPP41_ERR_TIMEOUT : code == 8 ? MPP41_ERR_BOUNDS : MPP41_ERR_CUDA,
                     "device-side error code %u at site 0x%x", code, site);

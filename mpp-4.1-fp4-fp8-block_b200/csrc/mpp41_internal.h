@@ -1,6 +1,7 @@
 // Internal launch interface shared by the .cu files of libmpp41.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -41,10 +42,32 @@ struct WqLaunch {
     uint32_t *tile_count;   // split-K fp16 output: per-tile arrival counters (clear)
 };
 
+bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols, uint64_t rows,
+              uint32_t bc, uint32_t br, CUtensorMapSwizzle sw);
+
 // OCP-MX quantization of fp32 [rows][depth] to E2M1 [rows][depth/2] + E8M0 [rows][depth/32].
 cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
                                   cudaStream_t st);
 // Returns 0 on success, 1 for an unsupported combination/shape, 2 for a CUDA error.
 int launch_wq_gemm(const WqLaunch &L, cudaStream_t st, const char **why);
+
+// One whole MLP layer as a single persistent cooperative kernel
+// (mpp41_mlp_fused.cuh). gate_epi is an Epi SwiGLU value; out_f16 selects fp16
+// output through `ws`. sync: device counters, zero on first use, left zero.
+struct FusedLaunch {
+    int wfmt, gate_epi;
+    bool out_f16;
+    const void *x, *wg, *wu, *wd;
+    const uint8_t *sg, *su, *sd;
+    void *mid, *out;
+    float *ws;
+    uint32_t *sync;
+    uint32_t *err;
+    uint32_t T, H, I, splits;
+};
+// Number of uint32 sync counters a launch needs.
+size_t fused_sync_words(uint32_t T, uint32_t H);
+// 0 = launched, 1 = this shape/format is not covered by the fused kernel, 2 = CUDA error.
+int launch_mlp_fused(const FusedLaunch &L, cudaStream_t st, const char **why);
 
 }  // namespace mpp41

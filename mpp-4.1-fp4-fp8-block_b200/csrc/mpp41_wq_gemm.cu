@@ -30,7 +30,7 @@ static EncodeTiledFn encode_fn()
 }
 
 // 2D row-major tensor [rows][cols] of `elem`-byte elements, tile box {bc, br}.
-static bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols,
+bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols,
                      uint64_t rows, uint32_t bc, uint32_t br, CUtensorMapSwizzle sw)
 {
     EncodeTiledFn fn = encode_fn();
@@ -91,18 +91,18 @@ static int launch_t(const WqLaunch &L, cudaStream_t st, const char **why)
     }
     const uint32_t smem = Cfg::smem_bytes(kps);
     if (smem > 227u * 1024u) { *why = "K range per CTA too large for shared memory"; return 1; }
-    static bool attr_set = false;   // per instantiation
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(wq_gemm_kernel<W, BN, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-            cudaSuccess) {
-            *why = "cudaFuncSetAttribute";
-            return 2;
-        }
-        attr_set = true;
+    // opt in to the dynamic shared memory this launch needs (idempotent, cheap)
+    cudaError_t e = cudaFuncSetAttribute(wq_gemm_kernel<W, BN, E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *why = cudaGetErrorString(e);
+        return 2;
     }
     const dim3 grid(L.N / Cfg::kCols, (L.M + kBM - 1) / kBM, splits);
     wq_gemm_kernel<W, BN, E><<<grid, kThreads, smem, st>>>(p);
-    if (cudaGetLastError() != cudaSuccess) { *why = "kernel launch"; return 2; }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) { *why = cudaGetErrorString(e); return 2; }
     return 0;
 }
 

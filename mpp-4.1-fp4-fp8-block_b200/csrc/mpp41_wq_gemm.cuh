@@ -244,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) wq_gemm_kernel(const __grid_const
     uint64_t *done = bars + 3 * kStages;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * kStages + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile uint32_t *s_last = tmem_slot + 2;   // split-K: this CTA finishes its tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t n_tile = blockIdx.x, m0 = blockIdx.y * kBM;
@@ -342,13 +343,40 @@ __global__ void __launch_bounds__(kThreads, 1) wq_gemm_kernel(const __grid_const
         // ------------------------------------------------ decode, then epilogue
         const uint32_t t = threadIdx.x - 64;   // 0..127
         if constexpr (W == W_MXFP4) {
+            // This CTA's scales: BN rows x kbc bytes. Rows are contiguous in the
+            // [N][K/32] plane, so with 16-byte aligned rows every thread issues its
+            // 16-byte loads back to back (one memory latency for the whole set).
             const uint32_t kb0 = k0 / 32, kblocks = p.K / 32;
-            for (uint32_t i = t; i < BN * kbc; i += 128) {
-                const uint32_t r = i / kbc, j = i % kbc;
-                uint32_t row = c0 + r;
-                const uint8_t *sp = p.scales0;
-                if (Cfg::kPair && r >= BN / 2) { row = c0 + r - BN / 2; sp = p.scales1; }
-                sScale[i] = (row < p.N) ? __ldg(sp + (size_t)row * kblocks + kb0 + j) : (uint8_t)127;
+            if ((kblocks & 15u) == 0 && (kb0 & 15u) == 0 && (kbc & 15u) == 0) {
+                const uint32_t per_row = kbc / 16, nchunk = BN * per_row;
+                for (uint32_t base = t; base < nchunk; base += 128 * 4) {
+                    uint4 v[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t c = base + 128u * j;
+                        if (c < nchunk) {
+                            const uint32_t r = c / per_row, q = c % per_row;
+                            uint32_t row = c0 + r;
+                            const uint8_t *sp = p.scales0;
+                            if (Cfg::kPair && r >= BN / 2) { row = c0 + r - BN / 2; sp = p.scales1; }
+                            v[j] = row < p.N ? __ldg(reinterpret_cast<const uint4 *>(sp + (size_t)row * kblocks + kb0) + q)
+                                             : make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t c = base + 128u * j;
+                        if (c < nchunk) reinterpret_cast<uint4 *>(sScale)[c] = v[j];
+                    }
+                }
+            } else {
+                for (uint32_t i = t; i < BN * kbc; i += 128) {
+                    const uint32_t r = i / kbc, j = i % kbc;
+                    uint32_t row = c0 + r;
+                    const uint8_t *sp = p.scales0;
+                    if (Cfg::kPair && r >= BN / 2) { row = c0 + r - BN / 2; sp = p.scales1; }
+                    sScale[i] = (row < p.N) ? __ldg(sp + (size_t)row * kblocks + kb0 + j) : (uint8_t)127;
+                }
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
         }
@@ -460,13 +488,12 @@ __global__ void __launch_bounds__(kThreads, 1) wq_gemm_kernel(const __grid_const
             if constexpr (E == EPI_SPLITK_F16) {
                 // Publish this CTA's partial, count arrivals per output tile; the
                 // last CTA of the tile converts the fp32 sum to fp16.
-                __shared__ uint32_t s_last;
                 __threadfence();
                 asm volatile("bar.sync 2, 128;" ::: "memory");
                 const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
-                if (threadIdx.x == 64) s_last = (atomicAdd(p.tile_count + tile, 1u) == gridDim.z - 1) ? 1u : 0u;
+                if (threadIdx.x == 64) *s_last = (atomicAdd(p.tile_count + tile, 1u) == gridDim.z - 1) ? 1u : 0u;
                 asm volatile("bar.sync 2, 128;" ::: "memory");
-                if (s_last) {
+                if (*s_last) {
                     __threadfence();
                     // 128 threads x 16 columns per row-pass: coalesced 64-byte row segments
                     const uint32_t r0 = threadIdx.x - 64;

@@ -149,3 +149,22 @@ def test_two_stage_api_matches_fused_call(ctx):
         ctx.synchronize()
         ga, gb = from_dev(a, dt, (T, H)), from_dev(b, dt, (T, H))
         assert rel_fro(ga, gb) <= 1e-6
+
+
+@pytest.mark.parametrize("flags", [0, mpp41.MLP_UNFUSED])
+@pytest.mark.parametrize("out_dtype", [mpp41.F16, mpp41.F32])
+def test_fused_and_unfused_paths_agree(ctx, flags, out_dtype):
+    """The single persistent layer kernel and the two-kernel path compute the
+    same layer; both against the oracle, repeatedly (self-resetting counters)."""
+    T, H, I = 256, 1024, 4096
+    d = O.baseline_mlp_inputs(T, H, I, seed=21)
+    dv = {k: to_dev(v) for k, v in d.items()}
+    desc = mpp41.mlp_desc(T, H, I, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, out_dtype, flags)
+    dt = np.float16 if out_dtype == mpp41.F16 else np.float32
+    d_out, d_scr = empty_dev(T * H * 4), empty_dev(mpp41.scratch_bytes(desc))
+    _, ref = O.mlp(0, O.W_MXFP4, 4, 1 if out_dtype == mpp41.F16 else 0, T, H, I, d["x"].view(np.uint16),
+                   d["wg"], d["wu"], d["wd"], d["sg"], d["su"], d["sd"])
+    for _ in range(3):
+        ctx.mlp(desc, dv["x"], dv["wg"], dv["wu"], dv["wd"], dv["sg"], dv["su"], dv["sd"], d_scr, d_out)
+        ctx.synchronize()
+        assert rel_fro(from_dev(d_out, dt, (T, H)), ref) <= TOL
