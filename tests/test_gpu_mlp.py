@@ -148,7 +148,8 @@ def test_two_stage_api_matches_fused_call(ctx):
         ctx.mlp_down(desc, s2, dv["wd"], dv["sd"], b, prepared=True)
         ctx.synchronize()
         ga, gb = from_dev(a, dt, (T, H)), from_dev(b, dt, (T, H))
-        assert rel_fro(ga, gb) <= 1e-6
+        # one persistent kernel vs two kernels: same math, different fp32 summation order
+        assert rel_fro(ga, gb) <= TOL
 
 
 @pytest.mark.parametrize("flags", [0, mpp41.MLP_UNFUSED])
