@@ -204,6 +204,28 @@ mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, con
                                  const void *wu, const void *wd, const uint8_t *sg, const uint8_t *su,
                                  const uint8_t *sd, void *scratch, void *out, int iterations, double *gpu_seconds);
 
+/* ---- one MLP layer without any device allocation. No counterpart in the
+ *      reference. For callers that may not call cudaMalloc (a host framework
+ *      that owns every device allocation through its own pool, a plugin
+ *      running while the process's allocator is locked): it needs no context
+ *      and no scratch argument. Its scratch -- the fp16 mid, the fp32 split-K
+ *      workspace, the kernel's counters -- is a fixed static device array of
+ *      MPP41_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps
+ *      until exit; layers needing more (mpp41_mlp_noalloc_scratch_bytes)
+ *      are rejected with MPP41_ERR_UNSUPPORTED_SHAPE. Same math as mpp41_mlp
+ *      for fp16 activations, packed weights (not MPP41_W_F16), fp16-mid SwiGLU
+ *      variants and F32/F16 output. Launches on `cuda_stream` (NULL = legacy
+ *      default stream) on the current device. The first call on a device looks
+ *      up the static array's device address (cudaGetSymbolAddress); make that
+ *      first call before any stream capture. All calls share the one array:
+ *      calls that overlap on the GPU (other streams, other host threads) race
+ *      and give wrong results -- serialise them. ---- */
+#define MPP41_NOALLOC_SCRATCH_BYTES (4u << 20)
+size_t mpp41_mlp_noalloc_scratch_bytes(const mpp41_mlp_desc *desc);
+mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *desc, const void *x, const void *wg, const void *wu,
+                               const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *out,
+                               void *cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -685,3 +685,8 @@ mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const 
 }
 
 }  // extern "C"
+
+// Lets other translation units of the library report through mpp41_last_error().
+namespace mpp41 {
+mpp41_status set_last_error(mpp41_status s, const char *msg) { return fail(s, "%s", msg); }
+}  // namespace mpp41

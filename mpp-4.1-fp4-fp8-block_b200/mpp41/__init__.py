@@ -100,6 +100,8 @@ def lib() -> C.CDLL:
         "mpp41_mlp_gate_up": ([vp, C.POINTER(MLPDesc)] + [vp] * 7, st),
         "mpp41_mlp_down": ([vp, C.POINTER(MLPDesc), vp, vp, vp, vp, C.c_int], st),
         "mpp41_quantize_mxfp4": ([vp, vp, u32, u32, vp, vp], st),
+        "mpp41_mlp_noalloc_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
+        "mpp41_mlp_noalloc": ([C.POINTER(MLPDesc)] + [vp] * 9, st),
         "mpp41_mlp_describe": ([C.c_char_p, u32, u32, u32, C.POINTER(MLPDesc)], st),
         "mpp41_mlp_benchmark": ([vp, C.POINTER(MLPDesc)] + [vp] * 9 + [C.c_int, C.POINTER(C.c_double)], st),
     }
@@ -144,6 +146,17 @@ def describe(gate_kernel: str, tokens: int, hidden: int, intermediate: int) -> M
 def mlp_desc(tokens, hidden, intermediate, wfmt=W_MXFP4, afmt=A_F16, epilogue=SWIGLU_HALF, out_dtype=F32,
              flags=0) -> MLPDesc:
     return MLPDesc(tokens, hidden, intermediate, wfmt, afmt, epilogue, out_dtype, flags)
+
+
+NOALLOC_SCRATCH_BYTES = 4 << 20
+
+
+def mlp_noalloc(desc: MLPDesc, x, wg, wu, wd, sg, su, sd, out, stream_handle=None):
+    """One MLP layer with no device allocation and no context (mpp41_mlp_noalloc):
+    for callers that may not allocate GPU memory. Uses the library's fixed static
+    scratch; overlapping calls race."""
+    _check(lib().mpp41_mlp_noalloc(C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(wd), _ptr(sg), _ptr(su),
+                                   _ptr(sd), _ptr(out), stream_handle))
 
 
 def scratch_bytes(desc: MLPDesc) -> int:
