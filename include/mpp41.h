@@ -113,6 +113,13 @@ mpp41_status mpp41_synchronize(mpp41_ctx *ctx);
 /* Device address of the context's 32-bit device error word. */
 uint32_t *mpp41_device_error_word(mpp41_ctx *ctx);
 
+/* Profiling aid with no reference counterpart: when `dev` is non-NULL, later
+ * fused MLP launches of this context write 32 counters per CTA into it
+ * (phase timestamps in ns and per-role wait/work SM cycles, slots as enum
+ * TraceSlot in csrc/mpp41_mlp_fused.cuh; zero the buffer first, sums
+ * accumulate). `words` >= 32 * number of SMs. NULL disables. */
+mpp41_status mpp41_set_trace(mpp41_ctx *ctx, unsigned long long *dev, size_t words);
+
 /* ---- buffers: replace device.makeBuffer / contents() ---- */
 mpp41_status mpp41_alloc(mpp41_ctx *ctx, size_t bytes, void **dev);
 mpp41_status mpp41_free(mpp41_ctx *ctx, void *dev);

@@ -18,6 +18,7 @@ struct mpp41_ctx {
     uint32_t *err;          // device error word
     uint32_t *sync;         // grid-wide counters of the fused layer kernel (kept zero between launches)
     size_t sync_words;
+    unsigned long long *trace;
     cudaEvent_t ev0, ev1;
 };
 
@@ -295,6 +296,7 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
         L.sync = ctx->sync;
         L.err = ctx->err;
         L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
+        L.trace = ctx->trace;
         L.splits = down_splits(d);
         if (L.out_f16 && L.splits == 1) L.splits = 2;   // the fp16 path always reduces through the workspace
         const char *why = "";
@@ -395,6 +397,16 @@ mpp41_status mpp41_set_stream(mpp41_ctx *ctx, void *s)
 void *mpp41_get_stream(mpp41_ctx *ctx) { return ctx ? ctx->stream : nullptr; }
 
 uint32_t *mpp41_device_error_word(mpp41_ctx *ctx) { return ctx ? ctx->err : nullptr; }
+
+mpp41_status mpp41_set_trace(mpp41_ctx *ctx, unsigned long long *dev, size_t words)
+{
+    NEED(ctx);
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+    if (dev && words < (size_t)128 * sms) return fail(MPP41_ERR_INVALID_ARGUMENT, "trace buffer needs 128 words per SM");
+    ctx->trace = dev;
+    return MPP41_OK;
+}
 
 mpp41_status mpp41_synchronize(mpp41_ctx *ctx)
 {

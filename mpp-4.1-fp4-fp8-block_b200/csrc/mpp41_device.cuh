@@ -70,6 +70,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity)
     return ok != 0;
 }
 
+// Non-blocking probe of a phase (acquire semantics when it reports complete).
+// Issue it early and consume the result late: its latency then overlaps other work.
+__device__ __forceinline__ uint32_t mbar_test(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok;
+}
+
 // Bounded wait for the phase with the given parity to complete. Gives up
 // after kWaitLimitNs, or early when another role of the CTA has set *abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,

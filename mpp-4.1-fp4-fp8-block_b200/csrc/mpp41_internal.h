@@ -64,6 +64,7 @@ struct FusedLaunch {
     uint32_t *sync;
     uint32_t *err;
     uint32_t T, H, I, splits;
+    unsigned long long *trace;   // optional per-CTA phase/wait counters (profiling)
 };
 // Number of uint32 sync counters a launch needs.
 size_t fused_sync_words(uint32_t T, uint32_t H);

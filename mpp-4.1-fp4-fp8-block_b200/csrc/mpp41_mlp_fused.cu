@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "mpp41_internal.h"
@@ -28,17 +29,15 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     p.n_gtiles = (L.I / 32) * ((L.T + kBM - 1) / kBM);
     p.n_dtiles = (L.H / kFBN) * L.splits * ((L.T + kBM - 1) / kBM);
     const uint32_t kbc_max = p.kbc_g > p.kbc_d ? p.kbc_g : p.kbc_d;
-    uint32_t rs = 16;
-    while (rs > 4 && Cfg::smem_bytes(rs, kbc_max) > 227u * 1024u) --rs;
-    const uint32_t smem = Cfg::smem_bytes(rs, kbc_max);
+    const uint32_t smem = Cfg::smem_bytes(kbc_max, kMaxStagesA);
     if (smem > 227u * 1024u) { *why = "shared memory"; return 1; }
-    p.raw_stages = rs;
     const uint64_t rawH = (uint64_t)L.H * wfmt_bits(W) / 8, rawI = (uint64_t)L.I * wfmt_bits(W) / 8;
+    if (rawH < (uint64_t)kChunkRow || rawI < (uint64_t)kChunkRow) { *why = "packed rows shorter than one chunk"; return 1; }
     bool ok = make_map(&p.tm_x, L.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.H, L.T, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) &&
               make_map(&p.tm_mid, L.mid, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.I, L.T, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) &&
-              make_map(&p.tm_wg, L.wg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, Cfg::kRawRow, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-              make_map(&p.tm_wu, L.wu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, Cfg::kRawRow, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-              make_map(&p.tm_wd, L.wd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawI, L.H, Cfg::kRawRow, kFBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+              make_map(&p.tm_wg, L.wg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, kChunkRow, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+              make_map(&p.tm_wu, L.wu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, kChunkRow, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+              make_map(&p.tm_wd, L.wd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawI, L.H, kChunkRow, kFBN, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (ok && W == W_MXFP4)
         ok = make_map(&p.tm_sg, L.sg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, p.kbc_g, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
              make_map(&p.tm_su, L.su, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, p.kbc_g, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
@@ -49,6 +48,7 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     p.ws = L.ws;
     p.sync = L.sync;
     p.err = L.err;
+    p.trace = L.trace;
 
     auto kern = mlp_fused_kernel<W, EG, F16>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

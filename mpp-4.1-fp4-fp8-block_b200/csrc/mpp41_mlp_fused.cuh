@@ -19,11 +19,17 @@
 // reference formats (MXFP4 E2M1 + E8M0, FP4, INT8/4/2, FP8) to fp16 in shared
 // memory; no TMA multicast is used anywhere.
 //
-// Warp roles (224 threads):
-//   warp 0      TMA producer of activation tiles (x for G, mid for D)
-//   warp 1      TMEM owner, single-thread MMA issuer (2 accumulators x 64 cols)
-//   warps 2..5  weight decode into the swizzled B ring, then tile epilogues
-//   warp 6      TMA producer of packed weight tiles (16-deep ring) and scales
+// Warp roles (448 threads):
+//   warps 0..3   TMA producers of activation tiles (x for G, mid for D), stages
+//                dealt round-robin: one warp completes about one bulk copy per
+//                memory round trip, so several warps keep several in flight
+//   warp 4       TMEM owner, single-thread MMA issuer (2 accumulators x 64 cols)
+//   warps 5..12  weight decode into the swizzled B ring (16 weights per thread
+//                per stage, two warps per scheduler), then tile epilogues
+//                (each warp: one TMEM lane quarter, one column half)
+//   warp 13      TMA producer of packed weights in 16 KB chunks (256 bytes x 64
+//                rows, i.e. 4-16 K stages per copy) and of the E8M0 scales
+// Pipeline barriers count one arrival per warp (after __syncwarp), not per thread.
 #pragma once
 
 #include <cuda.h>
@@ -36,9 +42,18 @@
 
 namespace mpp41 {
 
-constexpr int kFThreads = 224;
-constexpr int kFStagesAB = 6;      // activation + decoded-weight ring
+constexpr int kAProd = 4;          // activation producer warps 0..3 (stages round-robin)
+constexpr int kMmaWarp = 4;
+constexpr int kDec0 = 5;           // decode + epilogue warps 5..12
+constexpr int kDecWarps = 8;
+constexpr int kEpi = kDecWarps * 32;
+constexpr int kRawWarp = 13;       // weight / scale producer
+constexpr int kFThreads = 14 * 32;
+constexpr int kMaxStagesA = 8;     // activation ring depth (power of two: index math is masks)
+constexpr int kStagesB = 4;        // decoded-weight ring (power of two)
 constexpr int kFBN = 64;           // B rows per tile (G: 32 gate + 32 up)
+constexpr int kChunkRow = 256;     // packed weight bytes per row per TMA request (largest box extent)
+constexpr int kChunks = 3;         // packed weight chunk ring
 
 struct FusedParams {
     CUtensorMap tm_x;       // x [T][H] fp16, box {64, 128}, SW128
@@ -56,23 +71,50 @@ struct FusedParams {
     uint32_t splits;        // K splits of the down projection
     uint32_t kbc_g, kbc_d;  // scale bytes per row per tile
     uint32_t n_gtiles, n_dtiles;
-    uint32_t raw_stages;
+    unsigned long long *trace;  // optional: kTraceSlots per CTA (profiling aid)
 };
+
+// Trace slots per CTA (ns from %globaltimer for events, SM cycles for sums).
+enum TraceSlot : int {
+    TR_START = 0, TR_PROLOGUE = 1, TR_END = 2, TR_G_EPI_END = 3, TR_WAIT_END = 4, TR_D_EPI_END = 5, TR_SMID = 6,
+    TR_RAWP_WAIT_EMPTY = 8, TR_AP_WAIT_EMPTY = 9, TR_AP_WAIT_COUNTER = 10, TR_MMA_WAIT_A = 11, TR_MMA_WAIT_B = 12,
+    TR_MMA_WAIT_ACC = 13, TR_DEC_WAIT_RAW = 14, TR_DEC_WAIT_SLOT = 15, TR_DEC_WORK = 16, TR_EPI_G = 17,
+    TR_DEC_WAIT_ACC = 18, TR_EPI_D = 19, TR_CYCLES = 20, TR_MMA_ISSUE = 21, TR_MMA_STAGE = 32, TR_DEC_STAGE = 64,
+    TR_AP_STAGE = 96, kTraceSlots = 128
+};
+
+// mbar_wait that, while a trace is being recorded, adds the cycles it spent to `acc`.
+__device__ __forceinline__ bool mbar_wait_t(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *err,
+                                            uint32_t site, unsigned long long &acc, bool timed)
+{
+    if (!timed) return mbar_wait(bar, parity, abort, err, site);
+    const long long c0 = clock64();
+    const bool ok = mbar_wait(bar, parity, abort, err, site);
+    acc += (unsigned long long)(clock64() - c0);
+    return ok;
+}
+
+__device__ __forceinline__ long long clk_if(bool timed) { return timed ? clock64() : 0; }
 
 template <int W>
 struct FusedCfg {
-    static constexpr int kRawRow = kBK * wfmt_bits(W) / 8;
-    static constexpr uint32_t kRawBytes = kFBN * kRawRow;
+    static constexpr int kRawRow = kBK * wfmt_bits(W) / 8;       // packed bytes per row per 64-K stage
+    static constexpr uint32_t kSPC = kChunkRow / kRawRow;         // stages per weight chunk
+    static constexpr uint32_t kChunkBytes = kFBN * kChunkRow;     // 16 KB
     static constexpr uint32_t kABytes = kBM * 128;
     static constexpr uint32_t kBBytes = kFBN * 128;
-    static constexpr uint32_t kOffB = kFStagesAB * kABytes;
-    static constexpr uint32_t kOffRaw = kOffB + kFStagesAB * kBBytes;
-    __host__ __device__ static uint32_t off_scales(uint32_t raw_stages) { return kOffRaw + raw_stages * kRawBytes; }
+    // layout: [B ring][weight chunks][scales][activation ring (stages_a)]
+    static constexpr uint32_t kOffRaw = kStagesB * kBBytes;
+    static constexpr uint32_t kOffScales = kOffRaw + kChunks * kChunkBytes;
     __host__ __device__ static uint32_t scale_slot(uint32_t kbc_max) { return kFBN * kbc_max; }
-    static uint32_t smem_bytes(uint32_t raw_stages, uint32_t kbc_max)
+    __host__ __device__ static uint32_t off_a(uint32_t kbc_max)
     {
         const uint32_t sc = (W == W_MXFP4) ? 2 * scale_slot(kbc_max) : 0;
-        return 1024 + off_scales(raw_stages) + sc + 512;
+        return (kOffScales + sc + 1023u) & ~1023u;
+    }
+    static uint32_t smem_bytes(uint32_t kbc_max, uint32_t stages_a)
+    {
+        return 1024 + off_a(kbc_max) + stages_a * kABytes + 512;
     }
 };
 
@@ -106,7 +148,7 @@ __device__ __forceinline__ bool wait_counter(const uint32_t *p, uint32_t target,
     }
 }
 
-// Named barrier over the 128 epilogue threads that also ORs a predicate:
+// Named barrier over the 256 epilogue threads that also ORs a predicate:
 // every participant gets the same answer, so no thread can skip a later
 // barrier the others wait on.
 __device__ __forceinline__ bool epi_bar_any(bool pred)
@@ -115,12 +157,28 @@ __device__ __forceinline__ bool epi_bar_any(bool pred)
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.or.pred p, 1, 128, q;\n\t"
+        "bar.red.or.pred p, 1, 256, q;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(r)
         : "r"((uint32_t)pred)
         : "memory");
     return r != 0;
+}
+
+__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d)
+{
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
 }
 
 struct TileInfo {
@@ -156,52 +214,65 @@ template <int W, int EG, bool OUT_F16>
 __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_constant__ FusedParams p)
 {
     using Cfg = FusedCfg<W>;
+    constexpr uint32_t SPC = Cfg::kSPC;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t RS = p.raw_stages;
     const uint32_t kbc_max = p.kbc_g > p.kbc_d ? p.kbc_g : p.kbc_d;
-    uint8_t *sA = smem;
-    uint8_t *sB = smem + Cfg::kOffB;
+    constexpr uint32_t SA = kMaxStagesA;   // compile-time: the ring index math stays shifts and masks
+    uint8_t *sB = smem;
     uint8_t *sRaw = smem + Cfg::kOffRaw;
-    uint8_t *sSc = smem + Cfg::off_scales(RS);
+    uint8_t *sSc = smem + Cfg::kOffScales;
+    uint8_t *sA = smem + Cfg::off_a(kbc_max);
     const uint32_t sc_slot = (W == W_MXFP4) ? Cfg::scale_slot(kbc_max) : 0;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sSc + 2 * sc_slot);
-    uint64_t *raw_full = bars;                  // [RS]
-    uint64_t *raw_empty = raw_full + 16;        // [RS]
-    uint64_t *ab_full_a = raw_empty + 16;       // [6] activation tile landed
-    uint64_t *ab_full_b = ab_full_a + kFStagesAB;  // [6] decoded weights ready
-    uint64_t *ab_empty = ab_full_b + kFStagesAB;   // [6] MMA done with the stage
-    uint64_t *sc_full = ab_empty + kFStagesAB;  // [2]
-    uint64_t *sc_empty = sc_full + 2;           // [2]
-    uint64_t *acc_full = sc_empty + 2;          // [2]
-    uint64_t *acc_empty = acc_full + 2;         // [2]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sA + SA * Cfg::kABytes);
+    uint64_t *ck_full = bars;                       // [kChunks] packed weight chunk landed
+    uint64_t *ck_empty = ck_full + kChunks;         // [kChunks] chunk decoded
+    // Stage s uses activation slot s % SA and decoded-weight slot s % 4. One
+    // barrier pair per stage: full[s % SA] completes when the activation copy
+    // landed AND the 4 warps of the decode group owning stage s arrived; the
+    // MMA commits empty[s % SA]. A decode group reuses weight slot s % 4 after
+    // waiting for stage s-4 to be committed on empty[(s-4) % SA].
+    uint64_t *a_full = ck_empty + kChunks;          // [SA]
+    uint64_t *a_empty = a_full + kMaxStagesA;       // [SA]
+    uint64_t *sc_full = a_empty + kMaxStagesA;      // [2]
+    uint64_t *sc_empty = sc_full + 2;               // [2]
+    uint64_t *acc_full = sc_empty + 2;              // [2]
+    uint64_t *acc_empty = acc_full + 2;             // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile uint32_t *s_last = tmem_slot + 2;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ntiles = p.n_gtiles + p.n_dtiles;
+    unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceSlots : nullptr;
+    const long long clk0 = p.trace ? clock64() : 0;
+    unsigned long long tw0 = 0, tw1 = 0, tw2 = 0, tw3 = 0;   // per-role accumulators (trace only)
+    if (tr && threadIdx.x == 0) {
+        tr[TR_START] = globaltimer_ns();
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        tr[TR_SMID] = smid;
+    }
 
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < RS; ++s) {
-            mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], 128);
+        for (int s = 0; s < kChunks; ++s) {
+            mbar_init(&ck_full[s], 1);
+            mbar_init(&ck_empty[s], kDecWarps);
         }
-        for (int s = 0; s < kFStagesAB; ++s) {
-            mbar_init(&ab_full_a[s], 1);
-            mbar_init(&ab_full_b[s], 128);
-            mbar_init(&ab_empty[s], 1);
+        for (uint32_t s = 0; s < SA; ++s) {
+            mbar_init(&a_full[s], 1 + kDecWarps / 2);
+            mbar_init(&a_empty[s], 1);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&sc_full[s], 1);
-            mbar_init(&sc_empty[s], 128);
+            mbar_init(&sc_empty[s], kDecWarps);
             mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], 128);
+            mbar_init(&acc_empty[s], kDecWarps);
         }
         *abort = 0;
         fence_mbar_init();
     }
-    if (warp == 6 && lane == 0) {
+    if (warp == kRawWarp && lane == 0) {
         tma_prefetch_desc(&p.tm_wg);
         tma_prefetch_desc(&p.tm_wu);
         tma_prefetch_desc(&p.tm_wd);
@@ -215,7 +286,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         tma_prefetch_desc(&p.tm_x);
         tma_prefetch_desc(&p.tm_mid);
     }
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tmem_alloc(tmem_slot, 128);
         tmem_relinquish();
     }
@@ -223,11 +294,12 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (tr && threadIdx.x == 0) tr[TR_PROLOGUE] = globaltimer_ns();
 
-    if (warp == 6) {
-        // ------------------------------------------------ weight / scale producer
+    if (warp == kRawWarp) {
+        // ------------------------------------------------ packed weight / scale producer
         if (lane == 0) {
-            uint32_t gs = 0, ti_n = 0;
+            uint32_t gc = 0, ti_n = 0;
             for (uint32_t t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++ti_n) {
                 const TileInfo ti = tile_info(p, t);
                 if constexpr (W == W_MXFP4) {
@@ -243,53 +315,61 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                         tma_load_2d(dst, &p.tm_sd, (int32_t)(ti.kb * p.kbc_d), (int32_t)ti.c0, &sc_full[slot]);
                     }
                 }
-                const uint32_t kstage0 = ti.kb * ti.nk;
-                for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
-                    const uint32_t st = gs % RS, ph = (gs / RS) & 1u;
-                    if (!mbar_wait(&raw_empty[st], ph ^ 1u, abort, p.err, 0x602)) break;
-                    mbar_arrive_expect_tx(&raw_full[st], Cfg::kRawBytes);
-                    uint8_t *dst = sRaw + st * Cfg::kRawBytes;
-                    const int32_t kx = (int32_t)((kstage0 + s) * Cfg::kRawRow);
+                const uint32_t byte0 = ti.kb * ti.nk * Cfg::kRawRow;   // this tile's K range within the row
+                const uint32_t nck = (ti.nk + SPC - 1) / SPC;
+                for (uint32_t c = 0; c < nck; ++c, ++gc) {
+                    const uint32_t st = gc % kChunks, ph = (gc / kChunks) & 1u;
+                    if (!mbar_wait_t(&ck_empty[st], ph ^ 1u, abort, p.err, 0x602, tw0, tr != nullptr)) break;
+                    mbar_arrive_expect_tx(&ck_full[st], Cfg::kChunkBytes);
+                    uint8_t *dst = sRaw + st * Cfg::kChunkBytes;
+                    const int32_t kx = (int32_t)(byte0 + c * kChunkRow);
                     if (ti.is_g) {
-                        tma_load_2d(dst, &p.tm_wg, kx, (int32_t)ti.c0, &raw_full[st]);
-                        tma_load_2d(dst + 32 * Cfg::kRawRow, &p.tm_wu, kx, (int32_t)ti.c0, &raw_full[st]);
+                        tma_load_2d(dst, &p.tm_wg, kx, (int32_t)ti.c0, &ck_full[st]);
+                        tma_load_2d(dst + 32 * kChunkRow, &p.tm_wu, kx, (int32_t)ti.c0, &ck_full[st]);
                     } else {
-                        tma_load_2d(dst, &p.tm_wd, kx, (int32_t)ti.c0, &raw_full[st]);
+                        tma_load_2d(dst, &p.tm_wd, kx, (int32_t)ti.c0, &ck_full[st]);
                     }
                 }
             }
-            // no loads left in flight when the CTA exits
-            for (uint32_t t = (gs > RS ? gs - RS : 0); t < gs; ++t)
-                mbar_wait(&raw_full[t % RS], (t / RS) & 1u, nullptr, p.err, 0x603);
+            // no copies left in flight when the CTA exits
+            for (uint32_t t = (gc > kChunks ? gc - kChunks : 0); t < gc; ++t)
+                mbar_wait(&ck_full[t % kChunks], (t / kChunks) & 1u, nullptr, p.err, 0x603);
         }
-    } else if (warp == 0) {
-        // ------------------------------------------------ activation producer
+    } else if (warp < kAProd) {
+        // ------------------------------------------------ activation producers
         if (lane == 0) {
             uint32_t gs = 0;
             bool waited = false;
             for (uint32_t t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
                 const TileInfo ti = tile_info(p, t);
-                if (!ti.is_g && !waited) {
-                    // mid is written by other CTAs' G tiles (generic stores); wait for
-                    // all of them, then order those writes before our TMA reads
-                    if (!wait_counter(p.sync, p.n_gtiles, abort, p.err, 0x701)) break;
-                    fence_proxy_async_global();
-                    waited = true;
-                }
                 const CUtensorMap *tm = ti.is_g ? &p.tm_x : &p.tm_mid;
                 const uint32_t kstage0 = ti.kb * ti.nk;
+                bool ok = true;
                 for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
-                    const uint32_t st = gs % kFStagesAB, ph = (gs / kFStagesAB) & 1u;
-                    if (!mbar_wait(&ab_empty[st], ph ^ 1u, abort, p.err, 0x702)) break;
-                    mbar_arrive_expect_tx(&ab_full_a[st], Cfg::kABytes);
+                    if (gs % kAProd != (uint32_t)warp) continue;
+                    if (!ti.is_g && !waited) {
+                        // mid is written by other CTAs' G tiles (generic stores); wait
+                        // for all of them, then order those writes before our TMA reads
+                        const long long cw = clk_if(tr);
+                        if (!wait_counter(p.sync, p.n_gtiles, abort, p.err, 0x701)) { ok = false; break; }
+                        if (tr) tw1 += (unsigned long long)(clock64() - cw);
+                        if (tr && warp == 0) tr[TR_WAIT_END] = globaltimer_ns();
+                        fence_proxy_async_global();
+                        waited = true;
+                    }
+                    const uint32_t st = gs % SA, ph = (gs / SA) & 1u;
+                    if (!mbar_wait_t(&a_empty[st], ph ^ 1u, abort, p.err, 0x702, tw0, tr != nullptr)) { ok = false; break; }
+                    if (tr && gs < 32) tr[TR_AP_STAGE + gs] = (unsigned long long)(clock64() - clk0);
+                    mbar_arrive_expect_tx(&a_full[st], Cfg::kABytes);
                     tma_load_2d(sA + st * Cfg::kABytes, tm, (int32_t)((kstage0 + s) * kBK), (int32_t)ti.m0,
-                                &ab_full_a[st]);
+                                &a_full[st]);
                 }
+                if (!ok) break;
             }
-            for (uint32_t t = (gs > kFStagesAB ? gs - kFStagesAB : 0); t < gs; ++t)
-                mbar_wait(&ab_full_a[t % kFStagesAB], (t / kFStagesAB) & 1u, nullptr, p.err, 0x703);
+            for (uint32_t t = (gs > SA ? gs - SA : 0); t < gs; ++t)
+                if (t % kAProd == (uint32_t)warp) mbar_wait(&a_full[t % SA], (t / SA) & 1u, nullptr, p.err, 0x703);
         }
-    } else if (warp == 1) {
+    } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_f32(kBM, kFBN);
@@ -297,87 +377,118 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
             for (uint32_t t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++ti_n) {
                 const TileInfo ti = tile_info(p, t);
                 const uint32_t acc = ti_n & 1u;
-                if (!mbar_wait(&acc_empty[acc], ((ti_n >> 1) & 1u) ^ 1u, abort, p.err, 0x801)) break;
+                if (!mbar_wait_t(&acc_empty[acc], ((ti_n >> 1) & 1u) ^ 1u, abort, p.err, 0x801, tw2, tr != nullptr)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + acc * kFBN;
+                uint32_t ra = mbar_test(&a_full[gs % SA], (gs / SA) & 1u);
                 for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
-                    const uint32_t st = gs % kFStagesAB, ph = (gs / kFStagesAB) & 1u;
-                    if (!mbar_wait(&ab_full_a[st], ph, abort, p.err, 0x802)) break;
-                    if (!mbar_wait(&ab_full_b[st], ph, abort, p.err, 0x803)) break;
+                    const uint32_t sa = gs % SA, pa = (gs / SA) & 1u;
+                    const uint32_t sbb = gs % kStagesB;
+                    if (!ra && !mbar_wait_t(&a_full[sa], pa, abort, p.err, 0x802, tw0, tr != nullptr)) break;
+                    // probe the next stage now; the answer is needed only after this
+                    // stage's MMAs are issued
+                    const uint32_t gn = gs + 1;
+                    ra = (s + 1 < ti.nk) ? mbar_test(&a_full[gn % SA], (gn / SA) & 1u) : 0u;
+                    const long long cis = clk_if(tr);
                     tc_fence_after();
-                    const uint64_t ad = smem_desc_sw128(sA + st * Cfg::kABytes);
-                    const uint64_t bd = smem_desc_sw128(sB + st * Cfg::kBBytes);
+                    const uint64_t ad = smem_desc_sw128(sA + sa * Cfg::kABytes);
+                    const uint64_t bd = smem_desc_sw128(sB + sbb * Cfg::kBBytes);
 #pragma unroll
                     for (uint32_t k = 0; k < kBK / 16; ++k)
                         mma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (s | k) != 0u);
-                    mma_commit(&ab_empty[st]);
+                    mma_commit(&a_empty[sa]);
+                    if (tr) tw3 += (unsigned long long)(clock64() - cis);
+                    if (tr && gs < 32) tr[TR_MMA_STAGE + gs] = (unsigned long long)(clock64() - clk0);
                 }
                 mma_commit(&acc_full[acc]);
             }
         }
     } else {
         // ------------------------------------------------ decode + epilogue
-        const uint32_t t128 = threadIdx.x - 64;
-        const uint32_t quarter = warp & 3;
+        const uint32_t te = threadIdx.x - kDec0 * 32;   // 0..255
+        const uint32_t quarter = warp & 3;             // TMEM lanes 32*quarter..+31
+        const uint32_t colh = (warp - kDec0) >> 2;     // column half of the tile
         const uint32_t row = quarter * 32 + lane;
-        uint32_t gs = 0, ti_n = 0;
+        // decode: two groups of 4 warps take alternate stages; 32 weights per thread
+        const uint32_t grp = (warp - kDec0) >> 2;
+        const uint32_t tg = te & 127u, dr = tg >> 1, dh = tg & 1u;   // B row, half of the 64-wide stage
+        uint32_t gs = 0, gc = 0, ti_n = 0;
         for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti_n) {
             const TileInfo ti = tile_info(p, t);
             const uint32_t slot = ti_n & 1u;
             const uint32_t kbc = ti.is_g ? p.kbc_g : p.kbc_d;
             const uint8_t *scl = sSc + slot * sc_slot;
             if constexpr (W == W_MXFP4) mbar_wait(&sc_full[slot], (ti_n >> 1) & 1u, abort, p.err, 0x901);
+            uint32_t cst = 0;
             for (uint32_t s = 0; s < ti.nk && !*abort; ++s, ++gs) {
-                const uint32_t rst = gs % RS, rph = (gs / RS) & 1u;
-                const uint32_t st = gs % kFStagesAB, ph = (gs / kFStagesAB) & 1u;
-                if (!mbar_wait(&raw_full[rst], rph, abort, p.err, 0x902)) break;
-                if (!mbar_wait(&ab_empty[st], ph ^ 1u, abort, p.err, 0x903)) break;
-                const uint8_t *raw = sRaw + rst * Cfg::kRawBytes;
-                uint8_t *bt = sB + st * Cfg::kBBytes;
-                const uint32_t r = t128 >> 1, h = t128 & 1u;
-                uint32_t sb = 127u;
-                if constexpr (W == W_MXFP4) {
+                const uint32_t sc = s % SPC;
+                const bool mine = (gs & 1u) == grp;
+                if (sc == 0) {
+                    cst = gc % kChunks;
+                    if (!mbar_wait_t(&ck_full[cst], (gc / kChunks) & 1u, abort, p.err, 0x902, tw0, tr != nullptr)) break;
+                }
+                if (mine) {
+                    const uint32_t st = gs % kStagesB;
+                    if (gs >= kStagesB) {   // stage gs-4 (same weight slot) consumed by the MMA
+                        const uint32_t g3 = gs - kStagesB;
+                        if (!mbar_wait_t(&a_empty[g3 % SA], (g3 / SA) & 1u, abort, p.err, 0x903, tw1, tr != nullptr)) break;
+                    }
+                    const long long cdec = clk_if(tr);
+                    const uint8_t *raw = sRaw + cst * Cfg::kChunkBytes + dr * kChunkRow + sc * Cfg::kRawRow;
+                    uint32_t sb = 127u;
                     // G: rows 0..31 gate scales, 32..63 up scales, each kbc_g wide
-                    sb = scl[r * kbc + 2 * s + h];
-                }
-                uint32_t o[16];
-                decode_chunk<W>(raw + r * Cfg::kRawRow + h * (Cfg::kRawRow / 2), sb, o);
-                uint8_t *rowp = bt + r * 128;
+                    if constexpr (W == W_MXFP4) sb = scl[dr * kbc + 2 * s + dh];
+                    uint32_t o[16];
+                    decode_chunk<W>(raw + dh * (Cfg::kRawRow / 2), sb, o);
+                    uint8_t *rowp = sB + st * Cfg::kBBytes + dr * 128;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t phys = ((h * 4 + q) ^ (r & 7u)) * 16u;
-                    *reinterpret_cast<uint4 *>(rowp + phys) = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t phys = ((dh * 4 + q) ^ (dr & 7u)) * 16u;
+                        *reinterpret_cast<uint4 *>(rowp + phys) = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[gs % SA]);
+                    if (tr) tw2 += (unsigned long long)(clock64() - cdec);
+                    if (tr && te == 0 && gs < 32) tr[TR_DEC_STAGE + gs] = (unsigned long long)(clock64() - clk0);
                 }
-                fence_proxy_async_smem();
-                mbar_arrive(&raw_empty[rst]);
-                mbar_arrive(&ab_full_b[st]);
+                if ((sc == SPC - 1) || (s + 1 == ti.nk)) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ck_empty[cst]);
+                    ++gc;
+                }
             }
-            if constexpr (W == W_MXFP4) mbar_arrive(&sc_empty[slot]);
+            if constexpr (W == W_MXFP4) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sc_empty[slot]);
+            }
 
             // ---------------------------------------------- tile epilogue
             const uint32_t acc = ti_n & 1u;
-            mbar_wait(&acc_full[acc], (ti_n >> 1) & 1u, abort, p.err, 0x904);
+            mbar_wait_t(&acc_full[acc], (ti_n >> 1) & 1u, abort, p.err, 0x904, tw3, tr != nullptr);
+            const long long cepi = clk_if(tr);
             if (epi_bar_any(*abort != 0)) break;
             tc_fence_after();
             const uint32_t taddr = tmem + ((quarter * 32u) << 16) + acc * kFBN;
             const uint32_t m = ti.m0 + row;
             if (ti.is_g) {
-                uint32_t g[32], u[32];
-                tmem_ld_32x32b_x32(taddr, g);
-                tmem_ld_32x32b_x32(taddr + 32, u);
+                uint32_t g[16], u[16];
+                tmem_ld_32x32b_x16(taddr + colh * 16, g);
+                tmem_ld_32x32b_x16(taddr + 32 + colh * 16, u);
                 tmem_ld_wait();
                 tc_fence_before();
-                mbar_arrive(&acc_empty[acc]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
                 if (m < p.T) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(p.mid + (size_t)m * p.I + ti.c0);
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.mid + (size_t)m * p.I + ti.c0 + colh * 16);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
+                    for (int i = 0; i < 2; ++i) {
                         uint32_t w4[4];
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const int e = 8 * i + 2 * j;
-                            w4[j] = half2_bits(swiglu<EG>(__uint_as_float(g[e]), __uint_as_float(u[e])),
-                                               swiglu<EG>(__uint_as_float(g[e + 1]), __uint_as_float(u[e + 1])));
+                        for (int j2 = 0; j2 < 4; ++j2) {
+                            const int e = 8 * i + 2 * j2;
+                            w4[j2] = half2_bits(swiglu<EG>(__uint_as_float(g[e]), __uint_as_float(u[e])),
+                                                swiglu<EG>(__uint_as_float(g[e + 1]), __uint_as_float(u[e + 1])));
                         }
                         dst[i] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     }
@@ -389,45 +500,49 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     const uint32_t total = p.T * p.H / 4;
                     const uint32_t per = (total + p.n_gtiles - 1) / p.n_gtiles;
                     const uint32_t beg = t * per, end = min(beg + per, total);
-                    for (uint32_t i = beg + t128; i < end; i += 128) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (uint32_t i = beg + te; i < end; i += kEpi) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                // publish: stores -> visible to other CTAs' TMA (async proxy) reads
+                // publish: our generic stores ordered before other CTAs' TMA (async
+                // proxy) reads; one release by one thread after the CTA barrier
                 fence_proxy_async_global();
-                __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (t128 == 0) atomicAdd(p.sync, 1u);
-            } else {
-                (void)ld_acquire_gpu(p.sync);   // orders the clears above before our atomics
-                float4 *dst = reinterpret_cast<float4 *>((OUT_F16 ? p.ws : static_cast<float *>(p.out)) +
-                                                         (size_t)m * p.H + ti.c0);
-#pragma unroll 1
-                for (int cc = 0; cc < kFBN / 32; ++cc) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(taddr + cc * 32, v);
-                    tmem_ld_wait();
-                    if (m < p.T) {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            atomicAdd(dst + cc * 8 + i,
-                                      make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                                  __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
-                    }
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (te == 0) {
+                    __threadfence();
+                    atomicAdd(p.sync, 1u);
                 }
+                if (tr && te == 0) {
+                    tr[TR_G_EPI_END] = globaltimer_ns();
+                    tr[TR_EPI_G] += (unsigned long long)(clock64() - cepi);
+                }
+            } else {
+                (void)ld_acquire_gpu(p.sync);   // orders the clears above before our reductions
+                float *dst = (OUT_F16 ? p.ws : static_cast<float *>(p.out)) + (size_t)m * p.H + ti.c0 + colh * 32;
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(taddr + colh * 32, v);
+                tmem_ld_wait();
                 tc_fence_before();
-                mbar_arrive(&acc_empty[acc]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                if (m < p.T) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        red_add_v4(dst + 4 * i, __uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                   __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                }
+                if (tr && te == 0) tr[TR_EPI_D] += (unsigned long long)(clock64() - cepi);
                 if constexpr (OUT_F16) {
                     __threadfence();
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    asm volatile("bar.sync 1, 256;" ::: "memory");
                     const uint32_t tile = (ti.m0 / kBM) * (p.H / kFBN) + ti.c0 / kFBN;
-                    if (t128 == 0) {
+                    if (te == 0) {
                         const uint32_t prev = atomicAdd(p.sync + 2 + tile, 1u);
                         *s_last = (prev == p.splits - 1) ? 1u : 0u;
                         if (prev == p.splits - 1) atomicExch(p.sync + 2 + tile, 0u);   // reset for the next launch
                     }
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    asm volatile("bar.sync 1, 256;" ::: "memory");
                     if (*s_last) {
                         __threadfence();
-                        for (uint32_t i = t128; i < kBM * (kFBN / 8); i += 128) {
+                        for (uint32_t i = te; i < kBM * (kFBN / 8); i += kEpi) {
                             const uint32_t rr = i / (kFBN / 8), c8 = (i % (kFBN / 8)) * 8;
                             const uint32_t mm = ti.m0 + rr;
                             if (mm < p.T) {
@@ -448,13 +563,23 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
     // ---------------------------------------------------- teardown
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, 128);
     }
     // Every tile of this CTA is finished (no thread reads the grid counters any
     // more): count the CTA; the last one resets the counters for the next
     // launch on this stream.
+    if (tr) {
+        if (warp == kRawWarp && lane == 0) tr[TR_RAWP_WAIT_EMPTY] = tw0;
+        if (warp == 0 && lane == 0) { tr[TR_AP_WAIT_EMPTY] = tw0; tr[TR_AP_WAIT_COUNTER] = tw1; }
+        if (warp == kMmaWarp && lane == 0) { tr[TR_MMA_WAIT_A] = tw0; tr[TR_MMA_WAIT_B] = tw1; tr[TR_MMA_WAIT_ACC] = tw2; tr[TR_MMA_ISSUE] = tw3; }
+        if (threadIdx.x == kDec0 * 32) {
+            tr[TR_DEC_WAIT_RAW] = tw0; tr[TR_DEC_WAIT_SLOT] = tw1; tr[TR_DEC_WORK] = tw2; tr[TR_DEC_WAIT_ACC] = tw3;
+            tr[TR_D_EPI_END] = globaltimer_ns();
+        }
+        if (threadIdx.x == 0) { tr[TR_END] = globaltimer_ns(); tr[TR_CYCLES] = (unsigned long long)(clock64() - clk0); }
+    }
     if (threadIdx.x == 0 && atomicAdd(p.sync + 1, 1u) == gridDim.x - 1) {
         atomicExch(p.sync + 0, 0u);
         atomicExch(p.sync + 1, 0u);

@@ -103,36 +103,38 @@ template <int W>
 __device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_byte, uint32_t (&o)[16])
 {
     if constexpr (W == W_FP4 || W == W_MXFP4) {
+        // hardware E2M1 pair conversion (low nibble -> low half): the exact E2M1
+        // values in fp16; then value * 2^(s-127) with one exact fp16 multiply when
+        // 2^(s-127) is a normal fp16 (s in [113,142]); otherwise fp32 math and a
+        // single rounding, as half(float(lut) * e8m0) in mxfp4_dequant_*_half.
         const uint4 v = *reinterpret_cast<const uint4 *>(raw);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            uint32_t t[4];
-            e2m1x8_to_half2_scaled14(w[q], t);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) o[4 * q + i] = t[i];
+            asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+                "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+                : "=r"(o[4 * q]), "=r"(o[4 * q + 1]), "=r"(o[4 * q + 2]), "=r"(o[4 * q + 3])
+                : "r"(w[q]));
         }
-        // value = decoded * 2^14 * 2^(s-127). Exact fp16 products: one multiply by
-        // 2^(s-113) when that is a normal fp16 (s in [99,128]); two multiplies for
-        // s in [129,142]; otherwise fp32 math and a single rounding, which is what
-        // half(float(lut) * e8m0) gives in mxfp4_dequant_*_half.
-        const uint32_t s = (W == W_FP4) ? 127u : scale_byte;
-        if (s >= 99u && s <= 128u) {
-            const uint32_t f = (s - 98u) << 10;
-            const uint32_t f2 = f | (f << 16);
+        if constexpr (W == W_MXFP4) {
+            const uint32_t s = scale_byte;
+            if (s >= 113u && s <= 142u) {
+                if (s != 127u) {
+                    const uint32_t f = ((s - 112u) << 10) * 0x10001u;   // 2^(s-127) as fp16x2
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = hmul2_bits(o[i], f2);
-        } else if (s >= 129u && s <= 142u) {
-            const uint32_t fa = 0x78007800u;                      // 2^15
-            const uint32_t fb = ((s - 113u) << 10) * 0x10001u;    // 2^(s-128)
+                    for (int i = 0; i < 16; ++i) o[i] = hmul2_bits(o[i], f);
+                }
+            } else {
+                const float sf = e8m0_to_float(s);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = hmul2_bits(hmul2_bits(o[i], fa), fb);
-        } else {
-            const float sf = 16384.0f * e8m0_to_float(s);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                __half2 h = *reinterpret_cast<__half2 *>(&o[i]);
-                o[i] = half2_bits(__low2float(h) * sf, __high2float(h) * sf);
+                for (int i = 0; i < 16; ++i) {
+                    __half2 h = *reinterpret_cast<__half2 *>(&o[i]);
+                    o[i] = half2_bits(__low2float(h) * sf, __high2float(h) * sf);
+                }
             }
         }
     } else if constexpr (W == W_I4) {

@@ -81,6 +81,7 @@ def lib() -> C.CDLL:
         "mpp41_get_stream": ([vp], vp),
         "mpp41_synchronize": ([vp], st),
         "mpp41_device_error_word": ([vp], vp),
+        "mpp41_set_trace": ([vp, vp, sz], st),
         "mpp41_alloc": ([vp, sz, C.POINTER(vp)], st),
         "mpp41_free": ([vp, vp], st),
         "mpp41_upload": ([vp, vp, vp, sz], st),
@@ -201,6 +202,10 @@ class Context:
 
     def synchronize(self):
         _check(lib().mpp41_synchronize(self.h))
+
+    def set_trace(self, buf):
+        """Per-CTA counters of the fused MLP kernel into `buf` (zeroed int64 CUDA tensor); None disables."""
+        _check(lib().mpp41_set_trace(self.h, _ptr(buf), buf.numel() if buf is not None else 0))
 
     def error_word_ptr(self) -> int:
         return lib().mpp41_device_error_word(self.h)
