@@ -43,8 +43,8 @@ BYTES_LAYER = BYTES_W + T * H * 2 + T * H * 2
 ROTATE = 24
 METRIC = "MXFP4 fused-MLP µs/layer & TFLOP/s (% of roofline) at 1/2/4/8 B200"
 # DRAM bytes per launch of mlp_fused_kernel from one ncu capture of this
-# workload (profiles/mlp_fused_mxfp4_t128_h1024_i4096.md); None until captured.
-NCU_TRAFFIC_LAYER = None
+# workload (profiles/mlp_fused_mxfp4_t128_h1024_i4096.md).
+NCU_TRAFFIC_LAYER = 7001344
 
 
 def load_peaks():
