@@ -227,7 +227,7 @@ mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, con
  *      first call before any stream capture. All calls share the one array:
  *      calls that overlap on the GPU (other streams, other host threads) race
  *      and give wrong results -- serialise them. ---- */
-#define MPP41_NOALLOC_SCRATCH_BYTES (4u << 20)
+#define MPP41_NOALLOC_SCRATCH_BYTES (8u << 20)
 size_t mpp41_mlp_noalloc_scratch_bytes(const mpp41_mlp_desc *desc);
 mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *desc, const void *x, const void *wg, const void *wu,
                                const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *out,

@@ -154,8 +154,16 @@ uint32_t down_splits(const mpp41_mlp_desc *d)
     return pick_splits((d->hidden / 64) * ((d->tokens + 127) / 128), d->intermediate);
 }
 
-// Scratch layout: [mid][fp32 workspace T x H][tile counters] (the last two
-// only for fp16 output).
+uint32_t fused_splits(const mpp41_mlp_desc *d)
+{
+    const uint32_t s = down_splits(d);
+    return (d->out_dtype == MPP41_F16 && s == 1) ? 2 : s;   // fp16 output always reduces through the workspace
+}
+
+// Scratch layout: [mid][fp32 workspace T x H][tile counters] for the
+// two-kernel path (the last two only for fp16 output). The fused kernel uses
+// [mid][splits x T x H fp32 partials] over the same bytes; the total covers
+// both.
 struct ScratchLayout {
     size_t mid_bytes, ws_off, ws_bytes, cnt_off, cnt_bytes, total;
 };
@@ -173,6 +181,8 @@ ScratchLayout scratch_layout(const mpp41_mlp_desc *d)
         L.cnt_off = L.ws_off;
     }
     L.total = L.cnt_off + L.cnt_bytes;
+    const size_t fused = L.ws_off + fused_ws_bytes(d->tokens, d->hidden, fused_splits(d));
+    if (fused > L.total) L.total = fused;
     return L;
 }
 
@@ -292,13 +302,12 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
         L.x = x; L.wg = wg; L.wu = wu; L.wd = wd; L.sg = sg; L.su = su; L.sd = sd;
         L.mid = scratch;
         L.out = out;
-        L.ws = L.out_f16 ? reinterpret_cast<float *>(static_cast<uint8_t *>(scratch) + SL.ws_off) : nullptr;
+        L.ws = reinterpret_cast<float *>(static_cast<uint8_t *>(scratch) + SL.ws_off);
         L.sync = ctx->sync;
         L.err = ctx->err;
         L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
         L.trace = ctx->trace;
-        L.splits = down_splits(d);
-        if (L.out_f16 && L.splits == 1) L.splits = 2;   // the fp16 path always reduces through the workspace
+        L.splits = fused_splits(d);
         const char *why = "";
         const int rc = launch_mlp_fused(L, st, &why);
         if (rc == 0) return MPP41_OK;

@@ -60,7 +60,7 @@ struct FusedLaunch {
     const void *x, *wg, *wu, *wd;
     const uint8_t *sg, *su, *sd;
     void *mid, *out;
-    float *ws;
+    float *ws;                   // fused_ws_bytes(T, H, splits): fp32 split partials
     uint32_t *sync;
     uint32_t *err;
     uint32_t T, H, I, splits;
@@ -68,6 +68,8 @@ struct FusedLaunch {
 };
 // Number of uint32 sync counters a launch needs.
 size_t fused_sync_words(uint32_t T, uint32_t H);
+// Bytes of the fp32 workspace a launch needs (one T x H partial per K split).
+size_t fused_ws_bytes(uint32_t T, uint32_t H, uint32_t splits);
 // 0 = launched, 1 = this shape/format is not covered by the fused kernel, 2 = CUDA error.
 int launch_mlp_fused(const FusedLaunch &L, cudaStream_t st, const char **why);
 

@@ -13,6 +13,8 @@ namespace mpp41 {
 
 size_t fused_sync_words(uint32_t T, uint32_t H) { return 2 + (size_t)(H / kFBN) * ((T + kBM - 1) / kBM); }
 
+size_t fused_ws_bytes(uint32_t T, uint32_t H, uint32_t splits) { return (size_t)splits * T * H * 4; }
+
 template <int W, int EG, bool F16>
 static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
@@ -61,6 +63,9 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     const uint32_t ntiles = p.n_gtiles + p.n_dtiles;
     uint32_t grid = (uint32_t)(sms * per_sm);
     if (grid > ntiles) grid = ntiles;
+    // tiles go to CTAs round-robin, down tiles last: with no more down tiles
+    // than CTAs each CTA holds at most one and it is its final tile
+    p.d_spin = p.n_dtiles <= grid ? 1u : 0u;
 
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
@@ -100,7 +105,7 @@ static int launch_fw(const FusedLaunch &L, cudaStream_t st, const char **why)
 
 int launch_mlp_fused(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
-    if (L.H % kFBN || L.I % (kBK * L.splits) || L.I % 32) { *why = "shape"; return 1; }
+    if (L.H % kFBN || L.H % kFBK || L.I % (kFBK * L.splits) || L.I % 32) { *why = "shape"; return 1; }
     switch (L.wfmt) {
     case W_I8: return launch_fw<W_I8>(L, st, why);
     case W_I4: return launch_fw<W_I4>(L, st, why);

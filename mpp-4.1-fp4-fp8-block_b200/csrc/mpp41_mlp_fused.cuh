@@ -49,8 +49,9 @@ constexpr int kDecWarps = 8;
 constexpr int kEpi = kDecWarps * 32;
 constexpr int kRawWarp = 13;       // weight / scale producer
 constexpr int kFThreads = 14 * 32;
-constexpr int kMaxStagesA = 8;     // activation ring depth (power of two: index math is masks)
-constexpr int kStagesB = 4;        // decoded-weight ring (power of two)
+constexpr int kFBK = 128;          // K per pipeline stage: two 64-wide 128-byte swizzle atoms
+constexpr int kMaxStagesA = 4;     // activation ring depth (power of two: index math is masks)
+constexpr int kStagesB = 2;        // decoded-weight ring: one slot per decode group
 constexpr int kFBN = 64;           // B rows per tile (G: 32 gate + 32 up)
 constexpr int kChunkRow = 256;     // packed weight bytes per row per TMA request (largest box extent)
 constexpr int kChunks = 3;         // packed weight chunk ring
@@ -64,13 +65,14 @@ struct FusedParams {
     CUtensorMap tm_sd;          // E8M0 [H][I/32], box {kbc_d, 64}
     __half *mid;
     void *out;              // fp32 or fp16 [T][H]
-    float *ws;              // fp16 output: fp32 workspace [T][H]
+    float *ws;              // fp32 split partials [splits][T][H]
     uint32_t *sync;         // [0] finished G tiles, [1] finished CTAs, [2..] D tile arrivals (self-resetting)
     uint32_t *err;
     uint32_t T, H, I;
     uint32_t splits;        // K splits of the down projection
     uint32_t kbc_g, kbc_d;  // scale bytes per row per tile
     uint32_t n_gtiles, n_dtiles;
+    uint32_t d_spin;        // 1: each CTA holds at most one down tile, its last (splits may wait for each other)
     unsigned long long *trace;  // optional: kTraceSlots per CTA (profiling aid)
 };
 
@@ -79,7 +81,8 @@ enum TraceSlot : int {
     TR_START = 0, TR_PROLOGUE = 1, TR_END = 2, TR_G_EPI_END = 3, TR_WAIT_END = 4, TR_D_EPI_END = 5, TR_SMID = 6,
     TR_RAWP_WAIT_EMPTY = 8, TR_AP_WAIT_EMPTY = 9, TR_AP_WAIT_COUNTER = 10, TR_MMA_WAIT_A = 11, TR_MMA_WAIT_B = 12,
     TR_MMA_WAIT_ACC = 13, TR_DEC_WAIT_RAW = 14, TR_DEC_WAIT_SLOT = 15, TR_DEC_WORK = 16, TR_EPI_G = 17,
-    TR_DEC_WAIT_ACC = 18, TR_EPI_D = 19, TR_CYCLES = 20, TR_MMA_ISSUE = 21, TR_MMA_STAGE = 32, TR_DEC_STAGE = 64,
+    TR_DEC_WAIT_ACC = 18, TR_EPI_D = 19, TR_CYCLES = 20, TR_MMA_ISSUE = 21, TR_DEC_FIRST_RAW = 22, TR_DEC_FIRST_SC = 23, TR_MMA_FIRST_A = 24, TR_D_FENCED = 25, TR_D_COUNTED = 26, TR_D_CONVERTED = 27, TR_D_LAST = 28,
+    TR_G_ACC = 29, TR_G_STORED = 30, TR_G_PUBLISHED = 31, TR_D_ACC = 7, TR_D_STORED = 56, TR_D_ACC_WAITED = 57, TR_MMA_STAGE = 32, TR_DEC_STAGE = 64,
     TR_AP_STAGE = 96, kTraceSlots = 128
 };
 
@@ -98,11 +101,13 @@ __device__ __forceinline__ long long clk_if(bool timed) { return timed ? clock64
 
 template <int W>
 struct FusedCfg {
-    static constexpr int kRawRow = kBK * wfmt_bits(W) / 8;       // packed bytes per row per 64-K stage
+    static constexpr int kRawRow = kFBK * wfmt_bits(W) / 8;      // packed bytes per row per stage
     static constexpr uint32_t kSPC = kChunkRow / kRawRow;         // stages per weight chunk
     static constexpr uint32_t kChunkBytes = kFBN * kChunkRow;     // 16 KB
-    static constexpr uint32_t kABytes = kBM * 128;
-    static constexpr uint32_t kBBytes = kFBN * 128;
+    static constexpr uint32_t kAAtom = kBM * 128;                 // 128 rows x 64 K fp16
+    static constexpr uint32_t kBAtom = kFBN * 128;                // 64 rows x 64 K fp16
+    static constexpr uint32_t kABytes = 2 * kAAtom;
+    static constexpr uint32_t kBBytes = 2 * kBAtom;
     // layout: [B ring][weight chunks][scales][activation ring (stages_a)]
     static constexpr uint32_t kOffRaw = kStagesB * kBBytes;
     static constexpr uint32_t kOffScales = kOffRaw + kChunks * kChunkBytes;
@@ -198,14 +203,14 @@ __device__ __forceinline__ TileInfo tile_info(const FusedParams &p, uint32_t t)
         ti.c0 = (t % gch) * 32;
         ti.m0 = (t / gch) * kBM;
         ti.kb = 0;
-        ti.nk = p.H / kBK;
+        ti.nk = p.H / kFBK;
     } else {
         const uint32_t d = t - p.n_gtiles, nj = p.H / kFBN;
         ti.is_g = false;
         ti.c0 = (d % nj) * kFBN;
         ti.kb = (d / nj) % p.splits;
         ti.m0 = (d / (nj * p.splits)) * kBM;
-        ti.nk = p.I / p.splits / kBK;
+        ti.nk = p.I / p.splits / kFBK;
     }
     return ti;
 }
@@ -227,11 +232,11 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
     uint64_t *bars = reinterpret_cast<uint64_t *>(sA + SA * Cfg::kABytes);
     uint64_t *ck_full = bars;                       // [kChunks] packed weight chunk landed
     uint64_t *ck_empty = ck_full + kChunks;         // [kChunks] chunk decoded
-    // Stage s uses activation slot s % SA and decoded-weight slot s % 4. One
+    // Stage s uses activation slot s % SA and decoded-weight slot s % 2. One
     // barrier pair per stage: full[s % SA] completes when the activation copy
     // landed AND the 4 warps of the decode group owning stage s arrived; the
-    // MMA commits empty[s % SA]. A decode group reuses weight slot s % 4 after
-    // waiting for stage s-4 to be committed on empty[(s-4) % SA].
+    // MMA commits empty[s % SA]. A decode group reuses weight slot s % 2 after
+    // waiting for stage s-2 to be committed on empty[(s-2) % SA].
     uint64_t *a_full = ck_empty + kChunks;          // [SA]
     uint64_t *a_empty = a_full + kMaxStagesA;       // [SA]
     uint64_t *sc_full = a_empty + kMaxStagesA;      // [2]
@@ -361,8 +366,9 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     if (!mbar_wait_t(&a_empty[st], ph ^ 1u, abort, p.err, 0x702, tw0, tr != nullptr)) { ok = false; break; }
                     if (tr && gs < 32) tr[TR_AP_STAGE + gs] = (unsigned long long)(clock64() - clk0);
                     mbar_arrive_expect_tx(&a_full[st], Cfg::kABytes);
-                    tma_load_2d(sA + st * Cfg::kABytes, tm, (int32_t)((kstage0 + s) * kBK), (int32_t)ti.m0,
-                                &a_full[st]);
+                    const int32_t kx = (int32_t)((kstage0 + s) * kFBK);
+                    tma_load_2d(sA + st * Cfg::kABytes, tm, kx, (int32_t)ti.m0, &a_full[st]);
+                    tma_load_2d(sA + st * Cfg::kABytes + Cfg::kAAtom, tm, kx + kBK, (int32_t)ti.m0, &a_full[st]);
                 }
                 if (!ok) break;
             }
@@ -385,20 +391,24 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     const uint32_t sa = gs % SA, pa = (gs / SA) & 1u;
                     const uint32_t sbb = gs % kStagesB;
                     if (!ra && !mbar_wait_t(&a_full[sa], pa, abort, p.err, 0x802, tw0, tr != nullptr)) break;
+                    if (tr && gs == 0) tr[TR_MMA_FIRST_A] = (unsigned long long)(clock64() - clk0);
                     // probe the next stage now; the answer is needed only after this
                     // stage's MMAs are issued
                     const uint32_t gn = gs + 1;
                     ra = (s + 1 < ti.nk) ? mbar_test(&a_full[gn % SA], (gn / SA) & 1u) : 0u;
                     const long long cis = clk_if(tr);
                     tc_fence_after();
-                    const uint64_t ad = smem_desc_sw128(sA + sa * Cfg::kABytes);
-                    const uint64_t bd = smem_desc_sw128(sB + sbb * Cfg::kBBytes);
 #pragma unroll
-                    for (uint32_t k = 0; k < kBK / 16; ++k)
-                        mma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (s | k) != 0u);
+                    for (uint32_t j = 0; j < 2; ++j) {
+                        const uint64_t ad = smem_desc_sw128(sA + sa * Cfg::kABytes + j * Cfg::kAAtom);
+                        const uint64_t bd = smem_desc_sw128(sB + sbb * Cfg::kBBytes + j * Cfg::kBAtom);
+#pragma unroll
+                        for (uint32_t k = 0; k < kBK / 16; ++k)
+                            mma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (s | j | k) != 0u);
+                    }
                     mma_commit(&a_empty[sa]);
                     if (tr) tw3 += (unsigned long long)(clock64() - cis);
-                    if (tr && gs < 32) tr[TR_MMA_STAGE + gs] = (unsigned long long)(clock64() - clk0);
+                    if (tr && gs < 24) tr[TR_MMA_STAGE + gs] = (unsigned long long)(clock64() - clk0);
                 }
                 mma_commit(&acc_full[acc]);
             }
@@ -419,6 +429,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
             const uint32_t kbc = ti.is_g ? p.kbc_g : p.kbc_d;
             const uint8_t *scl = sSc + slot * sc_slot;
             if constexpr (W == W_MXFP4) mbar_wait(&sc_full[slot], (ti_n >> 1) & 1u, abort, p.err, 0x901);
+            if (tr && te == 0 && ti_n == 0) tr[TR_DEC_FIRST_SC] = (unsigned long long)(clock64() - clk0);
             uint32_t cst = 0;
             for (uint32_t s = 0; s < ti.nk && !*abort; ++s, ++gs) {
                 const uint32_t sc = s % SPC;
@@ -426,25 +437,32 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 if (sc == 0) {
                     cst = gc % kChunks;
                     if (!mbar_wait_t(&ck_full[cst], (gc / kChunks) & 1u, abort, p.err, 0x902, tw0, tr != nullptr)) break;
+                    if (tr && te == 0 && gc == 0) tr[TR_DEC_FIRST_RAW] = (unsigned long long)(clock64() - clk0);
                 }
                 if (mine) {
                     const uint32_t st = gs % kStagesB;
-                    if (gs >= kStagesB) {   // stage gs-4 (same weight slot) consumed by the MMA
+                    if (gs >= kStagesB) {   // stage gs-2 (same weight slot) consumed by the MMA
                         const uint32_t g3 = gs - kStagesB;
                         if (!mbar_wait_t(&a_empty[g3 % SA], (g3 / SA) & 1u, abort, p.err, 0x903, tw1, tr != nullptr)) break;
                     }
                     const long long cdec = clk_if(tr);
                     const uint8_t *raw = sRaw + cst * Cfg::kChunkBytes + dr * kChunkRow + sc * Cfg::kRawRow;
-                    uint32_t sb = 127u;
-                    // G: rows 0..31 gate scales, 32..63 up scales, each kbc_g wide
-                    if constexpr (W == W_MXFP4) sb = scl[dr * kbc + 2 * s + dh];
-                    uint32_t o[16];
-                    decode_chunk<W>(raw + dh * (Cfg::kRawRow / 2), sb, o);
-                    uint8_t *rowp = sB + st * Cfg::kBBytes + dr * 128;
+                    // this thread: row dr, K half dh (= swizzle atom dh: 64 weights, two
+                    // 32-wide scale blocks)
+                    uint8_t *rowp = sB + st * Cfg::kBBytes + dh * Cfg::kBAtom + dr * 128;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint32_t phys = ((dh * 4 + q) ^ (dr & 7u)) * 16u;
-                        *reinterpret_cast<uint4 *>(rowp + phys) = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                    for (int half = 0; half < 2; ++half) {
+                        uint32_t sb = 127u;
+                        // G: rows 0..31 gate scales, 32..63 up scales, each kbc_g wide
+                        if constexpr (W == W_MXFP4) sb = scl[dr * kbc + 4 * s + 2 * dh + half];
+                        uint32_t o[16];
+                        decode_chunk<W>(raw + (2 * dh + half) * (Cfg::kRawRow / 4), sb, o);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint32_t phys = ((half * 4 + q) ^ (dr & 7u)) * 16u;
+                            *reinterpret_cast<uint4 *>(rowp + phys) =
+                                make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                        }
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
@@ -476,6 +494,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 tmem_ld_32x32b_x16(taddr + colh * 16, g);
                 tmem_ld_32x32b_x16(taddr + 32 + colh * 16, u);
                 tmem_ld_wait();
+                if (tr && te == 0) tr[TR_G_ACC] = (unsigned long long)(clock64() - clk0);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -493,15 +512,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                         dst[i] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     }
                 }
-                // G tile t also clears its share of the down projection's
-                // accumulation target (out for fp32, the workspace for fp16)
-                {
-                    float4 *z = reinterpret_cast<float4 *>(OUT_F16 ? p.ws : static_cast<float *>(p.out));
-                    const uint32_t total = p.T * p.H / 4;
-                    const uint32_t per = (total + p.n_gtiles - 1) / p.n_gtiles;
-                    const uint32_t beg = t * per, end = min(beg + per, total);
-                    for (uint32_t i = beg + te; i < end; i += kEpi) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
+                if (tr && te == 0) tr[TR_G_STORED] = (unsigned long long)(clock64() - clk0);
                 // publish: our generic stores ordered before other CTAs' TMA (async
                 // proxy) reads; one release by one thread after the CTA barrier
                 fence_proxy_async_global();
@@ -511,50 +522,89 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     atomicAdd(p.sync, 1u);
                 }
                 if (tr && te == 0) {
+                    tr[TR_G_PUBLISHED] = (unsigned long long)(clock64() - clk0);
                     tr[TR_G_EPI_END] = globaltimer_ns();
                     tr[TR_EPI_G] += (unsigned long long)(clock64() - cepi);
                 }
             } else {
-                (void)ld_acquire_gpu(p.sync);   // orders the clears above before our reductions
-                float *dst = (OUT_F16 ? p.ws : static_cast<float *>(p.out)) + (size_t)m * p.H + ti.c0 + colh * 32;
+                // Down tile: store this split's fp32 partial tile (plain stores, no
+                // atomics), count the split, then sum the splits into out.
+                float *part = p.ws + ((size_t)ti.kb * p.T + m) * p.H + ti.c0 + colh * 32;
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(taddr + colh * 32, v);
                 tmem_ld_wait();
+                if (tr && te == 0) tr[TR_D_ACC] = (unsigned long long)(clock64() - clk0);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[acc]);
                 if (m < p.T) {
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
-                        red_add_v4(dst + 4 * i, __uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                   __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                        __stcg(reinterpret_cast<float4 *>(part) + i,
+                               make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                           __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
                 }
-                if (tr && te == 0) tr[TR_EPI_D] += (unsigned long long)(clock64() - cepi);
-                if constexpr (OUT_F16) {
-                    __threadfence();
-                    asm volatile("bar.sync 1, 256;" ::: "memory");
-                    const uint32_t tile = (ti.m0 / kBM) * (p.H / kFBN) + ti.c0 / kFBN;
-                    if (te == 0) {
-                        const uint32_t prev = atomicAdd(p.sync + 2 + tile, 1u);
-                        *s_last = (prev == p.splits - 1) ? 1u : 0u;
-                        if (prev == p.splits - 1) atomicExch(p.sync + 2 + tile, 0u);   // reset for the next launch
-                    }
-                    asm volatile("bar.sync 1, 256;" ::: "memory");
-                    if (*s_last) {
-                        __threadfence();
-                        for (uint32_t i = te; i < kBM * (kFBN / 8); i += kEpi) {
-                            const uint32_t rr = i / (kFBN / 8), c8 = (i % (kFBN / 8)) * 8;
-                            const uint32_t mm = ti.m0 + rr;
-                            if (mm < p.T) {
-                                const float *src = p.ws + (size_t)mm * p.H + ti.c0 + c8;
-                                const float4 a = __ldcg(reinterpret_cast<const float4 *>(src));
-                                const float4 b = __ldcg(reinterpret_cast<const float4 *>(src) + 1);
-                                *reinterpret_cast<uint4 *>(static_cast<__half *>(p.out) + (size_t)mm * p.H + ti.c0 + c8) =
-                                    make_uint4(half2_bits(a.x, a.y), half2_bits(a.z, a.w), half2_bits(b.x, b.y),
-                                               half2_bits(b.z, b.w));
-                            }
+                if (tr && te == 0) {
+                    tr[TR_EPI_D] += (unsigned long long)(clock64() - cepi);
+                    tr[TR_D_STORED] = (unsigned long long)(clock64() - clk0);
+                    tr[TR_D_ACC_WAITED] = (unsigned long long)(cepi - clk0);
+                }
+                __threadfence();
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (tr && te == 0) tr[TR_D_FENCED] = (unsigned long long)(clock64() - clk0);
+                uint32_t *cnt = p.sync + 2 + (ti.m0 / kBM) * (p.H / kFBN) + ti.c0 / kFBN;
+                if (te == 0) {
+                    const bool last = atomicAdd(cnt, 1u) == p.splits - 1;
+                    if (last) __threadfence();   // the other splits' partials are visible to us
+                    *s_last = last ? 1u : 0u;
+                }
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                uint32_t r0 = 0, r1 = 0;   // rows of the tile this CTA sums
+                if (p.d_spin) {
+                    // Every split of this tile is resident and this is each CTA's last
+                    // tile, so waiting cannot deadlock; each split then sums a
+                    // 1/splits band of rows in parallel.
+                    bool ok = true;
+                    if (te == 0 && !*s_last) ok = wait_counter(cnt, p.splits, abort, p.err, 0x905);
+                    if (epi_bar_any(!ok)) break;
+                    r0 = ti.kb * kBM / p.splits;
+                    r1 = (ti.kb + 1) * kBM / p.splits;
+                } else if (*s_last) {
+                    r1 = kBM;
+                }
+                if (tr && te == 0) { tr[TR_D_COUNTED] = (unsigned long long)(clock64() - clk0); tr[TR_D_LAST] = *s_last; }
+                const size_t split_stride = (size_t)p.T * p.H;
+                for (uint32_t i = r0 * (kFBN / 4) + te; i < r1 * (kFBN / 4); i += kEpi) {
+                    const uint32_t mm = ti.m0 + i / (kFBN / 4), c4 = (i % (kFBN / 4)) * 4;
+                    if (mm >= p.T) continue;
+                    const float *src = p.ws + (size_t)mm * p.H + ti.c0 + c4;
+                    float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (uint32_t j0 = 0; j0 < p.splits; j0 += 8) {
+                        // all eight loads in flight before the first add
+                        float4 q[8];
+#pragma unroll
+                        for (uint32_t j = 0; j < 8; ++j)
+                            q[j] = (j0 + j < p.splits)
+                                       ? __ldcg(reinterpret_cast<const float4 *>(src + (j0 + j) * split_stride))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (uint32_t j = 0; j < 8; ++j) {
+                            acc4.x += q[j].x; acc4.y += q[j].y; acc4.z += q[j].z; acc4.w += q[j].w;
                         }
                     }
+                    if constexpr (OUT_F16) {
+                        *reinterpret_cast<uint2 *>(static_cast<__half *>(p.out) + (size_t)mm * p.H + ti.c0 + c4) =
+                            make_uint2(half2_bits(acc4.x, acc4.y), half2_bits(acc4.z, acc4.w));
+                    } else {
+                        *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + (size_t)mm * p.H + ti.c0 + c4) = acc4;
+                    }
+                }
+                if (tr && te == 0) tr[TR_D_CONVERTED] = (unsigned long long)(clock64() - clk0);
+                // reset the tile counter for the next launch once no split reads it
+                if (p.d_spin) {
+                    if (te == 0 && atomicAdd(cnt, 1u) == 2 * p.splits - 1) atomicExch(cnt, 0u);
+                } else if (*s_last && te == 0) {
+                    atomicExch(cnt, 0u);
                 }
             }
         }

@@ -91,13 +91,19 @@ uint32_t splits_for(uint32_t T, uint32_t H, uint32_t I)
     return s;
 }
 
+uint32_t noalloc_splits(const mpp41_mlp_desc *d)
+{
+    const uint32_t s = splits_for(d->tokens, d->hidden, d->intermediate);
+    return (d->out_dtype == MPP41_F16 && s == 1) ? 2 : s;
+}
+
 }  // namespace
 
 extern "C" size_t mpp41_mlp_noalloc_scratch_bytes(const mpp41_mlp_desc *d)
 {
     if (!d) return 0;
     const size_t mid = ((size_t)d->tokens * d->intermediate * 2 + 255) & ~size_t(255);
-    return mid + (d->out_dtype == MPP41_F16 ? (size_t)d->tokens * d->hidden * 4 : 0);
+    return mid + mpp41::fused_ws_bytes(d->tokens, d->hidden, noalloc_splits(d));
 }
 
 extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x, const void *wg, const void *wu,
@@ -120,9 +126,10 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
     const size_t need = mpp41_mlp_noalloc_scratch_bytes(d);
     if (need > MPP41_NOALLOC_SCRATCH_BYTES)
         return err(MPP41_ERR_UNSUPPORTED_SHAPE,
-                   "layer needs %zu bytes of scratch (tokens x intermediate x 2%s); the static scratch of "
-                   "mpp41_mlp_noalloc holds %u bytes -- use mpp41_mlp with a caller-allocated buffer",
-                   need, d->out_dtype == MPP41_F16 ? " + tokens x hidden x 4" : "", (unsigned)MPP41_NOALLOC_SCRATCH_BYTES);
+                   "layer needs %zu bytes of scratch (tokens x intermediate x 2 + splits x tokens x hidden x 4); "
+                   "the static scratch of mpp41_mlp_noalloc holds %u bytes -- use mpp41_mlp with a "
+                   "caller-allocated buffer",
+                   need, (unsigned)MPP41_NOALLOC_SCRATCH_BYTES);
     if (fused_sync_words(d->tokens, d->hidden) > kSyncWords)
         return err(MPP41_ERR_UNSUPPORTED_SHAPE, "too many output tiles for the static counters");
     int dev = 0;
@@ -147,13 +154,11 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
     L.x = x; L.wg = wg; L.wu = wu; L.wd = wd; L.sg = sg; L.su = su; L.sd = sd;
     L.mid = P.scratch;
     L.out = out;
-    L.ws = L.out_f16 ? reinterpret_cast<float *>(P.scratch + (((size_t)d->tokens * d->intermediate * 2 + 255) & ~size_t(255)))
-                     : nullptr;
+    L.ws = reinterpret_cast<float *>(P.scratch + (((size_t)d->tokens * d->intermediate * 2 + 255) & ~size_t(255)));
     L.sync = P.sync;
     L.err = P.err;
     L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
-    L.splits = splits_for(d->tokens, d->hidden, d->intermediate);
-    if (L.out_f16 && L.splits == 1) L.splits = 2;
+    L.splits = noalloc_splits(d);
     const char *why = "";
     const int rc = launch_mlp_fused(L, st, &why);
     if (rc == 1) return err(MPP41_ERR_UNSUPPORTED_SHAPE, "mpp41_mlp_noalloc: %s", why);

@@ -213,7 +213,11 @@ __device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x)
 template <int E>
 __device__ __forceinline__ float swiglu(float g, float u)
 {
-    if constexpr (E == EPI_SWIGLU_FLOAT || E == EPI_SWIGLU_PLAIN) {
+    if constexpr (E == EPI_SWIGLU_PLAIN) {
+        // OCP-MX model rows (no reference bit pattern to match): hardware
+        // exp2 and fast divide; silu(g) -> 0 when exp(-g) overflows
+        return __fdividef(g, 1.0f + __expf(-g)) * u;
+    } else if constexpr (E == EPI_SWIGLU_FLOAT) {
         return (g / (1.0f + expf(-g))) * u;
     } else {
         if constexpr (E == EPI_SWIGLU_HALF_H) {

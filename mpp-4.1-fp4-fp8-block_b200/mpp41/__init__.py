@@ -20,7 +20,7 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
-LIB_PATH = os.path.join(PKG, "lib", "libmpp41.so")
+LIB_PATH = os.environ.get("MPP41_LIB") or os.path.join(PKG, "lib", "libmpp41.so")
 HEADER = os.path.join(ROOT, "include", "mpp41.h")
 
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED_SHAPE, ERR_NO_DEVICE, ERR_MISSING_KERNEL, ERR_OUT_OF_MEMORY, \
@@ -149,7 +149,7 @@ def mlp_desc(tokens, hidden, intermediate, wfmt=W_MXFP4, afmt=A_F16, epilogue=SW
     return MLPDesc(tokens, hidden, intermediate, wfmt, afmt, epilogue, out_dtype, flags)
 
 
-NOALLOC_SCRATCH_BYTES = 4 << 20
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
 def mlp_noalloc(desc: MLPDesc, x, wg, wu, wd, sg, su, sd, out, stream_handle=None):
