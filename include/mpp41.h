@@ -114,10 +114,11 @@ mpp41_status mpp41_synchronize(mpp41_ctx *ctx);
 uint32_t *mpp41_device_error_word(mpp41_ctx *ctx);
 
 /* Profiling aid with no reference counterpart: when `dev` is non-NULL, later
- * fused MLP launches of this context write 32 counters per CTA into it
- * (phase timestamps in ns and per-role wait/work SM cycles, slots as enum
- * TraceSlot in csrc/mpp41_mlp_fused.cuh; zero the buffer first, sums
- * accumulate). `words` >= 32 * number of SMs. NULL disables. */
+ * fused MLP launches of this context write 256 counters per CTA into it
+ * (phase timestamps in ns, per-role wait/work SM cycles and per-stage SM
+ * clock stamps, slots as enum TraceSlot in csrc/mpp41_mlp_fused.cuh; zero the
+ * buffer first, sums accumulate). `words` >= 256 * number of SMs. NULL
+ * disables. */
 mpp41_status mpp41_set_trace(mpp41_ctx *ctx, unsigned long long *dev, size_t words);
 
 /* ---- buffers: replace device.makeBuffer / contents() ---- */

@@ -154,10 +154,9 @@ uint32_t down_splits(const mpp41_mlp_desc *d)
     return pick_splits((d->hidden / 64) * ((d->tokens + 127) / 128), d->intermediate);
 }
 
-uint32_t fused_splits(const mpp41_mlp_desc *d)
+LayerPlan desc_plan(const mpp41_mlp_desc *d)
 {
-    const uint32_t s = down_splits(d);
-    return (d->out_dtype == MPP41_F16 && s == 1) ? 2 : s;   // fp16 output always reduces through the workspace
+    return plan_layer(d->tokens, d->hidden, d->intermediate, d->out_dtype == MPP41_F16);
 }
 
 // Scratch layout: [mid][fp32 workspace T x H][tile counters] for the
@@ -181,7 +180,7 @@ ScratchLayout scratch_layout(const mpp41_mlp_desc *d)
         L.cnt_off = L.ws_off;
     }
     L.total = L.cnt_off + L.cnt_bytes;
-    const size_t fused = L.ws_off + fused_ws_bytes(d->tokens, d->hidden, fused_splits(d));
+    const size_t fused = L.ws_off + desc_plan(d).ws_bytes;
     if (fused > L.total) L.total = fused;
     return L;
 }
@@ -293,7 +292,7 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
     if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su || !sd))
         return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate, up and down scales");
     if (!(d->flags & MPP41_MLP_UNFUSED) && d->wfmt != MPP41_W_F16 &&
-        fused_sync_words(d->tokens, d->hidden) <= ctx->sync_words) {
+        desc_plan(d).sync_words <= ctx->sync_words) {
         const ScratchLayout SL = scratch_layout(d);
         FusedLaunch L{};
         L.wfmt = d->wfmt;
@@ -307,9 +306,8 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
         L.err = ctx->err;
         L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
         L.trace = ctx->trace;
-        L.splits = fused_splits(d);
         const char *why = "";
-        const int rc = launch_mlp_fused(L, st, &why);
+        const int rc = launch_layer(desc_plan(d), L, st, &why);
         if (rc == 0) return MPP41_OK;
         if (rc == 2) return fail(MPP41_ERR_CUDA, "fused MLP kernel: %s", why);
     }
@@ -407,12 +405,15 @@ void *mpp41_get_stream(mpp41_ctx *ctx) { return ctx ? ctx->stream : nullptr; }
 
 uint32_t *mpp41_device_error_word(mpp41_ctx *ctx) { return ctx ? ctx->err : nullptr; }
 
+constexpr unsigned kTraceWords = 256;   // TraceSlot kTraceSlots of the fused kernel
+
 mpp41_status mpp41_set_trace(mpp41_ctx *ctx, unsigned long long *dev, size_t words)
 {
     NEED(ctx);
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
-    if (dev && words < (size_t)128 * sms) return fail(MPP41_ERR_INVALID_ARGUMENT, "trace buffer needs 128 words per SM");
+    if (dev && words < (size_t)kTraceWords * sms)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "trace buffer needs %u words per SM", kTraceWords);
     ctx->trace = dev;
     return MPP41_OK;
 }

@@ -44,6 +44,9 @@ struct WqLaunch {
 
 bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols, uint64_t rows,
               uint32_t bc, uint32_t br, CUtensorMapSwizzle sw);
+// fp16 [rows][cols] viewed as [cols/64][rows][64]: one copy of box {64, br, nblk}
+// lands nblk consecutive 128-byte-swizzled K atoms of br rows each.
+bool make_map_kblocks(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint32_t br, uint32_t nblk);
 
 // OCP-MX quantization of fp32 [rows][depth] to E2M1 [rows][depth/2] + E8M0 [rows][depth/32].
 cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
@@ -67,9 +70,33 @@ struct FusedLaunch {
     unsigned long long *trace;   // optional per-CTA phase/wait counters (profiling)
 };
 // Number of uint32 sync counters a launch needs.
-size_t fused_sync_words(uint32_t T, uint32_t H);
-// Bytes of the fp32 workspace a launch needs (one T x H partial per K split).
+size_t fused_sync_words(uint32_t T, uint32_t H, uint32_t I);
+// Bytes of the fp32 workspace a launch needs (one T x H partial per K split;
+// none without splits).
 size_t fused_ws_bytes(uint32_t T, uint32_t H, uint32_t splits);
+// K splits of the down projection the fused kernel uses for this shape.
+uint32_t fused_splits(uint32_t T, uint32_t H, uint32_t I);
+
+// Token-major variant of the fused layer kernel (mpp41_mlp_tok.cuh): same
+// launch description, its own workspace layout ([splits][T][H] fp32) and
+// counters.
+namespace tok {
+size_t sync_words(uint32_t T, uint32_t H);
+size_t ws_bytes(uint32_t T, uint32_t H, uint32_t splits);
+uint32_t splits(uint32_t T, uint32_t H, uint32_t I, bool out_f16);
+int launch(const FusedLaunch &L, cudaStream_t st, const char **why);
+}  // namespace tok
+
+// Which fused kernel runs a layer, with its K splits and the workspace and
+// counter words it needs. Depends on the shape only.
+struct LayerPlan {
+    bool token_major;
+    uint32_t splits;
+    size_t ws_bytes, sync_words;
+};
+LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16);
+// 0 = launched, 1 = shape/format not covered, 2 = CUDA error.
+int launch_layer(const LayerPlan &plan, FusedLaunch L, cudaStream_t st, const char **why);
 // 0 = launched, 1 = this shape/format is not covered by the fused kernel, 2 = CUDA error.
 int launch_mlp_fused(const FusedLaunch &L, cudaStream_t st, const char **why);
 

@@ -11,39 +11,105 @@
 
 namespace mpp41 {
 
-size_t fused_sync_words(uint32_t T, uint32_t H) { return 2 + (size_t)(H / kFBN) * ((T + kBM - 1) / kBM); }
+uint32_t fused_splits(uint32_t T, uint32_t H, uint32_t I);
 
-size_t fused_ws_bytes(uint32_t T, uint32_t H, uint32_t splits) { return (size_t)splits * T * H * 4; }
+static uint32_t fused_nt(uint32_t T) { return T >= (uint32_t)kMaxNT ? (uint32_t)kMaxNT : (T + 15u) & ~15u; }
+
+size_t fused_sync_words(uint32_t T, uint32_t H, uint32_t I)
+{
+    const uint32_t nt = fused_nt(T), n_mt = (T + nt - 1) / nt;
+    return 2 + (size_t)(H / kWRows) * n_mt + (size_t)fused_splits(T, H, I) * n_mt;
+}
+
+size_t fused_ws_bytes(uint32_t T, uint32_t H, uint32_t splits)
+{
+    const uint32_t nt = fused_nt(T);
+    return splits > 1 ? (size_t)splits * ((T + nt - 1) / nt) * nt * H * 4 : 0;
+}
+
+// K splits of the down projection. Tiles are dealt round-robin to at most
+// kAssumedSMs CTAs; each tile costs its K stages plus a fixed overhead (more
+// for split tiles, which reduce through the workspace). The split count with
+// the smallest busiest-CTA cost wins (fewest splits on ties). Depends on the
+// shape only, so the scratch size can be computed without a device.
+uint32_t fused_splits(uint32_t T, uint32_t H, uint32_t I)
+{
+    constexpr uint32_t kAssumedSMs = 148, kTileCost = 6, kSplitCost = 2;
+    const uint32_t nt = fused_nt(T), mt = (T + nt - 1) / nt;
+    const uint32_t n_g = (I / kGCh) * mt, g_cost = H / kFBK + kTileCost, nh = H / kWRows;
+    uint32_t best = 1;
+    uint64_t best_cost = ~0ull;
+    for (uint32_t s = 1; s <= 32; s *= 2) {
+        if (I % (s * kFBK)) break;
+        if (s > 1 && (I / s) % 512) break;   // split starts on a 16-byte scale boundary
+        const uint32_t n_d = nh * s * mt, d_cost = I / s / kFBK + kTileCost + (s > 1 ? kSplitCost : 0);
+        const uint32_t n = n_g + n_d, grid = n < kAssumedSMs ? n : kAssumedSMs;
+        uint64_t worst = 0;
+        for (uint32_t b = 0; b < grid; ++b) {
+            uint64_t c = 0;
+            for (uint32_t t = b; t < n; t += grid) c += t < n_g ? g_cost : d_cost;
+            if (c > worst) worst = c;
+        }
+        if (worst < best_cost) { best_cost = worst; best = s; }
+    }
+    return best;
+}
+
+LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16)
+{
+    constexpr uint32_t kAssumedSMs = 148;
+    LayerPlan pl{};
+    // The weight-major kernel gives each CTA one tile: with fewer G tiles than
+    // half the SMs (one 128-token tile of a small layer) each phase would
+    // leave most SMs idle, so such layers use the token-major kernel, whose
+    // CTAs all take a G tile and then a D tile.
+    pl.token_major = T > 64 && T <= 128 && H % 64 == 0 && I % 256 == 0 && (I / kGCh) * 2 < kAssumedSMs;
+    if (pl.token_major) {
+        pl.splits = tok::splits(T, H, I, out_f16);
+        pl.ws_bytes = tok::ws_bytes(T, H, pl.splits);
+        pl.sync_words = tok::sync_words(T, H);
+    } else {
+        pl.splits = fused_splits(T, H, I);
+        pl.ws_bytes = fused_ws_bytes(T, H, pl.splits);
+        pl.sync_words = fused_sync_words(T, H, I);
+    }
+    return pl;
+}
+
+int launch_layer(const LayerPlan &plan, FusedLaunch L, cudaStream_t st, const char **why)
+{
+    L.splits = plan.splits;
+    return plan.token_major ? tok::launch(L, st, why) : launch_mlp_fused(L, st, why);
+}
 
 template <int W, int EG, bool F16>
 static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
-    using Cfg = FusedCfg<W>;
     FusedParams p;
     memset(&p, 0, sizeof(p));
     p.T = L.T; p.H = L.H; p.I = L.I; p.splits = L.splits;
-    p.kbc_g = L.H / 32;
-    p.kbc_d = L.I / L.splits / 32;
-    if (W == W_MXFP4 && (p.kbc_g % 16 || p.kbc_g > 256 || p.kbc_d % 16 || p.kbc_d > 256)) {
-        *why = "scale tiles need (H/32) and (I/splits/32) multiples of 16 and at most 256";
-        return 1;
-    }
-    p.n_gtiles = (L.I / 32) * ((L.T + kBM - 1) / kBM);
-    p.n_dtiles = (L.H / kFBN) * L.splits * ((L.T + kBM - 1) / kBM);
-    const uint32_t kbc_max = p.kbc_g > p.kbc_d ? p.kbc_g : p.kbc_d;
-    const uint32_t smem = Cfg::smem_bytes(kbc_max, kMaxStagesA);
-    if (smem > 227u * 1024u) { *why = "shared memory"; return 1; }
+    p.NT = fused_nt(L.T);
+    const uint32_t mt = (L.T + p.NT - 1) / p.NT;
+    if (L.I % (L.splits * kFBK)) { *why = "intermediate not a multiple of splits x 128"; return 1; }
+    if (L.splits != fused_splits(L.T, L.H, L.I)) { *why = "splits differ from fused_splits (counter layout)"; return 1; }
     const uint64_t rawH = (uint64_t)L.H * wfmt_bits(W) / 8, rawI = (uint64_t)L.I * wfmt_bits(W) / 8;
     if (rawH < (uint64_t)kChunkRow || rawI < (uint64_t)kChunkRow) { *why = "packed rows shorter than one chunk"; return 1; }
-    bool ok = make_map(&p.tm_x, L.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.H, L.T, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) &&
-              make_map(&p.tm_mid, L.mid, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.I, L.T, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) &&
-              make_map(&p.tm_wg, L.wg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, kChunkRow, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-              make_map(&p.tm_wu, L.wu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, kChunkRow, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-              make_map(&p.tm_wd, L.wd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawI, L.H, kChunkRow, kFBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (W == W_MXFP4 && (L.H % 512 || L.I % 512 || (L.splits > 1 && (L.I / L.splits) % 512))) {
+        *why = "MXFP4 scale rows need hidden, intermediate and the K split to be multiples of 512";
+        return 1;
+    }
+    p.n_gtiles = (L.I / kGCh) * mt;
+    p.n_dtiles = (L.H / kWRows) * L.splits * mt;
+    p.g_per_slice = L.I / L.splits / kGCh;
+    if (L.splits > 1 && !L.ws) { *why = "workspace"; return 1; }
+    bool ok = make_map_kblocks(&p.tm_x, L.x, L.H, L.T, p.NT, 2) && make_map_kblocks(&p.tm_mid, L.mid, L.I, L.T, p.NT, 2) &&
+              make_map(&p.tm_wg, L.wg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, kChunkRow, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
+              make_map(&p.tm_wu, L.wu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, kChunkRow, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
+              make_map(&p.tm_wd, L.wd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawI, L.H, kChunkRow, kWRows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (ok && W == W_MXFP4)
-        ok = make_map(&p.tm_sg, L.sg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, p.kbc_g, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-             make_map(&p.tm_su, L.su, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, p.kbc_g, 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-             make_map(&p.tm_sd, L.sd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.I / 32, L.H, p.kbc_d, kFBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+        ok = make_map(&p.tm_sg, L.sg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, kScRow, kGCh, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+             make_map(&p.tm_su, L.su, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, kScRow, kGCh, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+             make_map(&p.tm_sd, L.sd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.I / 32, L.H, kScRow, kWRows, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!ok) { *why = "tensor maps (16-byte aligned bases and row pitches needed)"; return 1; }
     p.mid = static_cast<__half *>(L.mid);
     p.out = L.out;
@@ -53,6 +119,7 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     p.trace = L.trace;
 
     auto kern = mlp_fused_kernel<W, EG, F16>;
+    const uint32_t smem = kFusedSmem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) { cudaGetLastError(); *why = cudaGetErrorString(e); return 2; }
     int dev = 0, sms = 0, per_sm = 0;
@@ -61,7 +128,7 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFThreads, smem);
     if (e != cudaSuccess || per_sm < 1) { cudaGetLastError(); *why = "occupancy"; return 2; }
     const uint32_t ntiles = p.n_gtiles + p.n_dtiles;
-    uint32_t grid = (uint32_t)(sms * per_sm);
+    uint32_t grid = (uint32_t)sms;   // one CTA per SM: each holds all 512 TMEM columns
     if (grid > ntiles) grid = ntiles;
     // tiles go to CTAs round-robin, down tiles last: with no more down tiles
     // than CTAs each CTA holds at most one and it is its final tile
@@ -73,9 +140,14 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     cfg.blockDim = dim3(kFThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
+    // Programmatic stream serialization: this grid may launch while the previous
+    // kernel on the stream finishes (it only prefetches and decodes weights until
+    // griddepcontrol.wait). Every grid-wide wait of this kernel comes after that
+    // wait, when the previous grid has exited and all of this grid's CTAs (at
+    // most one per SM) can be resident.
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;   // every CTA resident: the grid-wide wait cannot starve
-    attr[0].val.cooperative = 1;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, p);
@@ -105,7 +177,7 @@ static int launch_fw(const FusedLaunch &L, cudaStream_t st, const char **why)
 
 int launch_mlp_fused(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
-    if (L.H % kFBN || L.H % kFBK || L.I % (kFBK * L.splits) || L.I % 32) { *why = "shape"; return 1; }
+    if (L.H % kWRows || L.I % kFBK || !L.splits) { *why = "hidden and intermediate must be multiples of 128"; return 1; }
     switch (L.wfmt) {
     case W_I8: return launch_fw<W_I8>(L, st, why);
     case W_I4: return launch_fw<W_I4>(L, st, why);

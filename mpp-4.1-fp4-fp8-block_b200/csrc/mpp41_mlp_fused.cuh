@@ -3,32 +3,34 @@
 //
 // The reference runs four dispatches per layer (gate GEMM, up GEMM, SwiGLU,
 // down GEMM; encodeMXFP4FusedMLP main.swift:2033-2135, encodeMPPMLP
-// 2636-2722). Here a cooperative grid of one CTA per SM walks two tile lists:
+// 2636-2722). Here a cooperative grid of one CTA per SM walks two tile lists.
+// The weights are the MMA's M side (128 rows per tile) and the tokens its N
+// side (NT <= 128 per tile):
 //
-//   G tiles  128 tokens x 32 channels: gate and up rows of the same channels
-//            decoded into one 64-row B operand, one kind::f16 MMA chain,
-//            SwiGLU applied to the TMEM accumulators, fp16 mid stored (L2)
-//   D tiles  128 tokens x 64 outputs x one K split of the down projection;
-//            fp32 partials reduced with vector atomics (fp32 output) or in a
-//            workspace whose last arriving CTA writes fp16 (fp16 output)
+//   G tiles  64 channels x NT tokens: gate and up rows of the same channels
+//            interleaved (row 2j = gate j, row 2j+1 = up j) so a lane pair holds
+//            both operands of the SwiGLU; fp16 mid staged in shared memory and
+//            stored row by row (L2)
+//   D tiles  128 outputs x NT tokens x one K split of the down projection;
+//            each split stores its fp32 partial tile, then the splits sum it
+//            band by band (or the last arriving split sums all of it)
 //
-// Every CTA finishes its G tiles before its D tiles; a D tile's activation
-// loads wait (bounded) on a grid-wide count of finished G tiles, but its
-// weight and scale loads are issued ahead, so the down projection's weight
-// stream overlaps the gate/up phase. Weights are decoded from the packed
-// reference formats (MXFP4 E2M1 + E8M0, FP4, INT8/4/2, FP8) to fp16 in shared
-// memory; no TMA multicast is used anywhere.
+// Packed weights (MXFP4 E2M1 + E8M0, FP4, INT8/4/2, FP8) are decoded by eight
+// warps straight into tensor memory, where tcgen05.mma reads its A operand
+// (kind::f16, A from TMEM, B = activations in 128-byte-swizzled shared
+// memory). Shared memory then only carries the activation stream and the
+// packed bytes. D tiles decode their weights while the G tiles still run; only
+// their activation (mid) loads wait, bounded, on a grid-wide count of finished
+// G tiles. No TMA multicast is used anywhere.
 //
-// Warp roles (448 threads):
-//   warps 0..3   TMA producers of activation tiles (x for G, mid for D), stages
-//                dealt round-robin: one warp completes about one bulk copy per
-//                memory round trip, so several warps keep several in flight
-//   warp 4       TMEM owner, single-thread MMA issuer (2 accumulators x 64 cols)
-//   warps 5..12  weight decode into the swizzled B ring (16 weights per thread
-//                per stage, two warps per scheduler), then tile epilogues
-//                (each warp: one TMEM lane quarter, one column half)
-//   warp 13      TMA producer of packed weights in 16 KB chunks (256 bytes x 64
-//                rows, i.e. 4-16 K stages per copy) and of the E8M0 scales
+// Warp roles (640 threads):
+//   warps 0..1   TMA producers of activation stages (warp w: stages s, s % 2 == w)
+//   warp 2       TMEM owner (512 columns), single-thread MMA issuer
+//   warp 3       TMA producer of packed weight chunks (128 B x 128 rows) and
+//                of E8M0 scale chunks (16 B x 128 rows)
+//   warps 4..19  weight decode into the TMEM stage ring (lane quarter = warp%4,
+//                K quarter = (warp-4)/4: 32 weights of one row per thread per
+//                stage), then tile epilogues (lane quarter, token quarter)
 // Pipeline barriers count one arrival per warp (after __syncwarp), not per thread.
 #pragma once
 
@@ -42,51 +44,70 @@
 
 namespace mpp41 {
 
-constexpr int kAProd = 4;          // activation producer warps 0..3 (stages round-robin)
-constexpr int kMmaWarp = 4;
-constexpr int kDec0 = 5;           // decode + epilogue warps 5..12
-constexpr int kDecWarps = 8;
+constexpr int kAProd = 2;          // activation producer warps 0..1 (warp w: stages with gs % 2 == w)
+constexpr int kMmaWarp = 2;
+constexpr int kRawWarp = 3;        // weight / scale producer
+constexpr int kDec0 = 4;           // decode + epilogue warps 4..19
+constexpr int kDecWarps = 16;
 constexpr int kEpi = kDecWarps * 32;
-constexpr int kRawWarp = 13;       // weight / scale producer
-constexpr int kFThreads = 14 * 32;
-constexpr int kFBK = 128;          // K per pipeline stage: two 64-wide 128-byte swizzle atoms
-constexpr int kMaxStagesA = 4;     // activation ring depth (power of two: index math is masks)
-constexpr int kStagesB = 2;        // decoded-weight ring: one slot per decode group
-constexpr int kFBN = 64;           // B rows per tile (G: 32 gate + 32 up)
-constexpr int kChunkRow = 256;     // packed weight bytes per row per TMA request (largest box extent)
-constexpr int kChunks = 3;         // packed weight chunk ring
+constexpr int kFThreads = 20 * 32;
+constexpr int kWRows = 128;        // weight rows per tile (MMA M)
+constexpr int kGCh = kWRows / 2;   // channels per G tile
+constexpr int kFBK = 128;          // K per stage: two 64-wide swizzle atoms of fp16 activations
+constexpr int kFStages = 4;         // stage ring depth (activation slot + TMEM weight slot), power of two
+constexpr int kMaxNT = 128;        // tokens per tile (MMA N), at most
+constexpr int kChunkRow = 128;     // packed bytes per row per weight chunk (one 128-byte swizzle row)
+constexpr int kChunks = 3;         // weight chunk ring
+constexpr uint32_t kChunkBytes = kWRows * kChunkRow;          // 16 KB
+constexpr int kScRow = 16;         // MXFP4 scale bytes per row per scale chunk (512 K)
+constexpr int kScChunks = 4;       // scale chunk ring
+constexpr uint32_t kScBytes = kWRows * kScRow;                // 2 KB
+constexpr uint32_t kStageBytes = kMaxNT * 2 * kFBK;           // activation slot (32 KB at NT = 128)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCols = kMaxNT;                         // fp32 columns per accumulator (2 of them)
+constexpr uint32_t kACol0 = 2 * kAccCols;                     // weight stage slot i at kACol0 + 64 i
+// shared memory layout (offsets from a 1024-aligned base)
+constexpr uint32_t kOffRaw = kFStages * kStageBytes;
+constexpr uint32_t kOffSc = kOffRaw + kChunks * kChunkBytes;
+constexpr uint32_t kOffMid = kOffSc + kScChunks * kScBytes;
+constexpr uint32_t kOffBar = kOffMid + kMaxNT * kGCh * 2;
+constexpr uint32_t kFusedSmem = 1024 + kOffBar + 512;
 
 struct FusedParams {
-    CUtensorMap tm_x;       // x [T][H] fp16, box {64, 128}, SW128
-    CUtensorMap tm_mid;     // mid [T][I] fp16, box {64, 128}, SW128
-    CUtensorMap tm_wg, tm_wu;   // raw [I][H*bits/8], box {raw_row, 32}
-    CUtensorMap tm_wd;          // raw [H][I*bits/8], box {raw_row, 64}
-    CUtensorMap tm_sg, tm_su;   // E8M0 [I][H/32], box {kbc_g, 32}
-    CUtensorMap tm_sd;          // E8M0 [H][I/32], box {kbc_d, 64}
+    CUtensorMap tm_x;           // x [T][H] fp16 as [H/64][T][64], box {64, NT, 2}, SW128
+    CUtensorMap tm_mid;         // mid [T][I] fp16 as [I/64][T][64], box {64, NT, 2}, SW128
+    CUtensorMap tm_wg, tm_wu;   // packed [I][H*bits/8], box {128, 64}, SW128
+    CUtensorMap tm_wd;          // packed [H][I*bits/8], box {128, 128}, SW128
+    CUtensorMap tm_sg, tm_su;   // E8M0 [I][H/32], box {16, 64}
+    CUtensorMap tm_sd;          // E8M0 [H][I/32], box {16, 128}
     __half *mid;
-    void *out;              // fp32 or fp16 [T][H]
-    float *ws;              // fp32 split partials [splits][T][H]
-    uint32_t *sync;         // [0] finished G tiles, [1] finished CTAs, [2..] D tile arrivals (self-resetting)
+    void *out;                  // fp32 or fp16 [T][H]
+    float *ws;                  // splits > 1: fp32 split partials, per split and output tile NT/4 x [128][4]
+    uint32_t *sync;             // [1] finished CTAs, [2..] D tile arrivals, then finished G tiles per
+                                // (token tile, K split of the down projection); all self-resetting
     uint32_t *err;
     uint32_t T, H, I;
-    uint32_t splits;        // K splits of the down projection
-    uint32_t kbc_g, kbc_d;  // scale bytes per row per tile
+    uint32_t NT;                // tokens per tile, multiple of 16
+    uint32_t splits;            // K splits of the down projection
     uint32_t n_gtiles, n_dtiles;
-    uint32_t d_spin;        // 1: each CTA holds at most one down tile, its last (splits may wait for each other)
+    uint32_t d_spin;            // 1: each CTA holds at most one down tile, its last (splits may wait for each other)
+    uint32_t g_per_slice;       // G tiles that write one split's K range of mid (per token tile)
     unsigned long long *trace;  // optional: kTraceSlots per CTA (profiling aid)
 };
 
-// Trace slots per CTA (ns from %globaltimer for events, SM cycles for sums).
+// Trace slots per CTA (ns from %globaltimer for events, SM cycles otherwise).
 enum TraceSlot : int {
     TR_START = 0, TR_PROLOGUE = 1, TR_END = 2, TR_G_EPI_END = 3, TR_WAIT_END = 4, TR_D_EPI_END = 5, TR_SMID = 6,
-    TR_RAWP_WAIT_EMPTY = 8, TR_AP_WAIT_EMPTY = 9, TR_AP_WAIT_COUNTER = 10, TR_MMA_WAIT_A = 11, TR_MMA_WAIT_B = 12,
+    TR_D_ACC = 7, TR_RAWP_WAIT_EMPTY = 8, TR_AP_WAIT_EMPTY = 9, TR_AP_WAIT_COUNTER = 10, TR_MMA_WAIT_A = 11, TR_G_COMPUTED = 12,
     TR_MMA_WAIT_ACC = 13, TR_DEC_WAIT_RAW = 14, TR_DEC_WAIT_SLOT = 15, TR_DEC_WORK = 16, TR_EPI_G = 17,
-    TR_DEC_WAIT_ACC = 18, TR_EPI_D = 19, TR_CYCLES = 20, TR_MMA_ISSUE = 21, TR_DEC_FIRST_RAW = 22, TR_DEC_FIRST_SC = 23, TR_MMA_FIRST_A = 24, TR_D_FENCED = 25, TR_D_COUNTED = 26, TR_D_CONVERTED = 27, TR_D_LAST = 28,
-    TR_G_ACC = 29, TR_G_STORED = 30, TR_G_PUBLISHED = 31, TR_D_ACC = 7, TR_D_STORED = 56, TR_D_ACC_WAITED = 57, TR_MMA_STAGE = 32, TR_DEC_STAGE = 64,
-    TR_AP_STAGE = 96, kTraceSlots = 128
+    TR_DEC_WAIT_ACC = 18, TR_EPI_D = 19, TR_CYCLES = 20, TR_MMA_ISSUE = 21, TR_DEC_FIRST_RAW = 22,
+    TR_DEC_FIRST_SC = 23, TR_MMA_FIRST_A = 24, TR_D_FENCED = 25, TR_D_COUNTED = 26, TR_D_CONVERTED = 27,
+    TR_D_LAST = 28, TR_G_ACC = 29, TR_G_STORED = 30, TR_G_PUBLISHED = 31, TR_MMA_STAGE = 32, TR_D_STORED = 56,
+    TR_D_ACC_WAITED = 57, TR_DEC_STAGE = 64, TR_AP_STAGE = 96, TR_DEC_RAW_READY = 128,
+    TR_DEC_START = 160, TR_MMA_WAIT_START = 192, TR_MMA_READY = 224, TR_WARP_DONE = 240,
+    kTraceSlots = 256
 };
 
-// mbar_wait that, while a trace is being recorded, adds the cycles it spent to `acc`.
 __device__ __forceinline__ bool mbar_wait_t(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *err,
                                             uint32_t site, unsigned long long &acc, bool timed)
 {
@@ -98,30 +119,6 @@ __device__ __forceinline__ bool mbar_wait_t(uint64_t *bar, uint32_t parity, vola
 }
 
 __device__ __forceinline__ long long clk_if(bool timed) { return timed ? clock64() : 0; }
-
-template <int W>
-struct FusedCfg {
-    static constexpr int kRawRow = kFBK * wfmt_bits(W) / 8;      // packed bytes per row per stage
-    static constexpr uint32_t kSPC = kChunkRow / kRawRow;         // stages per weight chunk
-    static constexpr uint32_t kChunkBytes = kFBN * kChunkRow;     // 16 KB
-    static constexpr uint32_t kAAtom = kBM * 128;                 // 128 rows x 64 K fp16
-    static constexpr uint32_t kBAtom = kFBN * 128;                // 64 rows x 64 K fp16
-    static constexpr uint32_t kABytes = 2 * kAAtom;
-    static constexpr uint32_t kBBytes = 2 * kBAtom;
-    // layout: [B ring][weight chunks][scales][activation ring (stages_a)]
-    static constexpr uint32_t kOffRaw = kStagesB * kBBytes;
-    static constexpr uint32_t kOffScales = kOffRaw + kChunks * kChunkBytes;
-    __host__ __device__ static uint32_t scale_slot(uint32_t kbc_max) { return kFBN * kbc_max; }
-    __host__ __device__ static uint32_t off_a(uint32_t kbc_max)
-    {
-        const uint32_t sc = (W == W_MXFP4) ? 2 * scale_slot(kbc_max) : 0;
-        return (kOffScales + sc + 1023u) & ~1023u;
-    }
-    static uint32_t smem_bytes(uint32_t kbc_max, uint32_t stages_a)
-    {
-        return 1024 + off_a(kbc_max) + stages_a * kABytes + 512;
-    }
-};
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p)
 {
@@ -142,7 +139,7 @@ __device__ __forceinline__ bool wait_counter(const uint32_t *p, uint32_t target,
     if (ld_acquire_gpu(p) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        __nanosleep(64);
+        __nanosleep(32);
         if (ld_acquire_gpu(p) >= target) return true;
         if (abort && *abort) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -153,7 +150,7 @@ __device__ __forceinline__ bool wait_counter(const uint32_t *p, uint32_t target,
     }
 }
 
-// Named barrier over the 256 epilogue threads that also ORs a predicate:
+// Named barrier over the 512 epilogue threads that also ORs a predicate:
 // every participant gets the same answer, so no thread can skip a later
 // barrier the others wait on.
 __device__ __forceinline__ bool epi_bar_any(bool pred)
@@ -162,7 +159,7 @@ __device__ __forceinline__ bool epi_bar_any(bool pred)
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.or.pred p, 1, 256, q;\n\t"
+        "bar.red.or.pred p, 1, 512, q;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(r)
         : "r"((uint32_t)pred)
@@ -170,78 +167,134 @@ __device__ __forceinline__ bool epi_bar_any(bool pred)
     return r != 0;
 }
 
-__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d)
-{
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
-}
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-// 32 lanes x 16 consecutive 32-bit TMEM columns.
-__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16])
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16, A read from tensor memory.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate)
 {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 lanes x 8 consecutive 32-bit TMEM columns; thread i reads lane (base+i).
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t *r)
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
         : "r"(taddr));
 }
+
+// 32 lanes x 4 consecutive 32-bit TMEM columns; thread i reads lane (base+i).
+__device__ __forceinline__ void tmem_ld_32x32b_x4(uint32_t taddr, uint32_t *r)
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+}
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns; thread i writes lane (base+i).
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit TMEM columns; thread i writes lane (base+i).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 struct TileInfo {
     bool is_g;
     uint32_t m0;      // first token
     uint32_t c0;      // G: first channel; D: first output column
     uint32_t kb;      // D: split index
+    uint32_t k0;      // first K element of the tile
     uint32_t nk;      // K stages
+    uint32_t rot;     // the tile walks its K stages starting at stage rot (a multiple of 4)
+    __device__ __forceinline__ uint32_t kstage(uint32_t s) const { return s + rot < nk ? s + rot : s + rot - nk; }
 };
 
 __device__ __forceinline__ TileInfo tile_info(const FusedParams &p, uint32_t t)
 {
     TileInfo ti;
-    const uint32_t gch = p.I / 32;
     if (t < p.n_gtiles) {
+        const uint32_t gch = p.I / kGCh;
         ti.is_g = true;
-        ti.c0 = (t % gch) * 32;
-        ti.m0 = (t / gch) * kBM;
+        ti.c0 = (t % gch) * kGCh;
+        ti.m0 = (t / gch) * p.NT;
         ti.kb = 0;
+        ti.k0 = 0;
         ti.nk = p.H / kFBK;
     } else {
-        const uint32_t d = t - p.n_gtiles, nj = p.H / kFBN;
+        const uint32_t d = t - p.n_gtiles, nh = p.H / kWRows, ks = p.I / p.splits;
         ti.is_g = false;
-        ti.c0 = (d % nj) * kFBN;
-        ti.kb = (d / nj) % p.splits;
-        ti.m0 = (d / (nj * p.splits)) * kBM;
-        ti.nk = p.I / p.splits / kFBK;
+        ti.c0 = (d % nh) * kWRows;
+        ti.kb = (d / nh) % p.splits;
+        ti.m0 = (d / (nh * p.splits)) * p.NT;
+        ti.k0 = ti.kb * ks;
+        ti.nk = ks / kFBK;
     }
+    // Tiles that read the same activations start at different K stages, so
+    // fewer CTAs request the same lines at once. Steps of 4 stages keep the
+    // weight and scale chunks whole.
+    ti.rot = (ti.nk % 4 == 0) ? (t % (ti.nk / 4)) * 4 : 0;
     return ti;
+}
+
+// Counter of finished G tiles feeding down split kb of token tile mt.
+__device__ __forceinline__ uint32_t *slice_counter(const FusedParams &p, uint32_t mt, uint32_t kb)
+{
+    const uint32_t n_mt = (p.T + p.NT - 1) / p.NT;
+    return p.sync + 2 + (p.H / kWRows) * n_mt + mt * p.splits + kb;
 }
 
 template <int W, int EG, bool OUT_F16>
 __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_constant__ FusedParams p)
 {
-    using Cfg = FusedCfg<W>;
-    constexpr uint32_t SPC = Cfg::kSPC;
+    constexpr uint32_t RB = kFBK * wfmt_bits(W) / 8;   // packed bytes per row per stage
+    constexpr uint32_t SPC = kChunkRow / RB;           // stages per weight chunk (1, 2 or 4)
+    constexpr uint32_t SPS = 4;                        // stages per scale chunk (16 B = 512 K)
+    constexpr uint32_t CB = chunk_bytes<W>();          // packed bytes per 32 weights
+    static_assert(SPC >= 1 && SPC * RB == kChunkRow, "stage must divide the chunk");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t kbc_max = p.kbc_g > p.kbc_d ? p.kbc_g : p.kbc_d;
-    constexpr uint32_t SA = kMaxStagesA;   // compile-time: the ring index math stays shifts and masks
     uint8_t *sB = smem;
-    uint8_t *sRaw = smem + Cfg::kOffRaw;
-    uint8_t *sSc = smem + Cfg::kOffScales;
-    uint8_t *sA = smem + Cfg::off_a(kbc_max);
-    const uint32_t sc_slot = (W == W_MXFP4) ? Cfg::scale_slot(kbc_max) : 0;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sA + SA * Cfg::kABytes);
+    uint8_t *sRaw = smem + kOffRaw;
+    uint8_t *sSc = smem + kOffSc;
+    __half *sMid = reinterpret_cast<__half *>(smem + kOffMid);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
     uint64_t *ck_full = bars;                       // [kChunks] packed weight chunk landed
     uint64_t *ck_empty = ck_full + kChunks;         // [kChunks] chunk decoded
-    // Stage s uses activation slot s % SA and decoded-weight slot s % 2. One
-    // barrier pair per stage: full[s % SA] completes when the activation copy
-    // landed AND the 4 warps of the decode group owning stage s arrived; the
-    // MMA commits empty[s % SA]. A decode group reuses weight slot s % 2 after
-    // waiting for stage s-2 to be committed on empty[(s-2) % SA].
-    uint64_t *a_full = ck_empty + kChunks;          // [SA]
-    uint64_t *a_empty = a_full + kMaxStagesA;       // [SA]
-    uint64_t *sc_full = a_empty + kMaxStagesA;      // [2]
-    uint64_t *sc_empty = sc_full + 2;               // [2]
-    uint64_t *acc_full = sc_empty + 2;              // [2]
+    uint64_t *sc_full = ck_empty + kChunks;         // [kScChunks] scale chunk landed
+    uint64_t *sc_empty = sc_full + kScChunks;       // [kScChunks] scale chunk used
+    // Stage s uses activation slot s % 4 and TMEM weight slot s % 4: full[s % 4]
+    // completes when the activation copy landed AND all 8 decode warps stored
+    // their weights; the MMA commits empty[s % 4], releasing both slots.
+    uint64_t *st_full = sc_empty + kScChunks;       // [kFStages]
+    uint64_t *st_empty = st_full + kFStages;         // [kFStages]
+    uint64_t *acc_full = st_empty + kFStages;        // [2]
     uint64_t *acc_empty = acc_full + 2;             // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -249,6 +302,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ntiles = p.n_gtiles + p.n_dtiles;
+    const uint32_t NT = p.NT;
     unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceSlots : nullptr;
     const long long clk0 = p.trace ? clock64() : 0;
     unsigned long long tw0 = 0, tw1 = 0, tw2 = 0, tw3 = 0;   // per-role accumulators (trace only)
@@ -264,13 +318,15 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
             mbar_init(&ck_full[s], 1);
             mbar_init(&ck_empty[s], kDecWarps);
         }
-        for (uint32_t s = 0; s < SA; ++s) {
-            mbar_init(&a_full[s], 1 + kDecWarps / 2);
-            mbar_init(&a_empty[s], 1);
-        }
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < kScChunks; ++s) {
             mbar_init(&sc_full[s], 1);
             mbar_init(&sc_empty[s], kDecWarps);
+        }
+        for (int s = 0; s < kFStages; ++s) {
+            mbar_init(&st_full[s], 1 + kDecWarps);
+            mbar_init(&st_empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
             mbar_init(&acc_full[s], 1);
             mbar_init(&acc_empty[s], kDecWarps);
         }
@@ -292,7 +348,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         tma_prefetch_desc(&p.tm_mid);
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(tmem_slot, 128);
+        tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -300,226 +356,306 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (tr && threadIdx.x == 0) tr[TR_PROLOGUE] = globaltimer_ns();
+    // The next layer's kernel may start on SMs this grid leaves free: it loads
+    // and decodes weights, and waits (griddepcontrol.wait) before it touches
+    // anything this kernel writes. Weights and scales are never written here.
+    pdl_launch_dependents();
 
     if (warp == kRawWarp) {
         // ------------------------------------------------ packed weight / scale producer
+        // Copies are issued in stage order so both rings release in that order.
         if (lane == 0) {
-            uint32_t gc = 0, ti_n = 0;
-            for (uint32_t t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++ti_n) {
+            uint32_t gc = 0, gsc = 0;
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; t < ntiles && ok && !*abort; t += gridDim.x) {
                 const TileInfo ti = tile_info(p, t);
-                if constexpr (W == W_MXFP4) {
-                    const uint32_t slot = ti_n & 1u;
-                    if (!mbar_wait(&sc_empty[slot], ((ti_n >> 1) & 1u) ^ 1u, abort, p.err, 0x601)) break;
-                    uint8_t *dst = sSc + slot * sc_slot;
-                    if (ti.is_g) {
-                        mbar_arrive_expect_tx(&sc_full[slot], 64u * p.kbc_g);
-                        tma_load_2d(dst, &p.tm_sg, 0, (int32_t)ti.c0, &sc_full[slot]);
-                        tma_load_2d(dst + 32 * p.kbc_g, &p.tm_su, 0, (int32_t)ti.c0, &sc_full[slot]);
-                    } else {
-                        mbar_arrive_expect_tx(&sc_full[slot], 64u * p.kbc_d);
-                        tma_load_2d(dst, &p.tm_sd, (int32_t)(ti.kb * p.kbc_d), (int32_t)ti.c0, &sc_full[slot]);
+                const int32_t row0 = (int32_t)ti.c0;
+                for (uint32_t s = 0; s < ti.nk; ++s) {
+                    if (W == W_MXFP4 && s % SPS == 0) {
+                        const uint32_t sl = gsc % kScChunks;
+                        if (!mbar_wait_t(&sc_empty[sl], ((gsc / kScChunks) & 1u) ^ 1u, abort, p.err, 0x601, tw0,
+                                         tr != nullptr)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&sc_full[sl], kScBytes);
+                        uint8_t *dst = sSc + sl * kScBytes;
+                        const int32_t kx = (int32_t)((ti.k0 + ti.kstage(s) * kFBK) / 32);
+                        if (ti.is_g) {
+                            tma_load_2d(dst, &p.tm_sg, kx, row0, &sc_full[sl]);
+                            tma_load_2d(dst + kGCh * kScRow, &p.tm_su, kx, row0, &sc_full[sl]);
+                        } else {
+                            tma_load_2d(dst, &p.tm_sd, kx, row0, &sc_full[sl]);
+                        }
+                        ++gsc;
                     }
-                }
-                const uint32_t byte0 = ti.kb * ti.nk * Cfg::kRawRow;   // this tile's K range within the row
-                const uint32_t nck = (ti.nk + SPC - 1) / SPC;
-                for (uint32_t c = 0; c < nck; ++c, ++gc) {
-                    const uint32_t st = gc % kChunks, ph = (gc / kChunks) & 1u;
-                    if (!mbar_wait_t(&ck_empty[st], ph ^ 1u, abort, p.err, 0x602, tw0, tr != nullptr)) break;
-                    mbar_arrive_expect_tx(&ck_full[st], Cfg::kChunkBytes);
-                    uint8_t *dst = sRaw + st * Cfg::kChunkBytes;
-                    const int32_t kx = (int32_t)(byte0 + c * kChunkRow);
-                    if (ti.is_g) {
-                        tma_load_2d(dst, &p.tm_wg, kx, (int32_t)ti.c0, &ck_full[st]);
-                        tma_load_2d(dst + 32 * kChunkRow, &p.tm_wu, kx, (int32_t)ti.c0, &ck_full[st]);
-                    } else {
-                        tma_load_2d(dst, &p.tm_wd, kx, (int32_t)ti.c0, &ck_full[st]);
+                    if (s % SPC == 0) {
+                        const uint32_t sl = gc % kChunks;
+                        if (!mbar_wait_t(&ck_empty[sl], ((gc / kChunks) & 1u) ^ 1u, abort, p.err, 0x602, tw0,
+                                         tr != nullptr)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&ck_full[sl], kChunkBytes);
+                        uint8_t *dst = sRaw + sl * kChunkBytes;
+                        const int32_t kx = (int32_t)(ti.k0 / kFBK * RB + ti.kstage(s) * RB);
+                        if (ti.is_g) {
+                            tma_load_2d(dst, &p.tm_wg, kx, row0, &ck_full[sl]);
+                            tma_load_2d(dst + kGCh * kChunkRow, &p.tm_wu, kx, row0, &ck_full[sl]);
+                        } else {
+                            tma_load_2d(dst, &p.tm_wd, kx, row0, &ck_full[sl]);
+                        }
+                        ++gc;
                     }
                 }
             }
             // no copies left in flight when the CTA exits
-            for (uint32_t t = (gc > kChunks ? gc - kChunks : 0); t < gc; ++t)
-                mbar_wait(&ck_full[t % kChunks], (t / kChunks) & 1u, nullptr, p.err, 0x603);
+            for (uint32_t c = (gc > kChunks ? gc - kChunks : 0); c < gc; ++c)
+                mbar_wait(&ck_full[c % kChunks], (c / kChunks) & 1u, nullptr, p.err, 0x603);
+            for (uint32_t c = (gsc > kScChunks ? gsc - kScChunks : 0); c < gsc; ++c)
+                mbar_wait(&sc_full[c % kScChunks], (c / kScChunks) & 1u, nullptr, p.err, 0x604);
         }
     } else if (warp < kAProd) {
         // ------------------------------------------------ activation producers
+        // stage gs goes to warp gs % 2 and uses slot gs % 4
         if (lane == 0) {
-            uint32_t gs = 0;
-            bool waited = false;
-            for (uint32_t t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+            pdl_wait_prior();   // activations and counters may come from the previous kernel
+            uint32_t gs = 0, last[2] = {0, 0}, waited_t = ~0u;
+            bool ok = true, any[2] = {false, false};
+            const uint32_t atom = NT * 128;
+            for (uint32_t t = blockIdx.x; t < ntiles && ok && !*abort; t += gridDim.x) {
                 const TileInfo ti = tile_info(p, t);
                 const CUtensorMap *tm = ti.is_g ? &p.tm_x : &p.tm_mid;
-                const uint32_t kstage0 = ti.kb * ti.nk;
-                bool ok = true;
                 for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
-                    if (gs % kAProd != (uint32_t)warp) continue;
-                    if (!ti.is_g && !waited) {
-                        // mid is written by other CTAs' G tiles (generic stores); wait
-                        // for all of them, then order those writes before our TMA reads
+                    if ((gs & 1u) != (uint32_t)warp) continue;
+                    if (!ti.is_g && waited_t != t) {
+                        // mid is written by other CTAs' G tiles (generic stores); wait for
+                        // the ones covering this split's K range, then order their writes
+                        // before our TMA reads
                         const long long cw = clk_if(tr);
-                        if (!wait_counter(p.sync, p.n_gtiles, abort, p.err, 0x701)) { ok = false; break; }
+                        if (!wait_counter(slice_counter(p, ti.m0 / NT, ti.kb), p.g_per_slice, abort, p.err, 0x701)) {
+                            ok = false;
+                            break;
+                        }
                         if (tr) tw1 += (unsigned long long)(clock64() - cw);
                         if (tr && warp == 0) tr[TR_WAIT_END] = globaltimer_ns();
                         fence_proxy_async_global();
-                        waited = true;
+                        waited_t = t;
                     }
-                    const uint32_t st = gs % SA, ph = (gs / SA) & 1u;
-                    if (!mbar_wait_t(&a_empty[st], ph ^ 1u, abort, p.err, 0x702, tw0, tr != nullptr)) { ok = false; break; }
+                    const uint32_t sl = gs & (kFStages - 1), use = gs / kFStages;
+                    if (!mbar_wait_t(&st_empty[sl], (use & 1u) ^ 1u, abort, p.err, 0x702, tw0, tr != nullptr)) {
+                        ok = false;
+                        break;
+                    }
                     if (tr && gs < 32) tr[TR_AP_STAGE + gs] = (unsigned long long)(clock64() - clk0);
-                    mbar_arrive_expect_tx(&a_full[st], Cfg::kABytes);
-                    const int32_t kx = (int32_t)((kstage0 + s) * kFBK);
-                    tma_load_2d(sA + st * Cfg::kABytes, tm, kx, (int32_t)ti.m0, &a_full[st]);
-                    tma_load_2d(sA + st * Cfg::kABytes + Cfg::kAAtom, tm, kx + kBK, (int32_t)ti.m0, &a_full[st]);
+                    mbar_arrive_expect_tx(&st_full[sl], 2 * atom);
+                    uint8_t *dst = sB + sl * kStageBytes;
+                    const int32_t kx = (int32_t)(ti.k0 + ti.kstage(s) * kFBK);
+                    tma_load_3d(dst, tm, 0, (int32_t)ti.m0, kx / 64, &st_full[sl]);
+                    last[sl >> 1] = gs;
+                    any[sl >> 1] = true;
                 }
-                if (!ok) break;
             }
-            for (uint32_t t = (gs > SA ? gs - SA : 0); t < gs; ++t)
-                if (t % kAProd == (uint32_t)warp) mbar_wait(&a_full[t % SA], (t / SA) & 1u, nullptr, p.err, 0x703);
+            // no copies left in flight when the CTA exits: the last use of each slot
+            for (int i = 0; i < 2; ++i)
+                if (any[i]) mbar_wait(&st_full[last[i] & (kFStages - 1)], (last[i] / kFStages) & 1u, nullptr, p.err, 0x703);
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(kBM, kFBN);
+            const uint32_t idesc = idesc_f16_f32(kWRows, (int)NT);
+            const uint32_t atom = NT * 128;
             uint32_t gs = 0, ti_n = 0;
             for (uint32_t t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++ti_n) {
                 const TileInfo ti = tile_info(p, t);
                 const uint32_t acc = ti_n & 1u;
                 if (!mbar_wait_t(&acc_empty[acc], ((ti_n >> 1) & 1u) ^ 1u, abort, p.err, 0x801, tw2, tr != nullptr)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + acc * kFBN;
-                uint32_t ra = mbar_test(&a_full[gs % SA], (gs / SA) & 1u);
+                const uint32_t d_tmem = tmem + acc * kAccCols;
+                bool ok = true;
                 for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
-                    const uint32_t sa = gs % SA, pa = (gs / SA) & 1u;
-                    const uint32_t sbb = gs % kStagesB;
-                    if (!ra && !mbar_wait_t(&a_full[sa], pa, abort, p.err, 0x802, tw0, tr != nullptr)) break;
+                    const uint32_t sl = gs & (kFStages - 1);
+                    if (tr && gs < 32) tr[TR_MMA_WAIT_START + gs] = (unsigned long long)(clock64() - clk0);
+                    if (!mbar_wait_t(&st_full[sl], (gs / kFStages) & 1u, abort, p.err, 0x802, tw0, tr != nullptr)) {
+                        ok = false;
+                        break;
+                    }
                     if (tr && gs == 0) tr[TR_MMA_FIRST_A] = (unsigned long long)(clock64() - clk0);
-                    // probe the next stage now; the answer is needed only after this
-                    // stage's MMAs are issued
-                    const uint32_t gn = gs + 1;
-                    ra = (s + 1 < ti.nk) ? mbar_test(&a_full[gn % SA], (gn / SA) & 1u) : 0u;
+                    if (tr && gs < 16) tr[TR_MMA_READY + gs] = (unsigned long long)(clock64() - clk0);
                     const long long cis = clk_if(tr);
                     tc_fence_after();
+                    const uint32_t a0 = tmem + kACol0 + sl * 64;
 #pragma unroll
                     for (uint32_t j = 0; j < 2; ++j) {
-                        const uint64_t ad = smem_desc_sw128(sA + sa * Cfg::kABytes + j * Cfg::kAAtom);
-                        const uint64_t bd = smem_desc_sw128(sB + sbb * Cfg::kBBytes + j * Cfg::kBAtom);
+                        const uint64_t bd = smem_desc_sw128(sB + sl * kStageBytes + j * atom);
 #pragma unroll
-                        for (uint32_t k = 0; k < kBK / 16; ++k)
-                            mma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (s | j | k) != 0u);
+                        for (uint32_t k = 0; k < 4; ++k)
+                            mma_f16_ts(d_tmem, a0 + j * 32 + k * 8, bd + 2 * k, idesc, (s | j | k) != 0u);
                     }
-                    mma_commit(&a_empty[sa]);
+                    mma_commit(&st_empty[sl]);
                     if (tr) tw3 += (unsigned long long)(clock64() - cis);
                     if (tr && gs < 24) tr[TR_MMA_STAGE + gs] = (unsigned long long)(clock64() - clk0);
                 }
+                if (!ok) break;
                 mma_commit(&acc_full[acc]);
             }
         }
     } else {
         // ------------------------------------------------ decode + epilogue
-        const uint32_t te = threadIdx.x - kDec0 * 32;   // 0..255
+        const uint32_t te = threadIdx.x - kDec0 * 32;   // 0..511
         const uint32_t quarter = warp & 3;             // TMEM lanes 32*quarter..+31
-        const uint32_t colh = (warp - kDec0) >> 2;     // column half of the tile
-        const uint32_t row = quarter * 32 + lane;
-        // decode: two groups of 4 warps take alternate stages; 32 weights per thread
-        const uint32_t grp = (warp - kDec0) >> 2;
-        const uint32_t tg = te & 127u, dr = tg >> 1, dh = tg & 1u;   // B row, half of the 64-wide stage
-        uint32_t gs = 0, gc = 0, ti_n = 0;
+        const uint32_t kq = (warp - kDec0) >> 2;       // decode: K quarter of the stage; epilogue: token quarter
+        const uint32_t r = quarter * 32 + lane;        // weight row of the tile = TMEM lane
+        const uint32_t lane_base = (quarter * 32u) << 16;
+        uint32_t gs = 0, gc = 0, gsc = 0, ti_n = 0;
         for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti_n) {
             const TileInfo ti = tile_info(p, t);
-            const uint32_t slot = ti_n & 1u;
-            const uint32_t kbc = ti.is_g ? p.kbc_g : p.kbc_d;
-            const uint8_t *scl = sSc + slot * sc_slot;
-            if constexpr (W == W_MXFP4) mbar_wait(&sc_full[slot], (ti_n >> 1) & 1u, abort, p.err, 0x901);
-            if (tr && te == 0 && ti_n == 0) tr[TR_DEC_FIRST_SC] = (unsigned long long)(clock64() - clk0);
-            uint32_t cst = 0;
-            for (uint32_t s = 0; s < ti.nk && !*abort; ++s, ++gs) {
-                const uint32_t sc = s % SPC;
-                const bool mine = (gs & 1u) == grp;
-                if (sc == 0) {
+            // packed row in the chunk: G rows interleave gate and up channels
+            const uint32_t rr = ti.is_g ? ((r & 1u) ? kGCh + (r >> 1) : (r >> 1)) : r;
+            bool ok = true;
+            const uint32_t sw = rr & 7u;
+            uint32_t cst = 0, scs = 0;
+            for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
+                const uint32_t sl = gs & (kFStages - 1);
+                if (s % SPC == 0) {
                     cst = gc % kChunks;
-                    if (!mbar_wait_t(&ck_full[cst], (gc / kChunks) & 1u, abort, p.err, 0x902, tw0, tr != nullptr)) break;
+                    if (!mbar_wait_t(&ck_full[cst], (gc / kChunks) & 1u, abort, p.err, 0x902, tw0, tr != nullptr)) {
+                        ok = false;
+                        break;
+                    }
                     if (tr && te == 0 && gc == 0) tr[TR_DEC_FIRST_RAW] = (unsigned long long)(clock64() - clk0);
+                    if (tr && te == 0 && gs < 32) tr[TR_DEC_RAW_READY + gs] = (unsigned long long)(clock64() - clk0);
                 }
-                if (mine) {
-                    const uint32_t st = gs % kStagesB;
-                    if (gs >= kStagesB) {   // stage gs-2 (same weight slot) consumed by the MMA
-                        const uint32_t g3 = gs - kStagesB;
-                        if (!mbar_wait_t(&a_empty[g3 % SA], (g3 / SA) & 1u, abort, p.err, 0x903, tw1, tr != nullptr)) break;
-                    }
-                    const long long cdec = clk_if(tr);
-                    const uint8_t *raw = sRaw + cst * Cfg::kChunkBytes + dr * kChunkRow + sc * Cfg::kRawRow;
-                    // this thread: row dr, K half dh (= swizzle atom dh: 64 weights, two
-                    // 32-wide scale blocks)
-                    uint8_t *rowp = sB + st * Cfg::kBBytes + dh * Cfg::kBAtom + dr * 128;
-#pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        uint32_t sb = 127u;
-                        // G: rows 0..31 gate scales, 32..63 up scales, each kbc_g wide
-                        if constexpr (W == W_MXFP4) sb = scl[dr * kbc + 4 * s + 2 * dh + half];
-                        uint32_t o[16];
-                        decode_chunk<W>(raw + (2 * dh + half) * (Cfg::kRawRow / 4), sb, o);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const uint32_t phys = ((half * 4 + q) ^ (dr & 7u)) * 16u;
-                            *reinterpret_cast<uint4 *>(rowp + phys) =
-                                make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-                        }
-                    }
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[gs % SA]);
-                    if (tr) tw2 += (unsigned long long)(clock64() - cdec);
-                    if (tr && te == 0 && gs < 32) tr[TR_DEC_STAGE + gs] = (unsigned long long)(clock64() - clk0);
+                if (W == W_MXFP4 && s % SPS == 0) {
+                    scs = gsc % kScChunks;
+                    if (!mbar_wait(&sc_full[scs], (gsc / kScChunks) & 1u, abort, p.err, 0x901)) { ok = false; break; }
                 }
-                if ((sc == SPC - 1) || (s + 1 == ti.nk)) {
+                if (gs >= kFStages) {   // MMA of stage gs-4 (same TMEM slot) completed
+                    if (!mbar_wait_t(&st_empty[sl], ((gs / kFStages) - 1u) & 1u, abort, p.err, 0x903, tw1,
+                                     tr != nullptr)) { ok = false; break; }
+                    tc_fence_after();
+                }
+                const long long cdec = clk_if(tr);
+                if (tr && te == 0 && gs < 32) tr[TR_DEC_START + gs] = (unsigned long long)(cdec - clk0);
+                const uint8_t *rowp = sRaw + cst * kChunkBytes + rr * kChunkRow;
+                // this thread: 32 weights = RB/4 packed bytes of row rr
+                const uint32_t off = (s % SPC) * RB + kq * CB;
+                uint32_t w[8];
+                if constexpr (CB == 8) {
+                    const uint2 v = *reinterpret_cast<const uint2 *>(rowp + ((((off >> 4) ^ sw) << 4) | (off & 8u)));
+                    w[0] = v.x; w[1] = v.y;
+                } else {
+#pragma unroll
+                    for (int q = 0; q < (int)CB / 16; ++q) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(rowp + ((((off >> 4) + q) ^ sw) << 4));
+                        w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+                    }
+                }
+                uint32_t sb = 127u;
+                if constexpr (W == W_MXFP4) sb = sSc[scs * kScBytes + rr * kScRow + (s % SPS) * 4 + kq];
+                uint32_t words[16];
+                decode_words<W>(w, sb, words);
+                tmem_st_32x32b_x16(tmem + lane_base + kACol0 + sl * 64 + kq * 16, words);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&st_full[sl]);
+                if (tr) tw2 += (unsigned long long)(clock64() - cdec);
+                if (tr && te == 0 && gs < 32) tr[TR_DEC_STAGE + gs] = (unsigned long long)(clock64() - clk0);
+                if (tr && lane == 0 && gs == 2) tr[TR_WARP_DONE + (warp - kDec0)] = (unsigned long long)(clock64() - clk0);
+                if (s % SPC == SPC - 1 || s + 1 == ti.nk) {
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&ck_empty[cst]);
                     ++gc;
                 }
-            }
-            if constexpr (W == W_MXFP4) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sc_empty[slot]);
+                if (W == W_MXFP4 && (s % SPS == SPS - 1 || s + 1 == ti.nk)) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sc_empty[scs]);
+                    ++gsc;
+                }
             }
 
+
             // ---------------------------------------------- tile epilogue
+            if (ti_n == 0) pdl_wait_prior();   // before the first write of mid / partials / out
             const uint32_t acc = ti_n & 1u;
-            mbar_wait_t(&acc_full[acc], (ti_n >> 1) & 1u, abort, p.err, 0x904, tw3, tr != nullptr);
+            if (ok) mbar_wait_t(&acc_full[acc], (ti_n >> 1) & 1u, abort, p.err, 0x904, tw3, tr != nullptr);
             const long long cepi = clk_if(tr);
             if (epi_bar_any(*abort != 0)) break;
             tc_fence_after();
-            const uint32_t taddr = tmem + ((quarter * 32u) << 16) + acc * kFBN;
-            const uint32_t m = ti.m0 + row;
-            if (ti.is_g) {
-                uint32_t g[16], u[16];
-                tmem_ld_32x32b_x16(taddr + colh * 16, g);
-                tmem_ld_32x32b_x16(taddr + 32 + colh * 16, u);
+            const uint32_t ncol = NT / 4;                  // tokens of this thread: [kq*ncol, +ncol)
+            const uint32_t taddr = tmem + lane_base + acc * kAccCols + kq * ncol;
+            // accumulator columns in blocks of 32; the last block's loads release it
+            const uint32_t j = r >> 1, is_up = lane & 1u;                // G: channel, gate/up
+            const uint32_t h = ti.c0 + r, t0 = ti.m0 + kq * ncol;        // D: output column, first token
+            // D: this split's partial tile, NT/4 blocks of [128 outputs][4 tokens]
+            const uint32_t n_mt = (p.T + NT - 1) / NT, tile_d = (ti.m0 / NT) * (p.H / kWRows) + ti.c0 / kWRows;
+            const size_t tile_floats = (size_t)NT * kWRows, split_floats = (size_t)n_mt * (p.H / kWRows) * tile_floats;
+            float *part = p.ws + ti.kb * split_floats + tile_d * tile_floats;
+            if (tr && te == 0) tr[ti.is_g ? TR_G_ACC : TR_D_ACC] = (unsigned long long)(clock64() - clk0);
+            for (uint32_t cb = 0; cb < ncol; cb += 32) {
+                uint32_t v[32];
+#pragma unroll
+                for (uint32_t c = 0; c < 32; c += 4)
+                    if (cb + c < ncol) tmem_ld_32x32b_x4(taddr + cb + c, v + c);
                 tmem_ld_wait();
-                if (tr && te == 0) tr[TR_G_ACC] = (unsigned long long)(clock64() - clk0);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[acc]);
-                if (m < p.T) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(p.mid + (size_t)m * p.I + ti.c0 + colh * 16);
+                if (cb + 32 >= ncol) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                }
+                if (ti.is_g) {
+                    // lane pair (2j, 2j+1) = (gate, up) of channel j: the even lane
+                    // finishes tokens 0..1 of each group of 4, the odd lane 2..3
 #pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        uint32_t w4[4];
+                    for (uint32_t c = 0; c < 32; c += 4) {
+                        if (cb + c < ncol) {
 #pragma unroll
-                        for (int j2 = 0; j2 < 4; ++j2) {
-                            const int e = 8 * i + 2 * j2;
-                            w4[j2] = half2_bits(swiglu<EG>(__uint_as_float(g[e]), __uint_as_float(u[e])),
-                                                swiglu<EG>(__uint_as_float(g[e + 1]), __uint_as_float(u[e + 1])));
+                            for (uint32_t i = 0; i < 2; ++i) {
+                                // compile-time indices only: v stays in registers
+                                const uint32_t mine = is_up ? v[c + 2 + i] : v[c + i];
+                                const uint32_t send = is_up ? v[c + i] : v[c + 2 + i];   // what the partner needs
+                                const uint32_t other = __shfl_xor_sync(0xffffffffu, send, 1);
+                                const float g = __uint_as_float(is_up ? other : mine);
+                                const float u = __uint_as_float(is_up ? mine : other);
+                                sMid[(kq * ncol + cb + c + is_up * 2 + i) * kGCh + j] =
+                                    __float2half_rn(swiglu<EG>(g, u));
+                            }
                         }
-                        dst[i] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     }
+                } else if (p.splits == 1) {
+#pragma unroll
+                    for (uint32_t i = 0; i < 32; ++i) {
+                        if (cb + i < ncol && t0 + cb + i < p.T) {
+                            const float f = __uint_as_float(v[i]);
+                            if constexpr (OUT_F16)
+                                static_cast<__half *>(p.out)[(size_t)(t0 + cb + i) * p.H + h] = __float2half_rn(f);
+                            else
+                                static_cast<float *>(p.out)[(size_t)(t0 + cb + i) * p.H + h] = f;
+                        }
+                    }
+                } else {
+                    // one float4 of 4 tokens per thread: a warp stores 512 contiguous bytes
+#pragma unroll
+                    for (uint32_t c = 0; c < 32; c += 4)
+                        if (cb + c < ncol)
+                            __stcg(reinterpret_cast<float4 *>(part) + ((kq * ncol + cb + c) / 4) * kWRows + r,
+                                   make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]),
+                                               __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3])));
+                }
+            }
+            if (ti.is_g) {
+                if (tr && te == 0) tr[TR_G_COMPUTED] = (unsigned long long)(clock64() - clk0);
+                epi_bar();
+                // fp16 mid rows: NT x 128 bytes to mid[m0 + t][c0 .. c0 + 64)
+                for (uint32_t i = te; i < NT * (kGCh / 8); i += kEpi) {
+                    const uint32_t tt = i / (kGCh / 8), q = i % (kGCh / 8);
+                    if (ti.m0 + tt < p.T)
+                        *reinterpret_cast<uint4 *>(p.mid + (size_t)(ti.m0 + tt) * p.I + ti.c0 + q * 8) =
+                            *reinterpret_cast<const uint4 *>(sMid + tt * kGCh + q * 8);
                 }
                 if (tr && te == 0) tr[TR_G_STORED] = (unsigned long long)(clock64() - clk0);
                 // publish: our generic stores ordered before other CTAs' TMA (async
                 // proxy) reads; one release by one thread after the CTA barrier
                 fence_proxy_async_global();
-                asm volatile("bar.sync 1, 256;" ::: "memory");
+                epi_bar();
                 if (te == 0) {
                     __threadfence();
-                    atomicAdd(p.sync, 1u);
+                    atomicAdd(slice_counter(p, ti.m0 / NT, ti.c0 / (p.I / p.splits)), 1u);
                 }
                 if (tr && te == 0) {
                     tr[TR_G_PUBLISHED] = (unsigned long long)(clock64() - clk0);
@@ -527,22 +663,9 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     tr[TR_EPI_G] += (unsigned long long)(clock64() - cepi);
                 }
             } else {
-                // Down tile: store this split's fp32 partial tile (plain stores, no
-                // atomics), count the split, then sum the splits into out.
-                float *part = p.ws + ((size_t)ti.kb * p.T + m) * p.H + ti.c0 + colh * 32;
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(taddr + colh * 32, v);
-                tmem_ld_wait();
-                if (tr && te == 0) tr[TR_D_ACC] = (unsigned long long)(clock64() - clk0);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[acc]);
-                if (m < p.T) {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        __stcg(reinterpret_cast<float4 *>(part) + i,
-                               make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                           __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
+                if (p.splits == 1) {
+                    if (tr && te == 0) tr[TR_EPI_D] += (unsigned long long)(clock64() - cepi);
+                    continue;
                 }
                 if (tr && te == 0) {
                     tr[TR_EPI_D] += (unsigned long long)(clock64() - cepi);
@@ -550,53 +673,56 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     tr[TR_D_ACC_WAITED] = (unsigned long long)(cepi - clk0);
                 }
                 __threadfence();
-                asm volatile("bar.sync 1, 256;" ::: "memory");
+                epi_bar();
                 if (tr && te == 0) tr[TR_D_FENCED] = (unsigned long long)(clock64() - clk0);
-                uint32_t *cnt = p.sync + 2 + (ti.m0 / kBM) * (p.H / kFBN) + ti.c0 / kFBN;
+                uint32_t *cnt = p.sync + 2 + tile_d;
                 if (te == 0) {
                     const bool last = atomicAdd(cnt, 1u) == p.splits - 1;
                     if (last) __threadfence();   // the other splits' partials are visible to us
                     *s_last = last ? 1u : 0u;
                 }
-                asm volatile("bar.sync 1, 256;" ::: "memory");
-                uint32_t r0 = 0, r1 = 0;   // rows of the tile this CTA sums
+                epi_bar();
+                const uint32_t nb = NT / 4;   // 4-token blocks of the tile
+                uint32_t b0 = 0, b1 = 0;      // blocks this CTA sums
                 if (p.d_spin) {
-                    // Every split of this tile is resident and this is each CTA's last
-                    // tile, so waiting cannot deadlock; each split then sums a
-                    // 1/splits band of rows in parallel.
-                    bool ok = true;
-                    if (te == 0 && !*s_last) ok = wait_counter(cnt, p.splits, abort, p.err, 0x905);
-                    if (epi_bar_any(!ok)) break;
-                    r0 = ti.kb * kBM / p.splits;
-                    r1 = (ti.kb + 1) * kBM / p.splits;
+                    // every split of this tile is resident and this is each CTA's
+                    // last tile, so waiting cannot deadlock; each split then sums a
+                    // 1/splits band of token blocks
+                    bool wok = true;
+                    if (te == 0 && !*s_last) wok = wait_counter(cnt, p.splits, abort, p.err, 0x905);
+                    if (epi_bar_any(!wok)) break;
+                    b0 = ti.kb * nb / p.splits;
+                    b1 = (ti.kb + 1) * nb / p.splits;
                 } else if (*s_last) {
-                    r1 = kBM;
+                    b1 = nb;
                 }
                 if (tr && te == 0) { tr[TR_D_COUNTED] = (unsigned long long)(clock64() - clk0); tr[TR_D_LAST] = *s_last; }
-                const size_t split_stride = (size_t)p.T * p.H;
-                for (uint32_t i = r0 * (kFBN / 4) + te; i < r1 * (kFBN / 4); i += kEpi) {
-                    const uint32_t mm = ti.m0 + i / (kFBN / 4), c4 = (i % (kFBN / 4)) * 4;
-                    if (mm >= p.T) continue;
-                    const float *src = p.ws + (size_t)mm * p.H + ti.c0 + c4;
-                    float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 *tile0 = reinterpret_cast<const float4 *>(p.ws + tile_d * tile_floats);
+                for (uint32_t i = b0 * kWRows + te; i < b1 * kWRows; i += kEpi) {
+                    const uint32_t blk = i / kWRows, hr = i % kWRows;
+                    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
                     for (uint32_t j0 = 0; j0 < p.splits; j0 += 8) {
                         // all eight loads in flight before the first add
                         float4 q[8];
 #pragma unroll
                         for (uint32_t j = 0; j < 8; ++j)
-                            q[j] = (j0 + j < p.splits)
-                                       ? __ldcg(reinterpret_cast<const float4 *>(src + (j0 + j) * split_stride))
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                            q[j] = (j0 + j < p.splits) ? __ldcg(tile0 + (j0 + j) * (split_floats / 4) + i)
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                         for (uint32_t j = 0; j < 8; ++j) {
-                            acc4.x += q[j].x; acc4.y += q[j].y; acc4.z += q[j].z; acc4.w += q[j].w;
+                            a4.x += q[j].x; a4.y += q[j].y; a4.z += q[j].z; a4.w += q[j].w;
                         }
                     }
-                    if constexpr (OUT_F16) {
-                        *reinterpret_cast<uint2 *>(static_cast<__half *>(p.out) + (size_t)mm * p.H + ti.c0 + c4) =
-                            make_uint2(half2_bits(acc4.x, acc4.y), half2_bits(acc4.z, acc4.w));
-                    } else {
-                        *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + (size_t)mm * p.H + ti.c0 + c4) = acc4;
+                    const float f4[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                    for (uint32_t e = 0; e < 4; ++e) {
+                        const uint32_t mm = ti.m0 + blk * 4 + e;
+                        if (mm < p.T) {
+                            if constexpr (OUT_F16)
+                                static_cast<__half *>(p.out)[(size_t)mm * p.H + ti.c0 + hr] = __float2half_rn(f4[e]);
+                            else
+                                static_cast<float *>(p.out)[(size_t)mm * p.H + ti.c0 + hr] = f4[e];
+                        }
                     }
                 }
                 if (tr && te == 0) tr[TR_D_CONVERTED] = (unsigned long long)(clock64() - clk0);
@@ -615,23 +741,24 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem, 128);
+        tmem_dealloc(tmem, kTmemCols);
     }
-    // Every tile of this CTA is finished (no thread reads the grid counters any
-    // more): count the CTA; the last one resets the counters for the next
-    // launch on this stream.
     if (tr) {
         if (warp == kRawWarp && lane == 0) tr[TR_RAWP_WAIT_EMPTY] = tw0;
         if (warp == 0 && lane == 0) { tr[TR_AP_WAIT_EMPTY] = tw0; tr[TR_AP_WAIT_COUNTER] = tw1; }
-        if (warp == kMmaWarp && lane == 0) { tr[TR_MMA_WAIT_A] = tw0; tr[TR_MMA_WAIT_B] = tw1; tr[TR_MMA_WAIT_ACC] = tw2; tr[TR_MMA_ISSUE] = tw3; }
+        if (warp == kMmaWarp && lane == 0) { tr[TR_MMA_WAIT_A] = tw0; tr[TR_MMA_WAIT_ACC] = tw2; tr[TR_MMA_ISSUE] = tw3; }
         if (threadIdx.x == kDec0 * 32) {
             tr[TR_DEC_WAIT_RAW] = tw0; tr[TR_DEC_WAIT_SLOT] = tw1; tr[TR_DEC_WORK] = tw2; tr[TR_DEC_WAIT_ACC] = tw3;
             tr[TR_D_EPI_END] = globaltimer_ns();
         }
         if (threadIdx.x == 0) { tr[TR_END] = globaltimer_ns(); tr[TR_CYCLES] = (unsigned long long)(clock64() - clk0); }
     }
+    // Every tile of this CTA is finished (no thread reads the grid counters any
+    // more): count the CTA; the last one resets the counters for the next
+    // launch on this stream.
     if (threadIdx.x == 0 && atomicAdd(p.sync + 1, 1u) == gridDim.x - 1) {
-        atomicExch(p.sync + 0, 0u);
+        const uint32_t n_mt = (p.T + NT - 1) / NT;
+        for (uint32_t i = 0; i < n_mt * p.splits; ++i) atomicExch(slice_counter(p, i / p.splits, i % p.splits), 0u);
         atomicExch(p.sync + 1, 0u);
     }
 }

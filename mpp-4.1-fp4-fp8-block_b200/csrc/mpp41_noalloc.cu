@@ -83,18 +83,9 @@ mpp41_status setup(int dev, DevPtrs *out)
 }
 
 // Same split rule as mpp41_mlp, so both entry points compute the same layer.
-uint32_t splits_for(uint32_t T, uint32_t H, uint32_t I)
+mpp41::LayerPlan noalloc_plan(const mpp41_mlp_desc *d)
 {
-    const uint32_t tiles = (H / 64) * ((T + 127) / 128);
-    uint32_t s = 1;
-    while (tiles * s * 2 <= 160 && (I % (64 * s * 2)) == 0 && I / (s * 2) >= 256) s *= 2;
-    return s;
-}
-
-uint32_t noalloc_splits(const mpp41_mlp_desc *d)
-{
-    const uint32_t s = splits_for(d->tokens, d->hidden, d->intermediate);
-    return (d->out_dtype == MPP41_F16 && s == 1) ? 2 : s;
+    return mpp41::plan_layer(d->tokens, d->hidden, d->intermediate, d->out_dtype == MPP41_F16);
 }
 
 }  // namespace
@@ -103,7 +94,7 @@ extern "C" size_t mpp41_mlp_noalloc_scratch_bytes(const mpp41_mlp_desc *d)
 {
     if (!d) return 0;
     const size_t mid = ((size_t)d->tokens * d->intermediate * 2 + 255) & ~size_t(255);
-    return mid + mpp41::fused_ws_bytes(d->tokens, d->hidden, noalloc_splits(d));
+    return mid + noalloc_plan(d).ws_bytes;
 }
 
 extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x, const void *wg, const void *wu,
@@ -130,7 +121,8 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
                    "the static scratch of mpp41_mlp_noalloc holds %u bytes -- use mpp41_mlp with a "
                    "caller-allocated buffer",
                    need, (unsigned)MPP41_NOALLOC_SCRATCH_BYTES);
-    if (fused_sync_words(d->tokens, d->hidden) > kSyncWords)
+    const LayerPlan plan = noalloc_plan(d);
+    if (plan.sync_words > kSyncWords)
         return err(MPP41_ERR_UNSUPPORTED_SHAPE, "too many output tiles for the static counters");
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -142,7 +134,7 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
     // Counters and error word must start at zero. The kernel leaves them zero,
     // but a launch that gave up may not have; clearing them is a memset, not an
     // allocation.
-    e = cudaMemsetAsync(P.sync, 0, fused_sync_words(d->tokens, d->hidden) * sizeof(uint32_t), st);
+    e = cudaMemsetAsync(P.sync, 0, plan.sync_words * sizeof(uint32_t), st);
     if (e == cudaSuccess) e = cudaMemsetAsync(P.err, 0, sizeof(uint32_t), st);
     if (e != cudaSuccess) return err(MPP41_ERR_CUDA, "clear counters: %s", cudaGetErrorString(e));
 
@@ -158,9 +150,8 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
     L.sync = P.sync;
     L.err = P.err;
     L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
-    L.splits = noalloc_splits(d);
     const char *why = "";
-    const int rc = launch_mlp_fused(L, st, &why);
+    const int rc = launch_layer(plan, L, st, &why);
     if (rc == 1) return err(MPP41_ERR_UNSUPPORTED_SHAPE, "mpp41_mlp_noalloc: %s", why);
     if (rc == 2) return err(MPP41_ERR_CUDA, "mpp41_mlp_noalloc: %s", why);
     return MPP41_OK;

@@ -96,19 +96,19 @@ struct WqCfg {
 };
 
 // ----------------------------------------------------------------- decode
-// Decode the 32 consecutive weights of one (row, half-stage) chunk into 16
-// fp16x2 words (element 2i in the low half of word i). `raw` points at the
-// chunk's packed bytes in shared memory.
+// Decode 32 consecutive weights, given as their packed bytes in wr (FP4/
+// INT4: wr[0..3]; INT2: wr[0..1]; 8-bit formats: wr[0..7]; little-endian,
+// element 0 in the lowest bits), into 16 fp16x2 words (element 2i in the low
+// half of word i).
 template <int W>
-__device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_byte, uint32_t (&o)[16])
+__device__ __forceinline__ void decode_words(const uint32_t (&wr)[8], uint32_t scale_byte, uint32_t (&o)[16])
 {
     if constexpr (W == W_FP4 || W == W_MXFP4) {
         // hardware E2M1 pair conversion (low nibble -> low half): the exact E2M1
         // values in fp16; then value * 2^(s-127) with one exact fp16 multiply when
         // 2^(s-127) is a normal fp16 (s in [113,142]); otherwise fp32 math and a
         // single rounding, as half(float(lut) * e8m0) in mxfp4_dequant_*_half.
-        const uint4 v = *reinterpret_cast<const uint4 *>(raw);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        const uint32_t *w = wr;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
@@ -138,8 +138,7 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_
             }
         }
     } else if constexpr (W == W_I4) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(raw);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        const uint32_t *w = wr;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const uint32_t lo = w[q] & 0x0F0F0F0Fu, hi = (w[q] >> 4) & 0x0F0F0F0Fu;
@@ -151,8 +150,7 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_
             }
         }
     } else if constexpr (W == W_I2) {
-        const uint2 v = *reinterpret_cast<const uint2 *>(raw);
-        const uint32_t w[2] = {v.x, v.y};
+        const uint32_t *w = wr;
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
 #pragma unroll
@@ -167,8 +165,7 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_
     } else if constexpr (W == W_I8) {
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(raw + 16 * q);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            const uint32_t *w = wr + 4 * q;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint32_t a = __byte_perm(w[i], 0x64646464u, 0x4140) ^ 0x00800080u;
@@ -180,8 +177,7 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_
     } else if constexpr (W == W_E4M3) {
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(raw + 16 * q);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            const uint32_t *w = wr + 4 * q;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
 #pragma unroll
@@ -196,8 +192,7 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_
     } else if constexpr (W == W_E5M2) {
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(raw + 16 * q);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            const uint32_t *w = wr + 4 * q;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 o[8 * q + 2 * i] = __byte_perm(w[i], 0u, 0x1404);      // E5M2 byte == fp16 high byte
@@ -205,6 +200,30 @@ __device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_
             }
         }
     }
+}
+
+
+// Packed bytes per 32 weights of format W.
+template <int W>
+__host__ __device__ constexpr int chunk_bytes() { return 32 * wfmt_bits(W) / 8; }
+
+// Decode the 32 consecutive weights at `raw` (shared memory, 8-byte aligned)
+// into 16 fp16x2 words.
+template <int W>
+__device__ __forceinline__ void decode_chunk(const uint8_t *raw, uint32_t scale_byte, uint32_t (&o)[16])
+{
+    uint32_t w[8];
+    if constexpr (chunk_bytes<W>() == 8) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(raw);
+        w[0] = v.x; w[1] = v.y;
+    } else {
+#pragma unroll
+        for (int q = 0; q < chunk_bytes<W>() / 16; ++q) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(raw + 16 * q);
+            w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+        }
+    }
+    decode_words<W>(w, scale_byte, o);
 }
 
 // ----------------------------------------------------------------- epilogue math
