@@ -14,7 +14,7 @@ namespace tok {
 
 size_t sync_words(uint32_t T, uint32_t H) { return 2 + (size_t)(H / kFBN) * ((T + kBM - 1) / kBM); }
 
-size_t ws_bytes(uint32_t T, uint32_t H, uint32_t splits) { return (size_t)splits * T * H * 4; }
+size_t ws_bytes(uint32_t T, uint32_t H, uint32_t splits) { return (size_t)splits * ((T + kBM - 1) / kBM) * kBM * H * 4; }
 
 // Enough CTAs to cover the SMs; each split keeps >= 256 of K; the fp16 output
 // always reduces through the workspace (at least 2 splits).

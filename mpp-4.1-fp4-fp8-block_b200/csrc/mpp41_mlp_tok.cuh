@@ -538,7 +538,12 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
             } else {
                 // Down tile: store this split's fp32 partial tile (plain stores, no
                 // atomics), count the split, then sum the splits into out.
-                float *part = p.ws + ((size_t)ti.kb * p.T + m) * p.H + ti.c0 + colh * 32;
+                // partial tiles are stored tile-native: per split and output tile,
+                // 16 column blocks of [128 rows][4 columns], so a warp's float4
+                // stores cover 512 contiguous bytes
+                const uint32_t n_mt = (p.T + kBM - 1) / kBM, tile_d = (ti.m0 / kBM) * (p.H / kFBN) + ti.c0 / kFBN;
+                const size_t tile4 = (size_t)kBM * kFBN / 4, split4 = (size_t)n_mt * (p.H / kFBN) * tile4;
+                float4 *part4 = reinterpret_cast<float4 *>(p.ws) + ti.kb * split4 + tile_d * tile4;
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(taddr + colh * 32, v);
                 tmem_ld_wait();
@@ -546,13 +551,11 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[acc]);
-                if (m < p.T) {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        __stcg(reinterpret_cast<float4 *>(part) + i,
-                               make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                           __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
-                }
+                for (int i = 0; i < 8; ++i)
+                    __stcg(part4 + (colh * 8 + i) * kBM + row,
+                           make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                       __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])));
                 if (tr && te == 0) {
                     tr[TR_EPI_D] += (unsigned long long)(clock64() - cepi);
                     tr[TR_D_STORED] = (unsigned long long)(clock64() - clk0);
@@ -561,7 +564,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 __threadfence();
                 asm volatile("bar.sync 1, 256;" ::: "memory");
                 if (tr && te == 0) tr[TR_D_FENCED] = (unsigned long long)(clock64() - clk0);
-                uint32_t *cnt = p.sync + 2 + (ti.m0 / kBM) * (p.H / kFBN) + ti.c0 / kFBN;
+                uint32_t *cnt = p.sync + 2 + tile_d;
                 if (te == 0) {
                     const bool last = atomicAdd(cnt, 1u) == p.splits - 1;
                     if (last) __threadfence();   // the other splits' partials are visible to us
@@ -582,30 +585,29 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     r1 = kBM;
                 }
                 if (tr && te == 0) { tr[TR_D_COUNTED] = (unsigned long long)(clock64() - clk0); tr[TR_D_LAST] = *s_last; }
-                const size_t split_stride = (size_t)p.T * p.H;
-                for (uint32_t i = r0 * (kFBN / 4) + te; i < r1 * (kFBN / 4); i += kEpi) {
-                    const uint32_t mm = ti.m0 + i / (kFBN / 4), c4 = (i % (kFBN / 4)) * 4;
+                const float4 *tile0 = reinterpret_cast<const float4 *>(p.ws) + tile_d * tile4;
+                const uint32_t nr = r1 - r0;
+                for (uint32_t i = te; i < nr * (kFBN / 4); i += kEpi) {
+                    const uint32_t c4 = i / nr, rw = r0 + i % nr, mm = ti.m0 + rw;
                     if (mm >= p.T) continue;
-                    const float *src = p.ws + (size_t)mm * p.H + ti.c0 + c4;
                     float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
                     for (uint32_t j0 = 0; j0 < p.splits; j0 += 8) {
                         // all eight loads in flight before the first add
                         float4 q[8];
 #pragma unroll
                         for (uint32_t j = 0; j < 8; ++j)
-                            q[j] = (j0 + j < p.splits)
-                                       ? __ldcg(reinterpret_cast<const float4 *>(src + (j0 + j) * split_stride))
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                            q[j] = (j0 + j < p.splits) ? __ldcg(tile0 + (j0 + j) * split4 + c4 * kBM + rw)
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                         for (uint32_t j = 0; j < 8; ++j) {
                             acc4.x += q[j].x; acc4.y += q[j].y; acc4.z += q[j].z; acc4.w += q[j].w;
                         }
                     }
                     if constexpr (OUT_F16) {
-                        *reinterpret_cast<uint2 *>(static_cast<__half *>(p.out) + (size_t)mm * p.H + ti.c0 + c4) =
+                        *reinterpret_cast<uint2 *>(static_cast<__half *>(p.out) + (size_t)mm * p.H + ti.c0 + c4 * 4) =
                             make_uint2(half2_bits(acc4.x, acc4.y), half2_bits(acc4.z, acc4.w));
                     } else {
-                        *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + (size_t)mm * p.H + ti.c0 + c4) = acc4;
+                        *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + (size_t)mm * p.H + ti.c0 + c4 * 4) = acc4;
                     }
                 }
                 if (tr && te == 0) tr[TR_D_CONVERTED] = (unsigned long long)(clock64() - clk0);
