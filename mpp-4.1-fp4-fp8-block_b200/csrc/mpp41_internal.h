@@ -81,7 +81,7 @@ uint32_t fused_splits(uint32_t T, uint32_t H, uint32_t I);
 // launch description, its own workspace layout ([splits][T][H] fp32) and
 // counters.
 namespace tok {
-size_t sync_words(uint32_t T, uint32_t H);
+size_t sync_words(uint32_t T, uint32_t H, uint32_t splits);
 size_t ws_bytes(uint32_t T, uint32_t H, uint32_t splits);
 uint32_t splits(uint32_t T, uint32_t H, uint32_t I, bool out_f16);
 int launch(const FusedLaunch &L, cudaStream_t st, const char **why);

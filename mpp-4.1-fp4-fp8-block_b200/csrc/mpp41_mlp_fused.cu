@@ -67,7 +67,7 @@ LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16)
     if (pl.token_major) {
         pl.splits = tok::splits(T, H, I, out_f16);
         pl.ws_bytes = tok::ws_bytes(T, H, pl.splits);
-        pl.sync_words = tok::sync_words(T, H);
+        pl.sync_words = tok::sync_words(T, H, pl.splits);
     } else {
         pl.splits = fused_splits(T, H, I);
         pl.ws_bytes = fused_ws_bytes(T, H, pl.splits);

@@ -12,7 +12,11 @@
 namespace mpp41 {
 namespace tok {
 
-size_t sync_words(uint32_t T, uint32_t H) { return 2 + (size_t)(H / kFBN) * ((T + kBM - 1) / kBM); }
+size_t sync_words(uint32_t T, uint32_t H, uint32_t splits)
+{
+    const size_t n_mt = (T + kBM - 1) / kBM;
+    return 2 + (size_t)(H / kFBN) * n_mt + splits * n_mt;
+}
 
 size_t ws_bytes(uint32_t T, uint32_t H, uint32_t splits) { return (size_t)splits * ((T + kBM - 1) / kBM) * kBM * H * 4; }
 

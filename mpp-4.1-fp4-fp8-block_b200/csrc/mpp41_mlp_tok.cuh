@@ -219,6 +219,13 @@ __device__ __forceinline__ TileInfo tile_info(const FusedParams &p, uint32_t t)
     return ti;
 }
 
+// Counter of finished G tiles feeding down split kb of token tile mt.
+__device__ __forceinline__ uint32_t *slice_counter(const FusedParams &p, uint32_t mt, uint32_t kb)
+{
+    const uint32_t n_mt = (p.T + kBM - 1) / kBM;
+    return p.sync + 2 + (p.H / kFBN) * n_mt + mt * p.splits + kb;
+}
+
 template <int W, int EG, bool OUT_F16>
 __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_constant__ FusedParams p)
 {
@@ -352,7 +359,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         if (lane == 0) {
             pdl_wait_prior();   // activations and counters may come from the previous kernel
             uint32_t gs = 0;
-            bool waited = false;
+            uint32_t waited_t = ~0u;
             for (uint32_t t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
                 const TileInfo ti = tile_info(p, t);
                 const CUtensorMap *tm = ti.is_g ? &p.tm_x : &p.tm_mid;
@@ -360,15 +367,17 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 bool ok = true;
                 for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
                     if (gs % kAProd != (uint32_t)warp) continue;
-                    if (!ti.is_g && !waited) {
+                    if (!ti.is_g && waited_t != t) {
                         // mid is written by other CTAs' G tiles (generic stores); wait
                         // for all of them, then order those writes before our TMA reads
                         const long long cw = clk_if(tr);
-                        if (!wait_counter(p.sync, p.n_gtiles, abort, p.err, 0x701)) { ok = false; break; }
+                        // only the G tiles that write this split's K range of mid
+                        if (!wait_counter(slice_counter(p, ti.m0 / kBM, ti.kb), p.I / p.splits / 32, abort, p.err,
+                                          0x701)) { ok = false; break; }
                         if (tr) tw1 += (unsigned long long)(clock64() - cw);
                         if (tr && warp == 0) tr[TR_WAIT_END] = globaltimer_ns();
                         fence_proxy_async_global();
-                        waited = true;
+                        waited_t = t;
                     }
                     const uint32_t st = gs % SA, ph = (gs / SA) & 1u;
                     if (!mbar_wait_t(&a_empty[st], ph ^ 1u, abort, p.err, 0x702, tw0, tr != nullptr)) { ok = false; break; }
@@ -528,7 +537,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 asm volatile("bar.sync 1, 256;" ::: "memory");
                 if (te == 0) {
                     __threadfence();
-                    atomicAdd(p.sync, 1u);
+                    atomicAdd(slice_counter(p, ti.m0 / kBM, ti.c0 / (p.I / p.splits)), 1u);
                 }
                 if (tr && te == 0) {
                     tr[TR_G_PUBLISHED] = (unsigned long long)(clock64() - clk0);
@@ -642,7 +651,8 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         if (threadIdx.x == 0) { tr[TR_END] = globaltimer_ns(); tr[TR_CYCLES] = (unsigned long long)(clock64() - clk0); }
     }
     if (threadIdx.x == 0 && atomicAdd(p.sync + 1, 1u) == gridDim.x - 1) {
-        atomicExch(p.sync + 0, 0u);
+        const uint32_t n_mt = (p.T + kBM - 1) / kBM;
+        for (uint32_t i = 0; i < n_mt * p.splits; ++i) atomicExch(slice_counter(p, i / p.splits, i % p.splits), 0u);
         atomicExch(p.sync + 1, 0u);
     }
 }
