@@ -83,6 +83,10 @@ const KernelInfo kKernels[] = {
     {"mpp_mlp_h_fp8e4m3_h_n128", K_GEMM, W_E4M3, EPI_STORE_F16, 0},
     {"mpp_mlp_h_fp8e5m2_f_n128", K_GEMM, W_E5M2, EPI_STORE_F32, 0},
     {"mpp_mlp_h_i2_f_n128", K_GEMM, W_I2, EPI_STORE_F32, 0},
+    // int8 activations, exact int32 accumulate (MPPMLPKernels.metal:61, 140, 152)
+    {"mpp_mlp_i8_i8_i32_n128", K_GEMM, W_I8, 0, 1},
+    {"mpp_mlp_i8_i4_i32_n128", K_GEMM, W_I4, 0, 1},
+    {"mpp_mlp_i8_i2_i32_n128", K_GEMM, W_I2, 0, 1},
     // MXFP4Kernels.metal:108-296, 361-383: one B200 kernel serves every
     // strategy the reference compares (the math is identical)
     {"mxfp4_fused_h_f_n128", K_GEMM, W_MXFP4, EPI_STORE_F32, 0},
@@ -216,11 +220,72 @@ int gate_up_epi(int epilogue)
                                          : (epilogue == MPP41_SWIGLU_FP32 ? EPI_SWIGLU_PLAIN : EPI_SWIGLU_HALF_H);
 }
 
+// Split-K factor of the int8 GEMM: enough 128x128 tiles to cover the SMs, each
+// split keeping >= 256 of K.
+uint32_t i8_splits(uint32_t m, uint32_t n, uint32_t k)
+{
+    const uint32_t tiles = ((n + 127) / 128) * ((m + 127) / 128);
+    uint32_t s = 1;
+    while (tiles * s * 2 <= 160 && k % (128 * s * 2) == 0 && k / (s * 2) >= 256) s *= 2;
+    return s;
+}
+
+// C int32 [m][n] = A int8 [m][k] x W[n][k] on `st` (clears C first when split).
+mpp41_status enqueue_i8_gemm(mpp41_ctx *ctx, int wfmt, const void *a, const void *w, void *c, uint32_t m,
+                             uint32_t n, uint32_t k, cudaStream_t st, const char *what)
+{
+    I8Launch L{};
+    L.wfmt = wfmt;
+    L.a = a; L.b0 = w; L.out = c;
+    L.M = m; L.N = n; L.K = k; L.ldc = n;
+    L.err = ctx->err;
+    L.splits = i8_splits(m, n, k);
+    L.epi = L.splits > 1 ? 1 : 0;
+    if (L.splits > 1) CK(cudaMemsetAsync(c, 0, (size_t)m * n * 4, st), "zero output");
+    const char *why = "";
+    const int rc = launch_i8_gemm(L, st, &why);
+    if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "%s: %s", what, why);
+    return MPP41_OK;
+}
+
+// int8-activation rows (W8A8 / W4A8 / W2A8): the gate/up pair GEMM ends in
+// mpp_mlp_swiglu_i8 (int8 mid in scratch), the down GEMM writes int32.
+bool is_i8_row(const mpp41_mlp_desc *d) { return d->afmt == MPP41_A_S8; }
+
+mpp41_status check_i8_row(const mpp41_mlp_desc *d)
+{
+    if (d->epilogue != MPP41_SWIGLU_I8 || d->out_dtype != MPP41_S32)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "int8-activation rows use the swiglu_i8 epilogue and int32 output");
+    if (d->wfmt != MPP41_W_I8 && d->wfmt != MPP41_W_I4 && d->wfmt != MPP41_W_I2)
+        return fail(MPP41_ERR_MISSING_KERNEL, "int8-activation rows take INT8, INT4 or INT2 weights");
+    return MPP41_OK;
+}
+
+mpp41_status enqueue_i8_gate_up(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,
+                                const void *wu, void *scratch, cudaStream_t st)
+{
+    I8Launch L{};
+    L.wfmt = d->wfmt;
+    L.epi = 2;
+    L.a = x; L.b0 = wg; L.b1 = wu; L.out = scratch;
+    L.M = d->tokens; L.N = d->intermediate; L.K = d->hidden; L.ldc = d->intermediate;
+    L.splits = 1;
+    L.err = ctx->err;
+    const char *why = "";
+    const int rc = launch_i8_gemm(L, st, &why);
+    if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "int8 gate/up GEMM: %s", why);
+    return MPP41_OK;
+}
+
 // Stage 1: mid = swiglu(x Wg^T, x Wu^T) into scratch; clears the split-K
 // accumulation target of stage 2 (out for fp32, the workspace for fp16).
 mpp41_status enqueue_gate_up(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg, const void *wu,
                              const uint8_t *sg, const uint8_t *su, void *scratch, void *out, cudaStream_t st)
 {
+    if (is_i8_row(d)) {
+        mpp41_status s = check_i8_row(d);
+        return s ? s : enqueue_i8_gate_up(ctx, d, x, wg, wu, scratch, st);
+    }
     mpp41_status s = check_fp16_row(d);
     if (s) return s;
     if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su))
@@ -252,6 +317,11 @@ mpp41_status enqueue_gate_up(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void
 mpp41_status enqueue_down(mpp41_ctx *ctx, const mpp41_mlp_desc *d, void *scratch, const void *wd, const uint8_t *sd,
                           void *out, bool prepared, cudaStream_t st)
 {
+    if (is_i8_row(d)) {
+        mpp41_status s = check_i8_row(d);
+        return s ? s : enqueue_i8_gemm(ctx, d->wfmt, scratch, wd, out, d->tokens, d->hidden, d->intermediate, st,
+                                       "int8 down GEMM");
+    }
     mpp41_status s = check_fp16_row(d);
     if (s) return s;
     if (d->wfmt == MPP41_W_MXFP4 && !sd) return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs down scales");
@@ -287,6 +357,13 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
                          const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *scratch,
                          void *out, cudaStream_t st)
 {
+    if (is_i8_row(d)) {
+        mpp41_status s = check_i8_row(d);
+        if (!s) s = enqueue_i8_gate_up(ctx, d, x, wg, wu, scratch, st);
+        if (!s) s = enqueue_i8_gemm(ctx, d->wfmt, scratch, wd, out, d->tokens, d->hidden, d->intermediate, st,
+                                    "int8 down GEMM");
+        return s;
+    }
     mpp41_status s = check_fp16_row(d);
     if (s) return s;
     if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su || !sd))
@@ -532,6 +609,7 @@ mpp41_status mpp41_gemm(mpp41_ctx *ctx, const char *name, const void *a, const v
     if (!a || !b || !c) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
     if (ki->arg0 == W_MXFP4 && !scales) return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 kernel needs scales");
     if (!m || !n || !k) return MPP41_OK;
+    if (ki->afmt == 1) return enqueue_i8_gemm(ctx, ki->arg0, a, b, c, m, n, k, ctx->stream, name);
     if (k % 64 || n % 64) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "n and k must be multiples of 64");
     WqLaunch L{};
     L.wfmt = ki->arg0;

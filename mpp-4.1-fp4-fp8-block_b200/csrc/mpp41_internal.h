@@ -11,6 +11,12 @@ namespace mpp41 {
 // Weight formats; values match enum mpp41_wfmt of include/mpp41.h.
 enum WFmt : int { W_F16 = 0, W_I8 = 1, W_I4 = 2, W_I2 = 3, W_FP4 = 4, W_E4M3 = 5, W_E5M2 = 6, W_MXFP4 = 7 };
 
+// Bits per packed weight.
+__host__ __device__ constexpr int wfmt_bits(int w)
+{
+    return (w == W_F16) ? 16 : (w == W_I4 || w == W_FP4 || w == W_MXFP4) ? 4 : (w == W_I2) ? 2 : 8;
+}
+
 cudaError_t launch_pack(int fmt, const float *in, size_t n, uint8_t *out, cudaStream_t st);
 cudaError_t launch_unpack(int fmt, const uint8_t *in, size_t n, float *out, cudaStream_t st);
 cudaError_t launch_roundtrip(int fmt, const float *in, uint8_t *packed, float *out, cudaStream_t st);
@@ -41,6 +47,19 @@ struct WqLaunch {
     float *ws;              // split-K fp16 output: fp32 workspace [M][ldc] (clear)
     uint32_t *tile_count;   // split-K fp16 output: per-tile arrival counters (clear)
 };
+
+// Integer tensor-core GEMM (mpp41_i8_gemm.cuh): A int8 [M][K] x B (INT8/INT4/
+// INT2 [N][K]) -> int32 [M][ldc] (epi 0 store, 1 split-K atomic add into a
+// cleared C), or epi 2: gate (b0) / up (b1) pair through mpp_mlp_swiglu_i8 to
+// an int8 mid [M][ldc].
+struct I8Launch {
+    int wfmt, epi;
+    const void *a, *b0, *b1;
+    void *out;
+    uint32_t M, N, K, ldc, splits;
+    uint32_t *err;
+};
+int launch_i8_gemm(const I8Launch &L, cudaStream_t st, const char **why);
 
 bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols, uint64_t rows,
               uint32_t bc, uint32_t br, CUtensorMapSwizzle sw);

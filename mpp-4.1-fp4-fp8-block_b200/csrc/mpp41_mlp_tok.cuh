@@ -276,7 +276,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
             mbar_init(&ck_empty[s], kDecWarps);
         }
         for (uint32_t s = 0; s < SA; ++s) {
-            mbar_init(&a_full[s], 1 + kDecWarps / 2);
+            mbar_init(&a_full[s], 1 + kDecWarps);
             mbar_init(&a_empty[s], 1);
         }
         for (int s = 0; s < 2; ++s) {
@@ -436,9 +436,8 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         const uint32_t quarter = warp & 3;             // TMEM lanes 32*quarter..+31
         const uint32_t colh = (warp - kDec0) >> 2;     // column half of the tile
         const uint32_t row = quarter * 32 + lane;
-        // decode: two groups of 4 warps take alternate stages; 32 weights per thread
-        const uint32_t grp = (warp - kDec0) >> 2;
-        const uint32_t tg = te & 127u, dr = tg >> 1, dh = tg & 1u;   // B row, half of the 64-wide stage
+        // decode: all 8 warps share every stage; 32 weights per thread
+        const uint32_t dr = te >> 2, dq = te & 3u;   // B row, K quarter of the 128-wide stage
         uint32_t gs = 0, gc = 0, ti_n = 0;
         for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti_n) {
             const TileInfo ti = tile_info(p, t);
@@ -450,13 +449,12 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
             uint32_t cst = 0;
             for (uint32_t s = 0; s < ti.nk && !*abort; ++s, ++gs) {
                 const uint32_t sc = s % SPC;
-                const bool mine = (gs & 1u) == grp;
                 if (sc == 0) {
                     cst = gc % kChunks;
                     if (!mbar_wait_t(&ck_full[cst], (gc / kChunks) & 1u, abort, p.err, 0x902, tw0, tr != nullptr)) break;
                     if (tr && te == 0 && gc == 0) tr[TR_DEC_FIRST_RAW] = (unsigned long long)(clock64() - clk0);
                 }
-                if (mine) {
+                {
                     const uint32_t st = gs % kStagesB;
                     if (gs >= kStagesB) {   // stage gs-2 (same weight slot) consumed by the MMA
                         const uint32_t g3 = gs - kStagesB;
@@ -464,22 +462,17 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     }
                     const long long cdec = clk_if(tr);
                     const uint8_t *raw = sRaw + cst * Cfg::kChunkBytes + dr * kChunkRow + sc * Cfg::kRawRow;
-                    // this thread: row dr, K half dh (= swizzle atom dh: 64 weights, two
-                    // 32-wide scale blocks)
-                    uint8_t *rowp = sB + st * Cfg::kBBytes + dh * Cfg::kBAtom + dr * 128;
+                    // this thread: row dr, K quarter dq = half (dq & 1) of swizzle atom dq >> 1
+                    uint8_t *rowp = sB + st * Cfg::kBBytes + (dq >> 1) * Cfg::kBAtom + dr * 128;
+                    uint32_t sb = 127u;
+                    // G: rows 0..31 gate scales, 32..63 up scales, each kbc_g wide
+                    if constexpr (W == W_MXFP4) sb = scl[dr * kbc + 4 * s + dq];
+                    uint32_t o[16];
+                    decode_chunk<W>(raw + dq * (Cfg::kRawRow / 4), sb, o);
 #pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        uint32_t sb = 127u;
-                        // G: rows 0..31 gate scales, 32..63 up scales, each kbc_g wide
-                        if constexpr (W == W_MXFP4) sb = scl[dr * kbc + 4 * s + 2 * dh + half];
-                        uint32_t o[16];
-                        decode_chunk<W>(raw + (2 * dh + half) * (Cfg::kRawRow / 4), sb, o);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const uint32_t phys = ((half * 4 + q) ^ (dr & 7u)) * 16u;
-                            *reinterpret_cast<uint4 *>(rowp + phys) =
-                                make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-                        }
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t phys = (((dq & 1u) * 4 + q) ^ (dr & 7u)) * 16u;
+                        *reinterpret_cast<uint4 *>(rowp + phys) = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
                     }
                     fence_proxy_async_smem();
                     __syncwarp();

@@ -45,11 +45,6 @@ enum Epi : int {
     EPI_SPLITK_F16 = 7,      // split-K: fp32 partials into a workspace, last CTA of a tile writes fp16
 };
 
-__host__ __device__ constexpr int wfmt_bits(int w)
-{
-    return (w == W_F16) ? 16 : (w == W_I4 || w == W_FP4 || w == W_MXFP4) ? 4 : (w == W_I2) ? 2 : 8;
-}
-
 constexpr int kBM = 128;        // tokens per tile (MMA M)
 constexpr int kBK = 64;         // K per stage: one 128-byte swizzle atom of fp16
 constexpr int kStages = 6;
