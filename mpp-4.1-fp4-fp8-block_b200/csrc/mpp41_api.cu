@@ -87,6 +87,9 @@ const KernelInfo kKernels[] = {
     {"mpp_mlp_i8_i8_i32_n128", K_GEMM, W_I8, 0, 1},
     {"mpp_mlp_i8_i4_i32_n128", K_GEMM, W_I4, 0, 1},
     {"mpp_mlp_i8_i2_i32_n128", K_GEMM, W_I2, 0, 1},
+    // fp32 activations (the swiglu_float mid) x half / INT8 weights (MPPMLPKernels.metal:164, 175)
+    {"mpp_mlp_f_h_f_n128", K_GEMM, W_F16, EPI_STORE_F32, 2},
+    {"mpp_mlp_f_i8_f_n128", K_GEMM, W_I8, EPI_STORE_F32, 2},
     // MXFP4Kernels.metal:108-296, 361-383: one B200 kernel serves every
     // strategy the reference compares (the math is identical)
     {"mxfp4_fused_h_f_n128", K_GEMM, W_MXFP4, EPI_STORE_F32, 0},
@@ -205,8 +208,11 @@ mpp41_status check_fp16_row(const mpp41_mlp_desc *d)
 {
     if (d->afmt != MPP41_A_F16)
         return fail(MPP41_ERR_MISSING_KERNEL, "int8-activation MLP rows are not available in this build");
-    if (d->epilogue == MPP41_SWIGLU_FLOAT || d->epilogue == MPP41_SWIGLU_I8)
-        return fail(MPP41_ERR_MISSING_KERNEL, "fp32-mid down projection (f_*_f) is not available in this build");
+    if (d->epilogue == MPP41_SWIGLU_I8)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "swiglu_i8 needs int8 activations");
+    if (d->epilogue == MPP41_SWIGLU_FLOAT && ((d->wfmt != MPP41_W_F16 && d->wfmt != MPP41_W_I8) || d->out_dtype != MPP41_F32))
+        return fail(MPP41_ERR_MISSING_KERNEL,
+                    "the fp32-mid rows (swiglu_float, then mpp_mlp_f_*_f) take half or INT8 weights and fp32 output");
     if (d->epilogue < 0 || d->epilogue > MPP41_SWIGLU_FP32)
         return fail(MPP41_ERR_INVALID_ARGUMENT, "bad epilogue %d", d->epilogue);
     if (d->out_dtype != MPP41_F32 && d->out_dtype != MPP41_F16)
@@ -216,8 +222,12 @@ mpp41_status check_fp16_row(const mpp41_mlp_desc *d)
 
 int gate_up_epi(int epilogue)
 {
-    return epilogue == MPP41_SWIGLU_HALF ? EPI_SWIGLU_HALF
-                                         : (epilogue == MPP41_SWIGLU_FP32 ? EPI_SWIGLU_PLAIN : EPI_SWIGLU_HALF_H);
+    switch (epilogue) {
+    case MPP41_SWIGLU_HALF: return EPI_SWIGLU_HALF;
+    case MPP41_SWIGLU_FP32: return EPI_SWIGLU_PLAIN;
+    case MPP41_SWIGLU_FLOAT: return EPI_SWIGLU_FLOAT;
+    default: return EPI_SWIGLU_HALF_H;
+    }
 }
 
 // Split-K factor of the int8 GEMM: enough 128x128 tiles to cover the SMs, each
@@ -244,6 +254,26 @@ mpp41_status enqueue_i8_gemm(mpp41_ctx *ctx, int wfmt, const void *a, const void
     if (L.splits > 1) CK(cudaMemsetAsync(c, 0, (size_t)m * n * 4, st), "zero output");
     const char *why = "";
     const int rc = launch_i8_gemm(L, st, &why);
+    if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "%s: %s", what, why);
+    return MPP41_OK;
+}
+
+// C fp32 [m][n] = A fp32 [m][k] x W[n][k] (half or INT8) on `st`; clears C
+// first when split.
+mpp41_status enqueue_f32_gemm(mpp41_ctx *ctx, int wfmt, const void *a, const void *w, void *c, uint32_t m,
+                              uint32_t n, uint32_t k, cudaStream_t st, const char *what)
+{
+    F32Launch L{};
+    L.wfmt = wfmt;
+    L.a = static_cast<const float *>(a); L.b = w; L.out = static_cast<float *>(c);
+    L.M = m; L.N = n; L.K = k; L.ldc = n;
+    L.err = ctx->err;
+    const uint32_t tiles = ((n + 127) / 128) * ((m + 127) / 128);
+    L.splits = 1;
+    while (tiles * L.splits * 2 <= 160 && k % (32 * L.splits * 2) == 0 && k / (L.splits * 2) >= 256) L.splits *= 2;
+    if (L.splits > 1) CK(cudaMemsetAsync(c, 0, (size_t)m * n * 4, st), "zero output");
+    const char *why = "";
+    const int rc = launch_f32_gemm(L, st, &why);
     if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "%s: %s", what, why);
     return MPP41_OK;
 }
@@ -298,7 +328,7 @@ mpp41_status enqueue_gate_up(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void
     g.out = scratch;
     g.M = d->tokens; g.N = d->intermediate; g.K = d->hidden; g.ldc = d->intermediate;
     g.err = ctx->err;
-    if (down_splits(d) > 1) {
+    if (down_splits(d) > 1 && d->epilogue != MPP41_SWIGLU_FLOAT) {   // the fp32-mid down GEMM clears its own output
         if (d->out_dtype == MPP41_F32 && out) {
             g.zero = out;
             g.zero_bytes = (size_t)d->tokens * d->hidden * 4;
@@ -324,6 +354,9 @@ mpp41_status enqueue_down(mpp41_ctx *ctx, const mpp41_mlp_desc *d, void *scratch
     }
     mpp41_status s = check_fp16_row(d);
     if (s) return s;
+    if (d->epilogue == MPP41_SWIGLU_FLOAT)   // fp32 mid: mpp_mlp_f_h_f_n128 / mpp_mlp_f_i8_f_n128
+        return enqueue_f32_gemm(ctx, d->wfmt, scratch, wd, out, d->tokens, d->hidden, d->intermediate, st,
+                                "fp32-mid down GEMM");
     if (d->wfmt == MPP41_W_MXFP4 && !sd) return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs down scales");
     const ScratchLayout SL = scratch_layout(d);
     WqLaunch dn{};
@@ -368,7 +401,7 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
     if (s) return s;
     if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su || !sd))
         return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate, up and down scales");
-    if (!(d->flags & MPP41_MLP_UNFUSED) && d->wfmt != MPP41_W_F16 &&
+    if (!(d->flags & MPP41_MLP_UNFUSED) && d->wfmt != MPP41_W_F16 && d->epilogue != MPP41_SWIGLU_FLOAT &&
         desc_plan(d).sync_words <= ctx->sync_words) {
         const ScratchLayout SL = scratch_layout(d);
         FusedLaunch L{};
@@ -610,6 +643,7 @@ mpp41_status mpp41_gemm(mpp41_ctx *ctx, const char *name, const void *a, const v
     if (ki->arg0 == W_MXFP4 && !scales) return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 kernel needs scales");
     if (!m || !n || !k) return MPP41_OK;
     if (ki->afmt == 1) return enqueue_i8_gemm(ctx, ki->arg0, a, b, c, m, n, k, ctx->stream, name);
+    if (ki->afmt == 2) return enqueue_f32_gemm(ctx, ki->arg0, a, b, c, m, n, k, ctx->stream, name);
     if (k % 64 || n % 64) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "n and k must be multiples of 64");
     WqLaunch L{};
     L.wfmt = ki->arg0;

@@ -61,6 +61,18 @@ struct I8Launch {
 };
 int launch_i8_gemm(const I8Launch &L, cudaStream_t st, const char **why);
 
+// fp32-activation GEMM (mpp41_f32_gemm.cuh): A fp32 [M][K] x B (half or INT8
+// [N][K]) -> fp32 [M][ldc]; splits > 1 adds into a cleared C.
+struct F32Launch {
+    int wfmt;
+    const float *a;
+    const void *b;
+    float *out;
+    uint32_t M, N, K, ldc, splits;
+    uint32_t *err;
+};
+int launch_f32_gemm(const F32Launch &L, cudaStream_t st, const char **why);
+
 bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols, uint64_t rows,
               uint32_t bc, uint32_t br, CUtensorMapSwizzle sw);
 // fp16 [rows][cols] viewed as [cols/64][rows][64]: one copy of box {64, br, nblk}

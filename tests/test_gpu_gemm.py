@@ -103,3 +103,18 @@ def test_unsupported_shape_is_reported(ctx):
     with pytest.raises(mpp41.MPP41Error) as e:
         ctx.gemm("mxfp4_probe_noscale_h_f_n64", d, d, d, 64, 128, 512)
     assert e.value.status == mpp41.ERR_MISSING_KERNEL
+
+
+@pytest.mark.parametrize("kernel,wfmt", [("mpp_mlp_f_h_f_n128", O.W_F16), ("mpp_mlp_f_i8_f_n128", O.W_I8)])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 512), (64, 128, 4096), (200, 192, 256)])
+def test_fp32_activation_rows(ctx, kernel, wfmt, m, n, k):
+    """fp32 A (the swiglu_float mid) on kind::tf32 with A split into a tf32 head
+    and its fp32 remainder: ~2^-21 relative per product, checked at 1e-5."""
+    a = (np.random.default_rng(m + n).standard_normal((m, k)) * 0.5).astype(np.float32)
+    w, _ = weights(wfmt, n, k, 0x7777 + k)
+    d_c = empty_dev(m * n * 4)
+    ctx.gemm(kernel, to_dev(a), to_dev(w), d_c, m, n, k, None)
+    ctx.synchronize()
+    got = from_dev(d_c, np.float32, (m, n))
+    ref = a.astype(np.float64) @ O.decode_weights(wfmt, w, None, n, k).T
+    assert rel_fro(got, ref) <= 1e-5, kernel

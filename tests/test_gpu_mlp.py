@@ -66,6 +66,7 @@ def test_mxfp4_reference_checksum_403573(ctx, golden):
 @pytest.mark.parametrize("gate_kernel", [
     "mxfp4_native_sp_h_f_n64", "mpp_mlp_h_i4_f_n128", "mpp_mlp_h_fp4_f_n128", "mpp_mlp_h_i2_f_n128",
     "mpp_mlp_h_fp8e4m3_f_n128", "mpp_mlp_h_fp8e5m2_f_n128", "mpp_mlp_h_fp8e4m3_h_n128",
+    "mpp_mlp_h_h_f_n128", "mpp_mlp_h_i8_f_n128",
 ])
 @pytest.mark.parametrize("T,H,I", [(128, 1024, 4096), (64, 256, 512), (1, 512, 1024), (200, 256, 768)])
 def test_mlp_rows(ctx, gate_kernel, T, H, I):
@@ -73,9 +74,13 @@ def test_mlp_rows(ctx, gate_kernel, T, H, I):
     fin = np.isfinite(ref)
     assert np.array_equal(np.isfinite(got), fin)
     assert rel_fro(got[fin], ref[fin]) <= TOL, gate_kernel
-    # the fused SwiGLU mid: identical except for rare one-ulp exp differences
-    diff = mid.astype(np.float64) != mid_ref.astype(np.float64)
-    assert diff.mean() < 1e-3
+    if mid_ref.dtype == np.float32:
+        # swiglu_float mid (then the fp32-activation down GEMM): expf vs exp(double)
+        assert rel_fro(mid, mid_ref) <= 1e-6
+    else:
+        # the fused SwiGLU mid: identical except for rare one-ulp exp differences
+        diff = mid.astype(np.float64) != mid_ref.astype(np.float64)
+        assert diff.mean() < 1e-3
 
 
 def test_mxfp4_wide_scales(ctx):
