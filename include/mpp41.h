@@ -174,6 +174,18 @@ mpp41_status mpp41_swiglu(mpp41_ctx *ctx, const char *kernel_name, const void *g
  *      scalar MLP (encodeMLP main.swift:2575-2634). ---- */
 mpp41_status mpp41_matmul_scalar(mpp41_ctx *ctx, const char *kernel_name, const void *a, const void *b, void *c,
                                  const mpp41_matmul_config *cfg);
+/* Tensor-core formulation of the same big-matmul rows (kernel names of
+ * mpp41_matmul_scalar, 2048^3 in BASELINE config 1): fp32 / int32 accumulation
+ * in tensor memory and one final rounding for half outputs.
+ * fp4_e2m1_matmul[_g8] (FP4 x FP4 -> fp32) and int4_int8_matmul (INT4 x INT4 ->
+ * int32) are exact, hence equal to the reference; the half-output rows are the
+ * exactly rounded sum, not the reference's serial-half-accumulate result.
+ * `workspace` (mpp41_matmul_workspace_bytes) holds A widened to the MMA's
+ * operand type for the rows whose A is FP4, INT4 or int8 (NULL when 0). */
+size_t mpp41_matmul_workspace_bytes(const char *kernel_name, const mpp41_matmul_config *cfg);
+mpp41_status mpp41_matmul(mpp41_ctx *ctx, const char *kernel_name, const void *a, const void *b, void *c,
+                          const mpp41_matmul_config *cfg, void *workspace);
+
 mpp41_status mpp41_mlp_scalar(mpp41_ctx *ctx, const char *gate_kernel_name, const char *down_kernel_name,
                               const void *x, const void *wg, const void *wu, void *mid, const void *wd, void *out,
                               const mpp41_mlp_config *cfg);

@@ -665,6 +665,50 @@ mpp41_status mpp41_gemm(mpp41_ctx *ctx, const char *name, const void *a, const v
     return MPP41_OK;
 }
 
+size_t mpp41_matmul_workspace_bytes(const char *name, const mpp41_matmul_config *cfg)
+{
+    const KernelInfo *k = find_kernel(name);
+    if (!k || k->kind != K_SCALAR_MM || !cfg) return 0;
+    const size_t mk = (size_t)cfg->rows * cfg->depth;
+    switch (k->arg0) {
+    case 0: case 3: return 2 * mk;   // A widened to fp16
+    case 4: return mk;               // A widened to int8
+    default: return 0;
+    }
+}
+
+mpp41_status mpp41_matmul(mpp41_ctx *ctx, const char *name, const void *a, const void *b, void *c,
+                          const mpp41_matmul_config *cfg, void *workspace)
+{
+    NEED(ctx);
+    const KernelInfo *k = find_kernel(name);
+    if (!k || k->kind != K_SCALAR_MM) return missing(name);
+    if (!cfg || !a || !b || !c) return fail(MPP41_ERR_INVALID_ARGUMENT, "null argument");
+    const uint32_t m = cfg->rows, n = cfg->columns, kk = cfg->depth;
+    if (!m || !n || !kk) return MPP41_OK;
+    if (kk % 128 || n % 64) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "depth must be a multiple of 128, columns of 64");
+    const size_t ws = mpp41_matmul_workspace_bytes(name, cfg);
+    if (ws && !workspace) return fail(MPP41_ERR_INVALID_ARGUMENT, "%s needs a %zu-byte workspace", name, ws);
+    cudaStream_t st = ctx->stream;
+    const int kind = k->arg0;
+    if (kind == 0 || kind == 3) CK(launch_widen(kind == 0 ? 0 : 1, a, (size_t)m * kk, workspace, st), "widen A");
+    if (kind == 4) {
+        CK(launch_widen(2, a, (size_t)m * kk, workspace, st), "widen A");
+        return enqueue_i8_gemm(ctx, W_I4, workspace, b, c, m, n, kk, st, name);
+    }
+    WqLaunch L{};
+    L.a = (kind == 0 || kind == 3) ? workspace : a;
+    L.b0 = b; L.out = c;
+    L.M = m; L.N = n; L.K = kk; L.ldc = n;
+    L.err = ctx->err;
+    L.wfmt = kind == 0 ? W_FP4 : kind == 1 ? W_FP4 : kind == 2 ? W_I4 : W_F16;
+    L.epi = kind == 0 ? EPI_STORE_F32 : EPI_STORE_F16;
+    const char *why = "";
+    const int rc = launch_wq_gemm(L, st, &why);
+    if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "%s: %s", name, why);
+    return MPP41_OK;
+}
+
 mpp41_status mpp41_swiglu(mpp41_ctx *ctx, const char *name, const void *gate, const void *up, void *mid,
                           const mpp41_mlp_config *cfg)
 {

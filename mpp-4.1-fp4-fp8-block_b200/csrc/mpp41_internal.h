@@ -19,6 +19,9 @@ __host__ __device__ constexpr int wfmt_bits(int w)
 
 cudaError_t launch_pack(int fmt, const float *in, size_t n, uint8_t *out, cudaStream_t st);
 cudaError_t launch_unpack(int fmt, const uint8_t *in, size_t n, float *out, cudaStream_t st);
+// Exact operand widening (n elements, n % 8 == 0): kind 0 E2M1 -> fp16,
+// 1 int8 -> fp16, 2 INT4 -> int8.
+cudaError_t launch_widen(int kind, const void *in, size_t n, void *out, cudaStream_t st);
 cudaError_t launch_roundtrip(int fmt, const float *in, uint8_t *packed, float *out, cudaStream_t st);
 cudaError_t launch_dequant(int lut, const uint8_t *packed, const uint8_t *scales, void *out, uint32_t rows,
                            uint32_t depth, cudaStream_t st);

@@ -419,6 +419,52 @@ cudaError_t launch_scalar_mlp(int wfmt, uint32_t T, uint32_t H, uint32_t I, cons
     return cudaGetLastError();
 }
 
+// Operand widening for the tensor-core big-matmul rows (HBM-bound, 8 elements
+// per thread): kind 0 E2M1 (low nibble first) -> fp16, 1 int8 -> fp16,
+// 2 INT4 ((n ^ 8) - 8, low nibble first) -> int8. All conversions are exact.
+__global__ void widen_kernel(int kind, const uint8_t *__restrict__ in, size_t n8, void *__restrict__ out)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+        if (kind == 0) {
+            const uint32_t w = reinterpret_cast<const uint32_t *>(in)[i];
+            uint32_t o[4];
+            asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+                "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+                "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+                : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+                : "r"(w));
+            reinterpret_cast<uint4 *>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        } else if (kind == 1) {
+            const uint2 w = reinterpret_cast<const uint2 *>(in)[i];
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t word = j < 2 ? w.x : w.y, sh = 16 * (j & 1);
+                const __half2 h = __floats2half2_rn((float)(int8_t)(word >> sh), (float)(int8_t)(word >> (sh + 8)));
+                o[j] = *reinterpret_cast<const uint32_t *>(&h);
+            }
+            reinterpret_cast<uint4 *>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        } else {
+            const uint32_t w = reinterpret_cast<const uint32_t *>(in)[i];
+            const uint32_t lo = __vsub4((w & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+            const uint32_t hi = __vsub4(((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+            reinterpret_cast<uint2 *>(out)[i] = make_uint2(__byte_perm(lo, hi, 0x5140), __byte_perm(lo, hi, 0x7362));
+        }
+    }
+}
+
+cudaError_t launch_widen(int kind, const void *in, size_t n, void *out, cudaStream_t st)
+{
+    const size_t n8 = n / 8;
+    if (!n8) return cudaSuccess;
+    const uint32_t blocks = (uint32_t)((n8 + 255) / 256 < 148u * 16u ? (n8 + 255) / 256 : 148u * 16u);
+    widen_kernel<<<blocks, 256, 0, st>>>(kind, static_cast<const uint8_t *>(in), n8, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_scalar_matmul(int kind, uint32_t M, uint32_t N, uint32_t K, const void *a, const void *b, void *c,
                                  cudaStream_t st)
 {

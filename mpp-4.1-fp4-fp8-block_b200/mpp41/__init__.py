@@ -95,6 +95,8 @@ def lib() -> C.CDLL:
         "mpp41_gemm": ([vp, C.c_char_p, vp, vp, vp, u32, u32, u32, vp], st),
         "mpp41_swiglu": ([vp, C.c_char_p, vp, vp, vp, C.POINTER(MLPConfig)], st),
         "mpp41_matmul_scalar": ([vp, C.c_char_p, vp, vp, vp, C.POINTER(MatmulConfig)], st),
+        "mpp41_matmul_workspace_bytes": ([C.c_char_p, C.POINTER(MatmulConfig)], sz),
+        "mpp41_matmul": ([vp, C.c_char_p, vp, vp, vp, C.POINTER(MatmulConfig), vp], st),
         "mpp41_mlp_scalar": ([vp, C.c_char_p, C.c_char_p, vp, vp, vp, vp, vp, vp, C.POINTER(MLPConfig)], st),
         "mpp41_mlp_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp": ([vp, C.POINTER(MLPDesc)] + [vp] * 9, st),
@@ -225,6 +227,16 @@ class Context:
 
     def gemm(self, kernel: str, a, b, c, m: int, n: int, k: int, scales=None):
         _check(lib().mpp41_gemm(self.h, kernel.encode(), _ptr(a), _ptr(b), _ptr(c), m, n, k, _ptr(scales)))
+
+    @staticmethod
+    def matmul_workspace_bytes(kernel: str, rows: int, columns: int, depth: int) -> int:
+        cfg = MatmulConfig(rows, columns, depth, 0)
+        return lib().mpp41_matmul_workspace_bytes(kernel.encode(), C.byref(cfg))
+
+    def matmul(self, kernel: str, a, b, c, rows: int, columns: int, depth: int, workspace=None):
+        """Tensor-core big-matmul row (mpp41_matmul)."""
+        cfg = MatmulConfig(rows, columns, depth, 0)
+        _check(lib().mpp41_matmul(self.h, kernel.encode(), _ptr(a), _ptr(b), _ptr(c), C.byref(cfg), _ptr(workspace)))
 
     def swiglu(self, kernel: str, gate, up, mid, tokens: int, hidden: int, intermediate: int):
         cfg = MLPConfig(tokens, hidden, intermediate)
