@@ -246,6 +246,27 @@ mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *desc, const void *x, const 
                                const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *out,
                                void *cuda_stream);
 
+/* ---- tensor parallelism (no counterpart in the
+ *      single-GPU reference). Rank r of P holds rows [r*I/P, (r+1)*I/P) of the
+ *      gate and up weights (and their scale rows) and the same columns of the
+ *      down weights, repacked contiguous [H][I/P] (scales [H][I/(32P)]). Each
+ *      rank computes its partial output with the fused layer kernel in fp32,
+ *      then the partials are summed across ranks (NCCL all-reduce on the
+ *      context's stream) into `out` on every rank. NCCL is loaded at run time
+ *      (libnccl.so.2); without it mpp41_comm_init fails with MPP41_ERR_COMM. ---- */
+#define MPP41_COMM_ID_BYTES 128
+/* Rank 0 creates the id and shares it with the other ranks (any channel). */
+mpp41_status mpp41_comm_unique_id(uint8_t id[MPP41_COMM_ID_BYTES]);
+/* Collective over all ranks; binds the communicator to the context's device. */
+mpp41_status mpp41_comm_init(mpp41_ctx *ctx, int nranks, int rank, const uint8_t id[MPP41_COMM_ID_BYTES]);
+void mpp41_comm_destroy(mpp41_ctx *ctx);
+/* Scratch of one rank for the global layer `desc` split over `nranks`. */
+size_t mpp41_mlp_tp_scratch_bytes(const mpp41_mlp_desc *desc, int nranks);
+/* `desc` describes the global layer; weights are this rank's shards. */
+mpp41_status mpp41_mlp_tp(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const void *wg_shard,
+                          const void *wu_shard, const void *wd_shard, const uint8_t *sg_shard,
+                          const uint8_t *su_shard, const uint8_t *sd_shard, void *scratch, void *out);
+
 #ifdef __cplusplus
 }
 #endif

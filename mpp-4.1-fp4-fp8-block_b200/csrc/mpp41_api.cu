@@ -11,16 +11,6 @@
 #include "mpp41_internal.h"
 #include "mpp41_wq_gemm.cuh"
 
-struct mpp41_ctx {
-    int device;
-    cudaStream_t own_stream;
-    cudaStream_t stream;
-    uint32_t *err;          // device error word
-    uint32_t *sync;         // grid-wide counters of the fused layer kernel (kept zero between launches)
-    size_t sync_words;
-    unsigned long long *trace;
-    cudaEvent_t ev0, ev1;
-};
 
 namespace {
 
@@ -490,6 +480,7 @@ void mpp41_destroy(mpp41_ctx *ctx)
     cudaFree(ctx->sync);
     cudaEventDestroy(ctx->ev0);
     cudaEventDestroy(ctx->ev1);
+    mpp41::comm_release(ctx);
     cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }

@@ -6,6 +6,8 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "mpp41.h"
+
 namespace mpp41 {
 
 // Weight formats; values match enum mpp41_wfmt of include/mpp41.h.
@@ -134,4 +136,26 @@ int launch_layer(const LayerPlan &plan, FusedLaunch L, cudaStream_t st, const ch
 // 0 = launched, 1 = this shape/format is not covered by the fused kernel, 2 = CUDA error.
 int launch_mlp_fused(const FusedLaunch &L, cudaStream_t st, const char **why);
 
+// Multi-GPU state of a context (mpp41_tp.cu); NULL until mpp41_comm_init.
+struct CommState;
+mpp41_status set_last_error(mpp41_status s, const char *msg);
+cudaError_t launch_f32_to_f16(const float *in, size_t n, void *out, cudaStream_t st);
+
+}  // namespace mpp41
+
+// The context: device, stream, device error word, fused-kernel counters.
+struct mpp41_ctx {
+    int device;
+    cudaStream_t own_stream;
+    cudaStream_t stream;
+    uint32_t *err;          // device error word
+    uint32_t *sync;         // grid-wide counters of the fused layer kernel (kept zero between launches)
+    size_t sync_words;
+    unsigned long long *trace;
+    cudaEvent_t ev0, ev1;
+    mpp41::CommState *comm = nullptr;
+};
+
+namespace mpp41 {
+void comm_release(mpp41_ctx *ctx);
 }  // namespace mpp41

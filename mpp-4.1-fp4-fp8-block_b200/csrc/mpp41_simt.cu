@@ -465,6 +465,20 @@ cudaError_t launch_widen(int kind, const void *in, size_t n, void *out, cudaStre
     return cudaGetLastError();
 }
 
+__global__ void f32_to_f16_kernel(const float *__restrict__ in, size_t n, __half *__restrict__ out)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __float2half_rn(in[i]);
+}
+
+cudaError_t launch_f32_to_f16(const float *in, size_t n, void *out, cudaStream_t st)
+{
+    if (!n) return cudaSuccess;
+    const uint32_t blocks = (uint32_t)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    f32_to_f16_kernel<<<blocks, 256, 0, st>>>(in, n, static_cast<__half *>(out));
+    return cudaGetLastError();
+}
+
 cudaError_t launch_scalar_matmul(int kind, uint32_t M, uint32_t N, uint32_t K, const void *a, const void *b, void *c,
                                  cudaStream_t st)
 {

@@ -1,0 +1,164 @@
+// Tensor-parallel MLP layer: local fused layer on this rank's slice of the
+// intermediate dimension, fp32 partial output, NCCL all-reduce (sum) over the
+// ranks. NCCL is resolved with dlopen so that the library loads (and its
+// single-GPU entry points work) on hosts without it.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "mpp41_internal.h"
+
+namespace mpp41 {
+
+namespace {
+
+struct NcclApi {
+    void *lib = nullptr;
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+    decltype(&ncclCommDestroy) comm_destroy = nullptr;
+    decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclGetErrorString) error_string = nullptr;
+};
+
+std::mutex g_nccl_mu;
+NcclApi g_nccl;
+
+mpp41_status err(mpp41_status s, const char *fmt, const char *detail)
+{
+    char buf[384];
+    snprintf(buf, sizeof(buf), fmt, detail ? detail : "");
+    return set_last_error(s, buf);
+}
+
+const NcclApi *nccl()
+{
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    if (g_nccl.lib) return &g_nccl;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return nullptr;
+    NcclApi a;
+    a.lib = h;
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.all_reduce || !a.error_string) return nullptr;
+    g_nccl = a;
+    return &g_nccl;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// The layer one rank computes: same shape with the intermediate slice, fp32
+// (or int32) output so the partial sums add exactly before the final rounding.
+mpp41_mlp_desc local_desc(const mpp41_mlp_desc *d, int nranks)
+{
+    mpp41_mlp_desc l = *d;
+    l.intermediate = d->intermediate / (uint32_t)nranks;
+    if (l.out_dtype == MPP41_F16) l.out_dtype = MPP41_F32;
+    return l;
+}
+
+}  // namespace
+
+struct CommState {
+    ncclComm_t comm = nullptr;
+    int nranks = 0, rank = 0;
+};
+
+void comm_release(mpp41_ctx *ctx)
+{
+    if (!ctx || !ctx->comm) return;
+    const NcclApi *a = nccl();
+    if (a && ctx->comm->comm) a->comm_destroy(ctx->comm->comm);
+    delete ctx->comm;
+    ctx->comm = nullptr;
+}
+
+}  // namespace mpp41
+
+using namespace mpp41;
+
+extern "C" {
+
+mpp41_status mpp41_comm_unique_id(uint8_t id[MPP41_COMM_ID_BYTES])
+{
+    if (!id) return err(MPP41_ERR_INVALID_ARGUMENT, "null id%s", nullptr);
+    const NcclApi *a = nccl();
+    if (!a) return err(MPP41_ERR_COMM, "libnccl.so.2 could not be loaded%s", nullptr);
+    ncclUniqueId uid;
+    const ncclResult_t r = a->get_unique_id(&uid);
+    if (r != ncclSuccess) return err(MPP41_ERR_COMM, "ncclGetUniqueId: %s", a->error_string(r));
+    static_assert(sizeof(uid.internal) == MPP41_COMM_ID_BYTES, "NCCL unique id size");
+    memcpy(id, uid.internal, MPP41_COMM_ID_BYTES);
+    return MPP41_OK;
+}
+
+mpp41_status mpp41_comm_init(mpp41_ctx *ctx, int nranks, int rank, const uint8_t id[MPP41_COMM_ID_BYTES])
+{
+    if (!ctx || !id) return err(MPP41_ERR_INVALID_ARGUMENT, "null context or id%s", nullptr);
+    if (nranks < 1 || rank < 0 || rank >= nranks) return err(MPP41_ERR_INVALID_ARGUMENT, "bad rank / nranks%s", nullptr);
+    const NcclApi *a = nccl();
+    if (!a) return err(MPP41_ERR_COMM, "libnccl.so.2 could not be loaded%s", nullptr);
+    comm_release(ctx);
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return err(MPP41_ERR_CUDA, "cudaSetDevice%s", nullptr);
+    ncclUniqueId uid;
+    memcpy(uid.internal, id, MPP41_COMM_ID_BYTES);
+    CommState *cs = new CommState();
+    const ncclResult_t r = a->comm_init_rank(&cs->comm, nranks, uid, rank);
+    if (r != ncclSuccess) {
+        delete cs;
+        return err(MPP41_ERR_COMM, "ncclCommInitRank: %s", a->error_string(r));
+    }
+    cs->nranks = nranks;
+    cs->rank = rank;
+    ctx->comm = cs;
+    return MPP41_OK;
+}
+
+void mpp41_comm_destroy(mpp41_ctx *ctx) { comm_release(ctx); }
+
+size_t mpp41_mlp_tp_scratch_bytes(const mpp41_mlp_desc *d, int nranks)
+{
+    if (!d || nranks < 1 || d->intermediate % (uint32_t)nranks) return 0;
+    const mpp41_mlp_desc l = local_desc(d, nranks);
+    size_t b = align256(mpp41_mlp_scratch_bytes(&l));
+    if (d->out_dtype == MPP41_F16) b += (size_t)d->tokens * d->hidden * 4;   // fp32 partial
+    return b;
+}
+
+mpp41_status mpp41_mlp_tp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,
+                          const void *wu, const void *wd, const uint8_t *sg, const uint8_t *su,
+                          const uint8_t *sd, void *scratch, void *out)
+{
+    if (!ctx || !d) return err(MPP41_ERR_INVALID_ARGUMENT, "null context or descriptor%s", nullptr);
+    if (!ctx->comm) return err(MPP41_ERR_COMM, "mpp41_comm_init has not been called on this context%s", nullptr);
+    const CommState *cs = ctx->comm;
+    if (d->intermediate % (uint32_t)(32 * cs->nranks))
+        return err(MPP41_ERR_UNSUPPORTED_SHAPE, "intermediate must split into 32-aligned slices per rank%s", nullptr);
+    if (d->out_dtype != MPP41_F32 && d->out_dtype != MPP41_F16 && d->out_dtype != MPP41_S32)
+        return err(MPP41_ERR_INVALID_ARGUMENT, "tensor-parallel output must be F32, F16 or S32%s", nullptr);
+    const mpp41_mlp_desc l = local_desc(d, cs->nranks);
+    const size_t local_scratch = align256(mpp41_mlp_scratch_bytes(&l));
+    const size_t n = (size_t)d->tokens * d->hidden;
+    void *partial = d->out_dtype == MPP41_F16 ? static_cast<uint8_t *>(scratch) + local_scratch : out;
+    mpp41_status s = mpp41_mlp(ctx, &l, x, wg, wu, wd, sg, su, sd, scratch, partial);
+    if (s) return s;
+    const NcclApi *a = nccl();
+    const ncclDataType_t dt = d->out_dtype == MPP41_S32 ? ncclInt32 : ncclFloat32;
+    const ncclResult_t r = a->all_reduce(partial, partial, n, dt, ncclSum, cs->comm, ctx->stream);
+    if (r != ncclSuccess) return err(MPP41_ERR_COMM, "ncclAllReduce: %s", a->error_string(r));
+    if (d->out_dtype == MPP41_F16) {
+        const cudaError_t e = launch_f32_to_f16(static_cast<const float *>(partial), n, out, ctx->stream);
+        if (e != cudaSuccess) return err(MPP41_ERR_CUDA, "fp16 conversion: %s", cudaGetErrorString(e));
+    }
+    return MPP41_OK;
+}
+
+}  // extern "C"

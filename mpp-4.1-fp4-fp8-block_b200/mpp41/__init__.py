@@ -107,6 +107,11 @@ def lib() -> C.CDLL:
         "mpp41_mlp_noalloc": ([C.POINTER(MLPDesc)] + [vp] * 9, st),
         "mpp41_mlp_describe": ([C.c_char_p, u32, u32, u32, C.POINTER(MLPDesc)], st),
         "mpp41_mlp_benchmark": ([vp, C.POINTER(MLPDesc)] + [vp] * 9 + [C.c_int, C.POINTER(C.c_double)], st),
+        "mpp41_comm_unique_id": ([vp], st),
+        "mpp41_comm_init": ([vp, C.c_int, C.c_int, vp], st),
+        "mpp41_comm_destroy": ([vp], None),
+        "mpp41_mlp_tp_scratch_bytes": ([C.POINTER(MLPDesc), C.c_int], sz),
+        "mpp41_mlp_tp": ([vp, C.POINTER(MLPDesc)] + [vp] * 9, st),
     }
     for name, (args, res) in sigs.items():
         f = getattr(L, name)
@@ -152,6 +157,18 @@ def mlp_desc(tokens, hidden, intermediate, wfmt=W_MXFP4, afmt=A_F16, epilogue=SW
 
 
 NOALLOC_SCRATCH_BYTES = 8 << 20
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL unique id (rank 0 creates it and shares it)."""
+    buf = (C.c_uint8 * COMM_ID_BYTES)()
+    _check(lib().mpp41_comm_unique_id(buf))
+    return bytes(buf)
+
+
+def tp_scratch_bytes(desc: "MLPDesc", nranks: int) -> int:
+    return lib().mpp41_mlp_tp_scratch_bytes(C.byref(desc), nranks)
 
 
 def mlp_noalloc(desc: MLPDesc, x, wg, wu, wd, sg, su, sd, out, stream_handle=None):
@@ -262,6 +279,18 @@ class Context:
     def mlp_down(self, desc: MLPDesc, scratch, wd, sd, out, prepared=False):
         _check(lib().mpp41_mlp_down(self.h, C.byref(desc), _ptr(scratch), _ptr(wd), _ptr(sd), _ptr(out),
                                     int(bool(prepared))))
+
+    # ---- tensor parallelism (mpp41_comm_*, mpp41_mlp_tp)
+    def comm_init(self, nranks: int, rank: int, unique_id: bytes):
+        buf = (C.c_uint8 * COMM_ID_BYTES).from_buffer_copy(unique_id)
+        _check(lib().mpp41_comm_init(self.h, nranks, rank, buf))
+
+    def comm_destroy(self):
+        lib().mpp41_comm_destroy(self.h)
+
+    def mlp_tp(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out):
+        _check(lib().mpp41_mlp_tp(self.h, C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(wd), _ptr(sg), _ptr(su),
+                                  _ptr(sd), _ptr(scratch), _ptr(out)))
 
     def quantize_mxfp4(self, w, rows: int, depth: int, packed, scales):
         _check(lib().mpp41_quantize_mxfp4(self.h, _ptr(w), rows, depth, _ptr(packed), _ptr(scales)))

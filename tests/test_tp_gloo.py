@@ -1,0 +1,68 @@
+"""Tensor-parallel sharding (mpp41.tp) on CPU: two gloo ranks each compute the
+MLP of their intermediate slice with the oracle (fp32 partial output), sum the
+partials with all_reduce and must reproduce the single-rank oracle layer. This
+checks the shard layout mpp41_mlp_tp relies on (gate/up rows, down columns and
+their E8M0 scale blocks) without a GPU."""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+for p in (os.path.join(ROOT, "mpp-4.1-fp4-fp8-block_b200"), os.path.join(ROOT, "oracle"), HERE):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import oracle as O  # noqa: E402
+from mpp41 import tp  # noqa: E402
+
+T, H, I = 8, 256, 512
+
+
+def layer(wfmt):
+    from gpu_data import weights
+    x = O.half_values(T * H, 11, 0.125).reshape(T, H)
+    wg, sg = weights(wfmt, I, H, 21)
+    wu, su = weights(wfmt, I, H, 22)
+    wd, sd = weights(wfmt, H, I, 23)
+    return x, wg, wu, wd, sg, su, sd
+
+
+def worker(rank, world, port, wfmt, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, wg, wu, wd, sg, su, sd = layer(wfmt)
+        s = tp.shard(wfmt, rank, world, H, I, wg, wu, wd, sg, su, sd)
+        epi = 1   # swiglu_half (per-element, so the slice split is exact)
+        _, part = O.mlp(0, wfmt, epi, 0, T, H, I // world, x.view(np.uint16), s["wg"], s["wu"], s["wd"],
+                        s["sg"], s["su"], s["sd"])
+        t = torch.from_numpy(part.astype(np.float64))
+        dist.all_reduce(t)
+        if rank == 0:
+            q.put(t.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("wfmt", [O.W_MXFP4, O.W_I4, O.W_I2, O.W_E4M3])
+def test_two_rank_shards_sum_to_the_layer(wfmt):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + wfmt * 7 + os.getpid() % 500
+    procs = [ctx.Process(target=worker, args=(r, 2, port, wfmt, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x, wg, wu, wd, sg, su, sd = layer(wfmt)
+    _, ref = O.mlp(0, wfmt, 1, 0, T, H, I, x.view(np.uint16), wg, wu, wd, sg, su, sd)
+    ref = ref.astype(np.float64)
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= 1e-6
