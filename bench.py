@@ -44,7 +44,7 @@ ROTATE = 24
 METRIC = "MXFP4 fused-MLP µs/layer & TFLOP/s (% of roofline) at 1/2/4/8 B200"
 # DRAM bytes per launch of mlp_fused_kernel from one ncu capture of this
 # workload (profiles/mlp_fused_mxfp4_t128_h1024_i4096.md).
-NCU_TRAFFIC_LAYER = 7001344
+NCU_TRAFFIC_LAYER = 7006720
 
 
 def load_peaks():
