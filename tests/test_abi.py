@@ -70,3 +70,11 @@ def test_create_without_device_reports_no_device():
     with pytest.raises(mpp41.MPP41Error) as e:
         mpp41.Context(0)
     assert e.value.status in (mpp41.ERR_NO_DEVICE, mpp41.ERR_CUDA)
+
+
+def test_probe_cli_builds_and_fails_cleanly_without_a_device():
+    import subprocess
+    probe = os.path.join(os.path.dirname(mpp41.PKG) if False else mpp41.PKG, "bin", "mpp41probe")
+    assert os.access(probe, os.X_OK)
+    r = subprocess.run([probe, "--no-such-flag"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 2 and "unknown argument" in r.stderr
