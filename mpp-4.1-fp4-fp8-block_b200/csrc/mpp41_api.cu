@@ -687,8 +687,26 @@ mpp41_status mpp41_matmul(mpp41_ctx *ctx, const char *name, const void *a, const
         CK(launch_widen(2, a, (size_t)m * kk, workspace, st), "widen A");
         return enqueue_i8_gemm(ctx, W_I4, workspace, b, c, m, n, kk, st, name);
     }
+    const void *a16 = (kind == 0 || kind == 3) ? workspace : a;
+    if (kind <= 2 && n % 128 == 0 && 2 + (size_t)(n / 128 + 1) * ((m + 127) / 128 + 1) <= ctx->sync_words) {
+        // weight-major tensor-core path: the fused layer kernel's down tiles as a
+        // plain GEMM (weights decoded into tensor memory, tokens as N)
+        FusedLaunch F{};
+        F.wfmt = kind == 2 ? W_I4 : W_FP4;
+        F.gate_epi = EPI_SWIGLU_PLAIN;
+        F.out_f16 = kind != 0;
+        F.mid = const_cast<void *>(a16);
+        F.wd = b; F.out = c;
+        F.sync = ctx->sync; F.err = ctx->err; F.trace = nullptr;
+        F.T = m; F.H = n; F.I = kk; F.splits = 1;
+        F.gemm_only = true;
+        const char *fwhy = "";
+        const int frc = launch_mlp_fused(F, st, &fwhy);
+        if (frc == 0) return MPP41_OK;
+        if (frc == 2) return fail(MPP41_ERR_CUDA, "%s: %s", name, fwhy);
+    }
     WqLaunch L{};
-    L.a = (kind == 0 || kind == 3) ? workspace : a;
+    L.a = a16;
     L.b0 = b; L.out = c;
     L.M = m; L.N = n; L.K = kk; L.ldc = n;
     L.err = ctx->err;

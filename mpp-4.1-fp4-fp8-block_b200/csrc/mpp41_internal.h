@@ -104,6 +104,9 @@ struct FusedLaunch {
     uint32_t *err;
     uint32_t T, H, I, splits;
     unsigned long long *trace;   // optional per-CTA phase/wait counters (profiling)
+    // GEMM only: out[T][H] = mid[T][I] x wd[H][I]^T (down tiles, no split, no
+    // gate/up phase); x / wg / wu / sg / su are not read
+    bool gemm_only = false;
 };
 // Number of uint32 sync counters a launch needs.
 size_t fused_sync_words(uint32_t T, uint32_t H, uint32_t I);

@@ -91,24 +91,37 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     p.NT = fused_nt(L.T);
     const uint32_t mt = (L.T + p.NT - 1) / p.NT;
     if (L.I % (L.splits * kFBK)) { *why = "intermediate not a multiple of splits x 128"; return 1; }
-    if (L.splits != fused_splits(L.T, L.H, L.I)) { *why = "splits differ from fused_splits (counter layout)"; return 1; }
+    if (L.gemm_only ? L.splits != 1 : L.splits != fused_splits(L.T, L.H, L.I)) {
+        *why = "splits differ from fused_splits (counter layout)";
+        return 1;
+    }
     const uint64_t rawH = (uint64_t)L.H * wfmt_bits(W) / 8, rawI = (uint64_t)L.I * wfmt_bits(W) / 8;
-    if (rawH < (uint64_t)kChunkRow || rawI < (uint64_t)kChunkRow) { *why = "packed rows shorter than one chunk"; return 1; }
-    if (W == W_MXFP4 && (L.H % 512 || L.I % 512 || (L.splits > 1 && (L.I / L.splits) % 512))) {
+    if ((!L.gemm_only && rawH < (uint64_t)kChunkRow) || rawI < (uint64_t)kChunkRow) {
+        *why = "packed rows shorter than one chunk";
+        return 1;
+    }
+    if (W == W_MXFP4 && ((!L.gemm_only && L.H % 512) || L.I % 512 || (L.splits > 1 && (L.I / L.splits) % 512))) {
         *why = "MXFP4 scale rows need hidden, intermediate and the K split to be multiples of 512";
         return 1;
     }
-    p.n_gtiles = (L.I / kGCh) * mt;
+    p.n_gtiles = L.gemm_only ? 0 : (L.I / kGCh) * mt;
     p.n_dtiles = (L.H / kWRows) * L.splits * mt;
-    p.g_per_slice = L.I / L.splits / kGCh;
+    p.g_per_slice = L.gemm_only ? 0 : L.I / L.splits / kGCh;
     if (L.splits > 1 && !L.ws) { *why = "workspace"; return 1; }
-    bool ok = make_map_kblocks(&p.tm_x, L.x, L.H, L.T, p.NT, 2) && make_map_kblocks(&p.tm_mid, L.mid, L.I, L.T, p.NT, 2) &&
-              make_map(&p.tm_wg, L.wg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, kChunkRow, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
-              make_map(&p.tm_wu, L.wu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, kChunkRow, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
+    // GEMM mode has no gate/up phase: its G maps are built over the down
+    // operands only so that they are valid, and are never read
+    const void *gx = L.gemm_only ? L.mid : L.x, *gg = L.gemm_only ? L.wd : L.wg, *gu = L.gemm_only ? L.wd : L.wu;
+    const uint64_t grow = L.gemm_only ? rawI : rawH;
+    const uint32_t gk = L.gemm_only ? L.I : L.H, gn = L.gemm_only ? L.H : L.I;
+    bool ok = make_map_kblocks(&p.tm_x, gx, gk, L.T, p.NT, 2) && make_map_kblocks(&p.tm_mid, L.mid, L.I, L.T, p.NT, 2) &&
+              make_map(&p.tm_wg, gg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, grow, gn, kChunkRow, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
+              make_map(&p.tm_wu, gu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, grow, gn, kChunkRow, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
               make_map(&p.tm_wd, L.wd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawI, L.H, kChunkRow, kWRows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (ok && W == W_MXFP4)
-        ok = make_map(&p.tm_sg, L.sg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, kScRow, kGCh, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-             make_map(&p.tm_su, L.su, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, kScRow, kGCh, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+        ok = make_map(&p.tm_sg, L.gemm_only ? L.sd : L.sg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gk / 32, gn, kScRow, kGCh,
+                      CU_TENSOR_MAP_SWIZZLE_NONE) &&
+             make_map(&p.tm_su, L.gemm_only ? L.sd : L.su, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, gk / 32, gn, kScRow, kGCh,
+                      CU_TENSOR_MAP_SWIZZLE_NONE) &&
              make_map(&p.tm_sd, L.sd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.I / 32, L.H, kScRow, kWRows, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!ok) { *why = "tensor maps (16-byte aligned bases and row pitches needed)"; return 1; }
     p.mid = static_cast<__half *>(L.mid);
