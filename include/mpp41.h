@@ -246,6 +246,18 @@ mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *desc, const void *x, const 
                                const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *out,
                                void *cuda_stream);
 
+/* ---- activation quantization (the epilogue after the layer, feeding the next
+ *      layer's low-precision GEMM; no reference counterpart). fp16 x [tokens]
+ *      [hidden]:
+ *      - mpp41_quantize_act_mxfp4: OCP-MX MXFP4 per 32-wide block along hidden,
+ *        same rule as mpp41_quantize_mxfp4 (W4A4 activations);
+ *      - mpp41_quantize_act_s8: per-token symmetric int8 (W8A8 activations),
+ *        scale[t] = absmax / 127, q = rint(x * 127 / absmax). ---- */
+mpp41_status mpp41_quantize_act_mxfp4(mpp41_ctx *ctx, const void *x, uint32_t tokens, uint32_t hidden, uint8_t *packed,
+                                      uint8_t *scales);
+mpp41_status mpp41_quantize_act_s8(mpp41_ctx *ctx, const void *x, uint32_t tokens, uint32_t hidden, int8_t *q,
+                                   float *scale);
+
 /* ---- tensor parallelism (no counterpart in the
  *      single-GPU reference). Rank r of P holds rows [r*I/P, (r+1)*I/P) of the
  *      gate and up weights (and their scale rows) and the same columns of the

@@ -831,6 +831,29 @@ mpp41_status mpp41_quantize_mxfp4(mpp41_ctx *ctx, const float *w, uint32_t rows,
     return MPP41_OK;
 }
 
+mpp41_status mpp41_quantize_act_mxfp4(mpp41_ctx *ctx, const void *x, uint32_t tokens, uint32_t hidden, uint8_t *packed,
+                                      uint8_t *scales)
+{
+    NEED(ctx);
+    if (hidden % 32) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "hidden must be a multiple of 32");
+    if (!tokens || !hidden) return MPP41_OK;
+    if (!x || !packed || !scales) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(packed) & 15u))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "x and packed must be 16-byte aligned");
+    CK(launch_quantize_mxfp4_f16(x, tokens, hidden, packed, scales, ctx->stream), "quantize activations");
+    return MPP41_OK;
+}
+
+mpp41_status mpp41_quantize_act_s8(mpp41_ctx *ctx, const void *x, uint32_t tokens, uint32_t hidden, int8_t *q,
+                                   float *scale)
+{
+    NEED(ctx);
+    if (!tokens || !hidden) return MPP41_OK;
+    if (!x || !q || !scale) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    CK(launch_quantize_act_s8(x, tokens, hidden, q, scale, ctx->stream), "quantize activations");
+    return MPP41_OK;
+}
+
 mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,
                                  const void *wu, const void *wd, const uint8_t *sg, const uint8_t *su,
                                  const uint8_t *sd, void *scratch, void *out, int iterations, double *gpu_seconds)

@@ -87,6 +87,11 @@ bool make_map_kblocks(CUtensorMap *m, const void *base, uint64_t cols, uint64_t 
 // OCP-MX quantization of fp32 [rows][depth] to E2M1 [rows][depth/2] + E8M0 [rows][depth/32].
 cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
                                   cudaStream_t st);
+// Activation quantization (fp16 in): OCP-MX MXFP4, and per-token int8 absmax.
+cudaError_t launch_quantize_mxfp4_f16(const void *x, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
+                                      cudaStream_t st);
+cudaError_t launch_quantize_act_s8(const void *x, uint32_t tokens, uint32_t hidden, int8_t *q, float *scale,
+                                   cudaStream_t st);
 // Returns 0 on success, 1 for an unsupported combination/shape, 2 for a CUDA error.
 int launch_wq_gemm(const WqLaunch &L, cudaStream_t st, const char **why);
 

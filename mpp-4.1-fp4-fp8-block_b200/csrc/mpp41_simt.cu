@@ -316,22 +316,38 @@ __global__ void scalar_matmul_kernel(int kind, uint32_t M, uint32_t N, uint32_t 
 // store of packed nibbles and one scale byte. There is no counterpart in the
 // reference (it draws random packed bytes); it produces the BASELINE config-0
 // weights and is checked bit for bit against the oracle's restatement.
-__global__ void quantize_mxfp4_kernel(const float *__restrict__ w, uint32_t rows, uint32_t depth,
+template <typename In>
+__global__ void quantize_mxfp4_kernel(const In *__restrict__ w, uint32_t rows, uint32_t depth,
                                       uint8_t *__restrict__ packed, uint8_t *__restrict__ scales)
 {
     const uint32_t kb = depth / 32;
     const size_t blocks = (size_t)rows * kb;
     for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < blocks; b += (size_t)gridDim.x * blockDim.x) {
         const uint32_t r = (uint32_t)(b / kb), j = (uint32_t)(b % kb);
-        const float4 *src = reinterpret_cast<const float4 *>(w + (size_t)r * depth + (size_t)j * 32);
         float v[32];
         float amax = 0.0f;
+        if constexpr (sizeof(In) == 4) {
+            const float4 *src = reinterpret_cast<const float4 *>(w + (size_t)r * depth + (size_t)j * 32);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 f = src[i];
-            v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+            for (int i = 0; i < 8; ++i) {
+                const float4 f = src[i];
+                v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+            }
+        } else {   // fp16 activations (exact in fp32)
+            const uint4 *src = reinterpret_cast<const uint4 *>(w + (size_t)r * depth + (size_t)j * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 u = src[i];
+                const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&ws[q]));
+                    v[8 * i + 2 * q] = f.x; v[8 * i + 2 * q + 1] = f.y;
+                }
+            }
         }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
         int e = 0;
         uint32_t code = 0;
         if (amax > 0.0f && isfinite(amax)) {
@@ -361,7 +377,53 @@ __global__ void quantize_mxfp4_kernel(const float *__restrict__ w, uint32_t rows
 cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
                                   cudaStream_t st)
 {
-    quantize_mxfp4_kernel<<<grid_for((size_t)rows * depth / 32, 256), 256, 0, st>>>(w, rows, depth, packed, scales);
+    quantize_mxfp4_kernel<float><<<grid_for((size_t)rows * depth / 32, 256), 256, 0, st>>>(w, rows, depth, packed, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_mxfp4_f16(const void *x, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
+                                      cudaStream_t st)
+{
+    quantize_mxfp4_kernel<__half><<<grid_for((size_t)rows * depth / 32, 256), 256, 0, st>>>(
+        static_cast<const __half *>(x), rows, depth, packed, scales);
+    return cudaGetLastError();
+}
+
+// Per-token symmetric int8 quantization of fp16 activations: scale = absmax /
+// 127 (0 for an all-zero row), q = rint(x * (127 / absmax)) in [-127, 127].
+// One CTA per token row.
+__global__ void quantize_act_s8_kernel(const __half *__restrict__ x, uint32_t tokens, uint32_t hidden,
+                                       int8_t *__restrict__ q, float *__restrict__ scale)
+{
+    __shared__ float warp_max[32];
+    for (uint32_t t = blockIdx.x; t < tokens; t += gridDim.x) {
+        const __half *row = x + (size_t)t * hidden;
+        float m = 0.0f;
+        for (uint32_t i = threadIdx.x; i < hidden; i += blockDim.x) m = fmaxf(m, fabsf(__half2float(row[i])));
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            m = threadIdx.x < blockDim.x / 32 ? warp_max[threadIdx.x] : 0.0f;
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (threadIdx.x == 0) warp_max[0] = m;
+        }
+        __syncthreads();
+        const float amax = warp_max[0];
+        const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+        for (uint32_t i = threadIdx.x; i < hidden; i += blockDim.x)
+            q[(size_t)t * hidden + i] = (int8_t)(int)rintf(fminf(fmaxf(__half2float(row[i]) * inv, -127.0f), 127.0f));
+        if (threadIdx.x == 0) scale[t] = amax / 127.0f;
+        __syncthreads();
+    }
+}
+
+cudaError_t launch_quantize_act_s8(const void *x, uint32_t tokens, uint32_t hidden, int8_t *q, float *scale,
+                                   cudaStream_t st)
+{
+    const unsigned grid = tokens < 148u * 8u ? tokens : 148u * 8u;
+    if (!grid) return cudaSuccess;
+    quantize_act_s8_kernel<<<grid, 256, 0, st>>>(static_cast<const __half *>(x), tokens, hidden, q, scale);
     return cudaGetLastError();
 }
 

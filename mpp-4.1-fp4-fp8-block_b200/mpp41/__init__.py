@@ -103,6 +103,8 @@ def lib() -> C.CDLL:
         "mpp41_mlp_gate_up": ([vp, C.POINTER(MLPDesc)] + [vp] * 7, st),
         "mpp41_mlp_down": ([vp, C.POINTER(MLPDesc), vp, vp, vp, vp, C.c_int], st),
         "mpp41_quantize_mxfp4": ([vp, vp, u32, u32, vp, vp], st),
+        "mpp41_quantize_act_mxfp4": ([vp, vp, u32, u32, vp, vp], st),
+        "mpp41_quantize_act_s8": ([vp, vp, u32, u32, vp, vp], st),
         "mpp41_mlp_noalloc_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp_noalloc": ([C.POINTER(MLPDesc)] + [vp] * 9, st),
         "mpp41_mlp_describe": ([C.c_char_p, u32, u32, u32, C.POINTER(MLPDesc)], st),
@@ -294,6 +296,12 @@ class Context:
 
     def quantize_mxfp4(self, w, rows: int, depth: int, packed, scales):
         _check(lib().mpp41_quantize_mxfp4(self.h, _ptr(w), rows, depth, _ptr(packed), _ptr(scales)))
+
+    def quantize_act_mxfp4(self, x, tokens: int, hidden: int, packed, scales):
+        _check(lib().mpp41_quantize_act_mxfp4(self.h, _ptr(x), tokens, hidden, _ptr(packed), _ptr(scales)))
+
+    def quantize_act_s8(self, x, tokens: int, hidden: int, q, scale):
+        _check(lib().mpp41_quantize_act_s8(self.h, _ptr(x), tokens, hidden, _ptr(q), _ptr(scale)))
 
     def mlp_benchmark(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out, iterations: int) -> float:
         secs = C.c_double()
