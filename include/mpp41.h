@@ -258,6 +258,27 @@ mpp41_status mpp41_quantize_act_mxfp4(mpp41_ctx *ctx, const void *x, uint32_t to
 mpp41_status mpp41_quantize_act_s8(mpp41_ctx *ctx, const void *x, uint32_t tokens, uint32_t hidden, int8_t *q,
                                    float *scale);
 
+/* ---- W4A4: activations as well as weights in MXFP4, multiplied on the FP4
+ *      tensor cores with the E8M0 block scales applied inside the MMA (no
+ *      reference counterpart: its FP4 rows keep fp16 activations; the weight
+ *      layout is the reference's, docs/MXFP4-MPP41-GUIDE.md:43-55).
+ *      - mpp41_matmul_mxf4: C[M][N] = A[M][K] B[N][K]^T, A and B packed E2M1
+ *        [rows][K/2] with E8M0 scales [rows][K/32]; C fp32 (c_f16 = 0) or fp16.
+ *        K % 512 == 0, N % 32 == 0, 16-byte aligned buffers.
+ *      - mpp41_mlp_w4a4: one MLP layer. x (fp16 [T][H]) is quantized with the
+ *        mpp41_quantize_act_mxfp4 rule; the gate/up GEMM's epilogue forms
+ *        silu(g) * u in fp32 and quantizes it with the same rule; the down
+ *        GEMM writes out [T][H] (fp32, or fp16 when out_f16). H % 512 == 0,
+ *        I % 512 == 0. scratch (mpp41_mlp_w4a4_scratch_bytes) holds, each
+ *        section 256-byte aligned: packed x [T][H/2], x scales [T][H/32],
+ *        packed mid [T][I/2], mid scales [T][I/32]. ---- */
+mpp41_status mpp41_matmul_mxf4(mpp41_ctx *ctx, const uint8_t *a, const uint8_t *sa, const uint8_t *b,
+                               const uint8_t *sb, void *c, uint32_t M, uint32_t N, uint32_t K, int c_f16);
+size_t mpp41_mlp_w4a4_scratch_bytes(uint32_t tokens, uint32_t hidden, uint32_t intermediate);
+mpp41_status mpp41_mlp_w4a4(mpp41_ctx *ctx, uint32_t tokens, uint32_t hidden, uint32_t intermediate, const void *x,
+                            const uint8_t *wg, const uint8_t *sg, const uint8_t *wu, const uint8_t *su,
+                            const uint8_t *wd, const uint8_t *sd, void *out, int out_f16, void *scratch);
+
 /* ---- tensor parallelism (no counterpart in the
  *      single-GPU reference). Rank r of P holds rows [r*I/P, (r+1)*I/P) of the
  *      gate and up weights (and their scale rows) and the same columns of the

@@ -854,6 +854,78 @@ mpp41_status mpp41_quantize_act_s8(mpp41_ctx *ctx, const void *x, uint32_t token
     return MPP41_OK;
 }
 
+// ------------------------------------------------------------------ W4A4
+static bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static size_t up256(size_t n) { return (n + 255) & ~size_t(255); }
+
+static mpp41_status enqueue_mxf4(mpp41_ctx *ctx, const MxLaunch &L, const char *what)
+{
+    const char *why = "";
+    const int rc = launch_mxf4_gemm(L, ctx->stream, &why);
+    if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "%s: %s", what, why);
+    return MPP41_OK;
+}
+
+mpp41_status mpp41_matmul_mxf4(mpp41_ctx *ctx, const uint8_t *a, const uint8_t *sa, const uint8_t *b,
+                               const uint8_t *sb, void *c, uint32_t M, uint32_t N, uint32_t K, int c_f16)
+{
+    NEED(ctx);
+    if (!M || !N || !K) return MPP41_OK;
+    if (!a || !sa || !b || !sb || !c) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if (!al16(a) || !al16(sa) || !al16(b) || !al16(sb) || !al16(c))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "buffers must be 16-byte aligned");
+    MxLaunch L{};
+    L.a = a; L.sa = sa;
+    L.b0 = L.b1 = b; L.sb0 = L.sb1 = sb;
+    L.b_rows = N; L.b0_row0 = 0; L.b1_row0 = 128; L.b_row_step = 256;
+    L.out = c; L.M = M; L.N = N; L.K = K; L.ldc = N;
+    L.epi = c_f16 ? 1 : 0;
+    L.err = ctx->err;
+    return enqueue_mxf4(ctx, L, "mxf4 GEMM");
+}
+
+size_t mpp41_mlp_w4a4_scratch_bytes(uint32_t T, uint32_t H, uint32_t I)
+{
+    return up256((size_t)T * H / 2) + up256((size_t)T * H / 32) + up256((size_t)T * I / 2) + up256((size_t)T * I / 32);
+}
+
+mpp41_status mpp41_mlp_w4a4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I, const void *x, const uint8_t *wg,
+                            const uint8_t *sg, const uint8_t *wu, const uint8_t *su, const uint8_t *wd,
+                            const uint8_t *sd, void *out, int out_f16, void *scratch)
+{
+    NEED(ctx);
+    if (!T || !H || !I) return MPP41_OK;
+    if (H % 512 || I % 512) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "hidden and intermediate must be multiples of 512");
+    if (!x || !wg || !sg || !wu || !su || !wd || !sd || !out || !scratch)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if (!al16(x) || !al16(wg) || !al16(sg) || !al16(wu) || !al16(su) || !al16(wd) || !al16(sd) || !al16(out) ||
+        (reinterpret_cast<uintptr_t>(scratch) & 255u))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "buffers must be 16-byte aligned (scratch 256-byte)");
+    uint8_t *xq = static_cast<uint8_t *>(scratch);
+    uint8_t *xs = xq + up256((size_t)T * H / 2);
+    uint8_t *mq = xs + up256((size_t)T * H / 32);
+    uint8_t *ms = mq + up256((size_t)T * I / 2);
+    CK(launch_quantize_mxfp4_f16(x, T, H, xq, xs, ctx->stream), "quantize activations");
+    MxLaunch g{};
+    g.a = xq; g.sa = xs;
+    g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
+    g.b_rows = I; g.b0_row0 = 0; g.b1_row0 = 0; g.b_row_step = 128;
+    g.out = mq; g.out_scales = ms;
+    g.M = T; g.N = I; g.K = H; g.ldc = I;
+    g.epi = 2;
+    g.err = ctx->err;
+    mpp41_status s = enqueue_mxf4(ctx, g, "W4A4 gate/up GEMM");
+    if (s != MPP41_OK) return s;
+    MxLaunch d{};
+    d.a = mq; d.sa = ms;
+    d.b0 = d.b1 = wd; d.sb0 = d.sb1 = sd;
+    d.b_rows = H; d.b0_row0 = 0; d.b1_row0 = 128; d.b_row_step = 256;
+    d.out = out; d.M = T; d.N = H; d.K = I; d.ldc = H;
+    d.epi = out_f16 ? 1 : 0;
+    d.err = ctx->err;
+    return enqueue_mxf4(ctx, d, "W4A4 down GEMM");
+}
+
 mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,
                                  const void *wu, const void *wd, const uint8_t *sg, const uint8_t *su,
                                  const uint8_t *sd, void *scratch, void *out, int iterations, double *gpu_seconds)

@@ -78,6 +78,23 @@ struct F32Launch {
 };
 int launch_f32_gemm(const F32Launch &L, cudaStream_t st, const char **why);
 
+// Block-scaled FP4 GEMM (W4A4, kind::mxf4): A [M][K/2] E2M1 + [M][K/32] E8M0
+// against B rows taken from two maps (b0 rows b0_row0 + t * b_row_step and b1
+// rows b1_row0 + t * b_row_step, 128 each, for column tile t). epi 0: fp32 C,
+// 1: fp16 C, 2: silu(gate) * up re-quantized to MXFP4 (out = packed mid
+// [M][ldc/2], out_scales = [M][ldc/32]).
+struct MxLaunch {
+    const void *a, *sa;
+    const void *b0, *sb0, *b1, *sb1;
+    uint32_t b_rows, b0_row0, b1_row0, b_row_step;
+    void *out;
+    uint8_t *out_scales;
+    uint32_t M, N, K, ldc;
+    int epi;
+    uint32_t *err;
+};
+int launch_mxf4_gemm(const MxLaunch &L, cudaStream_t st, const char **why);
+
 bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols, uint64_t rows,
               uint32_t bc, uint32_t br, CUtensorMapSwizzle sw);
 // fp16 [rows][cols] viewed as [cols/64][rows][64]: one copy of box {64, br, nblk}

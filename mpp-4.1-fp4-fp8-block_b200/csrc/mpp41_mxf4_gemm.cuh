@@ -1,0 +1,302 @@
+// Block-scaled FP4 GEMM on the FP4 tensor cores (W4A4):
+// C[m][n] = sum_k A[m][k] * B[n][k], both operands MXFP4 (E2M1 packed two per
+// byte, low nibble = even k, plus one E8M0 scale per 32 along k: the
+// reference's weight layout, docs/MXFP4-MPP41-GUIDE.md:43-55, used for the
+// activations too), fp32 accumulation, tcgen05.mma
+// kind::mxf4.block_scale.block32. Nothing is decoded: TMA lands the packed
+// tiles in 128-byte-swizzled shared memory and the MMA consumes them; only the
+// E8M0 scales pass through registers on their way into tensor memory.
+//
+// Scale factors in tensor memory (block32, one SM; the arrangement of CUTLASS
+// cute/atom/mma_traits_sm100.hpp tmem_sf_frg with four-fold lane replication):
+// for operand row r = 32 i + j, the scales of k-blocks 4g..4g+3 of a stage are
+// the 4 bytes of column (base + R/32 * g + i) at lane j of every lane quarter,
+// R = 128 rows for A and 256 for B. MMA number 2g + h of the stage (K = 64,
+// two scales) reads bytes 2h and 2h+1: the byte offset rides in address bits
+// 30-31 and in the instruction descriptor's scale-factor id.
+//
+// Epilogues: fp32 or fp16 C, or (SWIGLU_MX) the gate/up layer of a W4A4 MLP:
+// B rows 0..127 of the tile are gate rows, 128..255 the up rows of the same
+// 128 channels; each thread owns one token row, forms silu(g) * u and
+// re-quantizes it to MXFP4 in registers (32-blocks never straddle threads), so
+// the down GEMM reads the mid as its A operand directly.
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2..5 move each stage's scales into tensor memory, then run the
+// epilogue (warp w owns TMEM lane quarter w % 4).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "mpp41_device.cuh"
+#include "mpp41_internal.h"
+#include "mpp41_mx.cuh"
+
+namespace mpp41 {
+namespace mxf4 {
+
+enum Epi { EPI_F32 = 0, EPI_F16 = 1, EPI_SWIGLU_MX = 2 };
+
+constexpr int kBM = 128;          // rows of A per tile (MMA M)
+constexpr int kBN = 256;          // rows of B per tile (MMA N)
+constexpr int kBK = 256;          // K per stage: one 128-byte swizzle atom of packed E2M1
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kATile = kBM * 128;      // 16 KB
+constexpr uint32_t kBHalf = 128 * 128;      // 16 KB: 128 B rows
+constexpr uint32_t kBTile = kBN * 128;      // 32 KB
+// Scales: a TMA box needs a 16-byte inner extent, so each stage loads the
+// 16-byte strip holding its own 8 scale bytes per row and the neighbour's.
+constexpr uint32_t kSfRow = 16;
+constexpr uint32_t kSfaBytes = kBM * kSfRow;
+constexpr uint32_t kSfbBytes = kBN * kSfRow;
+constexpr uint32_t kSfaCols = kBM / 32 * 2, kSfbCols = kBN / 32 * 2;   // 8 and 16 columns per stage
+constexpr uint32_t kAccCols = kBN;
+constexpr uint32_t kSfCol0 = kAccCols;                                  // scale ring after the accumulator
+constexpr uint32_t kTmemCols = 512;
+static_assert(kSfCol0 + kStages * (kSfaCols + kSfbCols) <= kTmemCols, "tensor memory");
+
+constexpr uint32_t kOffB = kStages * kATile;
+constexpr uint32_t kOffSfa = kOffB + kStages * kBTile;
+constexpr uint32_t kOffSfb = kOffSfa + kStages * kSfaBytes;
+constexpr uint32_t kOffBar = kOffSfb + kStages * kSfbBytes;
+constexpr uint32_t kSmem = 1024 + kOffBar + 256;
+static_assert(kSmem <= 227 * 1024, "shared memory");
+
+// kind::mxf4 instruction descriptor: E2M1 x E2M1 (format 1), UE8M0 scales,
+// K = 64, both operands K-major (cute/arch/mma_sm100_desc.hpp InstrDescriptorBlockScaled).
+__host__ __device__ constexpr uint32_t idesc_mxf4(int M, int N, uint32_t sfa_id, uint32_t sfb_id)
+{
+    return (sfb_id << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
+           ((uint32_t)(M >> 4) << 24) | (sfa_id << 29);
+}
+
+__device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa, uint32_t sfb, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_x8(uint32_t taddr, const uint32_t (&r)[8])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+__device__ __forceinline__ void st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+struct Params {
+    CUtensorMap tm_a;         // packed A [M][K/2], box {128, 128}, SW128
+    CUtensorMap tm_b0;        // packed B rows of the tile's first half, box {128, 128}, SW128
+    CUtensorMap tm_b1;        // ... second half (the up weights for SWIGLU_MX)
+    CUtensorMap tm_sa;        // E8M0 A [M][K/32], box {16, 128}
+    CUtensorMap tm_sb0;       // E8M0 B, box {16, 128}
+    CUtensorMap tm_sb1;
+    uint32_t b0_row0, b1_row0;   // row of tile 0's first / second half in tm_b0 / tm_b1
+    uint32_t b_row_step;         // rows between consecutive column tiles in those maps
+    void *out;                   // fp32 / fp16 [M][ldc]; SWIGLU_MX: packed mid [M][ldc/2]
+    uint8_t *out_scales;         // SWIGLU_MX: mid scales [M][ldc/32]
+    uint32_t M, N, K, ldc;       // N = columns written (SWIGLU_MX: mid channels)
+    uint32_t *err;
+};
+
+__device__ __forceinline__ void load_u2(const uint8_t *p, uint32_t &lo, uint32_t &hi)
+{
+    const uint2 v = *reinterpret_cast<const uint2 *>(p);
+    lo = v.x;
+    hi = v.y;
+}
+
+template <int E>
+__global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_constant__ Params p)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem, *sB = smem + kOffB, *sSa = smem + kOffSfa, *sSb = smem + kOffSfb;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
+    uint64_t *full = bars;                 // [kStages] TMA landed
+    uint64_t *sf_ready = bars + kStages;   // [kStages] scales in tensor memory
+    uint64_t *empty = bars + 2 * kStages;  // [kStages] MMA done with the stage
+    uint64_t *done = bars + 3 * kStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * kStages + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t m0 = blockIdx.y * kBM;
+    const uint32_t nk = p.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&sf_ready[s], 4);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const int32_t rb0 = (int32_t)(p.b0_row0 + blockIdx.x * p.b_row_step);
+            const int32_t rb1 = (int32_t)(p.b1_row0 + blockIdx.x * p.b_row_step);
+            uint32_t s = 0;
+            for (; s < nk; ++s) {
+                const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
+                if (!mbar_wait(&empty[st], ph ^ 1u, abort, p.err, 0xC01)) break;
+                mbar_arrive_expect_tx(&full[st], kATile + kBTile + kSfaBytes + kSfbBytes);
+                const int32_t kb = (int32_t)(s * (kBK / 2)), ks = (int32_t)((s >> 1) * kSfRow);
+                tma_load_2d(sA + st * kATile, &p.tm_a, kb, (int32_t)m0, &full[st]);
+                tma_load_2d(sB + st * kBTile, &p.tm_b0, kb, rb0, &full[st]);
+                tma_load_2d(sB + st * kBTile + kBHalf, &p.tm_b1, kb, rb1, &full[st]);
+                tma_load_2d(sSa + st * kSfaBytes, &p.tm_sa, ks, (int32_t)m0, &full[st]);
+                tma_load_2d(sSb + st * kSfbBytes, &p.tm_sb0, ks, rb0, &full[st]);
+                tma_load_2d(sSb + st * kSfbBytes + 128 * kSfRow, &p.tm_sb1, ks, rb1, &full[st]);
+            }
+            // drain: no copy may still be landing when the CTA exits
+            for (uint32_t t = (s > kStages ? s - kStages : 0); t < s; ++t)
+                mbar_wait(&full[t % kStages], (t / kStages) & 1u, nullptr, p.err, 0xC02);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            for (uint32_t s = 0; s < nk; ++s) {
+                const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
+                if (!mbar_wait(&sf_ready[st], ph, abort, p.err, 0xC03)) break;
+                tc_fence_after();
+                const uint64_t ad = smem_desc_sw128(sA + st * kATile);
+                const uint64_t bd = smem_desc_sw128(sB + st * kBTile);
+                const uint32_t sfa0 = tmem + kSfCol0 + st * (kSfaCols + kSfbCols);
+                const uint32_t sfb0 = sfa0 + kSfaCols;
+#pragma unroll
+                for (uint32_t k = 0; k < kBK / 64; ++k) {   // 32 packed bytes = 64 K per MMA
+                    const uint32_t g = k >> 1, h = (k & 1u) * 2u;
+                    const uint32_t sfa = (sfa0 + (kBM / 32) * g) | (h << 30);
+                    const uint32_t sfb = (sfb0 + (kBN / 32) * g) | (h << 30);
+                    mma_mxf4(tmem, ad + 2 * k, bd + 2 * k, idesc_mxf4(kBM, kBN, h, h), sfa, sfb, (s | k) != 0u);
+                }
+                mma_commit(&empty[st]);
+            }
+            mma_commit(done);
+        }
+    } else {
+        // ------------------------------------------------ scales into tensor memory
+        const uint32_t quarter = warp & 3;
+        const uint32_t lane_base = (quarter * 32u) << 16;
+        for (uint32_t s = 0; s < nk; ++s) {
+            const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
+            // full[] of stage s follows empty[] of stage s - kStages, so the MMAs
+            // that read this slot's scale columns have completed
+            if (!mbar_wait(&full[st], ph, abort, p.err, 0xC04)) break;
+            tc_fence_after();
+            const uint32_t col = tmem + lane_base + kSfCol0 + st * (kSfaCols + kSfbCols);
+            const uint32_t off = (s & 1u) * 8u;
+            // every lane quarter writes the same copy: lane j of any quarter holds rows 32 i + j
+            uint32_t va[8], b0[8], b1[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                load_u2(sSa + st * kSfaBytes + (32 * i + lane) * kSfRow + off, va[i], va[4 + i]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                load_u2(sSb + st * kSfbBytes + (32 * i + lane) * kSfRow + off, b0[i], b1[i]);
+            tmem_st_x8(col, va);
+            tmem_st_x8(col + kSfaCols, b0);
+            tmem_st_x8(col + kSfaCols + 8, b1);
+            st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sf_ready[st]);
+        }
+        // ---------------------------------------------- epilogue
+        mbar_wait(done, 0, abort, p.err, 0xC05);
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const bool ok = (*abort == 0);
+        tc_fence_after();
+        const uint32_t m = m0 + quarter * 32 + lane;
+        const uint32_t acc = tmem + lane_base;
+        if (ok) {
+            if constexpr (E == EPI_SWIGLU_MX) {
+                const uint32_t c0 = blockIdx.x * 128;   // mid channel of column 0
+#pragma unroll 1
+                for (int cb = 0; cb < 4; ++cb) {
+                    uint32_t g[32], u[32];
+                    tmem_ld_32x32b_x32(acc + cb * 32, g);
+                    tmem_ld_32x32b_x32(acc + 128 + cb * 32, u);
+                    tmem_ld_wait();
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float gf = __uint_as_float(g[i]);
+                        v[i] = __fdividef(gf, 1.0f + __expf(-gf)) * __uint_as_float(u[i]);
+                    }
+                    uint4 pk;
+                    const uint32_t code = mx_quant32(v, pk);
+                    const uint32_t c = c0 + cb * 32;
+                    if (m < p.M && c < p.N) {
+                        *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(p.out) + (size_t)m * (p.ldc / 2) + c / 2) = pk;
+                        p.out_scales[(size_t)m * (p.ldc / 32) + c / 32] = (uint8_t)code;
+                    }
+                }
+            } else {
+                const uint32_t n0 = blockIdx.x * kBN;
+#pragma unroll 1
+                for (int cc = 0; cc < kBN / 32; ++cc) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(acc + cc * 32, v);
+                    tmem_ld_wait();
+                    const uint32_t col = n0 + cc * 32;
+                    if (m < p.M && col < p.N) {
+                        if constexpr (E == EPI_F32) {
+                            float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + (size_t)m * p.ldc + col);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                                     __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                        } else {
+                            uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(p.out) + (size_t)m * p.ldc + col);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                uint32_t w[4];
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    const __half2 h = __floats2half2_rn(__uint_as_float(v[8 * i + 2 * q]),
+                                                                        __uint_as_float(v[8 * i + 2 * q + 1]));
+                                    w[q] = *reinterpret_cast<const uint32_t *>(&h);
+                                }
+                                dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // ---------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        if (*abort) mbar_wait(done, 0, nullptr, p.err, 0xC06);   // let in-flight MMAs drain
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace mxf4
+}  // namespace mpp41

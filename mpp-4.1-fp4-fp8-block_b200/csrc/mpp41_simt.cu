@@ -8,6 +8,7 @@
 
 #include "mpp41_device.cuh"
 #include "mpp41_internal.h"
+#include "mpp41_mx.cuh"
 
 namespace mpp41 {
 
@@ -15,14 +16,8 @@ static unsigned grid_for(size_t work, int block);
 
 // ------------------------------------------------------------------ codecs
 // Hardware conversions: cvt.rn.satfinite.{e2m1x2,e4m3x2,e5m2x2}.f32 round to
-// nearest even and saturate to the largest finite value, which is the
-// behaviour the reference's pack<> shows (main.swift:112-130).
-__device__ __forceinline__ uint32_t enc_e2m1x2(float lo, float hi)
-{
-    uint16_t r;
-    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}" : "=h"(r) : "f"(hi), "f"(lo));
-    return r & 0xFFu;
-}
+// nearest even and saturate to the largest finite value (enc_e2m1x2 is in
+// mpp41_mx.cuh).
 __device__ __forceinline__ uint32_t enc_e4m3x2(float lo, float hi)
 {
     uint16_t r;
@@ -325,7 +320,6 @@ __global__ void quantize_mxfp4_kernel(const In *__restrict__ w, uint32_t rows, u
     for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < blocks; b += (size_t)gridDim.x * blockDim.x) {
         const uint32_t r = (uint32_t)(b / kb), j = (uint32_t)(b % kb);
         float v[32];
-        float amax = 0.0f;
         if constexpr (sizeof(In) == 4) {
             const float4 *src = reinterpret_cast<const float4 *>(w + (size_t)r * depth + (size_t)j * 32);
 #pragma unroll
@@ -346,29 +340,9 @@ __global__ void quantize_mxfp4_kernel(const In *__restrict__ w, uint32_t rows, u
                 }
             }
         }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        int e = 0;
-        uint32_t code = 0;
-        if (amax > 0.0f && isfinite(amax)) {
-            int ex;
-            frexpf(amax, &ex);              // amax = m * 2^ex, m in [0.5, 1): floor(log2) = ex - 1
-            e = ex - 1 - 2;
-            int c = e + 127;
-            c = c < 0 ? 0 : (c > 254 ? 254 : c);
-            code = (uint32_t)c;
-            e = c - 127;
-        }
-        const float inv = ldexpf(1.0f, -e);  // exact power of two
-        uint32_t out[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint32_t word = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) word |= enc_e2m1x2(v[8 * q + 2 * i] * inv, v[8 * q + 2 * i + 1] * inv) << (8 * i);
-            out[q] = word;
-        }
-        *reinterpret_cast<uint4 *>(packed + (size_t)r * (depth / 2) + (size_t)j * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+        uint4 pk;
+        const uint32_t code = mx_quant32(v, pk);
+        *reinterpret_cast<uint4 *>(packed + (size_t)r * (depth / 2) + (size_t)j * 16) = pk;
         scales[b] = (uint8_t)code;
     }
 }

@@ -105,6 +105,9 @@ def lib() -> C.CDLL:
         "mpp41_quantize_mxfp4": ([vp, vp, u32, u32, vp, vp], st),
         "mpp41_quantize_act_mxfp4": ([vp, vp, u32, u32, vp, vp], st),
         "mpp41_quantize_act_s8": ([vp, vp, u32, u32, vp, vp], st),
+        "mpp41_matmul_mxf4": ([vp] * 6 + [u32, u32, u32, C.c_int], st),
+        "mpp41_mlp_w4a4_scratch_bytes": ([u32, u32, u32], sz),
+        "mpp41_mlp_w4a4": ([vp, u32, u32, u32] + [vp] * 8 + [C.c_int, vp], st),
         "mpp41_mlp_noalloc_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp_noalloc": ([C.POINTER(MLPDesc)] + [vp] * 9, st),
         "mpp41_mlp_describe": ([C.c_char_p, u32, u32, u32, C.POINTER(MLPDesc)], st),
@@ -141,6 +144,20 @@ def _check(status: int):
     if status != OK:
         msg = lib().mpp41_last_error()
         raise MPP41Error(status, msg.decode() if msg else "")
+
+
+def w4a4_scratch_bytes(tokens: int, hidden: int, intermediate: int) -> int:
+    return lib().mpp41_mlp_w4a4_scratch_bytes(tokens, hidden, intermediate)
+
+
+def w4a4_scratch_layout(tokens: int, hidden: int, intermediate: int):
+    """Byte offsets of (packed x, x scales, packed mid, mid scales) in the W4A4 scratch."""
+    up = lambda n: (n + 255) & ~255
+    o0 = 0
+    o1 = o0 + up(tokens * hidden // 2)
+    o2 = o1 + up(tokens * hidden // 32)
+    o3 = o2 + up(tokens * intermediate // 2)
+    return o0, o1, o2, o3
 
 
 def has_kernel(name: str) -> bool:
@@ -302,6 +319,16 @@ class Context:
 
     def quantize_act_s8(self, x, tokens: int, hidden: int, q, scale):
         _check(lib().mpp41_quantize_act_s8(self.h, _ptr(x), tokens, hidden, _ptr(q), _ptr(scale)))
+
+    def matmul_mxf4(self, a, sa, b, sb, c, M: int, N: int, K: int, c_f16: bool = False):
+        """W4A4 GEMM: C[M][N] = A[M][K] B[N][K]^T, both MXFP4 (mpp41_matmul_mxf4)."""
+        _check(lib().mpp41_matmul_mxf4(self.h, _ptr(a), _ptr(sa), _ptr(b), _ptr(sb), _ptr(c), M, N, K, int(c_f16)))
+
+    def mlp_w4a4(self, tokens: int, hidden: int, intermediate: int, x, wg, sg, wu, su, wd, sd, out, scratch,
+                 out_f16: bool = False):
+        """One W4A4 MLP layer (mpp41_mlp_w4a4); scratch of w4a4_scratch_bytes()."""
+        _check(lib().mpp41_mlp_w4a4(self.h, tokens, hidden, intermediate, _ptr(x), _ptr(wg), _ptr(sg), _ptr(wu),
+                                    _ptr(su), _ptr(wd), _ptr(sd), _ptr(out), int(out_f16), _ptr(scratch)))
 
     def mlp_benchmark(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out, iterations: int) -> float:
         secs = C.c_double()

@@ -186,6 +186,25 @@ def quantize_mxfp4(w: np.ndarray):
     return packed, scales
 
 
+def w4a4_mlp(x, wg, sg, wu, su, wd, sd):
+    """W4A4 layer restated (no reference counterpart; its MXFP4 decode is
+    MXFP4Kernels.metal:26-29 and docs/MXFP4-MPP41-GUIDE.md:43-55): x is
+    quantized with the OCP-MX rule, gate/up products are exact (fp64),
+    mid = silu(g) * u in fp64 rounded to fp32, then quantized with the same
+    rule; the down product is exact on the decoded quantized mid.
+    Returns (xq, xs, mq, ms, out) with out fp64 [T][H]."""
+    T, H = x.shape
+    I = wg.shape[0]
+    xq, xs = quantize_mxfp4(np.asarray(x, np.float32))
+    xd = decode_weights(W_MXFP4, xq, xs, T, H)
+    g = xd @ decode_weights(W_MXFP4, wg, sg, I, H).T
+    u = xd @ decode_weights(W_MXFP4, wu, su, I, H).T
+    mid = (g / (1.0 + np.exp(-g)) * u).astype(np.float32)
+    mq, ms = quantize_mxfp4(mid)
+    out = decode_weights(W_MXFP4, mq, ms, T, I) @ decode_weights(W_MXFP4, wd, sd, H, I).T
+    return xq, xs, mq, ms, out
+
+
 def baseline_mlp_inputs(T=128, H=1024, I=4096, seed=0):
     """x ~ N(0,1) fp16, weights ~ N(0,0.02) fp32 quantized OCP-MX."""
     rng = np.random.default_rng(seed)
