@@ -279,6 +279,34 @@ mpp41_status mpp41_mlp_w4a4(mpp41_ctx *ctx, uint32_t tokens, uint32_t hidden, ui
                             const uint8_t *wg, const uint8_t *sg, const uint8_t *wu, const uint8_t *su,
                             const uint8_t *wd, const uint8_t *sd, void *out, int out_f16, void *scratch);
 
+/* ---- NVFP4 (the reference emulates it, README.md:383-389): E2M1 elements,
+ *      one UE4M3 scale per 16 along K, one fp32 tensor scale per tensor; on
+ *      the FP4 tensor cores through kind::mxf4nvf4 (block16). Quantization
+ *      (IEEE fp32, round to nearest even): g = amax(tensor) / 2688 (1 if
+ *      zero); s = UE4M3((amax(block16) / 6) / g), saturating; element =
+ *      E2M1(v / (decode(s) * g)); value = element * decode(s) * g.
+ *      - mpp41_quantize_nvfp4 (fp32 weights) / mpp41_quantize_act_nvfp4 (fp16
+ *        activations): packed [rows][depth/2], scales [rows][depth/16],
+ *        *tensor_scale (device float) = g.
+ *      - mpp41_matmul_nvf4: C = (A B^T) * ta * tb; K % 256, N % 32.
+ *      - mpp41_mlp_nvfp4: one W4A4 layer with NVFP4 activations and weights
+ *        (gate/up GEMM -> fp16 silu(g)*u -> NVFP4 -> down GEMM). H % 256,
+ *        I % 256. scratch (mpp41_mlp_nvfp4_scratch_bytes), sections 256-byte
+ *        aligned: packed x [T][H/2], x scales [T][H/16], fp16 mid [T][I],
+ *        packed mid [T][I/2], mid scales [T][I/16], tensor scales {x, mid}. ---- */
+mpp41_status mpp41_quantize_nvfp4(mpp41_ctx *ctx, const float *w, uint32_t rows, uint32_t depth, uint8_t *packed,
+                                  uint8_t *scales, float *tensor_scale);
+mpp41_status mpp41_quantize_act_nvfp4(mpp41_ctx *ctx, const void *x, uint32_t tokens, uint32_t hidden,
+                                      uint8_t *packed, uint8_t *scales, float *tensor_scale);
+mpp41_status mpp41_matmul_nvf4(mpp41_ctx *ctx, const uint8_t *a, const uint8_t *sa, const float *ta,
+                               const uint8_t *b, const uint8_t *sb, const float *tb, void *c, uint32_t M, uint32_t N,
+                               uint32_t K, int c_f16);
+size_t mpp41_mlp_nvfp4_scratch_bytes(uint32_t tokens, uint32_t hidden, uint32_t intermediate);
+mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t tokens, uint32_t hidden, uint32_t intermediate, const void *x,
+                             const uint8_t *wg, const uint8_t *sg, const float *tg, const uint8_t *wu,
+                             const uint8_t *su, const float *tu, const uint8_t *wd, const uint8_t *sd,
+                             const float *td, void *out, int out_f16, void *scratch);
+
 /* ---- tensor parallelism (no counterpart in the
  *      single-GPU reference). Rank r of P holds rows [r*I/P, (r+1)*I/P) of the
  *      gate and up weights (and their scale rows) and the same columns of the

@@ -457,6 +457,7 @@ mpp41_status mpp41_create(int device, mpp41_ctx **out)
     cudaError_t e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&c->err, sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&c->amax, sizeof(uint32_t));
     c->sync_words = 1u << 16;
     if (e == cudaSuccess) e = cudaMalloc(&c->sync, c->sync_words * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(c->sync, 0, c->sync_words * sizeof(uint32_t));
@@ -477,6 +478,7 @@ void mpp41_destroy(mpp41_ctx *ctx)
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->err);
+    cudaFree(ctx->amax);
     cudaFree(ctx->sync);
     cudaEventDestroy(ctx->ev0);
     cudaEventDestroy(ctx->ev1);
@@ -924,6 +926,118 @@ mpp41_status mpp41_mlp_w4a4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I, 
     d.epi = out_f16 ? 1 : 0;
     d.err = ctx->err;
     return enqueue_mxf4(ctx, d, "W4A4 down GEMM");
+}
+
+// ------------------------------------------------------------------ NVFP4
+mpp41_status mpp41_quantize_nvfp4(mpp41_ctx *ctx, const float *w, uint32_t rows, uint32_t depth, uint8_t *packed,
+                                  uint8_t *scales, float *tensor_scale)
+{
+    NEED(ctx);
+    if (depth % 16) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "depth must be a multiple of 16");
+    if (!rows || !depth) return MPP41_OK;
+    if (!w || !packed || !scales || !tensor_scale) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if (!al16(w) || (reinterpret_cast<uintptr_t>(packed) & 7u))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "w must be 16-byte and packed 8-byte aligned");
+    CK(launch_quantize_nvfp4(w, false, rows, depth, ctx->amax, packed, scales, tensor_scale, ctx->stream),
+       "quantize NVFP4");
+    return MPP41_OK;
+}
+
+mpp41_status mpp41_quantize_act_nvfp4(mpp41_ctx *ctx, const void *x, uint32_t tokens, uint32_t hidden,
+                                      uint8_t *packed, uint8_t *scales, float *tensor_scale)
+{
+    NEED(ctx);
+    if (hidden % 16) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "hidden must be a multiple of 16");
+    if (!tokens || !hidden) return MPP41_OK;
+    if (!x || !packed || !scales || !tensor_scale) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if ((reinterpret_cast<uintptr_t>(packed) & 7u)) return fail(MPP41_ERR_INVALID_ARGUMENT, "packed must be 8-byte aligned");
+    CK(launch_quantize_nvfp4(x, true, tokens, hidden, ctx->amax, packed, scales, tensor_scale, ctx->stream),
+       "quantize NVFP4 activations");
+    return MPP41_OK;
+}
+
+mpp41_status mpp41_matmul_nvf4(mpp41_ctx *ctx, const uint8_t *a, const uint8_t *sa, const float *ta,
+                               const uint8_t *b, const uint8_t *sb, const float *tb, void *c, uint32_t M, uint32_t N,
+                               uint32_t K, int c_f16)
+{
+    NEED(ctx);
+    if (!M || !N || !K) return MPP41_OK;
+    if (!a || !sa || !ta || !b || !sb || !tb || !c) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if (!al16(a) || !al16(sa) || !al16(b) || !al16(sb) || !al16(c))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "buffers must be 16-byte aligned");
+    MxLaunch L{};
+    L.a = a; L.sa = sa;
+    L.b0 = L.b1 = b; L.sb0 = L.sb1 = sb;
+    L.b_rows = N; L.b0_row0 = 0; L.b1_row0 = 128; L.b_row_step = 256;
+    L.out = c; L.M = M; L.N = N; L.K = K; L.ldc = N;
+    L.epi = c_f16 ? 1 : 0;
+    L.nv = true; L.ts_a = ta; L.ts_b0 = L.ts_b1 = tb;
+    L.err = ctx->err;
+    return enqueue_mxf4(ctx, L, "nvf4 GEMM");
+}
+
+namespace {
+struct NvScratch {
+    uint8_t *xq, *xs, *mq, *ms;
+    __half *mid;
+    float *ts;   // [0] x's tensor scale, [1] mid's
+    size_t bytes;
+};
+NvScratch nv_scratch(void *base, uint32_t T, uint32_t H, uint32_t I)
+{
+    NvScratch s{};
+    uint8_t *p = static_cast<uint8_t *>(base);
+    size_t o = 0;
+    auto take = [&](size_t n) { uint8_t *r = p ? p + o : nullptr; o += up256(n); return r; };
+    s.xq = take((size_t)T * H / 2);
+    s.xs = take((size_t)T * H / 16);
+    s.mid = reinterpret_cast<__half *>(take((size_t)T * I * 2));
+    s.mq = take((size_t)T * I / 2);
+    s.ms = take((size_t)T * I / 16);
+    s.ts = reinterpret_cast<float *>(take(2 * sizeof(float)));
+    s.bytes = o;
+    return s;
+}
+}  // namespace
+
+size_t mpp41_mlp_nvfp4_scratch_bytes(uint32_t T, uint32_t H, uint32_t I) { return nv_scratch(nullptr, T, H, I).bytes; }
+
+mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I, const void *x, const uint8_t *wg,
+                             const uint8_t *sg, const float *tg, const uint8_t *wu, const uint8_t *su,
+                             const float *tu, const uint8_t *wd, const uint8_t *sd, const float *td, void *out,
+                             int out_f16, void *scratch)
+{
+    NEED(ctx);
+    if (!T || !H || !I) return MPP41_OK;
+    if (H % 256 || I % 256) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "hidden and intermediate must be multiples of 256");
+    if (!x || !wg || !sg || !tg || !wu || !su || !tu || !wd || !sd || !td || !out || !scratch)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if (!al16(x) || !al16(wg) || !al16(sg) || !al16(wu) || !al16(su) || !al16(wd) || !al16(sd) || !al16(out) ||
+        (reinterpret_cast<uintptr_t>(scratch) & 255u))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "buffers must be 16-byte aligned (scratch 256-byte)");
+    const NvScratch s = nv_scratch(scratch, T, H, I);
+    cudaStream_t st = ctx->stream;
+    CK(launch_quantize_nvfp4(x, true, T, H, ctx->amax, s.xq, s.xs, s.ts, st), "quantize activations");
+    MxLaunch g{};
+    g.a = s.xq; g.sa = s.xs;
+    g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
+    g.b_rows = I; g.b0_row0 = 0; g.b1_row0 = 0; g.b_row_step = 128;
+    g.out = s.mid; g.M = T; g.N = I; g.K = H; g.ldc = I;
+    g.epi = 3;
+    g.nv = true; g.ts_a = s.ts; g.ts_b0 = tg; g.ts_b1 = tu;
+    g.err = ctx->err;
+    mpp41_status r = enqueue_mxf4(ctx, g, "NVFP4 gate/up GEMM");
+    if (r != MPP41_OK) return r;
+    CK(launch_quantize_nvfp4(s.mid, true, T, I, ctx->amax, s.mq, s.ms, s.ts + 1, st), "quantize mid");
+    MxLaunch d{};
+    d.a = s.mq; d.sa = s.ms;
+    d.b0 = d.b1 = wd; d.sb0 = d.sb1 = sd;
+    d.b_rows = H; d.b0_row0 = 0; d.b1_row0 = 128; d.b_row_step = 256;
+    d.out = out; d.M = T; d.N = H; d.K = I; d.ldc = H;
+    d.epi = out_f16 ? 1 : 0;
+    d.nv = true; d.ts_a = s.ts + 1; d.ts_b0 = d.ts_b1 = td;
+    d.err = ctx->err;
+    return enqueue_mxf4(ctx, d, "NVFP4 down GEMM");
 }
 
 mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,

@@ -82,7 +82,8 @@ int launch_f32_gemm(const F32Launch &L, cudaStream_t st, const char **why);
 // against B rows taken from two maps (b0 rows b0_row0 + t * b_row_step and b1
 // rows b1_row0 + t * b_row_step, 128 each, for column tile t). epi 0: fp32 C,
 // 1: fp16 C, 2: silu(gate) * up re-quantized to MXFP4 (out = packed mid
-// [M][ldc/2], out_scales = [M][ldc/32]).
+// [M][ldc/2], out_scales = [M][ldc/32]), 3: silu(gate) * up as fp16 [M][ldc].
+// nv: NVFP4 operands (scales [rows][K/16] UE4M3; C scaled by the tensor scales).
 struct MxLaunch {
     const void *a, *sa;
     const void *b0, *sb0, *b1, *sb1;
@@ -91,6 +92,8 @@ struct MxLaunch {
     uint8_t *out_scales;
     uint32_t M, N, K, ldc;
     int epi;
+    bool nv;                                // NVFP4 operands (UE4M3 per 16 + fp32 tensor scales)
+    const float *ts_a, *ts_b0, *ts_b1;      // NVFP4 tensor scales (device)
     uint32_t *err;
 };
 int launch_mxf4_gemm(const MxLaunch &L, cudaStream_t st, const char **why);
@@ -107,6 +110,10 @@ cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth,
 // Activation quantization (fp16 in): OCP-MX MXFP4, and per-token int8 absmax.
 cudaError_t launch_quantize_mxfp4_f16(const void *x, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
                                       cudaStream_t st);
+// NVFP4 quantization (fp32 or fp16 in) with a computed tensor scale; amax_tmp
+// is one device word of scratch.
+cudaError_t launch_quantize_nvfp4(const void *x, bool f16_in, uint32_t rows, uint32_t depth, uint32_t *amax_tmp,
+                                  uint8_t *packed, uint8_t *scales, float *tensor_scale, cudaStream_t st);
 cudaError_t launch_quantize_act_s8(const void *x, uint32_t tokens, uint32_t hidden, int8_t *q, float *scale,
                                    cudaStream_t st);
 // Returns 0 on success, 1 for an unsupported combination/shape, 2 for a CUDA error.
@@ -174,6 +181,7 @@ struct mpp41_ctx {
     cudaStream_t own_stream;
     cudaStream_t stream;
     uint32_t *err;          // device error word
+    uint32_t *amax;         // one word of scratch for tensor-maximum reductions
     uint32_t *sync;         // grid-wide counters of the fused layer kernel (kept zero between launches)
     size_t sync_words;
     unsigned long long *trace;

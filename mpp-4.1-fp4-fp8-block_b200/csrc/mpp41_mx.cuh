@@ -3,6 +3,7 @@
 // bytes for the same fp32 block.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cstdint>
 
 namespace mpp41 {
@@ -46,6 +47,57 @@ __device__ __forceinline__ uint32_t mx_quant32(const float (&v)[32], uint4 &pack
         out[q] = word;
     }
     packed = make_uint4(out[0], out[1], out[2], out[3]);
+    return code;
+}
+
+// ------------------------------------------------------------------ NVFP4
+// NVFP4: E2M1 elements, one UE4M3 scale per 16 and an fp32 tensor scale g.
+// Recipe (all steps IEEE fp32, round to nearest even):
+//   g = amax(tensor) / (6 * 448)            (1 for an all-zero tensor)
+//   s = E4M3((amax(block) / 6) / g)         (saturating; 0 when it underflows)
+//   q = E2M1(v / (decode(s) * g))           (0 when decode(s) == 0)
+// so value = q * decode(s) * g, and the largest block scale lands on 448.
+__host__ __device__ __forceinline__ float nvfp4_tensor_scale(float amax)
+{
+    return (amax > 0.0f && amax <= 3.4e38f) ? amax / 2688.0f : 1.0f;
+}
+
+__device__ __forceinline__ uint32_t enc_ue4m3(float s)
+{
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(s));
+    return r & 0xFFu;
+}
+
+__device__ __forceinline__ float dec_ue4m3(uint32_t code)
+{
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"((uint16_t)code));
+    return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+}
+
+// One block of 16 values -> 8 packed bytes (low nibble = even index) and the
+// UE4M3 scale byte.
+__device__ __forceinline__ uint32_t nv_quant16(const float (&v)[16], float g, uint2 &packed)
+{
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const uint32_t code = enc_ue4m3(__fdiv_rn(__fdiv_rn(amax, 6.0f), g));
+    const float denom = __fmul_rn(dec_ue4m3(code), g);
+    uint32_t out[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = denom > 0.0f ? __fdiv_rn(v[8 * q + 2 * i], denom) : 0.0f;
+            const float b = denom > 0.0f ? __fdiv_rn(v[8 * q + 2 * i + 1], denom) : 0.0f;
+            word |= enc_e2m1x2(a, b) << (8 * i);
+        }
+        out[q] = word;
+    }
+    packed = make_uint2(out[0], out[1]);
     return code;
 }
 

@@ -15,7 +15,15 @@
 // two scales) reads bytes 2h and 2h+1: the byte offset rides in address bits
 // 30-31 and in the instruction descriptor's scale-factor id.
 //
-// Epilogues: fp32 or fp16 C, or (SWIGLU_MX) the gate/up layer of a W4A4 MLP:
+// NVFP4 (NV = true): the same tiles with E2M1 elements, one UE4M3 scale per
+// 16 along k and an fp32 tensor scale per operand, on
+// kind::mxf4nvf4.block_scale.block16: an MMA (K = 64) takes four scales per
+// row, one full 32-bit column, so stage k-group k of row 32 i + j sits in
+// column base + R/32 * k + i with no byte offset. The two tensor scales
+// multiply the accumulator in the epilogue.
+//
+// Epilogues: fp32 or fp16 C, SWIGLU_F16 (silu(g) * u as fp16, the columns
+// arranged as below), or (SWIGLU_MX) the gate/up layer of a W4A4 MLP:
 // B rows 0..127 of the tile are gate rows, 128..255 the up rows of the same
 // 128 channels; each thread owns one token row, forms silu(g) * u and
 // re-quantizes it to MXFP4 in registers (32-blocks never straddle threads), so
@@ -37,7 +45,7 @@
 namespace mpp41 {
 namespace mxf4 {
 
-enum Epi { EPI_F32 = 0, EPI_F16 = 1, EPI_SWIGLU_MX = 2 };
+enum Epi { EPI_F32 = 0, EPI_F16 = 1, EPI_SWIGLU_MX = 2, EPI_SWIGLU_F16 = 3 };
 
 constexpr int kBM = 128;          // rows of A per tile (MMA M)
 constexpr int kBN = 256;          // rows of B per tile (MMA N)
@@ -47,16 +55,20 @@ constexpr int kThreads = 192;
 constexpr uint32_t kATile = kBM * 128;      // 16 KB
 constexpr uint32_t kBHalf = 128 * 128;      // 16 KB: 128 B rows
 constexpr uint32_t kBTile = kBN * 128;      // 32 KB
-// Scales: a TMA box needs a 16-byte inner extent, so each stage loads the
-// 16-byte strip holding its own 8 scale bytes per row and the neighbour's.
+// Scales: a TMA box needs a 16-byte inner extent. MXFP4 has 8 scale bytes per
+// row per stage, so each stage loads the 16-byte strip holding its own and the
+// neighbour's; NVFP4 has exactly 16.
 constexpr uint32_t kSfRow = 16;
 constexpr uint32_t kSfaBytes = kBM * kSfRow;
 constexpr uint32_t kSfbBytes = kBN * kSfRow;
-constexpr uint32_t kSfaCols = kBM / 32 * 2, kSfbCols = kBN / 32 * 2;   // 8 and 16 columns per stage
+// tensor-memory columns per stage: MXFP4 8 (A) + 16 (B), NVFP4 16 + 32
+template <bool NV> struct SfCols {
+    static constexpr uint32_t kA = kBM / 32 * (NV ? 4 : 2), kB = kBN / 32 * (NV ? 4 : 2);
+};
 constexpr uint32_t kAccCols = kBN;
 constexpr uint32_t kSfCol0 = kAccCols;                                  // scale ring after the accumulator
 constexpr uint32_t kTmemCols = 512;
-static_assert(kSfCol0 + kStages * (kSfaCols + kSfbCols) <= kTmemCols, "tensor memory");
+static_assert(kSfCol0 + kStages * (SfCols<true>::kA + SfCols<true>::kB) <= kTmemCols, "tensor memory");
 
 constexpr uint32_t kOffB = kStages * kATile;
 constexpr uint32_t kOffSfa = kOffB + kStages * kBTile;
@@ -71,6 +83,23 @@ __host__ __device__ constexpr uint32_t idesc_mxf4(int M, int N, uint32_t sfa_id,
 {
     return (sfb_id << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
            ((uint32_t)(M >> 4) << 24) | (sfa_id << 29);
+}
+
+// kind::mxf4nvf4 block16: E2M1 x E2M1, UE4M3 scales (bit 23 clear), K = 64.
+__host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N)
+{
+    return (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa, uint32_t sfb, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
 }
 
 __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -104,6 +133,8 @@ struct Params {
     void *out;                   // fp32 / fp16 [M][ldc]; SWIGLU_MX: packed mid [M][ldc/2]
     uint8_t *out_scales;         // SWIGLU_MX: mid scales [M][ldc/32]
     uint32_t M, N, K, ldc;       // N = columns written (SWIGLU_MX: mid channels)
+    // NVFP4: fp32 tensor scales (device) of A and of the two B maps
+    const float *ts_a, *ts_b0, *ts_b1;
     uint32_t *err;
 };
 
@@ -114,9 +145,10 @@ __device__ __forceinline__ void load_u2(const uint8_t *p, uint32_t &lo, uint32_t
     hi = v.y;
 }
 
-template <int E>
+template <int E, bool NV>
 __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_constant__ Params p)
 {
+    constexpr uint32_t kSfaCols = SfCols<NV>::kA, kSfbCols = SfCols<NV>::kB;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem, *sB = smem + kOffB, *sSa = smem + kOffSfa, *sSb = smem + kOffSfb;
@@ -161,7 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                 const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
                 if (!mbar_wait(&empty[st], ph ^ 1u, abort, p.err, 0xC01)) break;
                 mbar_arrive_expect_tx(&full[st], kATile + kBTile + kSfaBytes + kSfbBytes);
-                const int32_t kb = (int32_t)(s * (kBK / 2)), ks = (int32_t)((s >> 1) * kSfRow);
+                const int32_t kb = (int32_t)(s * (kBK / 2));
+                const int32_t ks = (int32_t)((NV ? s : (s >> 1)) * kSfRow);
                 tma_load_2d(sA + st * kATile, &p.tm_a, kb, (int32_t)m0, &full[st]);
                 tma_load_2d(sB + st * kBTile, &p.tm_b0, kb, rb0, &full[st]);
                 tma_load_2d(sB + st * kBTile + kBHalf, &p.tm_b1, kb, rb1, &full[st]);
@@ -186,10 +219,15 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                 const uint32_t sfb0 = sfa0 + kSfaCols;
 #pragma unroll
                 for (uint32_t k = 0; k < kBK / 64; ++k) {   // 32 packed bytes = 64 K per MMA
-                    const uint32_t g = k >> 1, h = (k & 1u) * 2u;
-                    const uint32_t sfa = (sfa0 + (kBM / 32) * g) | (h << 30);
-                    const uint32_t sfb = (sfb0 + (kBN / 32) * g) | (h << 30);
-                    mma_mxf4(tmem, ad + 2 * k, bd + 2 * k, idesc_mxf4(kBM, kBN, h, h), sfa, sfb, (s | k) != 0u);
+                    if constexpr (NV) {
+                        mma_nvf4(tmem, ad + 2 * k, bd + 2 * k, idesc_nvf4(kBM, kBN), sfa0 + (kBM / 32) * k,
+                                 sfb0 + (kBN / 32) * k, (s | k) != 0u);
+                    } else {
+                        const uint32_t g = k >> 1, h = (k & 1u) * 2u;
+                        const uint32_t sfa = (sfa0 + (kBM / 32) * g) | (h << 30);
+                        const uint32_t sfb = (sfb0 + (kBN / 32) * g) | (h << 30);
+                        mma_mxf4(tmem, ad + 2 * k, bd + 2 * k, idesc_mxf4(kBM, kBN, h, h), sfa, sfb, (s | k) != 0u);
+                    }
                 }
                 mma_commit(&empty[st]);
             }
@@ -206,18 +244,46 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
             if (!mbar_wait(&full[st], ph, abort, p.err, 0xC04)) break;
             tc_fence_after();
             const uint32_t col = tmem + lane_base + kSfCol0 + st * (kSfaCols + kSfbCols);
-            const uint32_t off = (s & 1u) * 8u;
             // every lane quarter writes the same copy: lane j of any quarter holds rows 32 i + j
-            uint32_t va[8], b0[8], b1[8];
+            if constexpr (NV) {
+                uint32_t va[16], vb[32];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                load_u2(sSa + st * kSfaBytes + (32 * i + lane) * kSfRow + off, va[i], va[4 + i]);
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(sSa + st * kSfaBytes + (32 * i + lane) * kSfRow);
+                    va[i] = v.x; va[4 + i] = v.y; va[8 + i] = v.z; va[12 + i] = v.w;
+                }
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                load_u2(sSb + st * kSfbBytes + (32 * i + lane) * kSfRow + off, b0[i], b1[i]);
-            tmem_st_x8(col, va);
-            tmem_st_x8(col + kSfaCols, b0);
-            tmem_st_x8(col + kSfaCols + 8, b1);
+                for (int i = 0; i < 8; ++i) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(sSb + st * kSfbBytes + (32 * i + lane) * kSfRow);
+                    vb[i] = v.x; vb[8 + i] = v.y; vb[16 + i] = v.z; vb[24 + i] = v.w;
+                }
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    uint32_t t[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) t[i] = va[8 * q + i];
+                    tmem_st_x8(col + 8 * q, t);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t t[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) t[i] = vb[8 * q + i];
+                    tmem_st_x8(col + kSfaCols + 8 * q, t);
+                }
+            } else {
+                const uint32_t off = (s & 1u) * 8u;
+                uint32_t va[8], b0[8], b1[8];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    load_u2(sSa + st * kSfaBytes + (32 * i + lane) * kSfRow + off, va[i], va[4 + i]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    load_u2(sSb + st * kSfbBytes + (32 * i + lane) * kSfRow + off, b0[i], b1[i]);
+                tmem_st_x8(col, va);
+                tmem_st_x8(col + kSfaCols, b0);
+                tmem_st_x8(col + kSfaCols + 8, b1);
+            }
             st_wait();
             tc_fence_before();
             __syncwarp();
@@ -230,8 +296,13 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
         tc_fence_after();
         const uint32_t m = m0 + quarter * 32 + lane;
         const uint32_t acc = tmem + lane_base;
+        float alpha0 = 1.0f, alpha1 = 1.0f;   // scale of the tile's first / second 128 columns
+        if constexpr (NV) {
+            alpha0 = *p.ts_a * *p.ts_b0;
+            alpha1 = *p.ts_a * *p.ts_b1;
+        }
         if (ok) {
-            if constexpr (E == EPI_SWIGLU_MX) {
+            if constexpr (E == EPI_SWIGLU_MX || E == EPI_SWIGLU_F16) {
                 const uint32_t c0 = blockIdx.x * 128;   // mid channel of column 0
 #pragma unroll 1
                 for (int cb = 0; cb < 4; ++cb) {
@@ -242,15 +313,29 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                     float v[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        const float gf = __uint_as_float(g[i]);
-                        v[i] = __fdividef(gf, 1.0f + __expf(-gf)) * __uint_as_float(u[i]);
+                        const float gf = __uint_as_float(g[i]) * alpha0;
+                        v[i] = __fdividef(gf, 1.0f + __expf(-gf)) * (__uint_as_float(u[i]) * alpha1);
                     }
-                    uint4 pk;
-                    const uint32_t code = mx_quant32(v, pk);
                     const uint32_t c = c0 + cb * 32;
-                    if (m < p.M && c < p.N) {
-                        *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(p.out) + (size_t)m * (p.ldc / 2) + c / 2) = pk;
-                        p.out_scales[(size_t)m * (p.ldc / 32) + c / 32] = (uint8_t)code;
+                    if constexpr (E == EPI_SWIGLU_MX) {
+                        uint4 pk;
+                        const uint32_t code = mx_quant32(v, pk);
+                        if (m < p.M && c < p.N) {
+                            *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(p.out) + (size_t)m * (p.ldc / 2) + c / 2) = pk;
+                            p.out_scales[(size_t)m * (p.ldc / 32) + c / 32] = (uint8_t)code;
+                        }
+                    } else if (m < p.M && c < p.N) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(p.out) + (size_t)m * p.ldc + c);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const __half2 h = __floats2half2_rn(v[8 * i + 2 * q], v[8 * i + 2 * q + 1]);
+                                w[q] = *reinterpret_cast<const uint32_t *>(&h);
+                            }
+                            dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
                     }
                 }
             } else {
@@ -260,6 +345,11 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(acc + cc * 32, v);
                     tmem_ld_wait();
+                    if constexpr (NV) {
+                        const float alpha = cc < 4 ? alpha0 : alpha1;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+                    }
                     const uint32_t col = n0 + cc * 32;
                     if (m < p.M && col < p.N) {
                         if constexpr (E == EPI_F32) {

@@ -347,6 +347,76 @@ __global__ void quantize_mxfp4_kernel(const In *__restrict__ w, uint32_t rows, u
     }
 }
 
+// ------------------------------------------------------------------ NVFP4 quantizer
+// Two passes: the tensor's absolute maximum (a block reduction, then one
+// atomicMax per block on the float's bits, which order like unsigned
+// integers for non-negative values), then one thread per 16-block applying
+// nv_quant16 with g from that maximum; thread 0 also stores g.
+template <typename In>
+__device__ __forceinline__ float load_f(const In *p, size_t i)
+{
+    if constexpr (sizeof(In) == 4) return p[i];
+    else return __half2float(p[i]);
+}
+
+template <typename In>
+__global__ void absmax_kernel(const In *__restrict__ x, size_t n, uint32_t *__restrict__ amax_bits)
+{
+    __shared__ float red[32];
+    float m = 0.0f;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(load_f(x, i)));
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        m = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0f;
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));
+    }
+}
+
+template <typename In>
+__global__ void quantize_nvfp4_kernel(const In *__restrict__ w, uint32_t rows, uint32_t depth,
+                                      const uint32_t *__restrict__ amax_bits, uint8_t *__restrict__ packed,
+                                      uint8_t *__restrict__ scales, float *__restrict__ tensor_scale)
+{
+    const float g = nvfp4_tensor_scale(__uint_as_float(*amax_bits));
+    if (blockIdx.x == 0 && threadIdx.x == 0) *tensor_scale = g;
+    const uint32_t kb = depth / 16;
+    const size_t blocks = (size_t)rows * kb;
+    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < blocks; b += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t r = (uint32_t)(b / kb), j = (uint32_t)(b % kb);
+        const In *src = w + (size_t)r * depth + (size_t)j * 16;
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = load_f(src, i);
+        uint2 pk;
+        const uint32_t code = nv_quant16(v, g, pk);
+        *reinterpret_cast<uint2 *>(packed + (size_t)r * (depth / 2) + (size_t)j * 8) = pk;
+        scales[b] = (uint8_t)code;
+    }
+}
+
+cudaError_t launch_quantize_nvfp4(const void *x, bool f16_in, uint32_t rows, uint32_t depth, uint32_t *amax_tmp,
+                                  uint8_t *packed, uint8_t *scales, float *tensor_scale, cudaStream_t st)
+{
+    const size_t n = (size_t)rows * depth;
+    cudaError_t e = cudaMemsetAsync(amax_tmp, 0, sizeof(uint32_t), st);
+    if (e != cudaSuccess) return e;
+    const unsigned g1 = grid_for(n, 256) < 148u * 4u ? grid_for(n, 256) : 148u * 4u;
+    if (f16_in) {
+        absmax_kernel<__half><<<g1, 256, 0, st>>>(static_cast<const __half *>(x), n, amax_tmp);
+        quantize_nvfp4_kernel<__half><<<grid_for(n / 16, 256), 256, 0, st>>>(
+            static_cast<const __half *>(x), rows, depth, amax_tmp, packed, scales, tensor_scale);
+    } else {
+        absmax_kernel<float><<<g1, 256, 0, st>>>(static_cast<const float *>(x), n, amax_tmp);
+        quantize_nvfp4_kernel<float><<<grid_for(n / 16, 256), 256, 0, st>>>(
+            static_cast<const float *>(x), rows, depth, amax_tmp, packed, scales, tensor_scale);
+    }
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
                                   cudaStream_t st)

@@ -108,6 +108,11 @@ def lib() -> C.CDLL:
         "mpp41_matmul_mxf4": ([vp] * 6 + [u32, u32, u32, C.c_int], st),
         "mpp41_mlp_w4a4_scratch_bytes": ([u32, u32, u32], sz),
         "mpp41_mlp_w4a4": ([vp, u32, u32, u32] + [vp] * 8 + [C.c_int, vp], st),
+        "mpp41_quantize_nvfp4": ([vp, vp, u32, u32, vp, vp, vp], st),
+        "mpp41_quantize_act_nvfp4": ([vp, vp, u32, u32, vp, vp, vp], st),
+        "mpp41_matmul_nvf4": ([vp] * 8 + [u32, u32, u32, C.c_int], st),
+        "mpp41_mlp_nvfp4_scratch_bytes": ([u32, u32, u32], sz),
+        "mpp41_mlp_nvfp4": ([vp, u32, u32, u32] + [vp] * 11 + [C.c_int, vp], st),
         "mpp41_mlp_noalloc_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp_noalloc": ([C.POINTER(MLPDesc)] + [vp] * 9, st),
         "mpp41_mlp_describe": ([C.c_char_p, u32, u32, u32, C.POINTER(MLPDesc)], st),
@@ -158,6 +163,23 @@ def w4a4_scratch_layout(tokens: int, hidden: int, intermediate: int):
     o2 = o1 + up(tokens * hidden // 32)
     o3 = o2 + up(tokens * intermediate // 2)
     return o0, o1, o2, o3
+
+
+def nvfp4_scratch_bytes(tokens: int, hidden: int, intermediate: int) -> int:
+    return lib().mpp41_mlp_nvfp4_scratch_bytes(tokens, hidden, intermediate)
+
+
+def nvfp4_scratch_layout(tokens: int, hidden: int, intermediate: int):
+    """Byte offsets of (packed x, x scales, fp16 mid, packed mid, mid scales, tensor scales) in the NVFP4 scratch."""
+    up = lambda n: (n + 255) & ~255
+    sizes = [tokens * hidden // 2, tokens * hidden // 16, tokens * intermediate * 2, tokens * intermediate // 2,
+             tokens * intermediate // 16]
+    offs, o = [], 0
+    for n in sizes:
+        offs.append(o)
+        o += up(n)
+    offs.append(o)
+    return tuple(offs)
 
 
 def has_kernel(name: str) -> bool:
@@ -323,6 +345,25 @@ class Context:
     def matmul_mxf4(self, a, sa, b, sb, c, M: int, N: int, K: int, c_f16: bool = False):
         """W4A4 GEMM: C[M][N] = A[M][K] B[N][K]^T, both MXFP4 (mpp41_matmul_mxf4)."""
         _check(lib().mpp41_matmul_mxf4(self.h, _ptr(a), _ptr(sa), _ptr(b), _ptr(sb), _ptr(c), M, N, K, int(c_f16)))
+
+    def quantize_nvfp4(self, w, rows: int, depth: int, packed, scales, tensor_scale):
+        """fp32 weights -> NVFP4 (mpp41_quantize_nvfp4); tensor_scale is a device float."""
+        _check(lib().mpp41_quantize_nvfp4(self.h, _ptr(w), rows, depth, _ptr(packed), _ptr(scales), _ptr(tensor_scale)))
+
+    def quantize_act_nvfp4(self, x, tokens: int, hidden: int, packed, scales, tensor_scale):
+        _check(lib().mpp41_quantize_act_nvfp4(self.h, _ptr(x), tokens, hidden, _ptr(packed), _ptr(scales),
+                                              _ptr(tensor_scale)))
+
+    def matmul_nvf4(self, a, sa, ta, b, sb, tb, c, M: int, N: int, K: int, c_f16: bool = False):
+        _check(lib().mpp41_matmul_nvf4(self.h, _ptr(a), _ptr(sa), _ptr(ta), _ptr(b), _ptr(sb), _ptr(tb), _ptr(c),
+                                       M, N, K, int(c_f16)))
+
+    def mlp_nvfp4(self, tokens: int, hidden: int, intermediate: int, x, wg, sg, tg, wu, su, tu, wd, sd, td, out,
+                  scratch, out_f16: bool = False):
+        """One NVFP4 W4A4 layer (mpp41_mlp_nvfp4); scratch of nvfp4_scratch_bytes()."""
+        _check(lib().mpp41_mlp_nvfp4(self.h, tokens, hidden, intermediate, _ptr(x), _ptr(wg), _ptr(sg), _ptr(tg),
+                                     _ptr(wu), _ptr(su), _ptr(tu), _ptr(wd), _ptr(sd), _ptr(td), _ptr(out),
+                                     int(out_f16), _ptr(scratch)))
 
     def mlp_w4a4(self, tokens: int, hidden: int, intermediate: int, x, wg, sg, wu, su, wd, sd, out, scratch,
                  out_f16: bool = False):

@@ -652,3 +652,57 @@ void orc_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *
         }
     }
 }
+
+/* NVFP4 (no reference counterpart beyond its emulation note, README.md:383-389):
+ * E2M1 elements, one UE4M3 scale per 16 along K, one fp32 tensor scale g.
+ * Every step is an IEEE single-precision operation rounded to nearest even:
+ *   g = amax(tensor) / 2688 (6 * 448), or 1 for an all-zero tensor;
+ *   s = UE4M3((amax(block) / 6) / g), saturating at 448;
+ *   element = E2M1(v / (decode(s) * g)), or 0 when decode(s) * g == 0. */
+float orc_nvfp4_tensor_scale(const float *w, size_t n)
+{
+    float amax = 0.0f;
+    for (size_t i = 0; i < n; ++i) amax = fmaxf(amax, fabsf(w[i]));
+    return (amax > 0.0f && isfinite(amax)) ? amax / 2688.0f : 1.0f;
+}
+
+void orc_quantize_nvfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
+                        float *tensor_scale)
+{
+    const float g = orc_nvfp4_tensor_scale(w, (size_t)rows * depth);
+    *tensor_scale = g;
+    for (uint32_t r = 0; r < rows; ++r) {
+        for (uint32_t j = 0; j < depth / 16; ++j) {
+            const float *b = w + (size_t)r * depth + (size_t)j * 16;
+            float amax = 0.0f;
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(b[i]));
+            volatile float s = amax / 6.0f;
+            s = s / g;
+            const uint8_t code = (uint8_t)(orc_e4m3_encode(s) & 0x7f);
+            scales[(size_t)r * (depth / 16) + j] = code;
+            volatile float denom = orc_e4m3_decode(code) * g;
+            for (int i = 0; i < 16; i += 2) {
+                float a = 0.0f, c = 0.0f;
+                if (denom > 0.0f) {
+                    volatile float qa = b[i] / denom, qc = b[i + 1] / denom;
+                    a = qa;
+                    c = qc;
+                }
+                const uint8_t lo = orc_e2m1_encode(a), hi = orc_e2m1_encode(c);
+                packed[(size_t)r * (depth / 2) + (size_t)j * 8 + i / 2] = (uint8_t)(lo | (hi << 4));
+            }
+        }
+    }
+}
+
+void orc_decode_nvfp4(const uint8_t *packed, const uint8_t *scales, float tensor_scale, uint32_t rows,
+                      uint32_t depth, double *out)
+{
+    for (uint32_t r = 0; r < rows; ++r)
+        for (uint32_t k = 0; k < depth; ++k) {
+            const uint8_t byte = packed[(size_t)r * (depth / 2) + k / 2];
+            const double e = orc_e2m1_decode((uint8_t)(byte >> ((k & 1) * 4)));
+            const double s = orc_e4m3_decode(scales[(size_t)r * (depth / 16) + k / 16]);
+            out[(size_t)r * depth + k] = e * s * (double)tensor_scale;
+        }
+}

@@ -89,6 +89,11 @@ void orc_mlp(int act, int wfmt, int epi, int out_kind,
 
 /* OCP-MX fp32 -> MXFP4 quantizer (E2M1 [rows][depth/2], E8M0 [rows][depth/32]). */
 void orc_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales);
+float orc_nvfp4_tensor_scale(const float *w, size_t n);
+void orc_quantize_nvfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
+                        float *tensor_scale);
+void orc_decode_nvfp4(const uint8_t *packed, const uint8_t *scales, float tensor_scale, uint32_t rows,
+                      uint32_t depth, double *out);
 
 /* CPU formulation of the MXFP4 MLP, timed as the CPU baseline: LUT dequant,
  * fp32 dot products, swiglu_half (plain = 0) or silu(g)*u without prescale

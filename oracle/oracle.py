@@ -64,6 +64,8 @@ def lib() -> C.CDLL:
         L.orc_mlp.argtypes = [C.c_int] * 4 + [u32] * 3 + [vp] * 9
         L.orc_mlp_mxfp4_cpu.argtypes = [u32] * 3 + [vp] * 8 + [C.c_int, u32, u32, C.c_int]
         L.orc_quantize_mxfp4.argtypes = [vp, u32, u32, vp, vp]
+        L.orc_quantize_nvfp4.argtypes = [vp, u32, u32, vp, vp, vp]
+        L.orc_decode_nvfp4.argtypes = [vp, vp, C.c_float, u32, u32, vp]
         L.orc_mlp_mxfp4_cpu.restype = C.c_int
         L.orc_scalar_mlp_gate_up.argtypes = [C.c_int, u32, u32, u32, vp, vp, vp, vp]
         L.orc_scalar_mlp_down.argtypes = [C.c_int, u32, u32, u32, vp, vp, vp]
@@ -184,6 +186,40 @@ def quantize_mxfp4(w: np.ndarray):
     scales = np.empty((rows, depth // 32), np.uint8)
     lib().orc_quantize_mxfp4(_p(w), rows, depth, _p(packed), _p(scales))
     return packed, scales
+
+
+def quantize_nvfp4(w: np.ndarray):
+    """NVFP4 fp32 [rows][depth] -> (packed [rows][depth/2], scales [rows][depth/16], tensor scale)."""
+    w = np.ascontiguousarray(w, np.float32)
+    rows, depth = w.shape
+    packed = np.empty((rows, depth // 2), np.uint8)
+    scales = np.empty((rows, depth // 16), np.uint8)
+    ts = np.zeros(1, np.float32)
+    lib().orc_quantize_nvfp4(_p(w), rows, depth, _p(packed), _p(scales), _p(ts))
+    return packed, scales, float(ts[0])
+
+
+def decode_nvfp4(packed, scales, tensor_scale, rows, depth) -> np.ndarray:
+    out = np.empty((rows, depth), np.float64)
+    lib().orc_decode_nvfp4(_p(np.ascontiguousarray(packed)), _p(np.ascontiguousarray(scales)),
+                           C.c_float(tensor_scale), rows, depth, _p(out))
+    return out
+
+
+def nvfp4_mlp(x, wg, sg, tg, wu, su, tu, wd, sd, td):
+    """NVFP4 W4A4 layer restated: x quantized (NVFP4 recipe), exact gate/up
+    products, mid = silu(g) * u in fp64 rounded to fp16 (the layer's stored
+    mid), quantized again, exact down product. Returns (xq, xs, tx, mid16, out)."""
+    T, H = x.shape
+    I = wg.shape[0]
+    xq, xs, tx = quantize_nvfp4(np.asarray(x, np.float32))
+    xd = decode_nvfp4(xq, xs, tx, T, H)
+    g = xd @ decode_nvfp4(wg, sg, tg, I, H).T
+    u = xd @ decode_nvfp4(wu, su, tu, I, H).T
+    mid = (g / (1.0 + np.exp(-g)) * u).astype(np.float16)
+    mq, ms, tm = quantize_nvfp4(mid.astype(np.float32))
+    out = decode_nvfp4(mq, ms, tm, T, I) @ decode_nvfp4(wd, sd, td, H, I).T
+    return xq, xs, tx, mid, out
 
 
 def w4a4_mlp(x, wg, sg, wu, su, wd, sd):
