@@ -307,6 +307,42 @@ mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t tokens, uint32_t hidden, u
                              const uint8_t *su, const float *tu, const uint8_t *wd, const uint8_t *sd,
                              const float *td, void *out, int out_f16, void *scratch);
 
+/* ---- mixture of experts (no reference counterpart: the
+ *      reference has one dense MLP). W4A4 experts on the FP4 tensor cores:
+ *      route: logits [T][E] fp32 -> top_k expert ids (descending logit, ties to
+ *        the lower id) and weights = softmax over the chosen logits (the full
+ *        softmax renormalised over the top k);
+ *      then x is quantized to MXFP4 once, its rows are grouped by expert
+ *      (within an expert in token order), the grouped gate/up GEMM applies
+ *      SwiGLU and re-quantizes the mid to MXFP4, the grouped down GEMM writes
+ *      fp32 rows, and out[t] = shared_expert(x[t]) + sum_j w[t][j] * row(t, j),
+ *      summed in slot order. Expert weights are stacked: wg/wu [E][I][H/2]
+ *      (scales [E][I][H/32]), wd [E][H][I/2] (scales [E][H][I/32]); the
+ *      optional shared expert (shared_intermediate > 0) uses one MLP's
+ *      layout. H, I and shared_intermediate % 512 == 0; E % 32 == 0, E <= 512;
+ *      1 <= top_k <= min(16, E). ---- */
+typedef struct {
+    uint32_t tokens, hidden, intermediate;
+    uint32_t experts, top_k;
+    uint32_t shared_intermediate;
+    int32_t out_f16;
+} mpp41_moe_desc;
+enum {
+    MPP41_MOE_XQ, MPP41_MOE_XS, MPP41_MOE_IDS, MPP41_MOE_WEIGHTS, MPP41_MOE_COUNTS, MPP41_MOE_OFFSETS,
+    MPP41_MOE_NTILES, MPP41_MOE_TILES, MPP41_MOE_PERM, MPP41_MOE_INV, MPP41_MOE_PQ, MPP41_MOE_PS, MPP41_MOE_MQ,
+    MPP41_MOE_MS, MPP41_MOE_Y, MPP41_MOE_SMQ, MPP41_MOE_SMS, MPP41_MOE_SY, MPP41_MOE_PARTS
+};
+/* Byte offsets of each scratch part (256-byte aligned) into offsets[MPP41_MOE_PARTS]
+ * (may be NULL); returns the total scratch size. */
+size_t mpp41_moe_scratch_layout(const mpp41_moe_desc *desc, size_t *offsets);
+mpp41_status mpp41_moe_route(mpp41_ctx *ctx, const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                             int32_t *ids, float *weights);
+mpp41_status mpp41_moe_w4a4(mpp41_ctx *ctx, const mpp41_moe_desc *desc, const void *x, const float *logits,
+                            const uint8_t *wg, const uint8_t *sg, const uint8_t *wu, const uint8_t *su,
+                            const uint8_t *wd, const uint8_t *sd, const uint8_t *shared_wg, const uint8_t *shared_sg,
+                            const uint8_t *shared_wu, const uint8_t *shared_su, const uint8_t *shared_wd,
+                            const uint8_t *shared_sd, void *out, void *scratch);
+
 /* ---- tensor parallelism (no counterpart in the
  *      single-GPU reference). Rank r of P holds rows [r*I/P, (r+1)*I/P) of the
  *      gate and up weights (and their scale rows) and the same columns of the

@@ -1018,6 +1018,7 @@ mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I,
     const NvScratch s = nv_scratch(scratch, T, H, I);
     cudaStream_t st = ctx->stream;
     CK(launch_quantize_nvfp4(x, true, T, H, ctx->amax, s.xq, s.xs, s.ts, st), "quantize activations");
+    CK(cudaMemsetAsync(ctx->amax, 0, sizeof(uint32_t), st), "clear the mid maximum");
     MxLaunch g{};
     g.a = s.xq; g.sa = s.xs;
     g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
@@ -1025,10 +1026,11 @@ mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I,
     g.out = s.mid; g.M = T; g.N = I; g.K = H; g.ldc = I;
     g.epi = 3;
     g.nv = true; g.ts_a = s.ts; g.ts_b0 = tg; g.ts_b1 = tu;
+    g.amax_out = ctx->amax;   // the gate/up epilogue reduces |mid| for the mid's tensor scale
     g.err = ctx->err;
     mpp41_status r = enqueue_mxf4(ctx, g, "NVFP4 gate/up GEMM");
     if (r != MPP41_OK) return r;
-    CK(launch_quantize_nvfp4(s.mid, true, T, I, ctx->amax, s.mq, s.ms, s.ts + 1, st), "quantize mid");
+    CK(launch_quantize_nvfp4(s.mid, true, T, I, ctx->amax, s.mq, s.ms, s.ts + 1, st, true), "quantize mid");
     MxLaunch d{};
     d.a = s.mq; d.sa = s.ms;
     d.b0 = d.b1 = wd; d.sb0 = d.sb1 = sd;
@@ -1038,6 +1040,130 @@ mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I,
     d.nv = true; d.ts_a = s.ts + 1; d.ts_b0 = d.ts_b1 = td;
     d.err = ctx->err;
     return enqueue_mxf4(ctx, d, "NVFP4 down GEMM");
+}
+
+// ------------------------------------------------------------------ MoE
+static mpp41_status check_moe(const mpp41_moe_desc *d)
+{
+    if (!d) return fail(MPP41_ERR_INVALID_ARGUMENT, "null MoE descriptor");
+    if (d->hidden % 512 || d->intermediate % 512 || d->shared_intermediate % 512)
+        return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "hidden and intermediate sizes must be multiples of 512");
+    if (!d->experts || d->experts % 32 || d->experts > 512)
+        return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "experts must be a multiple of 32, at most 512");
+    if (!d->top_k || d->top_k > 16 || d->top_k > d->experts)
+        return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "top_k must be in [1, min(16, experts)]");
+    return MPP41_OK;
+}
+
+size_t mpp41_moe_scratch_layout(const mpp41_moe_desc *d, size_t *offsets)
+{
+    if (!d) return 0;
+    const size_t T = d->tokens, H = d->hidden, I = d->intermediate, E = d->experts, R = T * d->top_k;
+    const size_t Is = d->shared_intermediate;
+    const size_t max_tiles = R / 128 + E + 1;
+    const size_t sizes[MPP41_MOE_PARTS] = {
+        T * H / 2, T * H / 32, R * 4, R * 4, E * 4, (E + 1) * 4, 4, max_tiles * 16, R * 4, R * 4,
+        R * H / 2, R * H / 32, R * I / 2, R * I / 32, R * H * 4, T * Is / 2, T * Is / 32, Is ? T * H * 4 : 0};
+    size_t o = 0;
+    for (int i = 0; i < MPP41_MOE_PARTS; ++i) {
+        if (offsets) offsets[i] = o;
+        o += up256(sizes[i]);
+    }
+    return o;
+}
+
+mpp41_status mpp41_moe_route(mpp41_ctx *ctx, const float *logits, uint32_t T, uint32_t E, uint32_t k, int32_t *ids,
+                             float *weights)
+{
+    NEED(ctx);
+    if (!E || E % 32 || E > 512 || !k || k > 16 || k > E)
+        return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "experts must be a multiple of 32 up to 512, top_k in [1, 16]");
+    if (!T) return MPP41_OK;
+    if (!logits || !ids || !weights) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    CK(launch_moe_route(logits, T, E, k, ids, weights, ctx->stream), "route");
+    return MPP41_OK;
+}
+
+mpp41_status mpp41_moe_w4a4(mpp41_ctx *ctx, const mpp41_moe_desc *d, const void *x, const float *logits,
+                            const uint8_t *wg, const uint8_t *sg, const uint8_t *wu, const uint8_t *su,
+                            const uint8_t *wd, const uint8_t *sd, const uint8_t *shared_wg, const uint8_t *shared_sg,
+                            const uint8_t *shared_wu, const uint8_t *shared_su, const uint8_t *shared_wd,
+                            const uint8_t *shared_sd, void *out, void *scratch)
+{
+    NEED(ctx);
+    mpp41_status s = check_moe(d);
+    if (s != MPP41_OK) return s;
+    const uint32_t T = d->tokens, H = d->hidden, I = d->intermediate, E = d->experts, k = d->top_k;
+    const uint32_t Is = d->shared_intermediate, R = T * k;
+    if (!T) return MPP41_OK;
+    if (!x || !logits || !wg || !sg || !wu || !su || !wd || !sd || !out || !scratch)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if (Is && (!shared_wg || !shared_sg || !shared_wu || !shared_su || !shared_wd || !shared_sd))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "shared expert weights missing");
+    if ((reinterpret_cast<uintptr_t>(scratch) & 255u) || !al16(x) || !al16(out))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "x and out must be 16-byte aligned, scratch 256-byte");
+    size_t off[MPP41_MOE_PARTS];
+    mpp41_moe_scratch_layout(d, off);
+    uint8_t *b = static_cast<uint8_t *>(scratch);
+    auto u8 = [&](int part) { return b + off[part]; };
+    auto u32 = [&](int part) { return reinterpret_cast<uint32_t *>(b + off[part]); };
+    cudaStream_t st = ctx->stream;
+    const uint32_t max_tiles = R / 128 + E + 1;
+    CK(launch_quantize_mxfp4_f16(x, T, H, u8(MPP41_MOE_XQ), u8(MPP41_MOE_XS), st), "quantize x");
+    CK(launch_moe_route(logits, T, E, k, reinterpret_cast<int32_t *>(u8(MPP41_MOE_IDS)),
+                        reinterpret_cast<float *>(u8(MPP41_MOE_WEIGHTS)), st), "route");
+    CK(launch_moe_permute(reinterpret_cast<int32_t *>(u8(MPP41_MOE_IDS)), R, E, 128, u32(MPP41_MOE_COUNTS),
+                          u32(MPP41_MOE_OFFSETS), reinterpret_cast<uint4 *>(u8(MPP41_MOE_TILES)), u32(MPP41_MOE_NTILES),
+                          u32(MPP41_MOE_PERM), u32(MPP41_MOE_INV), ctx->err, st), "permute");
+    const uint32_t *n_rows = u32(MPP41_MOE_OFFSETS) + E;
+    CK(launch_moe_gather(u8(MPP41_MOE_XQ), H / 2, u32(MPP41_MOE_PERM), k, n_rows, R, u8(MPP41_MOE_PQ), st), "gather x");
+    CK(launch_moe_gather(u8(MPP41_MOE_XS), H / 32, u32(MPP41_MOE_PERM), k, n_rows, R, u8(MPP41_MOE_PS), st),
+       "gather x scales");
+    MxLaunch g{};
+    g.a = u8(MPP41_MOE_PQ); g.sa = u8(MPP41_MOE_PS);
+    g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
+    g.b_rows = E * I; g.b0_row0 = 0; g.b1_row0 = 0; g.b_row_step = 128;
+    g.out = u8(MPP41_MOE_MQ); g.out_scales = u8(MPP41_MOE_MS);
+    g.M = R; g.N = I; g.K = H; g.ldc = I; g.epi = 2;
+    g.tiles = reinterpret_cast<const uint4 *>(u8(MPP41_MOE_TILES)); g.n_tiles = u32(MPP41_MOE_NTILES);
+    g.max_tiles = max_tiles; g.b_expert_rows = I;
+    g.err = ctx->err;
+    s = enqueue_mxf4(ctx, g, "MoE gate/up GEMM");
+    if (s != MPP41_OK) return s;
+    MxLaunch dn{};
+    dn.a = u8(MPP41_MOE_MQ); dn.sa = u8(MPP41_MOE_MS);
+    dn.b0 = dn.b1 = wd; dn.sb0 = dn.sb1 = sd;
+    dn.b_rows = E * H; dn.b0_row0 = 0; dn.b1_row0 = 128; dn.b_row_step = 256;
+    dn.out = u8(MPP41_MOE_Y); dn.M = R; dn.N = H; dn.K = I; dn.ldc = H; dn.epi = 0;
+    dn.tiles = g.tiles; dn.n_tiles = g.n_tiles; dn.max_tiles = max_tiles; dn.b_expert_rows = H;
+    dn.err = ctx->err;
+    s = enqueue_mxf4(ctx, dn, "MoE down GEMM");
+    if (s != MPP41_OK) return s;
+    const float *shared_y = nullptr;
+    if (Is) {
+        MxLaunch sg_{};
+        sg_.a = u8(MPP41_MOE_XQ); sg_.sa = u8(MPP41_MOE_XS);
+        sg_.b0 = shared_wg; sg_.sb0 = shared_sg; sg_.b1 = shared_wu; sg_.sb1 = shared_su;
+        sg_.b_rows = Is; sg_.b_row_step = 128;
+        sg_.out = u8(MPP41_MOE_SMQ); sg_.out_scales = u8(MPP41_MOE_SMS);
+        sg_.M = T; sg_.N = Is; sg_.K = H; sg_.ldc = Is; sg_.epi = 2;
+        sg_.err = ctx->err;
+        s = enqueue_mxf4(ctx, sg_, "shared expert gate/up GEMM");
+        if (s != MPP41_OK) return s;
+        MxLaunch sd_{};
+        sd_.a = u8(MPP41_MOE_SMQ); sd_.sa = u8(MPP41_MOE_SMS);
+        sd_.b0 = sd_.b1 = shared_wd; sd_.sb0 = sd_.sb1 = shared_sd;
+        sd_.b_rows = H; sd_.b1_row0 = 128; sd_.b_row_step = 256;
+        sd_.out = u8(MPP41_MOE_SY); sd_.M = T; sd_.N = H; sd_.K = Is; sd_.ldc = H; sd_.epi = 0;
+        sd_.err = ctx->err;
+        s = enqueue_mxf4(ctx, sd_, "shared expert down GEMM");
+        if (s != MPP41_OK) return s;
+        shared_y = reinterpret_cast<const float *>(u8(MPP41_MOE_SY));
+    }
+    CK(launch_moe_combine(reinterpret_cast<const float *>(u8(MPP41_MOE_Y)), u32(MPP41_MOE_INV),
+                          reinterpret_cast<const float *>(u8(MPP41_MOE_WEIGHTS)), T, k, H, shared_y, out,
+                          d->out_f16 != 0, st), "combine");
+    return MPP41_OK;
 }
 
 mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,

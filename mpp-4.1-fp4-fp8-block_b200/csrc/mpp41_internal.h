@@ -94,9 +94,24 @@ struct MxLaunch {
     int epi;
     bool nv;                                // NVFP4 operands (UE4M3 per 16 + fp32 tensor scales)
     const float *ts_a, *ts_b0, *ts_b1;      // NVFP4 tensor scales (device)
+    uint32_t *amax_out;                     // SWIGLU_F16: atomicMax of |mid| (float bits), or null
+    const uint4 *tiles;                     // grouped: {expert, row0, row_end, 0} per row tile (device)
+    const uint32_t *n_tiles;                // grouped: number of valid tiles (device)
+    uint32_t max_tiles, b_expert_rows;      // grouped: grid bound; B rows per expert
     uint32_t *err;
 };
 int launch_mxf4_gemm(const MxLaunch &L, cudaStream_t st, const char **why);
+
+// Mixture-of-experts pieces (mpp41_moe.cu).
+cudaError_t launch_moe_route(const float *logits, uint32_t T, uint32_t E, uint32_t k, int32_t *ids, float *weights,
+                             cudaStream_t st);
+cudaError_t launch_moe_permute(const int32_t *ids, uint32_t n, uint32_t E, uint32_t bm, uint32_t *counts,
+                               uint32_t *offsets, uint4 *tiles, uint32_t *n_tiles, uint32_t *perm_src, uint32_t *inv,
+                               uint32_t *err, cudaStream_t st);
+cudaError_t launch_moe_gather(const void *src, uint32_t row_bytes, const uint32_t *perm_src, uint32_t k,
+                              const uint32_t *n_rows, uint32_t max_rows, void *dst, cudaStream_t st);
+cudaError_t launch_moe_combine(const float *y, const uint32_t *inv, const float *w, uint32_t T, uint32_t k, uint32_t H,
+                               const float *shared_y, void *out, bool out_f16, cudaStream_t st);
 
 bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols, uint64_t rows,
               uint32_t bc, uint32_t br, CUtensorMapSwizzle sw);
@@ -111,9 +126,11 @@ cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth,
 cudaError_t launch_quantize_mxfp4_f16(const void *x, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
                                       cudaStream_t st);
 // NVFP4 quantization (fp32 or fp16 in) with a computed tensor scale; amax_tmp
-// is one device word of scratch.
+// is one device word of scratch (amax_ready: it already holds the tensor's
+// absolute maximum as float bits, so the reduction pass is skipped).
 cudaError_t launch_quantize_nvfp4(const void *x, bool f16_in, uint32_t rows, uint32_t depth, uint32_t *amax_tmp,
-                                  uint8_t *packed, uint8_t *scales, float *tensor_scale, cudaStream_t st);
+                                  uint8_t *packed, uint8_t *scales, float *tensor_scale, cudaStream_t st,
+                                  bool amax_ready = false);
 cudaError_t launch_quantize_act_s8(const void *x, uint32_t tokens, uint32_t hidden, int8_t *q, float *scale,
                                    cudaStream_t st);
 // Returns 0 on success, 1 for an unsupported combination/shape, 2 for a CUDA error.

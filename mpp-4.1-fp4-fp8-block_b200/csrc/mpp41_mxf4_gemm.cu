@@ -27,6 +27,8 @@ int launch_mxf4_gemm(const MxLaunch &L, cudaStream_t st, const char **why)
     p.M = L.M; p.N = L.N; p.K = L.K; p.ldc = L.ldc;
     p.b0_row0 = L.b0_row0; p.b1_row0 = L.b1_row0; p.b_row_step = L.b_row_step;
     p.ts_a = L.ts_a; p.ts_b0 = L.ts_b0; p.ts_b1 = L.ts_b1;
+    p.amax_out = L.amax_out;
+    p.tiles = L.tiles; p.n_tiles = L.n_tiles; p.b_expert_rows = L.b_expert_rows;
     p.err = L.err;
     const uint32_t sf_cols = L.K / (L.nv ? 16 : 32);
     const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -51,7 +53,9 @@ int launch_mxf4_gemm(const MxLaunch &L, cudaStream_t st, const char **why)
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
     if (e != cudaSuccess) { cudaGetLastError(); *why = cudaGetErrorString(e); return 2; }
     const uint32_t cols = swiglu ? 128 : kBN;
-    const dim3 grid((L.N + cols - 1) / cols, (L.M + kBM - 1) / kBM);
+    // grouped: L.max_tiles row tiles at most (the table's bound), L.M = all rows
+    const dim3 grid((L.N + cols - 1) / cols, L.tiles ? L.max_tiles : (L.M + kBM - 1) / kBM);
+    if (!grid.y) return 0;
     kern<<<grid, kThreads, kSmem, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) { *why = cudaGetErrorString(e); return 2; }

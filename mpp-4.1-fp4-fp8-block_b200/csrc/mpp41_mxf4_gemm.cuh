@@ -135,6 +135,13 @@ struct Params {
     uint32_t M, N, K, ldc;       // N = columns written (SWIGLU_MX: mid channels)
     // NVFP4: fp32 tensor scales (device) of A and of the two B maps
     const float *ts_a, *ts_b0, *ts_b1;
+    uint32_t *amax_out;          // SWIGLU_F16: atomicMax of |stored mid| as float bits (null: off)
+    // Grouped (MoE) launch: row tile blockIdx.y is tiles[blockIdx.y] = {expert,
+    // first row, end row, 0} while blockIdx.y < *n_tiles (other CTAs exit), and
+    // B rows are offset by expert * b_expert_rows. Null tiles: plain GEMM.
+    const uint4 *tiles;
+    const uint32_t *n_tiles;
+    uint32_t b_expert_rows;
     uint32_t *err;
 };
 
@@ -161,7 +168,14 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t m0 = blockIdx.y * kBM;
+    uint32_t m0 = blockIdx.y * kBM, m_end = p.M, b_off = 0;
+    if (p.tiles) {
+        if (blockIdx.y >= *p.n_tiles) return;   // whole CTA, before any barrier or allocation
+        const uint4 t = p.tiles[blockIdx.y];
+        m0 = t.y;
+        m_end = t.z;
+        b_off = t.x * p.b_expert_rows;
+    }
     const uint32_t nk = p.K / kBK;
 
     if (threadIdx.x == 0) {
@@ -186,8 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            const int32_t rb0 = (int32_t)(p.b0_row0 + blockIdx.x * p.b_row_step);
-            const int32_t rb1 = (int32_t)(p.b1_row0 + blockIdx.x * p.b_row_step);
+            const int32_t rb0 = (int32_t)(b_off + p.b0_row0 + blockIdx.x * p.b_row_step);
+            const int32_t rb1 = (int32_t)(b_off + p.b1_row0 + blockIdx.x * p.b_row_step);
             uint32_t s = 0;
             for (; s < nk; ++s) {
                 const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
@@ -304,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
         if (ok) {
             if constexpr (E == EPI_SWIGLU_MX || E == EPI_SWIGLU_F16) {
                 const uint32_t c0 = blockIdx.x * 128;   // mid channel of column 0
+                float vmax = 0.0f;   // rounding to fp16 is monotonic: max of rounded = rounded max
 #pragma unroll 1
                 for (int cb = 0; cb < 4; ++cb) {
                     uint32_t g[32], u[32];
@@ -320,11 +335,13 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                     if constexpr (E == EPI_SWIGLU_MX) {
                         uint4 pk;
                         const uint32_t code = mx_quant32(v, pk);
-                        if (m < p.M && c < p.N) {
+                        if (m < m_end && c < p.N) {
                             *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(p.out) + (size_t)m * (p.ldc / 2) + c / 2) = pk;
                             p.out_scales[(size_t)m * (p.ldc / 32) + c / 32] = (uint8_t)code;
                         }
-                    } else if (m < p.M && c < p.N) {
+                    } else if (m < m_end && c < p.N) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) vmax = fmaxf(vmax, fabsf(v[i]));
                         uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(p.out) + (size_t)m * p.ldc + c);
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
@@ -336,6 +353,13 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                             }
                             dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
                         }
+                    }
+                }
+                if constexpr (E == EPI_SWIGLU_F16) {
+                    if (p.amax_out) {
+                        float r = __half2float(__float2half_rn(vmax));
+                        for (int o = 16; o; o >>= 1) r = fmaxf(r, __shfl_xor_sync(0xffffffffu, r, o));
+                        if (lane == 0) atomicMax(p.amax_out, __float_as_uint(r));
                     }
                 }
             } else {
@@ -351,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                         for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
                     }
                     const uint32_t col = n0 + cc * 32;
-                    if (m < p.M && col < p.N) {
+                    if (m < m_end && col < p.N) {
                         if constexpr (E == EPI_F32) {
                             float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + (size_t)m * p.ldc + col);
 #pragma unroll

@@ -364,8 +364,19 @@ __global__ void absmax_kernel(const In *__restrict__ x, size_t n, uint32_t *__re
 {
     __shared__ float red[32];
     float m = 0.0f;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        m = fmaxf(m, fabsf(load_f(x, i)));
+    const size_t stride = (size_t)gridDim.x * blockDim.x, t0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if ((n % 8) == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {   // 16-byte loads
+        constexpr int kPer = 16 / sizeof(In);
+        const uint4 *v = reinterpret_cast<const uint4 *>(x);
+        for (size_t i = t0; i < n / kPer; i += stride) {
+            const uint4 u = v[i];
+            const In *e = reinterpret_cast<const In *>(&u);
+#pragma unroll
+            for (int q = 0; q < kPer; ++q) m = fmaxf(m, fabsf(load_f(e, q)));
+        }
+    } else {
+        for (size_t i = t0; i < n; i += stride) m = fmaxf(m, fabsf(load_f(x, i)));
+    }
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
     __syncthreads();
@@ -389,8 +400,24 @@ __global__ void quantize_nvfp4_kernel(const In *__restrict__ w, uint32_t rows, u
         const uint32_t r = (uint32_t)(b / kb), j = (uint32_t)(b % kb);
         const In *src = w + (size_t)r * depth + (size_t)j * 16;
         float v[16];
+        if constexpr (sizeof(In) == 4) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = load_f(src, i);
+            for (int i = 0; i < 4; ++i) {
+                const float4 f = reinterpret_cast<const float4 *>(src)[i];
+                v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const uint4 u = reinterpret_cast<const uint4 *>(src)[i];
+                const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&ws[q]));
+                    v[8 * i + 2 * q] = f.x; v[8 * i + 2 * q + 1] = f.y;
+                }
+            }
+        }
         uint2 pk;
         const uint32_t code = nv_quant16(v, g, pk);
         *reinterpret_cast<uint2 *>(packed + (size_t)r * (depth / 2) + (size_t)j * 8) = pk;
@@ -399,13 +426,23 @@ __global__ void quantize_nvfp4_kernel(const In *__restrict__ w, uint32_t rows, u
 }
 
 cudaError_t launch_quantize_nvfp4(const void *x, bool f16_in, uint32_t rows, uint32_t depth, uint32_t *amax_tmp,
-                                  uint8_t *packed, uint8_t *scales, float *tensor_scale, cudaStream_t st)
+                                  uint8_t *packed, uint8_t *scales, float *tensor_scale, cudaStream_t st,
+                                  bool amax_ready)
 {
     const size_t n = (size_t)rows * depth;
-    cudaError_t e = cudaMemsetAsync(amax_tmp, 0, sizeof(uint32_t), st);
-    if (e != cudaSuccess) return e;
-    const unsigned g1 = grid_for(n, 256) < 148u * 4u ? grid_for(n, 256) : 148u * 4u;
-    if (f16_in) {
+    if (!amax_ready) {
+        cudaError_t e = cudaMemsetAsync(amax_tmp, 0, sizeof(uint32_t), st);
+        if (e != cudaSuccess) return e;
+    }
+    const unsigned g1 = grid_for(n, 256) < 148u * 8u ? grid_for(n, 256) : 148u * 8u;
+    if (amax_ready) {
+        if (f16_in)
+            quantize_nvfp4_kernel<__half><<<grid_for(n / 16, 256), 256, 0, st>>>(
+                static_cast<const __half *>(x), rows, depth, amax_tmp, packed, scales, tensor_scale);
+        else
+            quantize_nvfp4_kernel<float><<<grid_for(n / 16, 256), 256, 0, st>>>(
+                static_cast<const float *>(x), rows, depth, amax_tmp, packed, scales, tensor_scale);
+    } else if (f16_in) {
         absmax_kernel<__half><<<g1, 256, 0, st>>>(static_cast<const __half *>(x), n, amax_tmp);
         quantize_nvfp4_kernel<__half><<<grid_for(n / 16, 256), 256, 0, st>>>(
             static_cast<const __half *>(x), rows, depth, amax_tmp, packed, scales, tensor_scale);

@@ -54,6 +54,16 @@ class MLPDesc(C.Structure):
                 ("flags", C.c_uint32)]
 
 
+class MoEDesc(C.Structure):
+    _fields_ = [("tokens", C.c_uint32), ("hidden", C.c_uint32), ("intermediate", C.c_uint32),
+                ("experts", C.c_uint32), ("top_k", C.c_uint32), ("shared_intermediate", C.c_uint32),
+                ("out_f16", C.c_int32)]
+
+
+MOE_PARTS = ("xq", "xs", "ids", "weights", "counts", "offsets", "n_tiles", "tiles", "perm", "inv", "pq", "ps",
+             "mq", "ms", "y", "smq", "sms", "sy")
+
+
 _lib = None
 
 
@@ -112,6 +122,9 @@ def lib() -> C.CDLL:
         "mpp41_quantize_act_nvfp4": ([vp, vp, u32, u32, vp, vp, vp], st),
         "mpp41_matmul_nvf4": ([vp] * 8 + [u32, u32, u32, C.c_int], st),
         "mpp41_mlp_nvfp4_scratch_bytes": ([u32, u32, u32], sz),
+        "mpp41_moe_scratch_layout": ([C.POINTER(MoEDesc), vp], sz),
+        "mpp41_moe_route": ([vp, vp, u32, u32, u32, vp, vp], st),
+        "mpp41_moe_w4a4": ([vp, C.POINTER(MoEDesc)] + [vp] * 16, st),
         "mpp41_mlp_nvfp4": ([vp, u32, u32, u32] + [vp] * 11 + [C.c_int, vp], st),
         "mpp41_mlp_noalloc_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp_noalloc": ([C.POINTER(MLPDesc)] + [vp] * 9, st),
@@ -180,6 +193,17 @@ def nvfp4_scratch_layout(tokens: int, hidden: int, intermediate: int):
         o += up(n)
     offs.append(o)
     return tuple(offs)
+
+
+def moe_desc(tokens, hidden, intermediate, experts, top_k, shared_intermediate=0, out_f16=False) -> MoEDesc:
+    return MoEDesc(tokens, hidden, intermediate, experts, top_k, shared_intermediate, int(out_f16))
+
+
+def moe_scratch_layout(desc: MoEDesc):
+    """(total bytes, {part name: byte offset}) of the MoE scratch."""
+    offs = (C.c_size_t * len(MOE_PARTS))()
+    total = lib().mpp41_moe_scratch_layout(C.byref(desc), offs)
+    return total, dict(zip(MOE_PARTS, list(offs)))
 
 
 def has_kernel(name: str) -> bool:
@@ -364,6 +388,15 @@ class Context:
         _check(lib().mpp41_mlp_nvfp4(self.h, tokens, hidden, intermediate, _ptr(x), _ptr(wg), _ptr(sg), _ptr(tg),
                                      _ptr(wu), _ptr(su), _ptr(tu), _ptr(wd), _ptr(sd), _ptr(td), _ptr(out),
                                      int(out_f16), _ptr(scratch)))
+
+    def moe_route(self, logits, tokens: int, experts: int, top_k: int, ids, weights):
+        _check(lib().mpp41_moe_route(self.h, _ptr(logits), tokens, experts, top_k, _ptr(ids), _ptr(weights)))
+
+    def moe_w4a4(self, desc: "MoEDesc", x, logits, wg, sg, wu, su, wd, sd, out, scratch, shared=None):
+        """One W4A4 mixture-of-experts layer (mpp41_moe_w4a4); shared = (wg, sg, wu, su, wd, sd) or None."""
+        sh = [_ptr(v) for v in shared] if shared is not None else [None] * 6
+        _check(lib().mpp41_moe_w4a4(self.h, C.byref(desc), _ptr(x), _ptr(logits), _ptr(wg), _ptr(sg), _ptr(wu),
+                                    _ptr(su), _ptr(wd), _ptr(sd), *sh, _ptr(out), _ptr(scratch)))
 
     def mlp_w4a4(self, tokens: int, hidden: int, intermediate: int, x, wg, sg, wu, su, wd, sd, out, scratch,
                  out_f16: bool = False):

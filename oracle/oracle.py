@@ -241,6 +241,55 @@ def w4a4_mlp(x, wg, sg, wu, su, wd, sd):
     return xq, xs, mq, ms, out
 
 
+def moe_route(logits: np.ndarray, k: int):
+    """Top-k by descending logit, ties to the lower expert id; weights =
+    softmax over the chosen logits (fp64)."""
+    order = np.argsort(-logits, axis=1, kind="stable")[:, :k]
+    chosen = np.take_along_axis(logits, order, axis=1).astype(np.float64)
+    e = np.exp(chosen - chosen[:, :1])
+    return order.astype(np.int32), e / e.sum(axis=1, keepdims=True)
+
+
+def moe_permutation(ids: np.ndarray, E: int):
+    """Rows grouped by expert, assignment order within an expert: perm[r] = assignment."""
+    flat = ids.reshape(-1)
+    perm = np.argsort(flat, kind="stable").astype(np.uint32)
+    counts = np.bincount(flat, minlength=E).astype(np.uint32)
+    return perm, counts
+
+
+def moe_w4a4(x, logits, k, wg, sg, wu, su, wd, sd, shared=None):
+    """W4A4 MoE restated: returns (ids, weights, perm, mq, ms, y, out) with y and
+    out fp64; each expert row follows w4a4_mlp's rules (x quantized once)."""
+    T, H = x.shape
+    E, I = wg.shape[0], wg.shape[1]
+    ids, w = moe_route(logits, k)
+    perm, counts = moe_permutation(ids, E)
+    xq, xs = quantize_mxfp4(np.asarray(x, np.float32))
+    xd = decode_weights(W_MXFP4, xq, xs, T, H)
+    R = T * k
+    mq = np.zeros((R, I // 2), np.uint8)
+    ms = np.zeros((R, I // 32), np.uint8)
+    y = np.zeros((R, H))
+    r0 = 0
+    for e in range(E):
+        rows = perm[r0:r0 + counts[e]]
+        if len(rows):
+            xr = xd[rows // k]
+            g = xr @ decode_weights(W_MXFP4, wg[e], sg[e], I, H).T
+            u = xr @ decode_weights(W_MXFP4, wu[e], su[e], I, H).T
+            q, qs = quantize_mxfp4((g / (1.0 + np.exp(-g)) * u).astype(np.float32))
+            mq[r0:r0 + len(rows)], ms[r0:r0 + len(rows)] = q, qs
+            y[r0:r0 + len(rows)] = decode_weights(W_MXFP4, q, qs, len(rows), I) @ decode_weights(W_MXFP4, wd[e], sd[e], H, I).T
+        r0 += counts[e]
+    inv = np.empty(R, np.int64)
+    inv[perm] = np.arange(R)
+    out = (w[:, :, None] * y[inv].reshape(T, k, H)).sum(axis=1)
+    if shared is not None:
+        out = out + w4a4_mlp(x, *shared)[-1]
+    return ids, w, perm, mq, ms, y, out
+
+
 def baseline_mlp_inputs(T=128, H=1024, I=4096, seed=0):
     """x ~ N(0,1) fp16, weights ~ N(0,0.02) fp32 quantized OCP-MX."""
     rng = np.random.default_rng(seed)

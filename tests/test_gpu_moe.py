@@ -1,0 +1,102 @@
+"""W4A4 mixture-of-experts layer against the oracle's restatement:
+- routing: expert ids exact (descending logit, ties to the lower id, exact
+  ties included), weights within 1e-6;
+- permutation: counts, row order (grouped by expert, assignment order inside)
+  and the gathered quantized rows exact;
+- experts: the mid's MXFP4 quantization as in the dense W4A4 test (at most
+  0.2 % of elements one E2M1 step apart), the down rows within 1e-5 of fp64
+  computed from the kernel's own mid;
+- combine: within 1e-6 of fp64 applied to the kernel's own rows; end to end
+  within 5 % of the largest output.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import empty_dev, from_dev, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def test_route_ties_and_weights(ctx):
+    T, E, k = 300, 64, 8
+    rng = np.random.default_rng(1)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    logits[0, :] = 0.0                      # all tied: experts 0..7
+    logits[1, 10] = logits[1, 3] = 9.0      # tie at the top: 3 before 10
+    d_ids, d_w = empty_dev(T * k * 4), empty_dev(T * k * 4)
+    ctx.moe_route(to_dev(logits), T, E, k, d_ids, d_w)
+    ids, w = O.moe_route(logits, k)
+    got_ids = from_dev(d_ids, np.int32, (T, k))
+    assert np.array_equal(got_ids, ids)
+    assert list(got_ids[0]) == list(range(8)) and list(got_ids[1][:2]) == [3, 10]
+    assert np.allclose(from_dev(d_w, np.float32, (T, k)), w, rtol=1e-6, atol=1e-7)
+
+
+def _experts(rng, E, rows, cols):
+    w = (rng.standard_normal((E * rows, cols)) * 0.02).astype(np.float32)
+    q, s = O.quantize_mxfp4(w)
+    return q.reshape(E, rows, cols // 2), s.reshape(E, rows, cols // 32)
+
+
+@pytest.mark.parametrize("T,H,I,E,k,Is", [(64, 512, 512, 32, 4, 0), (200, 1024, 512, 64, 8, 1024), (1, 512, 512, 32, 2, 512)])
+def test_moe_w4a4(ctx, T, H, I, E, k, Is):
+    import mpp41
+    rng = np.random.default_rng(T + E)
+    x = rng.standard_normal((T, H)).astype(np.float16)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    logits[:, 5] += 3.0    # one popular expert: more than one row tile
+    wg, sg = _experts(rng, E, I, H)
+    wu, su = _experts(rng, E, I, H)
+    wd, sd = _experts(rng, E, H, I)
+    shared = None
+    if Is:
+        shared = []
+        for r, c in ((Is, H), (Is, H), (H, Is)):
+            shared += list(O.quantize_mxfp4((rng.standard_normal((r, c)) * 0.02).astype(np.float32)))
+        shared = [shared[0], shared[1], shared[2], shared[3], shared[4], shared[5]]
+    desc = mpp41.moe_desc(T, H, I, E, k, Is)
+    total, off = mpp41.moe_scratch_layout(desc)
+    scratch = empty_dev(total)
+    out = empty_dev(T * H * 4)
+    dev_shared = [to_dev(a) for a in shared] if shared else None
+    ctx.moe_w4a4(desc, to_dev(x), to_dev(logits), to_dev(wg), to_dev(sg), to_dev(wu), to_dev(su), to_dev(wd),
+                 to_dev(sd), out, scratch, shared=dev_shared)
+    ctx.synchronize()
+    sh = (shared[0], shared[1], shared[2], shared[3], shared[4], shared[5]) if shared else None
+    ids, w, perm, mq, ms, y, out_ref = O.moe_w4a4(x, logits, k, wg, sg, wu, su, wd, sd,
+                                                  shared=(sh[0], sh[1], sh[2], sh[3], sh[4], sh[5]) if sh else None)
+    raw = from_dev(scratch, np.uint8, (total,))
+    part = lambda name, dt, shape: raw[off[name]:off[name] + int(np.prod(shape)) * np.dtype(dt).itemsize].view(dt).reshape(shape)
+    R = T * k
+    assert np.array_equal(part("ids", np.int32, (T, k)), ids)
+    assert np.allclose(part("weights", np.float32, (T, k)), w, rtol=1e-6, atol=1e-7)
+    assert np.array_equal(part("counts", np.uint32, (E,)), np.bincount(ids.reshape(-1), minlength=E))
+    assert np.array_equal(part("perm", np.uint32, (R,)), perm)
+    xq, xs = O.quantize_mxfp4(x.astype(np.float32))
+    assert np.array_equal(part("pq", np.uint8, (R, H // 2)), xq[perm // k])
+    assert np.array_equal(part("ps", np.uint8, (R, H // 32)), xs[perm // k])
+    g_mq, g_ms = part("mq", np.uint8, (R, I // 2)), part("ms", np.uint8, (R, I // 32))
+    gm = O.decode_weights(O.W_MXFP4, g_mq, g_ms, R, I)
+    rm = O.decode_weights(O.W_MXFP4, mq, ms, R, I)
+    assert (gm != rm).mean() <= 2e-3
+    g_y = part("y", np.float32, (R, H)).astype(np.float64)
+    counts = np.bincount(ids.reshape(-1), minlength=E)
+    r0 = 0
+    for e in range(E):
+        n = counts[e]
+        if n:
+            own = gm[r0:r0 + n] @ O.decode_weights(O.W_MXFP4, wd[e], sd[e], H, I).T
+            row = np.abs(own).max(axis=1, keepdims=True) + 1e-30
+            assert np.all(np.abs(g_y[r0:r0 + n] - own) <= 1e-5 * row)
+        r0 += n
+    got = from_dev(out, np.float32, (T, H)).astype(np.float64)
+    inv = np.empty(R, np.int64)
+    inv[perm] = np.arange(R)
+    w32 = part("weights", np.float32, (T, k)).astype(np.float64)
+    mine = (w32[:, :, None] * g_y[inv].reshape(T, k, H)).sum(axis=1)
+    if Is:
+        mine = mine + part("sy", np.float32, (T, H)).astype(np.float64)
+    scale = np.abs(mine).max() + 1e-30
+    assert np.all(np.abs(got - mine) <= 1e-6 * scale)
+    assert np.abs(got - out_ref).max() <= 0.05 * np.abs(out_ref).max()
