@@ -343,6 +343,30 @@ mpp41_status mpp41_moe_w4a4(mpp41_ctx *ctx, const mpp41_moe_desc *desc, const vo
                             const uint8_t *shared_wu, const uint8_t *shared_su, const uint8_t *shared_wd,
                             const uint8_t *shared_sd, void *out, void *scratch);
 
+/* ---- expert parallelism: the same layer with the E experts split over the
+ *      communicator's P ranks (mpp41_comm_init), rank r holding experts
+ *      [r E/P, (r+1) E/P) (wg/wu/wd and scales stacked over those only) and
+ *      its own `tokens` tokens. Each rank routes and groups its assignments,
+ *      the per-expert counts are all-gathered (one host synchronisation
+ *      sizes the exchanges), the quantized rows and scales go to the owning
+ *      ranks (NCCL send/recv), the experts run on the rows received
+ *      (regrouped expert-major), the fp32 rows come back the same way and
+ *      each rank combines its own tokens. Every per-row computation and the
+ *      combine order match mpp41_moe_w4a4, so the result is identical to it.
+ *      capacity bounds the rows one rank may receive (P * tokens * top_k
+ *      always suffices); scratch: mpp41_moe_ep_scratch_layout. ---- */
+enum {
+    MPP41_MOE_EP_ALLC, MPP41_MOE_EP_SEGS, MPP41_MOE_EP_TILES, MPP41_MOE_EP_NTILES, MPP41_MOE_EP_RQ,
+    MPP41_MOE_EP_RS, MPP41_MOE_EP_GQ, MPP41_MOE_EP_GS, MPP41_MOE_EP_GMQ, MPP41_MOE_EP_GMS, MPP41_MOE_EP_GY,
+    MPP41_MOE_EP_RY, MPP41_MOE_EP_PARTS
+};
+size_t mpp41_moe_ep_scratch_layout(const mpp41_moe_desc *desc, int nranks, uint32_t capacity, size_t *offsets);
+mpp41_status mpp41_moe_ep(mpp41_ctx *ctx, const mpp41_moe_desc *desc, uint32_t capacity, const void *x,
+                          const float *logits, const uint8_t *wg, const uint8_t *sg, const uint8_t *wu,
+                          const uint8_t *su, const uint8_t *wd, const uint8_t *sd, const uint8_t *shared_wg,
+                          const uint8_t *shared_sg, const uint8_t *shared_wu, const uint8_t *shared_su,
+                          const uint8_t *shared_wd, const uint8_t *shared_sd, void *out, void *scratch);
+
 /* ---- tensor parallelism (no counterpart in the
  *      single-GPU reference). Rank r of P holds rows [r*I/P, (r+1)*I/P) of the
  *      gate and up weights (and their scale rows) and the same columns of the

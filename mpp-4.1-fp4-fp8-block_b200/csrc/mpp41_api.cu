@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <vector>
 #include <string>
 
 #include "../../include/mpp41.h"
@@ -1084,6 +1085,110 @@ mpp41_status mpp41_moe_route(mpp41_ctx *ctx, const float *logits, uint32_t T, ui
     return MPP41_OK;
 }
 
+namespace {
+// Scratch views of the single-GPU layout.
+struct MoeBuf {
+    uint8_t *b;
+    size_t off[MPP41_MOE_PARTS];
+    uint8_t *u8(int part) const { return b + off[part]; }
+    uint32_t *u32(int part) const { return reinterpret_cast<uint32_t *>(b + off[part]); }
+    float *f32(int part) const { return reinterpret_cast<float *>(b + off[part]); }
+};
+
+mpp41_status moe_check_ptrs(const mpp41_moe_desc *d, const void *x, const float *logits, const void *wg,
+                            const void *sg, const void *wu, const void *su, const void *wd, const void *sd,
+                            const void *const shared[6], const void *out, const void *scratch)
+{
+    if (!x || !logits || !wg || !sg || !wu || !su || !wd || !sd || !out || !scratch)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if (d->shared_intermediate)
+        for (int i = 0; i < 6; ++i)
+            if (!shared[i]) return fail(MPP41_ERR_INVALID_ARGUMENT, "shared expert weights missing");
+    if ((reinterpret_cast<uintptr_t>(scratch) & 255u) || !al16(x) || !al16(out))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "x and out must be 16-byte aligned, scratch 256-byte");
+    return MPP41_OK;
+}
+
+// Quantize x, route, group this rank's assignments by expert (all E experts)
+// and gather the quantized rows into that order.
+mpp41_status moe_front(mpp41_ctx *ctx, const mpp41_moe_desc *d, const void *x, const float *logits, const MoeBuf &m)
+{
+    const uint32_t T = d->tokens, H = d->hidden, E = d->experts, k = d->top_k, R = T * k;
+    cudaStream_t st = ctx->stream;
+    CK(launch_quantize_mxfp4_f16(x, T, H, m.u8(MPP41_MOE_XQ), m.u8(MPP41_MOE_XS), st), "quantize x");
+    CK(launch_moe_route(logits, T, E, k, reinterpret_cast<int32_t *>(m.u8(MPP41_MOE_IDS)), m.f32(MPP41_MOE_WEIGHTS),
+                        st), "route");
+    CK(launch_moe_permute(reinterpret_cast<int32_t *>(m.u8(MPP41_MOE_IDS)), R, E, 128, m.u32(MPP41_MOE_COUNTS),
+                          m.u32(MPP41_MOE_OFFSETS), reinterpret_cast<uint4 *>(m.u8(MPP41_MOE_TILES)),
+                          m.u32(MPP41_MOE_NTILES), m.u32(MPP41_MOE_PERM), m.u32(MPP41_MOE_INV), ctx->err, st),
+       "permute");
+    const uint32_t *n_rows = m.u32(MPP41_MOE_OFFSETS) + E;
+    CK(launch_moe_gather(m.u8(MPP41_MOE_XQ), H / 2, m.u32(MPP41_MOE_PERM), k, n_rows, R, m.u8(MPP41_MOE_PQ), st),
+       "gather x");
+    CK(launch_moe_gather(m.u8(MPP41_MOE_XS), H / 32, m.u32(MPP41_MOE_PERM), k, n_rows, R, m.u8(MPP41_MOE_PS), st),
+       "gather x scales");
+    return MPP41_OK;
+}
+
+// Grouped expert MLP over rows already grouped by expert: aq/as -> y [rows][H] fp32.
+mpp41_status moe_experts(mpp41_ctx *ctx, uint32_t H, uint32_t I, uint32_t E, uint32_t rows, uint32_t max_tiles,
+                         const uint4 *tiles, const uint32_t *n_tiles, const uint8_t *aq, const uint8_t *as,
+                         const uint8_t *wg, const uint8_t *sg, const uint8_t *wu, const uint8_t *su,
+                         const uint8_t *wd, const uint8_t *sd, uint8_t *mq, uint8_t *ms, float *y)
+{
+    if (!rows) return MPP41_OK;
+    MxLaunch g{};
+    g.a = aq; g.sa = as;
+    g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
+    g.b_rows = E * I; g.b0_row0 = 0; g.b1_row0 = 0; g.b_row_step = 128;
+    g.out = mq; g.out_scales = ms;
+    g.M = rows; g.N = I; g.K = H; g.ldc = I; g.epi = 2;
+    g.tiles = tiles; g.n_tiles = n_tiles; g.max_tiles = max_tiles; g.b_expert_rows = I;
+    g.err = ctx->err;
+    mpp41_status s = enqueue_mxf4(ctx, g, "MoE gate/up GEMM");
+    if (s != MPP41_OK) return s;
+    MxLaunch dn{};
+    dn.a = mq; dn.sa = ms;
+    dn.b0 = dn.b1 = wd; dn.sb0 = dn.sb1 = sd;
+    dn.b_rows = E * H; dn.b0_row0 = 0; dn.b1_row0 = 128; dn.b_row_step = 256;
+    dn.out = y; dn.M = rows; dn.N = H; dn.K = I; dn.ldc = H; dn.epi = 0;
+    dn.tiles = tiles; dn.n_tiles = n_tiles; dn.max_tiles = max_tiles; dn.b_expert_rows = H;
+    dn.err = ctx->err;
+    return enqueue_mxf4(ctx, dn, "MoE down GEMM");
+}
+
+// Shared expert on this rank's quantized x, then the weighted combine.
+mpp41_status moe_back(mpp41_ctx *ctx, const mpp41_moe_desc *d, const void *const shared[6], const MoeBuf &m,
+                      void *out)
+{
+    const uint32_t T = d->tokens, H = d->hidden, Is = d->shared_intermediate;
+    const float *shared_y = nullptr;
+    if (Is) {
+        MxLaunch g{};
+        g.a = m.u8(MPP41_MOE_XQ); g.sa = m.u8(MPP41_MOE_XS);
+        g.b0 = shared[0]; g.sb0 = shared[1]; g.b1 = shared[2]; g.sb1 = shared[3];
+        g.b_rows = Is; g.b_row_step = 128;
+        g.out = m.u8(MPP41_MOE_SMQ); g.out_scales = m.u8(MPP41_MOE_SMS);
+        g.M = T; g.N = Is; g.K = H; g.ldc = Is; g.epi = 2;
+        g.err = ctx->err;
+        mpp41_status s = enqueue_mxf4(ctx, g, "shared expert gate/up GEMM");
+        if (s != MPP41_OK) return s;
+        MxLaunch dn{};
+        dn.a = m.u8(MPP41_MOE_SMQ); dn.sa = m.u8(MPP41_MOE_SMS);
+        dn.b0 = dn.b1 = shared[4]; dn.sb0 = dn.sb1 = shared[5];
+        dn.b_rows = H; dn.b1_row0 = 128; dn.b_row_step = 256;
+        dn.out = m.u8(MPP41_MOE_SY); dn.M = T; dn.N = H; dn.K = Is; dn.ldc = H; dn.epi = 0;
+        dn.err = ctx->err;
+        s = enqueue_mxf4(ctx, dn, "shared expert down GEMM");
+        if (s != MPP41_OK) return s;
+        shared_y = m.f32(MPP41_MOE_SY);
+    }
+    CK(launch_moe_combine(m.f32(MPP41_MOE_Y), m.u32(MPP41_MOE_INV), m.f32(MPP41_MOE_WEIGHTS), T, d->top_k, H,
+                          shared_y, out, d->out_f16 != 0, ctx->stream), "combine");
+    return MPP41_OK;
+}
+}  // namespace
+
 mpp41_status mpp41_moe_w4a4(mpp41_ctx *ctx, const mpp41_moe_desc *d, const void *x, const float *logits,
                             const uint8_t *wg, const uint8_t *sg, const uint8_t *wu, const uint8_t *su,
                             const uint8_t *wd, const uint8_t *sd, const uint8_t *shared_wg, const uint8_t *shared_sg,
@@ -1093,77 +1198,129 @@ mpp41_status mpp41_moe_w4a4(mpp41_ctx *ctx, const mpp41_moe_desc *d, const void 
     NEED(ctx);
     mpp41_status s = check_moe(d);
     if (s != MPP41_OK) return s;
-    const uint32_t T = d->tokens, H = d->hidden, I = d->intermediate, E = d->experts, k = d->top_k;
-    const uint32_t Is = d->shared_intermediate, R = T * k;
-    if (!T) return MPP41_OK;
-    if (!x || !logits || !wg || !sg || !wu || !su || !wd || !sd || !out || !scratch)
-        return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
-    if (Is && (!shared_wg || !shared_sg || !shared_wu || !shared_su || !shared_wd || !shared_sd))
-        return fail(MPP41_ERR_INVALID_ARGUMENT, "shared expert weights missing");
-    if ((reinterpret_cast<uintptr_t>(scratch) & 255u) || !al16(x) || !al16(out))
-        return fail(MPP41_ERR_INVALID_ARGUMENT, "x and out must be 16-byte aligned, scratch 256-byte");
-    size_t off[MPP41_MOE_PARTS];
-    mpp41_moe_scratch_layout(d, off);
-    uint8_t *b = static_cast<uint8_t *>(scratch);
-    auto u8 = [&](int part) { return b + off[part]; };
-    auto u32 = [&](int part) { return reinterpret_cast<uint32_t *>(b + off[part]); };
-    cudaStream_t st = ctx->stream;
-    const uint32_t max_tiles = R / 128 + E + 1;
-    CK(launch_quantize_mxfp4_f16(x, T, H, u8(MPP41_MOE_XQ), u8(MPP41_MOE_XS), st), "quantize x");
-    CK(launch_moe_route(logits, T, E, k, reinterpret_cast<int32_t *>(u8(MPP41_MOE_IDS)),
-                        reinterpret_cast<float *>(u8(MPP41_MOE_WEIGHTS)), st), "route");
-    CK(launch_moe_permute(reinterpret_cast<int32_t *>(u8(MPP41_MOE_IDS)), R, E, 128, u32(MPP41_MOE_COUNTS),
-                          u32(MPP41_MOE_OFFSETS), reinterpret_cast<uint4 *>(u8(MPP41_MOE_TILES)), u32(MPP41_MOE_NTILES),
-                          u32(MPP41_MOE_PERM), u32(MPP41_MOE_INV), ctx->err, st), "permute");
-    const uint32_t *n_rows = u32(MPP41_MOE_OFFSETS) + E;
-    CK(launch_moe_gather(u8(MPP41_MOE_XQ), H / 2, u32(MPP41_MOE_PERM), k, n_rows, R, u8(MPP41_MOE_PQ), st), "gather x");
-    CK(launch_moe_gather(u8(MPP41_MOE_XS), H / 32, u32(MPP41_MOE_PERM), k, n_rows, R, u8(MPP41_MOE_PS), st),
-       "gather x scales");
-    MxLaunch g{};
-    g.a = u8(MPP41_MOE_PQ); g.sa = u8(MPP41_MOE_PS);
-    g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
-    g.b_rows = E * I; g.b0_row0 = 0; g.b1_row0 = 0; g.b_row_step = 128;
-    g.out = u8(MPP41_MOE_MQ); g.out_scales = u8(MPP41_MOE_MS);
-    g.M = R; g.N = I; g.K = H; g.ldc = I; g.epi = 2;
-    g.tiles = reinterpret_cast<const uint4 *>(u8(MPP41_MOE_TILES)); g.n_tiles = u32(MPP41_MOE_NTILES);
-    g.max_tiles = max_tiles; g.b_expert_rows = I;
-    g.err = ctx->err;
-    s = enqueue_mxf4(ctx, g, "MoE gate/up GEMM");
+    if (!d->tokens) return MPP41_OK;
+    const void *const shared[6] = {shared_wg, shared_sg, shared_wu, shared_su, shared_wd, shared_sd};
+    s = moe_check_ptrs(d, x, logits, wg, sg, wu, su, wd, sd, shared, out, scratch);
     if (s != MPP41_OK) return s;
-    MxLaunch dn{};
-    dn.a = u8(MPP41_MOE_MQ); dn.sa = u8(MPP41_MOE_MS);
-    dn.b0 = dn.b1 = wd; dn.sb0 = dn.sb1 = sd;
-    dn.b_rows = E * H; dn.b0_row0 = 0; dn.b1_row0 = 128; dn.b_row_step = 256;
-    dn.out = u8(MPP41_MOE_Y); dn.M = R; dn.N = H; dn.K = I; dn.ldc = H; dn.epi = 0;
-    dn.tiles = g.tiles; dn.n_tiles = g.n_tiles; dn.max_tiles = max_tiles; dn.b_expert_rows = H;
-    dn.err = ctx->err;
-    s = enqueue_mxf4(ctx, dn, "MoE down GEMM");
+    MoeBuf m;
+    m.b = static_cast<uint8_t *>(scratch);
+    mpp41_moe_scratch_layout(d, m.off);
+    s = moe_front(ctx, d, x, logits, m);
     if (s != MPP41_OK) return s;
-    const float *shared_y = nullptr;
-    if (Is) {
-        MxLaunch sg_{};
-        sg_.a = u8(MPP41_MOE_XQ); sg_.sa = u8(MPP41_MOE_XS);
-        sg_.b0 = shared_wg; sg_.sb0 = shared_sg; sg_.b1 = shared_wu; sg_.sb1 = shared_su;
-        sg_.b_rows = Is; sg_.b_row_step = 128;
-        sg_.out = u8(MPP41_MOE_SMQ); sg_.out_scales = u8(MPP41_MOE_SMS);
-        sg_.M = T; sg_.N = Is; sg_.K = H; sg_.ldc = Is; sg_.epi = 2;
-        sg_.err = ctx->err;
-        s = enqueue_mxf4(ctx, sg_, "shared expert gate/up GEMM");
-        if (s != MPP41_OK) return s;
-        MxLaunch sd_{};
-        sd_.a = u8(MPP41_MOE_SMQ); sd_.sa = u8(MPP41_MOE_SMS);
-        sd_.b0 = sd_.b1 = shared_wd; sd_.sb0 = sd_.sb1 = shared_sd;
-        sd_.b_rows = H; sd_.b1_row0 = 128; sd_.b_row_step = 256;
-        sd_.out = u8(MPP41_MOE_SY); sd_.M = T; sd_.N = H; sd_.K = Is; sd_.ldc = H; sd_.epi = 0;
-        sd_.err = ctx->err;
-        s = enqueue_mxf4(ctx, sd_, "shared expert down GEMM");
-        if (s != MPP41_OK) return s;
-        shared_y = reinterpret_cast<const float *>(u8(MPP41_MOE_SY));
+    const uint32_t R = d->tokens * d->top_k;
+    s = moe_experts(ctx, d->hidden, d->intermediate, d->experts, R, R / 128 + d->experts + 1,
+                    reinterpret_cast<const uint4 *>(m.u8(MPP41_MOE_TILES)), m.u32(MPP41_MOE_NTILES),
+                    m.u8(MPP41_MOE_PQ), m.u8(MPP41_MOE_PS), wg, sg, wu, su, wd, sd, m.u8(MPP41_MOE_MQ),
+                    m.u8(MPP41_MOE_MS), m.f32(MPP41_MOE_Y));
+    if (s != MPP41_OK) return s;
+    return moe_back(ctx, d, shared, m, out);
+}
+
+// ------------------------------------------------------------------ expert parallel
+size_t mpp41_moe_ep_scratch_layout(const mpp41_moe_desc *d, int nranks, uint32_t capacity, size_t *offsets)
+{
+    if (!d || nranks < 1 || d->experts % (uint32_t)nranks) return 0;
+    const size_t P = (size_t)nranks, E = d->experts, El = E / P, H = d->hidden, I = d->intermediate, C = capacity;
+    size_t o = mpp41_moe_scratch_layout(d, nullptr);
+    const size_t sizes[MPP41_MOE_EP_PARTS] = {P * E * 4, P * El * 16, (C / 128 + El + 1) * 16, 4,
+                                              C * H / 2, C * H / 32, C * H / 2, C * H / 32, C * I / 2, C * I / 32,
+                                              C * H * 4, C * H * 4};
+    for (int i = 0; i < MPP41_MOE_EP_PARTS; ++i) {
+        if (offsets) offsets[i] = o;
+        o += up256(sizes[i]);
     }
-    CK(launch_moe_combine(reinterpret_cast<const float *>(u8(MPP41_MOE_Y)), u32(MPP41_MOE_INV),
-                          reinterpret_cast<const float *>(u8(MPP41_MOE_WEIGHTS)), T, k, H, shared_y, out,
-                          d->out_f16 != 0, st), "combine");
-    return MPP41_OK;
+    return o;
+}
+
+mpp41_status mpp41_moe_ep(mpp41_ctx *ctx, const mpp41_moe_desc *d, uint32_t capacity, const void *x,
+                          const float *logits, const uint8_t *wg, const uint8_t *sg, const uint8_t *wu,
+                          const uint8_t *su, const uint8_t *wd, const uint8_t *sd, const uint8_t *shared_wg,
+                          const uint8_t *shared_sg, const uint8_t *shared_wu, const uint8_t *shared_su,
+                          const uint8_t *shared_wd, const uint8_t *shared_sd, void *out, void *scratch)
+{
+    NEED(ctx);
+    mpp41_status s = check_moe(d);
+    if (s != MPP41_OK) return s;
+    const int P = comm_size(ctx), rank = comm_rank(ctx);
+    if (P < 1) return fail(MPP41_ERR_COMM, "mpp41_comm_init has not been called on this context");
+    if (d->experts % (uint32_t)P) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "experts must divide over the ranks");
+    const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, El = E / (uint32_t)P, k = d->top_k;
+    const void *const shared[6] = {shared_wg, shared_sg, shared_wu, shared_su, shared_wd, shared_sd};
+    if (d->tokens) {
+        s = moe_check_ptrs(d, x, logits, wg, sg, wu, su, wd, sd, shared, out, scratch);
+        if (s != MPP41_OK) return s;
+    } else if (!scratch) {
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "null scratch");
+    }
+    MoeBuf m;
+    m.b = static_cast<uint8_t *>(scratch);
+    mpp41_moe_scratch_layout(d, m.off);
+    size_t eo[MPP41_MOE_EP_PARTS];
+    mpp41_moe_ep_scratch_layout(d, P, capacity, eo);
+    auto ep = [&](int part) { return m.b + eo[part]; };
+    cudaStream_t st = ctx->stream;
+    if (d->tokens) {
+        s = moe_front(ctx, d, x, logits, m);
+        if (s != MPP41_OK) return s;
+    } else {
+        CK(cudaMemsetAsync(m.u32(MPP41_MOE_COUNTS), 0, E * 4, st), "clear counts");
+    }
+    // every rank's per-expert counts; the host sizes the exchanges from them
+    s = comm_allgather(ctx, m.u32(MPP41_MOE_COUNTS), ep(MPP41_MOE_EP_ALLC), E * 4);
+    if (s != MPP41_OK) return s;
+    std::vector<uint32_t> allc((size_t)P * E);
+    CK(cudaMemcpyAsync(allc.data(), ep(MPP41_MOE_EP_ALLC), allc.size() * 4, cudaMemcpyDeviceToHost, st),
+       "read expert counts");
+    CK(cudaStreamSynchronize(st), "read expert counts");
+    std::vector<size_t> send_rows(P, 0), recv_rows(P, 0), send_off(P, 0), recv_off(P, 0);
+    for (int p = 0; p < P; ++p)
+        for (uint32_t le = 0; le < El; ++le) {
+            send_rows[p] += allc[(size_t)rank * E + (size_t)p * El + le];
+            recv_rows[p] += allc[(size_t)p * E + (size_t)rank * El + le];
+        }
+    size_t total_recv = 0, total_send = 0;
+    for (int p = 0; p < P; ++p) {
+        send_off[p] = total_send;
+        recv_off[p] = total_recv;
+        total_send += send_rows[p];
+        total_recv += recv_rows[p];
+    }
+    if (total_recv > capacity)
+        return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "rank %d receives %zu rows, capacity is %u", rank, total_recv,
+                    capacity);
+    auto scaled = [&](const std::vector<size_t> &v, size_t unit) {
+        std::vector<size_t> r(v.size());
+        for (size_t i = 0; i < v.size(); ++i) r[i] = v[i] * unit;
+        return r;
+    };
+    // dispatch: quantized rows and their scales, grouped by destination rank
+    s = comm_alltoallv(ctx, m.u8(MPP41_MOE_PQ), scaled(send_rows, H / 2).data(), scaled(send_off, H / 2).data(),
+                       ep(MPP41_MOE_EP_RQ), scaled(recv_rows, H / 2).data(), scaled(recv_off, H / 2).data());
+    if (s != MPP41_OK) return s;
+    s = comm_alltoallv(ctx, m.u8(MPP41_MOE_PS), scaled(send_rows, H / 32).data(), scaled(send_off, H / 32).data(),
+                       ep(MPP41_MOE_EP_RS), scaled(recv_rows, H / 32).data(), scaled(recv_off, H / 32).data());
+    if (s != MPP41_OK) return s;
+    // received rows are source-major; the experts want them expert-major
+    const uint32_t max_tiles = capacity / 128 + El + 1;
+    uint4 *segs = reinterpret_cast<uint4 *>(ep(MPP41_MOE_EP_SEGS));
+    CK(launch_moe_ep_plan(reinterpret_cast<const uint32_t *>(ep(MPP41_MOE_EP_ALLC)), P, E, rank, 128, segs,
+                          reinterpret_cast<uint4 *>(ep(MPP41_MOE_EP_TILES)),
+                          reinterpret_cast<uint32_t *>(ep(MPP41_MOE_EP_NTILES)), st), "plan");
+    CK(launch_moe_segments(ep(MPP41_MOE_EP_RQ), ep(MPP41_MOE_EP_GQ), H / 2, segs, P * El, false, st), "group rows");
+    CK(launch_moe_segments(ep(MPP41_MOE_EP_RS), ep(MPP41_MOE_EP_GS), H / 32, segs, P * El, false, st), "group scales");
+    s = moe_experts(ctx, H, I, El, (uint32_t)total_recv, max_tiles, reinterpret_cast<const uint4 *>(ep(MPP41_MOE_EP_TILES)),
+                    reinterpret_cast<const uint32_t *>(ep(MPP41_MOE_EP_NTILES)), ep(MPP41_MOE_EP_GQ),
+                    ep(MPP41_MOE_EP_GS), wg, sg, wu, su, wd, sd, ep(MPP41_MOE_EP_GMQ), ep(MPP41_MOE_EP_GMS),
+                    reinterpret_cast<float *>(ep(MPP41_MOE_EP_GY)));
+    if (s != MPP41_OK) return s;
+    CK(launch_moe_segments(ep(MPP41_MOE_EP_GY), ep(MPP41_MOE_EP_RY), H * 4, segs, P * El, true, st), "ungroup rows");
+    // combine exchange: fp32 rows go back to the ranks that own the tokens, in
+    // the order those ranks sent them (their expert-major local order)
+    s = comm_alltoallv(ctx, ep(MPP41_MOE_EP_RY), scaled(recv_rows, H * 4).data(), scaled(recv_off, H * 4).data(),
+                       m.u8(MPP41_MOE_Y), scaled(send_rows, H * 4).data(), scaled(send_off, H * 4).data());
+    if (s != MPP41_OK) return s;
+    if (!d->tokens) return MPP41_OK;
+    return moe_back(ctx, d, shared, m, out);
 }
 
 mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x, const void *wg,

@@ -110,6 +110,10 @@ cudaError_t launch_moe_permute(const int32_t *ids, uint32_t n, uint32_t E, uint3
                                uint32_t *err, cudaStream_t st);
 cudaError_t launch_moe_gather(const void *src, uint32_t row_bytes, const uint32_t *perm_src, uint32_t k,
                               const uint32_t *n_rows, uint32_t max_rows, void *dst, cudaStream_t st);
+cudaError_t launch_moe_ep_plan(const uint32_t *allc, uint32_t P, uint32_t E, uint32_t rank, uint32_t bm, uint4 *segs,
+                               uint4 *tiles, uint32_t *n_tiles, cudaStream_t st);
+cudaError_t launch_moe_segments(const void *src, void *dst, uint32_t row_bytes, const uint4 *segs, uint32_t nsegs,
+                                bool to_recv, cudaStream_t st);
 cudaError_t launch_moe_combine(const float *y, const uint32_t *inv, const float *w, uint32_t T, uint32_t k, uint32_t H,
                                const float *shared_y, void *out, bool out_f16, cudaStream_t st);
 
@@ -208,4 +212,9 @@ struct mpp41_ctx {
 
 namespace mpp41 {
 void comm_release(mpp41_ctx *ctx);
+int comm_size(const mpp41_ctx *ctx);
+int comm_rank(const mpp41_ctx *ctx);
+mpp41_status comm_allgather(mpp41_ctx *ctx, const void *send, void *recv, size_t bytes_per_rank);
+mpp41_status comm_alltoallv(mpp41_ctx *ctx, const void *send, const size_t *send_bytes, const size_t *send_off,
+                            void *recv, const size_t *recv_bytes, const size_t *recv_off);
 }  // namespace mpp41

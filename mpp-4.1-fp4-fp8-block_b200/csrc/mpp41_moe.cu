@@ -180,6 +180,47 @@ __global__ void combine_kernel(const float *__restrict__ y, const uint32_t *__re
     }
 }
 
+// Expert parallel: from every rank's per-expert counts allc[P][E], the
+// segments {row in the receive buffer (source-major), row in the grouped
+// buffer (expert-major), rows} of (source s, local expert le) at [s * El + le],
+// and the row-tile table of the grouped buffer. One thread: P * El is small.
+__global__ void ep_plan_kernel(const uint32_t *__restrict__ allc, uint32_t P, uint32_t E, uint32_t rank, uint32_t bm,
+                               uint4 *__restrict__ segs, uint4 *__restrict__ tiles, uint32_t *__restrict__ n_tiles)
+{
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const uint32_t El = E / P;
+    uint32_t base = 0;
+    for (uint32_t s = 0; s < P; ++s)
+        for (uint32_t le = 0; le < El; ++le) {
+            const uint32_t n = allc[(size_t)s * E + (size_t)rank * El + le];
+            segs[s * El + le] = make_uint4(base, 0u, n, 0u);
+            base += n;
+        }
+    uint32_t off = 0, nt = 0;
+    for (uint32_t le = 0; le < El; ++le) {
+        const uint32_t start = off;
+        for (uint32_t s = 0; s < P; ++s) {
+            segs[s * El + le].y = off;
+            off += segs[s * El + le].z;
+        }
+        for (uint32_t r = start; r < off; r += bm) tiles[nt++] = make_uint4(le, r, off, 0u);
+    }
+    *n_tiles = nt;
+}
+
+// One CTA per segment: a contiguous copy of rows * row_bytes bytes between
+// the receive layout and the grouped layout (either direction).
+__global__ void segments_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, uint32_t row_bytes,
+                                const uint4 *__restrict__ segs, bool to_recv)
+{
+    const uint4 sg = segs[blockIdx.x];
+    const size_t from = (size_t)(to_recv ? sg.y : sg.x) * row_bytes, to = (size_t)(to_recv ? sg.x : sg.y) * row_bytes;
+    const size_t n16 = (size_t)sg.z * row_bytes / 16;
+    const uint4 *s = reinterpret_cast<const uint4 *>(src + from);
+    uint4 *d = reinterpret_cast<uint4 *>(dst + to);
+    for (size_t i = threadIdx.x; i < n16; i += blockDim.x) d[i] = s[i];
+}
+
 }  // namespace moe
 
 static unsigned grid_cap(size_t work, unsigned block, unsigned cap)
@@ -214,6 +255,22 @@ cudaError_t launch_moe_gather(const void *src, uint32_t row_bytes, const uint32_
     if (!max_rows) return cudaSuccess;
     moe::gather_rows_kernel<<<grid_cap((size_t)max_rows * 32, 256, 148 * 8), 256, 0, st>>>(
         static_cast<const uint8_t *>(src), row_bytes, perm_src, k, n_rows, static_cast<uint8_t *>(dst));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_ep_plan(const uint32_t *allc, uint32_t P, uint32_t E, uint32_t rank, uint32_t bm, uint4 *segs,
+                               uint4 *tiles, uint32_t *n_tiles, cudaStream_t st)
+{
+    moe::ep_plan_kernel<<<1, 32, 0, st>>>(allc, P, E, rank, bm, segs, tiles, n_tiles);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_segments(const void *src, void *dst, uint32_t row_bytes, const uint4 *segs, uint32_t nsegs,
+                                bool to_recv, cudaStream_t st)
+{
+    if (!nsegs) return cudaSuccess;
+    moe::segments_kernel<<<nsegs, 256, 0, st>>>(static_cast<const uint8_t *>(src), static_cast<uint8_t *>(dst),
+                                                row_bytes, segs, to_recv);
     return cudaGetLastError();
 }
 

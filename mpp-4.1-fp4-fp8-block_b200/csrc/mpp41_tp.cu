@@ -23,6 +23,11 @@ struct NcclApi {
     decltype(&ncclCommDestroy) comm_destroy = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclSend) send = nullptr;
+    decltype(&ncclRecv) recv = nullptr;
+    decltype(&ncclGroupStart) group_start = nullptr;
+    decltype(&ncclGroupEnd) group_end = nullptr;
 };
 
 std::mutex g_nccl_mu;
@@ -48,7 +53,14 @@ const NcclApi *nccl()
     a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
-    if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.all_reduce || !a.error_string) return nullptr;
+    a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
+    a.send = reinterpret_cast<decltype(a.send)>(dlsym(h, "ncclSend"));
+    a.recv = reinterpret_cast<decltype(a.recv)>(dlsym(h, "ncclRecv"));
+    a.group_start = reinterpret_cast<decltype(a.group_start)>(dlsym(h, "ncclGroupStart"));
+    a.group_end = reinterpret_cast<decltype(a.group_end)>(dlsym(h, "ncclGroupEnd"));
+    if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.all_reduce || !a.error_string ||
+        !a.all_gather || !a.send || !a.recv || !a.group_start || !a.group_end)
+        return nullptr;
     g_nccl = a;
     return &g_nccl;
 }
@@ -71,6 +83,41 @@ struct CommState {
     ncclComm_t comm = nullptr;
     int nranks = 0, rank = 0;
 };
+
+int comm_size(const mpp41_ctx *ctx) { return ctx && ctx->comm ? ctx->comm->nranks : 0; }
+int comm_rank(const mpp41_ctx *ctx) { return ctx && ctx->comm ? ctx->comm->rank : -1; }
+
+mpp41_status comm_allgather(mpp41_ctx *ctx, const void *send, void *recv, size_t bytes_per_rank)
+{
+    const NcclApi *a = nccl();
+    if (!a || !ctx->comm) return err(MPP41_ERR_COMM, "no communicator%s", nullptr);
+    const ncclResult_t r = a->all_gather(send, recv, bytes_per_rank, ncclUint8, ctx->comm->comm, ctx->stream);
+    if (r != ncclSuccess) return err(MPP41_ERR_COMM, "ncclAllGather: %s", a->error_string(r));
+    return MPP41_OK;
+}
+
+// Personalised all-to-all in one NCCL group: rank p gets send_bytes[p] bytes
+// from send + send_off[p]; recv_bytes[s] bytes from rank s land at recv + recv_off[s].
+mpp41_status comm_alltoallv(mpp41_ctx *ctx, const void *send, const size_t *send_bytes, const size_t *send_off,
+                            void *recv, const size_t *recv_bytes, const size_t *recv_off)
+{
+    const NcclApi *a = nccl();
+    if (!a || !ctx->comm) return err(MPP41_ERR_COMM, "no communicator%s", nullptr);
+    const int P = ctx->comm->nranks;
+    ncclResult_t r = a->group_start();
+    for (int p = 0; p < P && r == ncclSuccess; ++p) {
+        if (send_bytes[p])
+            r = a->send(static_cast<const uint8_t *>(send) + send_off[p], send_bytes[p], ncclUint8, p, ctx->comm->comm,
+                        ctx->stream);
+        if (r == ncclSuccess && recv_bytes[p])
+            r = a->recv(static_cast<uint8_t *>(recv) + recv_off[p], recv_bytes[p], ncclUint8, p, ctx->comm->comm,
+                        ctx->stream);
+    }
+    const ncclResult_t r2 = a->group_end();
+    if (r != ncclSuccess) return err(MPP41_ERR_COMM, "ncclSend/ncclRecv: %s", a->error_string(r));
+    if (r2 != ncclSuccess) return err(MPP41_ERR_COMM, "ncclGroupEnd: %s", a->error_string(r2));
+    return MPP41_OK;
+}
 
 void comm_release(mpp41_ctx *ctx)
 {

@@ -125,6 +125,8 @@ def lib() -> C.CDLL:
         "mpp41_moe_scratch_layout": ([C.POINTER(MoEDesc), vp], sz),
         "mpp41_moe_route": ([vp, vp, u32, u32, u32, vp, vp], st),
         "mpp41_moe_w4a4": ([vp, C.POINTER(MoEDesc)] + [vp] * 16, st),
+        "mpp41_moe_ep_scratch_layout": ([C.POINTER(MoEDesc), C.c_int, u32, vp], sz),
+        "mpp41_moe_ep": ([vp, C.POINTER(MoEDesc), u32] + [vp] * 16, st),
         "mpp41_mlp_nvfp4": ([vp, u32, u32, u32] + [vp] * 11 + [C.c_int, vp], st),
         "mpp41_mlp_noalloc_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp_noalloc": ([C.POINTER(MLPDesc)] + [vp] * 9, st),
@@ -204,6 +206,10 @@ def moe_scratch_layout(desc: MoEDesc):
     offs = (C.c_size_t * len(MOE_PARTS))()
     total = lib().mpp41_moe_scratch_layout(C.byref(desc), offs)
     return total, dict(zip(MOE_PARTS, list(offs)))
+
+
+def moe_ep_scratch_bytes(desc: MoEDesc, nranks: int, capacity: int) -> int:
+    return lib().mpp41_moe_ep_scratch_layout(C.byref(desc), nranks, capacity, None)
 
 
 def has_kernel(name: str) -> bool:
@@ -397,6 +403,12 @@ class Context:
         sh = [_ptr(v) for v in shared] if shared is not None else [None] * 6
         _check(lib().mpp41_moe_w4a4(self.h, C.byref(desc), _ptr(x), _ptr(logits), _ptr(wg), _ptr(sg), _ptr(wu),
                                     _ptr(su), _ptr(wd), _ptr(sd), *sh, _ptr(out), _ptr(scratch)))
+
+    def moe_ep(self, desc: "MoEDesc", capacity: int, x, logits, wg, sg, wu, su, wd, sd, out, scratch, shared=None):
+        """Expert-parallel MoE layer (mpp41_moe_ep) over this context's communicator; w* hold this rank's experts."""
+        sh = [_ptr(v) for v in shared] if shared is not None else [None] * 6
+        _check(lib().mpp41_moe_ep(self.h, C.byref(desc), capacity, _ptr(x), _ptr(logits), _ptr(wg), _ptr(sg),
+                                  _ptr(wu), _ptr(su), _ptr(wd), _ptr(sd), *sh, _ptr(out), _ptr(scratch)))
 
     def mlp_w4a4(self, tokens: int, hidden: int, intermediate: int, x, wg, sg, wu, su, wd, sd, out, scratch,
                  out_f16: bool = False):
