@@ -1244,7 +1244,7 @@ mpp41_status mpp41_moe_ep(mpp41_ctx *ctx, const mpp41_moe_desc *d, uint32_t capa
     const int P = comm_size(ctx), rank = comm_rank(ctx);
     if (P < 1) return fail(MPP41_ERR_COMM, "mpp41_comm_init has not been called on this context");
     if (d->experts % (uint32_t)P) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "experts must divide over the ranks");
-    const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, El = E / (uint32_t)P, k = d->top_k;
+    const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, El = E / (uint32_t)P;
     const void *const shared[6] = {shared_wg, shared_sg, shared_wu, shared_su, shared_wd, shared_sd};
     if (d->tokens) {
         s = moe_check_ptrs(d, x, logits, wg, sg, wu, su, wd, sd, shared, out, scratch);

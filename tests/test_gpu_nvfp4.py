@@ -52,7 +52,7 @@ def _rand_nv(rng, rows, K, lo=None, hi=None):
     return packed, scales
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (200, 96, 768), (1, 512, 1024)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (200, 96, 768), (1, 512, 1024), (640, 512, 1024)])
 def test_nvf4_gemm_bit_exact(ctx, M, N, K):
     rng = np.random.default_rng(M + N * 3 + K)
     a, sa = _rand_nv(rng, M, K)
@@ -88,7 +88,7 @@ def _weights(rng, rows, cols):
     return O.quantize_nvfp4(w)
 
 
-@pytest.mark.parametrize("T,H,I", [(128, 1024, 4096), (77, 512, 768)])
+@pytest.mark.parametrize("T,H,I", [(128, 1024, 4096), (77, 512, 768), (300, 512, 512)])
 def test_nvfp4_mlp(ctx, T, H, I):
     import mpp41
     rng = np.random.default_rng(T + I)

@@ -31,7 +31,8 @@ def _layer(T, H, I, seed):
     return d["x"], d["wg"], d["wu"], d["wd"], d["sg"], d["su"], d["sd"]
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 512), (200, 96, 1536), (1, 512, 1024), (300, 544, 512)])
+# ragged row tiles (200, 300) and several full row tiles (1024)
+@pytest.mark.parametrize("M,N,K", [(128, 256, 512), (200, 96, 1536), (1, 512, 1024), (300, 544, 512), (1024, 768, 2048)])
 def test_mxf4_gemm_bit_exact(ctx, M, N, K):
     rng = np.random.default_rng(M * 7 + N + K)
     a, sa = _rand_mx(rng, M, K)
@@ -70,7 +71,7 @@ def test_mxf4_gemm_rejects_bad_shapes(ctx):
         ctx.matmul_mxf4(d, d, d, d, d, 128, 100, 512)   # N % 32
 
 
-@pytest.mark.parametrize("T,H,I", [(128, 1024, 4096), (77, 512, 1024), (1, 1024, 512)])
+@pytest.mark.parametrize("T,H,I", [(128, 1024, 4096), (77, 512, 1024), (1, 1024, 512), (384, 1024, 1024)])
 def test_w4a4_mlp(ctx, T, H, I):
     import mpp41
     x, wg, wu, wd, sg, su, sd = _layer(T, H, I, seed=T + H)
