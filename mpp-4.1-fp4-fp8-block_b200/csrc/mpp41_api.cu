@@ -880,7 +880,7 @@ mpp41_status mpp41_matmul_mxf4(mpp41_ctx *ctx, const uint8_t *a, const uint8_t *
     MxLaunch L{};
     L.a = a; L.sa = sa;
     L.b0 = L.b1 = b; L.sb0 = L.sb1 = sb;
-    L.b_rows = N; L.b0_row0 = 0; L.b1_row0 = 128; L.b_row_step = 256;
+    L.b_rows = N;
     L.out = c; L.M = M; L.N = N; L.K = K; L.ldc = N;
     L.epi = c_f16 ? 1 : 0;
     L.err = ctx->err;
@@ -912,7 +912,7 @@ mpp41_status mpp41_mlp_w4a4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I, 
     MxLaunch g{};
     g.a = xq; g.sa = xs;
     g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
-    g.b_rows = I; g.b0_row0 = 0; g.b1_row0 = 0; g.b_row_step = 128;
+    g.b_rows = I;
     g.out = mq; g.out_scales = ms;
     g.M = T; g.N = I; g.K = H; g.ldc = I;
     g.epi = 2;
@@ -922,7 +922,7 @@ mpp41_status mpp41_mlp_w4a4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I, 
     MxLaunch d{};
     d.a = mq; d.sa = ms;
     d.b0 = d.b1 = wd; d.sb0 = d.sb1 = sd;
-    d.b_rows = H; d.b0_row0 = 0; d.b1_row0 = 128; d.b_row_step = 256;
+    d.b_rows = H;
     d.out = out; d.M = T; d.N = H; d.K = I; d.ldc = H;
     d.epi = out_f16 ? 1 : 0;
     d.err = ctx->err;
@@ -969,7 +969,7 @@ mpp41_status mpp41_matmul_nvf4(mpp41_ctx *ctx, const uint8_t *a, const uint8_t *
     MxLaunch L{};
     L.a = a; L.sa = sa;
     L.b0 = L.b1 = b; L.sb0 = L.sb1 = sb;
-    L.b_rows = N; L.b0_row0 = 0; L.b1_row0 = 128; L.b_row_step = 256;
+    L.b_rows = N;
     L.out = c; L.M = M; L.N = N; L.K = K; L.ldc = N;
     L.epi = c_f16 ? 1 : 0;
     L.nv = true; L.ts_a = ta; L.ts_b0 = L.ts_b1 = tb;
@@ -1023,7 +1023,7 @@ mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I,
     MxLaunch g{};
     g.a = s.xq; g.sa = s.xs;
     g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
-    g.b_rows = I; g.b0_row0 = 0; g.b1_row0 = 0; g.b_row_step = 128;
+    g.b_rows = I;
     g.out = s.mid; g.M = T; g.N = I; g.K = H; g.ldc = I;
     g.epi = 3;
     g.nv = true; g.ts_a = s.ts; g.ts_b0 = tg; g.ts_b1 = tu;
@@ -1035,7 +1035,7 @@ mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I,
     MxLaunch d{};
     d.a = s.mq; d.sa = s.ms;
     d.b0 = d.b1 = wd; d.sb0 = d.sb1 = sd;
-    d.b_rows = H; d.b0_row0 = 0; d.b1_row0 = 128; d.b_row_step = 256;
+    d.b_rows = H;
     d.out = out; d.M = T; d.N = H; d.K = I; d.ldc = H;
     d.epi = out_f16 ? 1 : 0;
     d.nv = true; d.ts_a = s.ts + 1; d.ts_b0 = d.ts_b1 = td;
@@ -1140,7 +1140,7 @@ mpp41_status moe_experts(mpp41_ctx *ctx, uint32_t H, uint32_t I, uint32_t E, uin
     MxLaunch g{};
     g.a = aq; g.sa = as;
     g.b0 = wg; g.sb0 = sg; g.b1 = wu; g.sb1 = su;
-    g.b_rows = E * I; g.b0_row0 = 0; g.b1_row0 = 0; g.b_row_step = 128;
+    g.b_rows = E * I;
     g.out = mq; g.out_scales = ms;
     g.M = rows; g.N = I; g.K = H; g.ldc = I; g.epi = 2;
     g.tiles = tiles; g.n_tiles = n_tiles; g.max_tiles = max_tiles; g.b_expert_rows = I;
@@ -1150,7 +1150,7 @@ mpp41_status moe_experts(mpp41_ctx *ctx, uint32_t H, uint32_t I, uint32_t E, uin
     MxLaunch dn{};
     dn.a = mq; dn.sa = ms;
     dn.b0 = dn.b1 = wd; dn.sb0 = dn.sb1 = sd;
-    dn.b_rows = E * H; dn.b0_row0 = 0; dn.b1_row0 = 128; dn.b_row_step = 256;
+    dn.b_rows = E * H;
     dn.out = y; dn.M = rows; dn.N = H; dn.K = I; dn.ldc = H; dn.epi = 0;
     dn.tiles = tiles; dn.n_tiles = n_tiles; dn.max_tiles = max_tiles; dn.b_expert_rows = H;
     dn.err = ctx->err;
@@ -1167,7 +1167,7 @@ mpp41_status moe_back(mpp41_ctx *ctx, const mpp41_moe_desc *d, const void *const
         MxLaunch g{};
         g.a = m.u8(MPP41_MOE_XQ); g.sa = m.u8(MPP41_MOE_XS);
         g.b0 = shared[0]; g.sb0 = shared[1]; g.b1 = shared[2]; g.sb1 = shared[3];
-        g.b_rows = Is; g.b_row_step = 128;
+        g.b_rows = Is;
         g.out = m.u8(MPP41_MOE_SMQ); g.out_scales = m.u8(MPP41_MOE_SMS);
         g.M = T; g.N = Is; g.K = H; g.ldc = Is; g.epi = 2;
         g.err = ctx->err;
@@ -1176,7 +1176,7 @@ mpp41_status moe_back(mpp41_ctx *ctx, const mpp41_moe_desc *d, const void *const
         MxLaunch dn{};
         dn.a = m.u8(MPP41_MOE_SMQ); dn.sa = m.u8(MPP41_MOE_SMS);
         dn.b0 = dn.b1 = shared[4]; dn.sb0 = dn.sb1 = shared[5];
-        dn.b_rows = H; dn.b1_row0 = 128; dn.b_row_step = 256;
+        dn.b_rows = H;
         dn.out = m.u8(MPP41_MOE_SY); dn.M = T; dn.N = H; dn.K = Is; dn.ldc = H; dn.epi = 0;
         dn.err = ctx->err;
         s = enqueue_mxf4(ctx, dn, "shared expert down GEMM");

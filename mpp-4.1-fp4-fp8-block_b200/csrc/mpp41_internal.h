@@ -79,15 +79,15 @@ struct F32Launch {
 int launch_f32_gemm(const F32Launch &L, cudaStream_t st, const char **why);
 
 // Block-scaled FP4 GEMM (W4A4, kind::mxf4): A [M][K/2] E2M1 + [M][K/32] E8M0
-// against B rows taken from two maps (b0 rows b0_row0 + t * b_row_step and b1
-// rows b1_row0 + t * b_row_step, 128 each, for column tile t). epi 0: fp32 C,
+// against B [N][K/2]; with the SwiGLU epilogues b0 holds the gate rows and b1
+// the up rows, otherwise b0 == b1. epi 0: fp32 C,
 // 1: fp16 C, 2: silu(gate) * up re-quantized to MXFP4 (out = packed mid
 // [M][ldc/2], out_scales = [M][ldc/32]), 3: silu(gate) * up as fp16 [M][ldc].
 // nv: NVFP4 operands (scales [rows][K/16] UE4M3; C scaled by the tensor scales).
 struct MxLaunch {
     const void *a, *sa;
     const void *b0, *sb0, *b1, *sb1;
-    uint32_t b_rows, b0_row0, b1_row0, b_row_step;
+    uint32_t b_rows;                        // rows of the B maps
     void *out;
     uint8_t *out_scales;
     uint32_t M, N, K, ldc;

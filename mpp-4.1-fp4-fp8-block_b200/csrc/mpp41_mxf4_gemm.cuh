@@ -11,7 +11,7 @@
 // cute/atom/mma_traits_sm100.hpp tmem_sf_frg with four-fold lane replication):
 // for operand row r = 32 i + j, the scales of k-blocks 4g..4g+3 of a stage are
 // the 4 bytes of column (base + R/32 * g + i) at lane j of every lane quarter,
-// R = 128 rows for A and 256 for B. MMA number 2g + h of the stage (K = 64,
+// R = 128 rows for A and BN for B. MMA number 2g + h of the stage (K = 64,
 // two scales) reads bytes 2h and 2h+1: the byte offset rides in address bits
 // 30-31 and in the instruction descriptor's scale-factor id.
 //
@@ -24,8 +24,8 @@
 //
 // Epilogues: fp32 or fp16 C, SWIGLU_F16 (silu(g) * u as fp16, the columns
 // arranged as below), or (SWIGLU_MX) the gate/up layer of a W4A4 MLP:
-// B rows 0..127 of the tile are gate rows, 128..255 the up rows of the same
-// 128 channels; each thread owns one token row, forms silu(g) * u and
+// B rows 0..BN/2-1 of the tile are gate rows, BN/2..BN-1 the up rows of the
+// same BN/2 channels; each thread owns one token row, forms silu(g) * u and
 // re-quantizes it to MXFP4 in registers (32-blocks never straddle threads), so
 // the down GEMM reads the mid as its A operand directly.
 //
@@ -48,34 +48,40 @@ namespace mxf4 {
 enum Epi { EPI_F32 = 0, EPI_F16 = 1, EPI_SWIGLU_MX = 2, EPI_SWIGLU_F16 = 3 };
 
 constexpr int kBM = 128;          // rows of A per tile (MMA M)
-constexpr int kBN = 256;          // rows of B per tile (MMA N)
 constexpr int kBK = 256;          // K per stage: one 128-byte swizzle atom of packed E2M1
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr uint32_t kATile = kBM * 128;      // 16 KB
-constexpr uint32_t kBHalf = 128 * 128;      // 16 KB: 128 B rows
-constexpr uint32_t kBTile = kBN * 128;      // 32 KB
 // Scales: a TMA box needs a 16-byte inner extent. MXFP4 has 8 scale bytes per
 // row per stage, so each stage loads the 16-byte strip holding its own and the
 // neighbour's; NVFP4 has exactly 16.
 constexpr uint32_t kSfRow = 16;
 constexpr uint32_t kSfaBytes = kBM * kSfRow;
-constexpr uint32_t kSfbBytes = kBN * kSfRow;
-// tensor-memory columns per stage: MXFP4 8 (A) + 16 (B), NVFP4 16 + 32
-template <bool NV> struct SfCols {
-    static constexpr uint32_t kA = kBM / 32 * (NV ? 4 : 2), kB = kBN / 32 * (NV ? 4 : 2);
-};
-constexpr uint32_t kAccCols = kBN;
-constexpr uint32_t kSfCol0 = kAccCols;                                  // scale ring after the accumulator
-constexpr uint32_t kTmemCols = 512;
-static_assert(kSfCol0 + kStages * (SfCols<true>::kA + SfCols<true>::kB) <= kTmemCols, "tensor memory");
 
-constexpr uint32_t kOffB = kStages * kATile;
-constexpr uint32_t kOffSfa = kOffB + kStages * kBTile;
-constexpr uint32_t kOffSfb = kOffSfa + kStages * kSfaBytes;
-constexpr uint32_t kOffBar = kOffSfb + kStages * kSfbBytes;
-constexpr uint32_t kSmem = 1024 + kOffBar + 256;
-static_assert(kSmem <= 227 * 1024, "shared memory");
+// Column tile BN = MMA N (rows of B per tile). 256: one CTA per SM, 4 stages,
+// all 512 tensor-memory columns. 128: two CTAs per SM (3 stages, 256 columns
+// each), so one CTA's pipeline fill and epilogue overlap the other's weight
+// stream -- the shape for weight-streaming launches (few rows per tile).
+template <int BN> struct Tile {
+    static constexpr int kStages = BN == 256 ? 4 : 3;
+    static constexpr int kCtasPerSm = BN == 256 ? 1 : 2;
+    static constexpr uint32_t kHalfRows = BN / 2;               // B rows per TMA box (two boxes per stage)
+    static constexpr uint32_t kBHalf = kHalfRows * 128;
+    static constexpr uint32_t kBTile = BN * 128;
+    static constexpr uint32_t kSfbBytes = BN * kSfRow;
+    static constexpr uint32_t kTmemCols = BN == 256 ? 512 : 256;
+    static constexpr uint32_t kOffB = kStages * kATile;
+    static constexpr uint32_t kOffSfa = kOffB + kStages * kBTile;
+    static constexpr uint32_t kOffSfb = kOffSfa + kStages * kSfaBytes;
+    static constexpr uint32_t kOffBar = kOffSfb + kStages * kSfbBytes;
+    static constexpr uint32_t kSmem = 1024 + kOffBar + 256;
+    static_assert((kSmem + 1024) * kCtasPerSm <= 228 * 1024, "shared memory");
+};
+// tensor-memory columns per stage: 2 (MXFP4) or 4 (NVFP4) per 32 operand rows;
+// the accumulator takes the first BN columns, the scale ring follows
+template <bool NV, int BN> struct SfCols {
+    static constexpr uint32_t kA = kBM / 32 * (NV ? 4 : 2), kB = BN / 32 * (NV ? 4 : 2);
+    static_assert(BN + Tile<BN>::kStages * (kA + kB) <= Tile<BN>::kTmemCols, "tensor memory");
+};
 
 // kind::mxf4 instruction descriptor: E2M1 x E2M1 (format 1), UE8M0 scales,
 // K = 64, both operands K-major (cute/arch/mma_sm100_desc.hpp InstrDescriptorBlockScaled).
@@ -142,6 +148,7 @@ struct Params {
     const uint4 *tiles;
     const uint32_t *n_tiles;
     uint32_t b_expert_rows;
+    uint32_t col_tiles;          // persistent kernel: column tiles per row tile
     uint32_t *err;
 };
 
@@ -152,14 +159,18 @@ __device__ __forceinline__ void load_u2(const uint8_t *p, uint32_t &lo, uint32_t
     hi = v.y;
 }
 
-template <int E, bool NV>
-__global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_constant__ Params p)
+template <int E, bool NV, int BN>
+__global__ void __launch_bounds__(kThreads, Tile<BN>::kCtasPerSm) mxf4_gemm_kernel(const __grid_constant__ Params p)
 {
-    constexpr uint32_t kSfaCols = SfCols<NV>::kA, kSfbCols = SfCols<NV>::kB;
+    using Tl = Tile<BN>;
+    constexpr int kStages = Tl::kStages;
+    constexpr uint32_t kSfaCols = SfCols<NV, BN>::kA, kSfbCols = SfCols<NV, BN>::kB;
+    constexpr uint32_t kSfCol0 = BN;   // scale ring after the accumulator
+    constexpr int RB = BN / 32;        // B row groups of 32
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sA = smem, *sB = smem + kOffB, *sSa = smem + kOffSfa, *sSb = smem + kOffSfb;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
+    uint8_t *sA = smem, *sB = smem + Tl::kOffB, *sSa = smem + Tl::kOffSfa, *sSb = smem + Tl::kOffSfb;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Tl::kOffBar);
     uint64_t *full = bars;                 // [kStages] TMA landed
     uint64_t *sf_ready = bars + kStages;   // [kStages] scales in tensor memory
     uint64_t *empty = bars + 2 * kStages;  // [kStages] MMA done with the stage
@@ -189,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_alloc(tmem_slot, Tl::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -206,15 +217,15 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
             for (; s < nk; ++s) {
                 const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
                 if (!mbar_wait(&empty[st], ph ^ 1u, abort, p.err, 0xC01)) break;
-                mbar_arrive_expect_tx(&full[st], kATile + kBTile + kSfaBytes + kSfbBytes);
+                mbar_arrive_expect_tx(&full[st], kATile + Tl::kBTile + kSfaBytes + Tl::kSfbBytes);
                 const int32_t kb = (int32_t)(s * (kBK / 2));
                 const int32_t ks = (int32_t)((NV ? s : (s >> 1)) * kSfRow);
                 tma_load_2d(sA + st * kATile, &p.tm_a, kb, (int32_t)m0, &full[st]);
-                tma_load_2d(sB + st * kBTile, &p.tm_b0, kb, rb0, &full[st]);
-                tma_load_2d(sB + st * kBTile + kBHalf, &p.tm_b1, kb, rb1, &full[st]);
+                tma_load_2d(sB + st * Tl::kBTile, &p.tm_b0, kb, rb0, &full[st]);
+                tma_load_2d(sB + st * Tl::kBTile + Tl::kBHalf, &p.tm_b1, kb, rb1, &full[st]);
                 tma_load_2d(sSa + st * kSfaBytes, &p.tm_sa, ks, (int32_t)m0, &full[st]);
-                tma_load_2d(sSb + st * kSfbBytes, &p.tm_sb0, ks, rb0, &full[st]);
-                tma_load_2d(sSb + st * kSfbBytes + 128 * kSfRow, &p.tm_sb1, ks, rb1, &full[st]);
+                tma_load_2d(sSb + st * Tl::kSfbBytes, &p.tm_sb0, ks, rb0, &full[st]);
+                tma_load_2d(sSb + st * Tl::kSfbBytes + Tl::kHalfRows * kSfRow, &p.tm_sb1, ks, rb1, &full[st]);
             }
             // drain: no copy may still be landing when the CTA exits
             for (uint32_t t = (s > kStages ? s - kStages : 0); t < s; ++t)
@@ -228,19 +239,19 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                 if (!mbar_wait(&sf_ready[st], ph, abort, p.err, 0xC03)) break;
                 tc_fence_after();
                 const uint64_t ad = smem_desc_sw128(sA + st * kATile);
-                const uint64_t bd = smem_desc_sw128(sB + st * kBTile);
+                const uint64_t bd = smem_desc_sw128(sB + st * Tl::kBTile);
                 const uint32_t sfa0 = tmem + kSfCol0 + st * (kSfaCols + kSfbCols);
                 const uint32_t sfb0 = sfa0 + kSfaCols;
 #pragma unroll
                 for (uint32_t k = 0; k < kBK / 64; ++k) {   // 32 packed bytes = 64 K per MMA
                     if constexpr (NV) {
-                        mma_nvf4(tmem, ad + 2 * k, bd + 2 * k, idesc_nvf4(kBM, kBN), sfa0 + (kBM / 32) * k,
-                                 sfb0 + (kBN / 32) * k, (s | k) != 0u);
+                        mma_nvf4(tmem, ad + 2 * k, bd + 2 * k, idesc_nvf4(kBM, BN), sfa0 + (kBM / 32) * k,
+                                 sfb0 + RB * k, (s | k) != 0u);
                     } else {
                         const uint32_t g = k >> 1, h = (k & 1u) * 2u;
                         const uint32_t sfa = (sfa0 + (kBM / 32) * g) | (h << 30);
-                        const uint32_t sfb = (sfb0 + (kBN / 32) * g) | (h << 30);
-                        mma_mxf4(tmem, ad + 2 * k, bd + 2 * k, idesc_mxf4(kBM, kBN, h, h), sfa, sfb, (s | k) != 0u);
+                        const uint32_t sfb = (sfb0 + RB * g) | (h << 30);
+                        mma_mxf4(tmem, ad + 2 * k, bd + 2 * k, idesc_mxf4(kBM, BN, h, h), sfa, sfb, (s | k) != 0u);
                     }
                 }
                 mma_commit(&empty[st]);
@@ -260,16 +271,16 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
             const uint32_t col = tmem + lane_base + kSfCol0 + st * (kSfaCols + kSfbCols);
             // every lane quarter writes the same copy: lane j of any quarter holds rows 32 i + j
             if constexpr (NV) {
-                uint32_t va[16], vb[32];
+                uint32_t va[16], vb[4 * RB];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const uint4 v = *reinterpret_cast<const uint4 *>(sSa + st * kSfaBytes + (32 * i + lane) * kSfRow);
                     va[i] = v.x; va[4 + i] = v.y; va[8 + i] = v.z; va[12 + i] = v.w;
                 }
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint4 v = *reinterpret_cast<const uint4 *>(sSb + st * kSfbBytes + (32 * i + lane) * kSfRow);
-                    vb[i] = v.x; vb[8 + i] = v.y; vb[16 + i] = v.z; vb[24 + i] = v.w;
+                for (int i = 0; i < RB; ++i) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(sSb + st * Tl::kSfbBytes + (32 * i + lane) * kSfRow);
+                    vb[i] = v.x; vb[RB + i] = v.y; vb[2 * RB + i] = v.z; vb[3 * RB + i] = v.w;
                 }
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
@@ -279,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                     tmem_st_x8(col + 8 * q, t);
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < RB / 2; ++q) {
                     uint32_t t[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) t[i] = vb[8 * q + i];
@@ -287,16 +298,21 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                 }
             } else {
                 const uint32_t off = (s & 1u) * 8u;
-                uint32_t va[8], b0[8], b1[8];
+                uint32_t va[8], vb[2 * RB];
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
                     load_u2(sSa + st * kSfaBytes + (32 * i + lane) * kSfRow + off, va[i], va[4 + i]);
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    load_u2(sSb + st * kSfbBytes + (32 * i + lane) * kSfRow + off, b0[i], b1[i]);
+                for (int i = 0; i < RB; ++i)
+                    load_u2(sSb + st * Tl::kSfbBytes + (32 * i + lane) * kSfRow + off, vb[i], vb[RB + i]);
                 tmem_st_x8(col, va);
-                tmem_st_x8(col + kSfaCols, b0);
-                tmem_st_x8(col + kSfaCols + 8, b1);
+#pragma unroll
+                for (int q = 0; q < RB / 4; ++q) {
+                    uint32_t t[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) t[i] = vb[8 * q + i];
+                    tmem_st_x8(col + kSfaCols + 8 * q, t);
+                }
             }
             st_wait();
             tc_fence_before();
@@ -310,20 +326,20 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
         tc_fence_after();
         const uint32_t m = m0 + quarter * 32 + lane;
         const uint32_t acc = tmem + lane_base;
-        float alpha0 = 1.0f, alpha1 = 1.0f;   // scale of the tile's first / second 128 columns
+        float alpha0 = 1.0f, alpha1 = 1.0f;   // scale of the tile's first / second BN/2 columns
         if constexpr (NV) {
             alpha0 = *p.ts_a * *p.ts_b0;
             alpha1 = *p.ts_a * *p.ts_b1;
         }
         if (ok) {
             if constexpr (E == EPI_SWIGLU_MX || E == EPI_SWIGLU_F16) {
-                const uint32_t c0 = blockIdx.x * 128;   // mid channel of column 0
+                const uint32_t c0 = blockIdx.x * (BN / 2);   // mid channel of column 0
                 float vmax = 0.0f;   // rounding to fp16 is monotonic: max of rounded = rounded max
 #pragma unroll 1
-                for (int cb = 0; cb < 4; ++cb) {
+                for (int cb = 0; cb < BN / 64; ++cb) {
                     uint32_t g[32], u[32];
                     tmem_ld_32x32b_x32(acc + cb * 32, g);
-                    tmem_ld_32x32b_x32(acc + 128 + cb * 32, u);
+                    tmem_ld_32x32b_x32(acc + BN / 2 + cb * 32, u);
                     tmem_ld_wait();
                     float v[32];
 #pragma unroll
@@ -363,14 +379,14 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
                     }
                 }
             } else {
-                const uint32_t n0 = blockIdx.x * kBN;
+                const uint32_t n0 = blockIdx.x * BN;
 #pragma unroll 1
-                for (int cc = 0; cc < kBN / 32; ++cc) {
+                for (int cc = 0; cc < BN / 32; ++cc) {
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(acc + cc * 32, v);
                     tmem_ld_wait();
                     if constexpr (NV) {
-                        const float alpha = cc < 4 ? alpha0 : alpha1;
+                        const float alpha = cc < BN / 64 ? alpha0 : alpha1;
 #pragma unroll
                         for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
                     }
@@ -408,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) mxf4_gemm_kernel(const __grid_con
     if (warp == 1) {
         if (*abort) mbar_wait(done, 0, nullptr, p.err, 0xC06);   // let in-flight MMAs drain
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc(tmem, Tl::kTmemCols);
     }
 }
 
