@@ -1,0 +1,171 @@
+"""Timings of the FP4-tensor-core rows that sit beside the headline layer:
+W4A4 and NVFP4 MLP layers, the plain block-scaled GEMMs and the MoE layer
+(BASELINE config 3 at T=4096 and config 4 per GPU).
+
+    python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row moe
+    python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row w4a4 --shape 4096,4096,14336
+    python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row mxf4_gemm --shape 8192,8192,8192 --once
+
+One JSON line per row: device time per call (CUDA events on the launching
+stream around a CUDA graph of back-to-back calls, median of 5 replays, after
+3 warm-up calls), TFLOP/s, and the fraction of a peak: the FP4 rows against
+4x the measured dense bf16 peak (MEASURED_PEAKS.json; kind::mxf4 issues 4x the
+kind::f16 rate), the weight-streaming rows against the measured HBM copy
+bandwidth for their algorithmic bytes. Weights are random packed bytes (every
+E2M1 code) with block scales near 1; inputs larger than L2 are used as they
+are, smaller weight sets are rotated through copies that together exceed L2.
+`--once` runs 2 warm-up calls and one call, for profilers.
+"""
+import argparse
+import json
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+if os.path.dirname(HERE) not in sys.path:
+    sys.path.insert(0, os.path.dirname(HERE))
+
+import torch  # noqa: E402
+
+import mpp41  # noqa: E402
+
+L2_BYTES = 126 << 20
+
+
+def peaks():
+    path = os.path.join(os.path.dirname(os.path.dirname(HERE)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d.get("hbm_gbs", 6650.0)), float(d.get("bf16_tflops", 1590.0)), "measured"
+    except (OSError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def rand_fp4(rows, k, copies, nv=False):
+    sf = 16 if nv else 32
+    q = torch.randint(0, 256, (copies, rows * k // 2), dtype=torch.uint8, device="cuda")
+    s = torch.full((copies, rows * k // sf), 0x38 if nv else 127, dtype=torch.uint8, device="cuda")
+    return q, s
+
+
+def timed(ctx, st, run, once):
+    if once:
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        return None
+    for _ in range(3):
+        run()
+    reps = 10
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for _ in range(reps):
+            run()
+    g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record(st)
+        g.replay()
+        b.record(st)
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3 / reps)
+    return sorted(ts)[2]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--row", required=True, choices=["w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe"])
+    ap.add_argument("--shape", default=None, help="T,H,I (layers), M,N,K (GEMMs), T,H,I,E,k,shared_I (moe)")
+    ap.add_argument("--once", action="store_true")
+    args = ap.parse_args()
+    hbm, bf16, src = peaks()
+    fp4_peak = 4 * bf16
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    ctx = mpp41.Context(0)
+    ctx.set_stream(st.cuda_stream)
+    one = torch.ones(1, device="cuda")
+    line = {"row": args.row}
+    if args.row in ("w4a4", "nvfp4"):
+        T, H, I = (int(v) for v in (args.shape or "4096,4096,14336").split(","))
+        nv = args.row == "nvfp4"
+        wbytes = 3 * H * I * (0.5 + (1 / 16 if nv else 1 / 32))
+        cp = max(1, int(-(-L2_BYTES // wbytes))) if wbytes < L2_BYTES else 1
+        wg, sg = rand_fp4(I, H, cp, nv)
+        wu, su = rand_fp4(I, H, cp, nv)
+        wd, sd = rand_fp4(H, I, cp, nv)
+        x = torch.randn(T * H, device="cuda").half()
+        out = torch.empty(T * H, dtype=torch.float16, device="cuda")
+        scr = torch.empty((mpp41.nvfp4_scratch_bytes if nv else mpp41.w4a4_scratch_bytes)(T, H, I),
+                          dtype=torch.uint8, device="cuda")
+        it = [0]
+
+        def run():
+            i = it[0] % cp
+            it[0] += 1
+            if nv:
+                ctx.mlp_nvfp4(T, H, I, x, wg[i], sg[i], one, wu[i], su[i], one, wd[i], sd[i], one, out, scr, True)
+            else:
+                ctx.mlp_w4a4(T, H, I, x, wg[i], sg[i], wu[i], su[i], wd[i], sd[i], out, scr, True)
+        flops = 6.0 * T * H * I
+        abytes = wbytes + T * H * 2 * 2
+        line.update(config={"T": T, "H": H, "I": I}, weight_copies=cp)
+    elif args.row in ("mxf4_gemm", "nvf4_gemm"):
+        M, N, K = (int(v) for v in (args.shape or "8192,8192,8192").split(","))
+        nv = args.row == "nvf4_gemm"
+        bbytes = N * K * (0.5 + (1 / 16 if nv else 1 / 32))
+        cp = max(1, int(-(-L2_BYTES // bbytes))) if bbytes < L2_BYTES else 1
+        a, sa = rand_fp4(M, K, 1, nv)
+        b, sb = rand_fp4(N, K, cp, nv)
+        c = torch.empty(M * N, dtype=torch.float16, device="cuda")
+        it = [0]
+
+        def run():
+            i = it[0] % cp
+            it[0] += 1
+            if nv:
+                ctx.matmul_nvf4(a[0], sa[0], one, b[i], sb[i], one, c, M, N, K, True)
+            else:
+                ctx.matmul_mxf4(a[0], sa[0], b[i], sb[i], c, M, N, K, True)
+        flops = 2.0 * M * N * K
+        abytes = bbytes + M * K * (0.5 + 1 / 32) + M * N * 2
+        line.update(config={"M": M, "N": N, "K": K}, weight_copies=cp)
+    else:
+        T, H, I, E, k, Is = (int(v) for v in (args.shape or "512,7168,2048,32,8,2048").split(","))
+        wg, sg = rand_fp4(E * I, H, 1)
+        wu, su = rand_fp4(E * I, H, 1)
+        wd, sd = rand_fp4(E * H, I, 1)
+        sh = []
+        for r, c_ in ((Is, H), (Is, H), (H, Is)):
+            q, s = rand_fp4(r, c_, 1)
+            sh += [q[0], s[0]]
+        x = torch.randn(T * H, device="cuda").half()
+        logits = torch.randn(T * E, device="cuda")
+        desc = mpp41.moe_desc(T, H, I, E, k, Is, out_f16=True)
+        total, _ = mpp41.moe_scratch_layout(desc)
+        scr = torch.empty(total, dtype=torch.uint8, device="cuda")
+        out = torch.empty(T * H, dtype=torch.float16, device="cuda")
+
+        def run():
+            ctx.moe_w4a4(desc, x, logits, wg[0], sg[0], wu[0], su[0], wd[0], sd[0], out, scr,
+                         shared=sh if Is else None)
+        flops = 6.0 * T * H * (k * I + Is)
+        abytes = 3 * H * (E * I + Is) * (0.5 + 1 / 32) + T * H * 2 * 2 + T * E * 4
+        line.update(config={"T": T, "H": H, "I": I, "experts": E, "top_k": k, "shared_I": Is})
+    us = timed(ctx, st, run, args.once)
+    if us is None:
+        print(json.dumps({"row": args.row, "once": True}))
+        return
+    tflops = flops / us / 1e6
+    gbs = abytes / us / 1e3
+    line.update(us=round(us, 2), tflops=round(tflops, 1), algorithmic_bytes=int(abytes), gbs=round(gbs, 1),
+                frac_fp4_peak=round(tflops / fp4_peak, 3), frac_hbm=round(gbs / hbm, 3),
+                peaks={"fp4_tflops": fp4_peak, "hbm_gbs": hbm, "source": src + " (fp4 = 4 x bf16)"})
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()
