@@ -258,6 +258,25 @@ mpp41_status mpp41_quantize_act_mxfp4(mpp41_ctx *ctx, const void *x, uint32_t to
 mpp41_status mpp41_quantize_act_s8(mpp41_ctx *ctx, const void *x, uint32_t tokens, uint32_t hidden, int8_t *q,
                                    float *scale);
 
+/* ---- scaled integer layers W8A8 / W4A8 / W2A8 (the serving form of the
+ *      reference's int8-activation rows, whose scales it leaves out):
+ *      - mpp41_quantize_weights_int: fp32 [rows][depth] -> INT8/INT4/INT2 in the
+ *        reference's packed layouts, per-row symmetric: scale = amax/qmax
+ *        (qmax 127/7/1; 1 for a zero row), q = rint(w/scale) clamped to ±qmax;
+ *      - mpp41_mlp_w8a8: x fp16 -> per-token int8 (mpp41_quantize_act_s8 rule),
+ *        gate/up on kind::i8 (exact int32), dequant ((float)acc*sx[t])*sw[n],
+ *        silu(g)*u -> fp16 mid, per-token int8 mid, down GEMM, dequant -> fp16
+ *        out [T][H]. wfmt MPP41_W_I8/I4/I2; H, I % 128 == 0. scratch
+ *        (mpp41_mlp_w8a8_scratch_bytes), 256-byte aligned sections: int8 x
+ *        [T][H], x scales [T] fp32, fp16 mid [T][I], int8 mid [T][I], mid
+ *        scales [T]. ---- */
+mpp41_status mpp41_quantize_weights_int(mpp41_ctx *ctx, const float *w, uint32_t rows, uint32_t depth, int bits,
+                                        void *packed, float *scales);
+size_t mpp41_mlp_w8a8_scratch_bytes(uint32_t tokens, uint32_t hidden, uint32_t intermediate);
+mpp41_status mpp41_mlp_w8a8(mpp41_ctx *ctx, int wfmt, uint32_t tokens, uint32_t hidden, uint32_t intermediate,
+                            const void *x, const void *wg, const float *sg, const void *wu, const float *su,
+                            const void *wd, const float *sd, void *out, void *scratch);
+
 /* ---- W4A4: activations as well as weights in MXFP4, multiplied on the FP4
  *      tensor cores with the E8M0 block scales applied inside the MMA (no
  *      reference counterpart: its FP4 rows keep fp16 activations; the weight

@@ -1043,6 +1043,67 @@ mpp41_status mpp41_mlp_nvfp4(mpp41_ctx *ctx, uint32_t T, uint32_t H, uint32_t I,
     return enqueue_mxf4(ctx, d, "NVFP4 down GEMM");
 }
 
+// ------------------------------------------------------------------ scaled W8A8 / W4A8 / W2A8
+mpp41_status mpp41_quantize_weights_int(mpp41_ctx *ctx, const float *w, uint32_t rows, uint32_t depth, int bits,
+                                        void *packed, float *scales)
+{
+    NEED(ctx);
+    if (bits != 8 && bits != 4 && bits != 2) return fail(MPP41_ERR_INVALID_ARGUMENT, "bits must be 8, 4 or 2");
+    if (depth % 8) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "depth must be a multiple of 8");
+    if (!rows || !depth) return MPP41_OK;
+    if (!w || !packed || !scales) return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    CK(launch_quantize_int_rows(w, rows, depth, bits, static_cast<uint8_t *>(packed), scales, ctx->stream),
+       "quantize weights");
+    return MPP41_OK;
+}
+
+size_t mpp41_mlp_w8a8_scratch_bytes(uint32_t T, uint32_t H, uint32_t I)
+{
+    return up256((size_t)T * H) + up256((size_t)T * 4) + up256((size_t)T * I * 2) + up256((size_t)T * I) +
+           up256((size_t)T * 4);
+}
+
+mpp41_status mpp41_mlp_w8a8(mpp41_ctx *ctx, int wfmt, uint32_t T, uint32_t H, uint32_t I, const void *x,
+                            const void *wg, const float *sg, const void *wu, const float *su, const void *wd,
+                            const float *sd, void *out, void *scratch)
+{
+    NEED(ctx);
+    if (wfmt != MPP41_W_I8 && wfmt != MPP41_W_I4 && wfmt != MPP41_W_I2)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "weights must be INT8, INT4 or INT2");
+    if (!T || !H || !I) return MPP41_OK;
+    if (H % 128 || I % 128) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "hidden and intermediate must be multiples of 128");
+    if (!x || !wg || !sg || !wu || !su || !wd || !sd || !out || !scratch)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
+    if (!al16(x) || !al16(wg) || !al16(wu) || !al16(wd) || !al16(out) || (reinterpret_cast<uintptr_t>(scratch) & 255u))
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "buffers must be 16-byte aligned (scratch 256-byte)");
+    uint8_t *xq = static_cast<uint8_t *>(scratch);
+    float *xs = reinterpret_cast<float *>(xq + up256((size_t)T * H));
+    __half *mid = reinterpret_cast<__half *>(reinterpret_cast<uint8_t *>(xs) + up256((size_t)T * 4));
+    uint8_t *mq = reinterpret_cast<uint8_t *>(mid) + up256((size_t)T * I * 2);
+    float *ms = reinterpret_cast<float *>(mq + up256((size_t)T * I));
+    cudaStream_t st = ctx->stream;
+    CK(launch_quantize_act_s8(x, T, H, reinterpret_cast<int8_t *>(xq), xs, st), "quantize x");
+    I8Launch g{};
+    g.wfmt = wfmt; g.epi = 3;
+    g.a = xq; g.b0 = wg; g.b1 = wu; g.out = mid;
+    g.row_scale = xs; g.col_scale0 = sg; g.col_scale1 = su;
+    g.M = T; g.N = I; g.K = H; g.ldc = I; g.splits = 1;
+    g.err = ctx->err;
+    const char *why = "";
+    int rc = launch_i8_gemm(g, st, &why);
+    if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "W8A8 gate/up GEMM: %s", why);
+    CK(launch_quantize_act_s8(mid, T, I, reinterpret_cast<int8_t *>(mq), ms, st), "quantize mid");
+    I8Launch d{};
+    d.wfmt = wfmt; d.epi = 4;
+    d.a = mq; d.b0 = wd; d.out = out;
+    d.row_scale = ms; d.col_scale0 = sd;
+    d.M = T; d.N = H; d.K = I; d.ldc = H; d.splits = 1;
+    d.err = ctx->err;
+    rc = launch_i8_gemm(d, st, &why);
+    if (rc) return fail(rc == 1 ? MPP41_ERR_UNSUPPORTED_SHAPE : MPP41_ERR_CUDA, "W8A8 down GEMM: %s", why);
+    return MPP41_OK;
+}
+
 // ------------------------------------------------------------------ MoE
 static mpp41_status check_moe(const mpp41_moe_desc *d)
 {

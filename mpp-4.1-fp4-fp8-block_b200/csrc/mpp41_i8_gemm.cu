@@ -14,13 +14,18 @@ template <int W, int E>
 static int launch_t(const I8Launch &L, cudaStream_t st, const char **why)
 {
     using Cf = Cfg<W>;
-    constexpr bool kPair = (E == I8_SWIGLU);
+    constexpr bool kPair = (E == I8_SWIGLU || E == I8_DQ_SWIGLU);
     const uint32_t splits = (E == I8_ATOMIC) ? L.splits : 1;
     if (!splits || L.K % (kBK * splits)) { *why = "K must be a multiple of 128 x splits"; return 1; }
     if (L.N % (kPair ? kBN / 2 : 32)) { *why = "N must be a multiple of 32 (64 for the gate/up pair)"; return 1; }
     Params p;
     memset(&p, 0, sizeof(p));
     p.out = L.out;
+    p.row_scale = L.row_scale; p.col_scale0 = L.col_scale0; p.col_scale1 = L.col_scale1;
+    if ((E == I8_DQ || E == I8_DQ_SWIGLU) && (!L.row_scale || !L.col_scale0 || (kPair && !L.col_scale1))) {
+        *why = "scaled epilogues need the row and column scales";
+        return 1;
+    }
     p.M = L.M; p.N = L.N; p.K = L.K; p.ldc = L.ldc;
     p.k_per_split = L.K / splits;
     p.err = L.err;
@@ -53,6 +58,8 @@ static int launch_w(const I8Launch &L, cudaStream_t st, const char **why)
     case I8_STORE: return launch_t<W, I8_STORE>(L, st, why);
     case I8_ATOMIC: return launch_t<W, I8_ATOMIC>(L, st, why);
     case I8_SWIGLU: return launch_t<W, I8_SWIGLU>(L, st, why);
+    case I8_DQ_SWIGLU: return launch_t<W, I8_DQ_SWIGLU>(L, st, why);
+    case I8_DQ: return launch_t<W, I8_DQ>(L, st, why);
     }
     *why = "epilogue";
     return 1;

@@ -17,6 +17,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cstdint>
 
 #include "mpp41_device.cuh"
@@ -33,12 +34,18 @@ constexpr int kThreads = 192;
 constexpr uint32_t kATile = kBM * kBK;   // 16 KB
 constexpr uint32_t kBTile = kBN * kBK;   // 16 KB
 
-enum I8Epi : int { I8_STORE = 0, I8_ATOMIC = 1, I8_SWIGLU = 2 };
+// I8_DQ_SWIGLU / I8_DQ: the scaled W8A8 layer. The int32 sums are dequantized
+// as ((float)acc * row_scale[m]) * col_scale[n] (two fp32 products, in this
+// order); the pair form then writes silu(g) * u as fp16, the other fp16 C.
+enum I8Epi : int { I8_STORE = 0, I8_ATOMIC = 1, I8_SWIGLU = 2, I8_DQ_SWIGLU = 3, I8_DQ = 4 };
 
 struct Params {
     CUtensorMap tm_a;         // int8 [M][K], box {128, 128}, SW128
     CUtensorMap tm_b0, tm_b1; // INT8: [N][K] box {128, rows}, SW128; INT4/INT2: packed bytes, box {raw_row, rows}
-    void *out;                // int32 [M][ldc] or (I8_SWIGLU) int8 mid [M][ldc]
+    void *out;                // int32 [M][ldc], (I8_SWIGLU) int8 mid, (I8_DQ*) fp16 [M][ldc]
+    const float *row_scale;   // I8_DQ*: per-row (token) scale of A
+    const float *col_scale0;  // I8_DQ*: per-output-channel scale of B (gate rows for the pair)
+    const float *col_scale1;  // I8_DQ_SWIGLU: up rows
     uint32_t M, N, K, ldc;
     uint32_t k_per_split;
     uint32_t *err;
@@ -100,7 +107,7 @@ template <int W, int E>
 __global__ void __launch_bounds__(kThreads, 1) i8_gemm_kernel(const __grid_constant__ Params p)
 {
     using C = Cfg<W>;
-    constexpr bool kPair = (E == I8_SWIGLU);
+    constexpr bool kPair = (E == I8_SWIGLU || E == I8_DQ_SWIGLU);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
@@ -224,7 +231,25 @@ __global__ void __launch_bounds__(kThreads, 1) i8_gemm_kernel(const __grid_const
                     tmem_ld_32x32b_x32(taddr + kBN / 2 + cc * 32, u);
                     tmem_ld_wait();
                     const uint32_t col = c0 + cc * 32;
-                    if (m < p.M && col < p.N) {
+                    if constexpr (E == I8_DQ_SWIGLU) {
+                        if (m < p.M && col < p.N) {
+                            const float rs = p.row_scale[m];
+                            uint32_t w[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float gf = ((float)(int32_t)g[2 * i] * rs) * p.col_scale0[col + 2 * i];
+                                const float uf = ((float)(int32_t)u[2 * i] * rs) * p.col_scale1[col + 2 * i];
+                                const float gf2 = ((float)(int32_t)g[2 * i + 1] * rs) * p.col_scale0[col + 2 * i + 1];
+                                const float uf2 = ((float)(int32_t)u[2 * i + 1] * rs) * p.col_scale1[col + 2 * i + 1];
+                                const __half2 h = __floats2half2_rn(__fdividef(gf, 1.0f + __expf(-gf)) * uf,
+                                                                    __fdividef(gf2, 1.0f + __expf(-gf2)) * uf2);
+                                w[i] = *reinterpret_cast<const uint32_t *>(&h);
+                            }
+                            uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(p.out) + (size_t)m * p.ldc + col);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                        }
+                    } else if (m < p.M && col < p.N) {
                         uint32_t w[8];
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
@@ -248,7 +273,19 @@ __global__ void __launch_bounds__(kThreads, 1) i8_gemm_kernel(const __grid_const
                     const uint32_t col = c0 + cc * 32;
                     if (m < p.M && col < p.N) {
                         int32_t *dst = static_cast<int32_t *>(p.out) + (size_t)m * p.ldc + col;
-                        if constexpr (E == I8_ATOMIC) {
+                        if constexpr (E == I8_DQ) {
+                            const float rs = p.row_scale[m];
+                            uint32_t w[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const __half2 h = __floats2half2_rn(((float)(int32_t)v[2 * i] * rs) * p.col_scale0[col + 2 * i],
+                                                                    ((float)(int32_t)v[2 * i + 1] * rs) * p.col_scale0[col + 2 * i + 1]);
+                                w[i] = *reinterpret_cast<const uint32_t *>(&h);
+                            }
+                            uint4 *hd = reinterpret_cast<uint4 *>(static_cast<__half *>(p.out) + (size_t)m * p.ldc + col);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) hd[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                        } else if constexpr (E == I8_ATOMIC) {
 #pragma unroll
                             for (int i = 0; i < 32; ++i) atomicAdd(dst + i, (int32_t)v[i]);
                         } else {

@@ -58,9 +58,10 @@ struct WqLaunch {
 // cleared C), or epi 2: gate (b0) / up (b1) pair through mpp_mlp_swiglu_i8 to
 // an int8 mid [M][ldc].
 struct I8Launch {
-    int wfmt, epi;
+    int wfmt, epi;   // epi: 0 int32, 1 int32 split-K add, 2 swiglu_i8 pair, 3 dequant + SwiGLU -> fp16 pair, 4 dequant -> fp16
     const void *a, *b0, *b1;
     void *out;
+    const float *row_scale, *col_scale0, *col_scale1;   // epi 3 and 4
     uint32_t M, N, K, ldc, splits;
     uint32_t *err;
 };
@@ -135,6 +136,9 @@ cudaError_t launch_quantize_mxfp4_f16(const void *x, uint32_t rows, uint32_t dep
 cudaError_t launch_quantize_nvfp4(const void *x, bool f16_in, uint32_t rows, uint32_t depth, uint32_t *amax_tmp,
                                   uint8_t *packed, uint8_t *scales, float *tensor_scale, cudaStream_t st,
                                   bool amax_ready = false);
+// Per-row symmetric INT8/INT4/INT2 weights with fp32 row scales.
+cudaError_t launch_quantize_int_rows(const float *w, uint32_t rows, uint32_t depth, int bits, uint8_t *packed,
+                                     float *scales, cudaStream_t st);
 cudaError_t launch_quantize_act_s8(const void *x, uint32_t tokens, uint32_t hidden, int8_t *q, float *scale,
                                    cudaStream_t st);
 // Returns 0 on success, 1 for an unsupported combination/shape, 2 for a CUDA error.

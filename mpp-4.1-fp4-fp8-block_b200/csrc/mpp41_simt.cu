@@ -454,6 +454,54 @@ cudaError_t launch_quantize_nvfp4(const void *x, bool f16_in, uint32_t rows, uin
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ symmetric integer weights
+// Per-output-row symmetric quantization of fp32 weights [rows][depth] to
+// INT8/INT4/INT2 in the reference's packed layouts (INT4 two per byte, low
+// nibble = even k; INT2 four per byte, LSB pair first; two's complement):
+// qmax = 127 / 7 / 1, scale = amax(row) / qmax (1 for an all-zero row),
+// q = rint(w / scale) clamped to [-qmax, qmax]. One CTA per row.
+__global__ void quantize_int_rows_kernel(const float *__restrict__ w, uint32_t rows, uint32_t depth, int bits,
+                                         uint8_t *__restrict__ packed, float *__restrict__ scales)
+{
+    __shared__ float red[32];
+    const float qmax = bits == 8 ? 127.0f : (bits == 4 ? 7.0f : 1.0f);
+    for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float *row = w + (size_t)r * depth;
+        float m = 0.0f;
+        for (uint32_t i = threadIdx.x; i < depth; i += blockDim.x) m = fmaxf(m, fabsf(row[i]));
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            m = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0f;
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (threadIdx.x == 0) red[0] = m;
+        }
+        __syncthreads();
+        const float scale = red[0] > 0.0f ? red[0] / qmax : 1.0f;
+        const int per = 8 / bits;   // values per byte
+        uint8_t *out = packed + (size_t)r * (depth / (uint32_t)per);
+        for (uint32_t byte = threadIdx.x; byte < depth / (uint32_t)per; byte += blockDim.x) {
+            uint32_t b = 0;
+            for (int j = 0; j < per; ++j) {
+                const float q = fminf(fmaxf(rintf(row[byte * per + j] / scale), -qmax), qmax);
+                b |= ((uint32_t)(int)q & ((1u << bits) - 1u)) << (bits * j);
+            }
+            out[byte] = (uint8_t)b;
+        }
+        if (threadIdx.x == 0) scales[r] = scale;
+        __syncthreads();
+    }
+}
+
+cudaError_t launch_quantize_int_rows(const float *w, uint32_t rows, uint32_t depth, int bits, uint8_t *packed,
+                                     float *scales, cudaStream_t st)
+{
+    if (!rows) return cudaSuccess;
+    quantize_int_rows_kernel<<<rows < 148u * 8u ? rows : 148u * 8u, 256, 0, st>>>(w, rows, depth, bits, packed, scales);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
                                   cudaStream_t st)

@@ -123,6 +123,9 @@ def lib() -> C.CDLL:
         "mpp41_matmul_nvf4": ([vp] * 8 + [u32, u32, u32, C.c_int], st),
         "mpp41_mlp_nvfp4_scratch_bytes": ([u32, u32, u32], sz),
         "mpp41_moe_scratch_layout": ([C.POINTER(MoEDesc), vp], sz),
+        "mpp41_quantize_weights_int": ([vp, vp, u32, u32, C.c_int, vp, vp], st),
+        "mpp41_mlp_w8a8_scratch_bytes": ([u32, u32, u32], sz),
+        "mpp41_mlp_w8a8": ([vp, C.c_int, u32, u32, u32] + [vp] * 9, st),
         "mpp41_moe_route": ([vp, vp, u32, u32, u32, vp, vp], st),
         "mpp41_moe_w4a4": ([vp, C.POINTER(MoEDesc)] + [vp] * 16, st),
         "mpp41_moe_ep_scratch_layout": ([C.POINTER(MoEDesc), C.c_int, u32, vp], sz),
@@ -210,6 +213,20 @@ def moe_scratch_layout(desc: MoEDesc):
 
 def moe_ep_scratch_bytes(desc: MoEDesc, nranks: int, capacity: int) -> int:
     return lib().mpp41_moe_ep_scratch_layout(C.byref(desc), nranks, capacity, None)
+
+
+def w8a8_scratch_bytes(tokens: int, hidden: int, intermediate: int) -> int:
+    return lib().mpp41_mlp_w8a8_scratch_bytes(tokens, hidden, intermediate)
+
+
+def w8a8_scratch_layout(tokens: int, hidden: int, intermediate: int):
+    """Byte offsets of (int8 x, x scales, fp16 mid, int8 mid, mid scales) in the W8A8 scratch."""
+    up = lambda n: (n + 255) & ~255
+    offs, o = [], 0
+    for n in (tokens * hidden, tokens * 4, tokens * intermediate * 2, tokens * intermediate, tokens * 4):
+        offs.append(o)
+        o += up(n)
+    return tuple(offs)
 
 
 def has_kernel(name: str) -> bool:
@@ -409,6 +426,15 @@ class Context:
         sh = [_ptr(v) for v in shared] if shared is not None else [None] * 6
         _check(lib().mpp41_moe_ep(self.h, C.byref(desc), capacity, _ptr(x), _ptr(logits), _ptr(wg), _ptr(sg),
                                   _ptr(wu), _ptr(su), _ptr(wd), _ptr(sd), *sh, _ptr(out), _ptr(scratch)))
+
+    def quantize_weights_int(self, w, rows: int, depth: int, bits: int, packed, scales):
+        """fp32 weights -> per-row symmetric INT8/INT4/INT2 + fp32 row scales (mpp41_quantize_weights_int)."""
+        _check(lib().mpp41_quantize_weights_int(self.h, _ptr(w), rows, depth, bits, _ptr(packed), _ptr(scales)))
+
+    def mlp_w8a8(self, wfmt: int, tokens: int, hidden: int, intermediate: int, x, wg, sg, wu, su, wd, sd, out, scratch):
+        """Scaled W8A8 / W4A8 / W2A8 layer (mpp41_mlp_w8a8); scratch of w8a8_scratch_bytes()."""
+        _check(lib().mpp41_mlp_w8a8(self.h, wfmt, tokens, hidden, intermediate, _ptr(x), _ptr(wg), _ptr(sg), _ptr(wu),
+                                    _ptr(su), _ptr(wd), _ptr(sd), _ptr(out), _ptr(scratch)))
 
     def mlp_w4a4(self, tokens: int, hidden: int, intermediate: int, x, wg, sg, wu, su, wd, sd, out, scratch,
                  out_f16: bool = False):

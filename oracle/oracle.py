@@ -290,6 +290,34 @@ def moe_w4a4(x, logits, k, wg, sg, wu, su, wd, sd, shared=None):
     return ids, w, perm, mq, ms, y, out
 
 
+def quantize_int_rows(w: np.ndarray, bits: int):
+    """Per-row symmetric integer weights (no reference counterpart; its int rows
+    carry no scales): scale = amax/qmax (fp32; 1 for a zero row), q =
+    rint(w/scale) clamped to +-qmax, packed like PackedNumericKernels.metal:25-33
+    (INT4 low nibble = even k, INT2 LSB pair first). Returns (packed, scales)."""
+    w = np.ascontiguousarray(w, np.float32)
+    qmax = np.float32({8: 127, 4: 7, 2: 1}[bits])
+    amax = np.abs(w).max(axis=1)
+    scale = np.where(amax > 0, amax / qmax, np.float32(1)).astype(np.float32)
+    q = np.clip(np.rint(w / scale[:, None]), -qmax, qmax).astype(np.int64)
+    per = 8 // bits
+    q = (q & ((1 << bits) - 1)).reshape(w.shape[0], -1, per)
+    packed = np.zeros(q.shape[:2], np.int64)
+    for j in range(per):
+        packed |= q[:, :, j] << (bits * j)
+    return packed.astype(np.uint8), scale
+
+
+def quantize_act_s8(x: np.ndarray):
+    """Per-token int8 (the rule of mpp41_quantize_act_s8): inv = 127/amax,
+    q = rint(clip(x*inv, +-127)), scale = amax/127, all fp32."""
+    xf = np.asarray(x, np.float32)
+    amax = np.abs(xf).max(axis=1)
+    inv = np.where(amax > 0, np.float32(127.0) / np.where(amax > 0, amax, 1), 0).astype(np.float32)
+    q = np.rint(np.clip(xf * inv[:, None], -127, 127)).astype(np.int8)
+    return q, (amax / np.float32(127)).astype(np.float32)
+
+
 def baseline_mlp_inputs(T=128, H=1024, I=4096, seed=0):
     """x ~ N(0,1) fp16, weights ~ N(0,0.02) fp32 quantized OCP-MX."""
     rng = np.random.default_rng(seed)
