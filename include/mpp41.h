@@ -398,6 +398,12 @@ mpp41_status mpp41_moe_ep(mpp41_ctx *ctx, const mpp41_moe_desc *desc, uint32_t c
 /* Rank 0 creates the id and shares it with the other ranks (any channel). */
 mpp41_status mpp41_comm_unique_id(uint8_t id[MPP41_COMM_ID_BYTES]);
 /* Collective over all ranks; binds the communicator to the context's device. */
+/* Before mpp41_comm_destroy, destroy any CUDA graph that captured
+ * mpp41_mlp_tp or mpp41_moe_ep calls: NCCL keeps resources for captured
+ * operations until their graph is destroyed. mpp41_mlp_tp sums the partials
+ * with NCCL; MPP41_TP_ALLREDUCE=oneshot selects a one-shot all-reduce over
+ * CUDA-IPC-mapped peer buffers (bounded waits, same sum order on every rank)
+ * for partials up to 2 MiB. */
 mpp41_status mpp41_comm_init(mpp41_ctx *ctx, int nranks, int rank, const uint8_t id[MPP41_COMM_ID_BYTES]);
 void mpp41_comm_destroy(mpp41_ctx *ctx);
 /* Scratch of one rank for the global layer `desc` split over `nranks`. */

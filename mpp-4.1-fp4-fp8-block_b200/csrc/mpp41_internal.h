@@ -215,6 +215,15 @@ struct mpp41_ctx {
 };
 
 namespace mpp41 {
+// One-shot all-reduce over peer memory (mpp41_allreduce.cu): data[s] = rank
+// s's fp32 partial for this call, flags[s] = rank s's flag slots (one per rank).
+constexpr int kMaxPeers = 8;
+struct ArPeers {
+    const float *data[kMaxPeers];
+    uint32_t *flags[kMaxPeers];
+};
+cudaError_t launch_oneshot_allreduce(const ArPeers &pe, int P, int rank, uint32_t epoch, size_t n, void *out,
+                                     bool out_f16, uint32_t *err, cudaStream_t st);
 void comm_release(mpp41_ctx *ctx);
 int comm_size(const mpp41_ctx *ctx);
 int comm_rank(const mpp41_ctx *ctx);

@@ -5,6 +5,8 @@ W4A4 and NVFP4 MLP layers, the plain block-scaled GEMMs and the MoE layer
     python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row moe
     python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row w4a4 --shape 4096,4096,14336
     python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row mxf4_gemm --shape 8192,8192,8192 --once
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 --master-port 29511 \
+        mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row tp --shape 16,4096,14336
 
 One JSON line per row: device time per call (CUDA events on the launching
 stream around a CUDA graph of back-to-back calls, median of 5 replays, after
@@ -14,9 +16,14 @@ kind::f16 rate), the weight-streaming rows against the measured HBM copy
 bandwidth for their algorithmic bytes. Weights are random packed bytes (every
 E2M1 code) with block scales near 1; inputs larger than L2 are used as they
 are, smaller weight sets are rotated through copies that together exceed L2.
-`--once` runs 2 warm-up calls and one call, for profilers.
+`--once` runs 2 warm-up calls and one call, for profilers. `--row tp` (under
+torchrun, one process per GPU) times the tensor-parallel layer
+(mpp41_mlp_tp, MXFP4 weights, fp16 out) with the one-shot peer-memory
+all-reduce (MPP41_TP_ALLREDUCE=oneshot) and with NCCL: a CUDA graph of 20
+back-to-back calls between CUDA events, max over ranks.
 """
 import argparse
+import gc
 import json
 import os
 import sys
@@ -77,10 +84,12 @@ def timed(ctx, st, run, once):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--row", required=True, choices=["w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe"])
+    ap.add_argument("--row", required=True, choices=["w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe", "tp"])
     ap.add_argument("--shape", default=None, help="T,H,I (layers), M,N,K (GEMMs), T,H,I,E,k,shared_I (moe)")
     ap.add_argument("--once", action="store_true")
     args = ap.parse_args()
+    if args.row == "tp":
+        return tp_row(args)
     hbm, bf16, src = peaks()
     fp4_peak = 4 * bf16
     st = torch.cuda.Stream()
@@ -165,6 +174,76 @@ def main():
                 frac_fp4_peak=round(tflops / fp4_peak, 3), frac_hbm=round(gbs / hbm, 3),
                 peaks={"fp4_tflops": fp4_peak, "hbm_gbs": hbm, "source": src + " (fp4 = 4 x bf16)"})
     print(json.dumps(line))
+
+
+def tp_row(args):
+    import numpy as np
+    import torch.distributed as dist
+    from mpp41 import tp
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    dist.init_process_group("gloo")
+    T, H, I = (int(v) for v in (args.shape or "16,4096,14336").split(","))
+    idt = torch.zeros(mpp41.COMM_ID_BYTES, dtype=torch.uint8)
+    if rank == 0:
+        idt = torch.from_numpy(np.frombuffer(mpp41.comm_unique_id(), np.uint8).copy())
+    dist.broadcast(idt, 0)
+    torch.cuda.set_device(rank)
+    ctx = mpp41.Context(rank)
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    ctx.set_stream(st.cuda_stream)
+    ctx.comm_init(world, rank, bytes(idt.numpy().tobytes()))
+    rng = np.random.default_rng(0)
+    wg = rng.integers(0, 256, (I, H // 2), dtype=np.uint8)
+    wu = rng.integers(0, 256, (I, H // 2), dtype=np.uint8)
+    wd = rng.integers(0, 256, (H, I // 2), dtype=np.uint8)
+    sg = np.full((I, H // 32), 120, np.uint8)
+    su = np.full((I, H // 32), 120, np.uint8)
+    sd = np.full((H, I // 32), 120, np.uint8)
+    s = tp.shard(mpp41.W_MXFP4, rank, world, H, I, wg, wu, wd, sg, su, sd)
+    to = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.uint8).reshape(-1).copy()).cuda()
+    w = [to(s[k]) for k in ("wg", "wu", "wd", "sg", "su", "sd")]
+    desc = mpp41.mlp_desc(T, H, I, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F16)
+    scr = torch.empty(mpp41.tp_scratch_bytes(desc, world), dtype=torch.uint8, device="cuda")
+    x = torch.randn(T * H, device="cuda").half()
+    out = torch.empty(T * H, dtype=torch.float16, device="cuda")
+    res = {}
+    for path in ("oneshot", "nccl"):
+        if path == "oneshot":
+            os.environ["MPP41_TP_ALLREDUCE"] = "oneshot"
+        else:
+            os.environ.pop("MPP41_TP_ALLREDUCE", None)
+        for _ in range(5):
+            ctx.mlp_tp(desc, x, *w, scr, out)
+        ctx.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(20):
+                ctx.mlp_tp(desc, x, *w, scr, out)
+        ctx.synchronize()
+        dist.barrier()
+        g.replay()
+        ctx.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record(st)
+        g.replay()
+        b.record(st)
+        ctx.synchronize()
+        us = torch.tensor([a.elapsed_time(b) * 1e3 / 20])
+        # a graph holding NCCL kernels must be gone before the communicator is destroyed
+        del g
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.all_reduce(us, op=dist.ReduceOp.MAX)
+        res[path] = round(float(us[0]), 2)
+    os.environ.pop("MPP41_TP_ALLREDUCE", None)
+    dist.barrier()
+    if rank == 0:
+        print(json.dumps({"row": "tp", "config": {"T": T, "H": H, "I": I, "ranks": world},
+                          "us_per_layer": res, "tflops_oneshot": round(6.0 * T * H * I / res["oneshot"] / 1e6, 1)}))
+    ctx.comm_destroy()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":
