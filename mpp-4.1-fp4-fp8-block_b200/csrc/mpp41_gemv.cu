@@ -1,0 +1,267 @@
+// Decode-sized MLP layer (T <= 16 tokens) with FP4 weights (MXFP4 or unscaled
+// FP4), the W4A16 math of the fused layer -- exact E2M1 x fp16 products, fp32
+// sums, SwiGLU on the fp32 gate/up sums, fp16 mid -- as two weight-streaming
+// kernels (gate/up + SwiGLU, then down). With so few tokens the layer is a
+// stream of 4-bit weights; decoding them into shared or tensor memory for
+// tcgen05 costs more than the stream itself, so here the packed bytes go from
+// global memory straight into registers, are expanded with
+// cvt.rn.f16x2.e2m1x2 into the A fragments of mma.sync.m16n8k16 (fp32
+// accumulate), and the tokens are the N = 8 side (two N tiles above 8).
+//
+// Per warp: 16 weight rows; per 32-wide K block (one E8M0 scale per row) two
+// MMAs sum into a fresh fragment that is then scaled by the block scale and
+// added to the running fp32 sums (scale 2^(s-127) built as s << 23: byte 0
+// gives 0 and 255 infinity, as the reference's e8m0_to_float,
+// MXFP4Kernels.metal:26-29). K order inside a block is permuted the same way
+// for weights and activations (lane t of a row group takes the block's bytes
+// 4t..4t+3, i.e. k = 8t..8t+7), which leaves every block sum unchanged. The
+// warps of a CTA split K (strided over 128-wide chunks) and add their partial
+// sums through shared memory in warp order.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "mpp41_device.cuh"
+#include "mpp41_internal.h"
+#include "mpp41_wq_gemm.cuh"
+
+namespace mpp41 {
+namespace gemv {
+
+constexpr int kGateWarps = 8;    // K split of the gate/up kernel (16 channels per CTA)
+constexpr int kDownWarps = 16;   // K split of the down kernel (16 output rows per CTA)
+
+__device__ __forceinline__ uint32_t e2m1x2_to_h2(uint32_t byte)
+{
+    uint32_t h2;
+    asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "r"(byte));
+    return h2;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float e8m0(uint32_t s) { return __uint_as_float(s << 23); }
+
+// One 32-wide K block of one 16-row weight group against NT token tiles:
+// wg = this lane's 4 bytes of row g, wg8 = of row g + 8; x[nt] = the lane's 8
+// activations (k = 8t..8t+7) of token nt*8 + g; the block sums go to tmp.
+template <int NT>
+__device__ __forceinline__ void block_mma(uint32_t wg, uint32_t wg8, const uint4 (&x)[NT], float (&tmp)[NT][4])
+{
+    const uint32_t a0s0 = e2m1x2_to_h2(wg & 0xFFu), a2s0 = e2m1x2_to_h2((wg >> 8) & 0xFFu);
+    const uint32_t a1s0 = e2m1x2_to_h2(wg8 & 0xFFu), a3s0 = e2m1x2_to_h2((wg8 >> 8) & 0xFFu);
+    const uint32_t a0s1 = e2m1x2_to_h2((wg >> 16) & 0xFFu), a2s1 = e2m1x2_to_h2(wg >> 24);
+    const uint32_t a1s1 = e2m1x2_to_h2((wg8 >> 16) & 0xFFu), a3s1 = e2m1x2_to_h2(wg8 >> 24);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.0f;
+        mma16816(tmp[nt], a0s0, a1s0, a2s0, a3s0, x[nt].x, x[nt].y);
+        mma16816(tmp[nt], a0s1, a1s1, a2s1, a3s1, x[nt].z, x[nt].w);
+    }
+}
+
+// Activations of token n, k = 8t..8t+7 of block kb (zeros past the last token).
+__device__ __forceinline__ uint4 load_x(const __half *x, uint32_t T, uint32_t K, uint32_t n, uint32_t kb, uint32_t t)
+{
+    if (n >= T) return make_uint4(0, 0, 0, 0);
+    return __ldg(reinterpret_cast<const uint4 *>(x + (size_t)n * K + (size_t)kb * 32 + 8 * t));
+}
+
+// Weight bytes of row r, block kb, lane t (4 bytes); scales of 4 consecutive blocks.
+__device__ __forceinline__ uint32_t load_w(const uint8_t *w, uint32_t K, uint32_t r, uint32_t kb, uint32_t t)
+{
+    return __ldg(reinterpret_cast<const uint32_t *>(w + (size_t)r * (K / 2) + (size_t)kb * 16 + 4 * t));
+}
+
+template <bool SCALED>
+__device__ __forceinline__ uint32_t load_s4(const uint8_t *s, uint32_t K, uint32_t r, uint32_t kb4)
+{
+    if constexpr (!SCALED) return 0x7F7F7F7Fu;   // 2^0 for every block
+    return __ldg(reinterpret_cast<const uint32_t *>(s + (size_t)r * (K / 32) + (size_t)kb4 * 4));
+}
+
+// ---------------------------------------------------------------- gate/up + SwiGLU
+// CTA: 16 channels [c0, c0+16) of gate and up, kGateWarps warps splitting K = H.
+template <bool SCALED, int EG, int NT>
+__global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *__restrict__ x, const uint8_t *__restrict__ wg,
+                                                                  const uint8_t *__restrict__ wu, const uint8_t *__restrict__ sg,
+                                                                  const uint8_t *__restrict__ su, __half *__restrict__ mid,
+                                                                  uint32_t T, uint32_t H, uint32_t I)
+{
+    __shared__ float part[kGateWarps][2][NT][4][32];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const uint32_t c0 = blockIdx.x * 16;
+    float ag[NT][4] = {}, au[NT][4] = {};
+    const uint32_t chunks = H / 128;
+    for (uint32_t ch = warp; ch < chunks; ch += kGateWarps) {
+        const uint32_t sg4 = load_s4<SCALED>(sg, H, c0 + g, ch), sg48 = load_s4<SCALED>(sg, H, c0 + g + 8, ch);
+        const uint32_t su4 = load_s4<SCALED>(su, H, c0 + g, ch), su48 = load_s4<SCALED>(su, H, c0 + g + 8, ch);
+        uint32_t wgr[4], wgr8[4], wur[4], wur8[4];
+        uint4 xv[4][NT];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t kb = ch * 4 + b;
+            wgr[b] = load_w(wg, H, c0 + g, kb, t);
+            wgr8[b] = load_w(wg, H, c0 + g + 8, kb, t);
+            wur[b] = load_w(wu, H, c0 + g, kb, t);
+            wur8[b] = load_w(wu, H, c0 + g + 8, kb, t);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = load_x(x, T, H, nt * 8 + g, kb, t);
+        }
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            float tmp[NT][4];
+            const float s0 = e8m0((sg4 >> (8 * b)) & 0xFFu), s8 = e8m0((sg48 >> (8 * b)) & 0xFFu);
+            block_mma<NT>(wgr[b], wgr8[b], xv[b], tmp);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                ag[nt][0] = fmaf(tmp[nt][0], s0, ag[nt][0]);
+                ag[nt][1] = fmaf(tmp[nt][1], s0, ag[nt][1]);
+                ag[nt][2] = fmaf(tmp[nt][2], s8, ag[nt][2]);
+                ag[nt][3] = fmaf(tmp[nt][3], s8, ag[nt][3]);
+            }
+            const float u0 = e8m0((su4 >> (8 * b)) & 0xFFu), u8 = e8m0((su48 >> (8 * b)) & 0xFFu);
+            block_mma<NT>(wur[b], wur8[b], xv[b], tmp);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                au[nt][0] = fmaf(tmp[nt][0], u0, au[nt][0]);
+                au[nt][1] = fmaf(tmp[nt][1], u0, au[nt][1]);
+                au[nt][2] = fmaf(tmp[nt][2], u8, au[nt][2]);
+                au[nt][3] = fmaf(tmp[nt][3], u8, au[nt][3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            part[warp][0][nt][i][lane] = ag[nt][i];
+            part[warp][1][nt][i][lane] = au[nt][i];
+        }
+    __syncthreads();
+    // thread -> (fragment element i, lane l, tile nt): sum the warps in order, SwiGLU, store
+    for (uint32_t e = threadIdx.x; e < NT * 4 * 32; e += blockDim.x) {
+        const uint32_t l = e & 31, i = (e >> 5) & 3, nt = e >> 7;
+        float gs = 0.0f, us = 0.0f;
+        for (int w = 0; w < kGateWarps; ++w) {
+            gs += part[w][0][nt][i][l];
+            us += part[w][1][nt][i][l];
+        }
+        // fragment element i of lane l: row (l>>2) + 8*(i>>1), token 2*(l&3) + (i&1)
+        const uint32_t ch = c0 + (l >> 2) + 8 * (i >> 1), tok = nt * 8 + 2 * (l & 3) + (i & 1);
+        if (tok < T && ch < I) mid[(size_t)tok * I + ch] = __float2half_rn(swiglu<EG>(gs, us));
+    }
+}
+
+// ---------------------------------------------------------------- down
+// CTA: 16 output columns [h0, h0+16), kDownWarps warps splitting K = I.
+template <bool SCALED, bool OUT_F16, int NT>
+__global__ void __launch_bounds__(kDownWarps * 32) down_kernel(const __half *__restrict__ mid, const uint8_t *__restrict__ wd,
+                                                               const uint8_t *__restrict__ sd, void *__restrict__ out,
+                                                               uint32_t T, uint32_t H, uint32_t I)
+{
+    __shared__ float part[kDownWarps][NT][4][32];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const uint32_t h0 = blockIdx.x * 16;
+    float acc[NT][4] = {};
+    const uint32_t chunks = I / 128;
+    for (uint32_t ch = warp; ch < chunks; ch += kDownWarps) {
+        const uint32_t s4 = load_s4<SCALED>(sd, I, h0 + g, ch), s48 = load_s4<SCALED>(sd, I, h0 + g + 8, ch);
+        uint32_t wr[4], wr8[4];
+        uint4 xv[4][NT];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t kb = ch * 4 + b;
+            wr[b] = load_w(wd, I, h0 + g, kb, t);
+            wr8[b] = load_w(wd, I, h0 + g + 8, kb, t);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = load_x(mid, T, I, nt * 8 + g, kb, t);
+        }
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            float tmp[NT][4];
+            const float s0 = e8m0((s4 >> (8 * b)) & 0xFFu), s8 = e8m0((s48 >> (8 * b)) & 0xFFu);
+            block_mma<NT>(wr[b], wr8[b], xv[b], tmp);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                acc[nt][0] = fmaf(tmp[nt][0], s0, acc[nt][0]);
+                acc[nt][1] = fmaf(tmp[nt][1], s0, acc[nt][1]);
+                acc[nt][2] = fmaf(tmp[nt][2], s8, acc[nt][2]);
+                acc[nt][3] = fmaf(tmp[nt][3], s8, acc[nt][3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) part[warp][nt][i][lane] = acc[nt][i];
+    __syncthreads();
+    for (uint32_t e = threadIdx.x; e < NT * 4 * 32; e += blockDim.x) {
+        const uint32_t l = e & 31, i = (e >> 5) & 3, nt = e >> 7;
+        float s = 0.0f;
+        for (int w = 0; w < kDownWarps; ++w) s += part[w][nt][i][l];
+        const uint32_t h = h0 + (l >> 2) + 8 * (i >> 1), tok = nt * 8 + 2 * (l & 3) + (i & 1);
+        if (tok < T && h < H) {
+            if constexpr (OUT_F16) static_cast<__half *>(out)[(size_t)tok * H + h] = __float2half_rn(s);
+            else static_cast<float *>(out)[(size_t)tok * H + h] = s;
+        }
+    }
+}
+
+template <bool SCALED, int EG, int NT>
+int launch_nt(const FusedLaunch &L, cudaStream_t st)
+{
+    gate_up_kernel<SCALED, EG, NT><<<L.I / 16, kGateWarps * 32, 0, st>>>(
+        static_cast<const __half *>(L.x), static_cast<const uint8_t *>(L.wg), static_cast<const uint8_t *>(L.wu), L.sg,
+        L.su, static_cast<__half *>(L.mid), L.T, L.H, L.I);
+    if (L.out_f16)
+        down_kernel<SCALED, true, NT><<<L.H / 16, kDownWarps * 32, 0, st>>>(
+            static_cast<const __half *>(L.mid), static_cast<const uint8_t *>(L.wd), L.sd, L.out, L.T, L.H, L.I);
+    else
+        down_kernel<SCALED, false, NT><<<L.H / 16, kDownWarps * 32, 0, st>>>(
+            static_cast<const __half *>(L.mid), static_cast<const uint8_t *>(L.wd), L.sd, L.out, L.T, L.H, L.I);
+    return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+template <bool SCALED, int EG>
+int launch_eg(const FusedLaunch &L, cudaStream_t st)
+{
+    return L.T <= 8 ? launch_nt<SCALED, EG, 1>(L, st) : launch_nt<SCALED, EG, 2>(L, st);
+}
+
+template <bool SCALED>
+int launch_s(const FusedLaunch &L, cudaStream_t st, const char **why)
+{
+    switch (L.gate_epi) {
+    case EPI_SWIGLU_PLAIN: return launch_eg<SCALED, EPI_SWIGLU_PLAIN>(L, st);
+    case EPI_SWIGLU_HALF: return launch_eg<SCALED, EPI_SWIGLU_HALF>(L, st);
+    case EPI_SWIGLU_HALF_H: return launch_eg<SCALED, EPI_SWIGLU_HALF_H>(L, st);
+    default: *why = "SwiGLU variant"; return 1;
+    }
+}
+
+}  // namespace gemv
+
+bool gemv_covers(uint32_t T, uint32_t H, uint32_t I, int wfmt)
+{
+    return T >= 1 && T <= 16 && (wfmt == W_MXFP4 || wfmt == W_FP4) && H % 128 == 0 && I % 128 == 0;
+}
+
+int launch_gemv_layer(const FusedLaunch &L, cudaStream_t st, const char **why)
+{
+    if (!gemv_covers(L.T, L.H, L.I, L.wfmt)) { *why = "shape or format"; return 1; }
+    const int rc = L.wfmt == W_MXFP4 ? gemv::launch_s<true>(L, st, why) : gemv::launch_s<false>(L, st, why);
+    if (rc == 2) *why = cudaGetErrorString(cudaGetLastError());
+    return rc;
+}
+
+}  // namespace mpp41

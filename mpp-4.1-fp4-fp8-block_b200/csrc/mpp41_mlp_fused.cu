@@ -78,6 +78,8 @@ LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16)
 
 int launch_layer(const LayerPlan &plan, FusedLaunch L, cudaStream_t st, const char **why)
 {
+    // decode-sized batches of FP4 weights: weight-streaming GEMV kernels
+    if (!L.gemm_only && gemv_covers(L.T, L.H, L.I, L.wfmt)) return launch_gemv_layer(L, st, why);
     L.splits = plan.splits;
     return plan.token_major ? tok::launch(L, st, why) : launch_mlp_fused(L, st, why);
 }

@@ -1,6 +1,6 @@
-"""Timings of the FP4-tensor-core rows that sit beside the headline layer:
-W4A4 and NVFP4 MLP layers, the plain block-scaled GEMMs and the MoE layer
-(BASELINE config 3 at T=4096 and config 4 per GPU).
+"""Timings of the rows that sit beside the headline layer: the exact W4A16
+MXFP4 layer at other shapes, the W4A4 and NVFP4 layers,
+the plain block-scaled GEMMs and the MoE layer (config 4 per GPU).
 
     python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row moe
     python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row w4a4 --shape 4096,4096,14336
@@ -84,7 +84,7 @@ def timed(ctx, st, run, once):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--row", required=True, choices=["w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe", "tp"])
+    ap.add_argument("--row", required=True, choices=["w4a16", "w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe", "tp"])
     ap.add_argument("--shape", default=None, help="T,H,I (layers), M,N,K (GEMMs), T,H,I,E,k,shared_I (moe)")
     ap.add_argument("--once", action="store_true")
     args = ap.parse_args()
@@ -98,7 +98,28 @@ def main():
     ctx.set_stream(st.cuda_stream)
     one = torch.ones(1, device="cuda")
     line = {"row": args.row}
-    if args.row in ("w4a4", "nvfp4"):
+    if args.row == "w4a16":
+        # the exact W4A16 MXFP4 layer (mpp41_mlp): BASELINE config 3 at T <= 128
+        T, H, I = (int(v) for v in (args.shape or "1,4096,14336").split(","))
+        wbytes = 3 * H * I * (0.5 + 1 / 32)
+        cp = max(1, int(-(-L2_BYTES // wbytes))) if wbytes < L2_BYTES else 1
+        wg, sg = rand_fp4(I, H, cp)
+        wu, su = rand_fp4(I, H, cp)
+        wd, sd = rand_fp4(H, I, cp)
+        x = torch.randn(T * H, device="cuda").half()
+        out = torch.empty(T * H, dtype=torch.float16, device="cuda")
+        desc = mpp41.mlp_desc(T, H, I, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F16)
+        scr = torch.empty(mpp41.scratch_bytes(desc), dtype=torch.uint8, device="cuda")
+        it = [0]
+
+        def run():
+            i = it[0] % cp
+            it[0] += 1
+            ctx.mlp(desc, x, wg[i], wu[i], wd[i], sg[i], su[i], sd[i], scr, out)
+        flops = 6.0 * T * H * I
+        abytes = wbytes + T * H * 2 * 2
+        line.update(config={"T": T, "H": H, "I": I}, weight_copies=cp)
+    elif args.row in ("w4a4", "nvfp4"):
         T, H, I = (int(v) for v in (args.shape or "4096,4096,14336").split(","))
         nv = args.row == "nvfp4"
         wbytes = 3 * H * I * (0.5 + (1 / 16 if nv else 1 / 32))

@@ -95,6 +95,26 @@ def test_mxfp4_token_counts(ctx, T):
     assert rel_fro(got, ref) <= TOL
 
 
+# T <= 16 with FP4 weights runs the weight-streaming GEMV kernels (mma.sync on
+# registers, per-32-block scaling of the fp32 sums): 1..8 tokens use one N tile
+# of 8, 9..16 two; H and I cover several K chunks per warp and ragged CTA counts
+@pytest.mark.parametrize("gate_kernel", ["mxfp4_native_sp_h_f_n64", "mpp_mlp_h_fp4_f_n128"])
+@pytest.mark.parametrize("T,H,I", [(1, 1024, 4096), (5, 512, 1024), (8, 2048, 2048), (9, 1024, 1536),
+                                   (16, 4096, 14336)])
+def test_gemv_decode_sizes(ctx, gate_kernel, T, H, I):
+    got, ref, mid, mid_ref = run_mlp(ctx, gate_kernel, T, H, I)
+    assert rel_fro(got, ref) <= TOL, gate_kernel
+    diff = mid.astype(np.float64) != mid_ref.astype(np.float64)
+    assert diff.mean() < 1e-3
+
+
+def test_gemv_wide_scales(ctx):
+    got, ref, _, _ = run_mlp(ctx, "mxfp4_native_sp_h_f_n64", 3, 512, 1024, wide=True)
+    fin = np.isfinite(ref)
+    assert np.array_equal(np.isfinite(got), fin)
+    assert rel_fro(got[fin], ref[fin]) <= TOL
+
+
 def test_benchmark_entry_point(ctx):
     T, H, I = 128, 1024, 4096
     d = O.reference_mlp_inputs(T, H, I)
