@@ -8,7 +8,7 @@
 // cvt.rn.f16x2.e2m1x2 into the A fragments of mma.sync.m16n8k16 (fp32
 // accumulate), and the tokens are the N = 8 side (two N tiles above 8).
 //
-// Per warp: 16 weight rows; per 32-wide K block (one E8M0 scale per row) two
+// Per warp: 16 weight rows, staged chunk by chunk in shared memory; per 32-wide K block (one E8M0 scale per row) two
 // MMAs sum into a fresh fragment that is then scaled by the block scale and
 // added to the running fp32 sums (scale 2^(s-127) built as s << 23: byte 0
 // gives 0 and 255 infinity, as the reference's e8m0_to_float,
@@ -51,6 +51,34 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 
 __device__ __forceinline__ float e8m0(uint32_t s) { return __uint_as_float(s << 23); }
 
+// Weight staging: each warp copies its 16 rows x 64 bytes (one 128-wide K
+// chunk) of each weight matrix into shared memory with 16-byte cp.async
+// (full sectors), kStage chunks ahead. Rows are 80 bytes apart, so the
+// fragment reads (lane g, t: row g, bytes 16b + 4t) hit 32 distinct banks.
+constexpr int kStage = 3;
+constexpr uint32_t kRowPitch = 80;
+constexpr uint32_t kMatBytes = 16 * kRowPitch;   // one 16-row chunk of one matrix
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Lane l copies segments l and l + 32 of the chunk: row = seg / 4, 16 bytes at
+// (seg % 4) * 16 of the chunk's 64 bytes in that row.
+__device__ __forceinline__ void stage_chunk(uint8_t *dst, const uint8_t *w, uint32_t K, uint32_t r0, uint32_t ch,
+                                            uint32_t lane)
+{
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t seg = lane + 32 * i, row = seg >> 2, part = seg & 3;
+        cp_async16(dst + row * kRowPitch + part * 16, w + (size_t)(r0 + row) * (K / 2) + (size_t)ch * 64 + part * 16);
+    }
+}
+
 // One 32-wide K block of one 16-row weight group against NT token tiles:
 // wg = this lane's 4 bytes of row g, wg8 = of row g + 8; x[nt] = the lane's 8
 // activations (k = 8t..8t+7) of token nt*8 + g; the block sums go to tmp.
@@ -76,12 +104,7 @@ __device__ __forceinline__ uint4 load_x(const __half *x, uint32_t T, uint32_t K,
     return __ldg(reinterpret_cast<const uint4 *>(x + (size_t)n * K + (size_t)kb * 32 + 8 * t));
 }
 
-// Weight bytes of row r, block kb, lane t (4 bytes); scales of 4 consecutive blocks.
-__device__ __forceinline__ uint32_t load_w(const uint8_t *w, uint32_t K, uint32_t r, uint32_t kb, uint32_t t)
-{
-    return __ldg(reinterpret_cast<const uint32_t *>(w + (size_t)r * (K / 2) + (size_t)kb * 16 + 4 * t));
-}
-
+// Scales of 4 consecutive blocks of row r.
 template <bool SCALED>
 __device__ __forceinline__ uint32_t load_s4(const uint8_t *s, uint32_t K, uint32_t r, uint32_t kb4)
 {
@@ -97,31 +120,55 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *
                                                                   const uint8_t *__restrict__ su, __half *__restrict__ mid,
                                                                   uint32_t T, uint32_t H, uint32_t I)
 {
-    __shared__ float part[kGateWarps][2][NT][4][32];
+    extern __shared__ __align__(16) uint8_t wsm[];   // weight ring, then (aliased) the partial sums
+    float(*part)[2][NT][4][32] = reinterpret_cast<float(*)[2][NT][4][32]>(wsm);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const uint32_t c0 = blockIdx.x * 16;
     float ag[NT][4] = {}, au[NT][4] = {};
     const uint32_t chunks = H / 128;
+    uint8_t *ring = wsm + warp * (kStage * 2 * kMatBytes);   // [stage][gate, up]
+    // prologue: the first kStage - 1 chunks of this warp in flight
+    uint32_t issued = warp;
+#pragma unroll
+    for (int st = 0; st < kStage - 1; ++st) {
+        if (issued < chunks) {
+            stage_chunk(ring + st * 2 * kMatBytes, wg, H, c0, issued, lane);
+            stage_chunk(ring + st * 2 * kMatBytes + kMatBytes, wu, H, c0, issued, lane);
+        }
+        cp_commit();
+        issued += kGateWarps;
+    }
+    uint32_t slot = 0;
     for (uint32_t ch = warp; ch < chunks; ch += kGateWarps) {
+        {   // keep kStage - 1 chunks in flight
+            const uint32_t fill = (slot + kStage - 1) % kStage;
+            if (issued < chunks) {
+                stage_chunk(ring + fill * 2 * kMatBytes, wg, H, c0, issued, lane);
+                stage_chunk(ring + fill * 2 * kMatBytes + kMatBytes, wu, H, c0, issued, lane);
+            }
+            cp_commit();
+            issued += kGateWarps;
+        }
         const uint32_t sg4 = load_s4<SCALED>(sg, H, c0 + g, ch), sg48 = load_s4<SCALED>(sg, H, c0 + g + 8, ch);
         const uint32_t su4 = load_s4<SCALED>(su, H, c0 + g, ch), su48 = load_s4<SCALED>(su, H, c0 + g + 8, ch);
-        uint32_t wgr[4], wgr8[4], wur[4], wur8[4];
         uint4 xv[4][NT];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const uint32_t kb = ch * 4 + b;
-            wgr[b] = load_w(wg, H, c0 + g, kb, t);
-            wgr8[b] = load_w(wg, H, c0 + g + 8, kb, t);
-            wur[b] = load_w(wu, H, c0 + g, kb, t);
-            wur8[b] = load_w(wu, H, c0 + g + 8, kb, t);
+        for (int b = 0; b < 4; ++b)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = load_x(x, T, H, nt * 8 + g, kb, t);
-        }
+            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = load_x(x, T, H, nt * 8 + g, ch * 4 + b, t);
+        cp_wait<kStage - 1>();
+        __syncwarp();
+        const uint8_t *cg = ring + slot * 2 * kMatBytes, *cu = cg + kMatBytes;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
             float tmp[NT][4];
+            const uint32_t off = b * 16 + 4 * t;
+            const uint32_t wgr = *reinterpret_cast<const uint32_t *>(cg + g * kRowPitch + off);
+            const uint32_t wgr8 = *reinterpret_cast<const uint32_t *>(cg + (g + 8) * kRowPitch + off);
+            const uint32_t wur = *reinterpret_cast<const uint32_t *>(cu + g * kRowPitch + off);
+            const uint32_t wur8 = *reinterpret_cast<const uint32_t *>(cu + (g + 8) * kRowPitch + off);
             const float s0 = e8m0((sg4 >> (8 * b)) & 0xFFu), s8 = e8m0((sg48 >> (8 * b)) & 0xFFu);
-            block_mma<NT>(wgr[b], wgr8[b], xv[b], tmp);
+            block_mma<NT>(wgr, wgr8, xv[b], tmp);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 ag[nt][0] = fmaf(tmp[nt][0], s0, ag[nt][0]);
@@ -130,7 +177,7 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *
                 ag[nt][3] = fmaf(tmp[nt][3], s8, ag[nt][3]);
             }
             const float u0 = e8m0((su4 >> (8 * b)) & 0xFFu), u8 = e8m0((su48 >> (8 * b)) & 0xFFu);
-            block_mma<NT>(wur[b], wur8[b], xv[b], tmp);
+            block_mma<NT>(wur, wur8, xv[b], tmp);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 au[nt][0] = fmaf(tmp[nt][0], u0, au[nt][0]);
@@ -139,7 +186,11 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *
                 au[nt][3] = fmaf(tmp[nt][3], u8, au[nt][3]);
             }
         }
+        __syncwarp();   // the slot is refilled next iteration
+        slot = (slot + 1) % kStage;
     }
+    cp_wait<0>();
+    __syncthreads();   // every warp is done with the ring the partial sums reuse
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -169,28 +220,45 @@ __global__ void __launch_bounds__(kDownWarps * 32) down_kernel(const __half *__r
                                                                const uint8_t *__restrict__ sd, void *__restrict__ out,
                                                                uint32_t T, uint32_t H, uint32_t I)
 {
-    __shared__ float part[kDownWarps][NT][4][32];
+    extern __shared__ __align__(16) uint8_t wsm[];
+    float(*part)[NT][4][32] = reinterpret_cast<float(*)[NT][4][32]>(wsm);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const uint32_t h0 = blockIdx.x * 16;
     float acc[NT][4] = {};
     const uint32_t chunks = I / 128;
+    uint8_t *ring = wsm + warp * (kStage * kMatBytes);
+    uint32_t issued = warp;
+#pragma unroll
+    for (int st = 0; st < kStage - 1; ++st) {
+        if (issued < chunks) stage_chunk(ring + st * kMatBytes, wd, I, h0, issued, lane);
+        cp_commit();
+        issued += kDownWarps;
+    }
+    uint32_t slot = 0;
     for (uint32_t ch = warp; ch < chunks; ch += kDownWarps) {
+        {
+            const uint32_t fill = (slot + kStage - 1) % kStage;
+            if (issued < chunks) stage_chunk(ring + fill * kMatBytes, wd, I, h0, issued, lane);
+            cp_commit();
+            issued += kDownWarps;
+        }
         const uint32_t s4 = load_s4<SCALED>(sd, I, h0 + g, ch), s48 = load_s4<SCALED>(sd, I, h0 + g + 8, ch);
-        uint32_t wr[4], wr8[4];
         uint4 xv[4][NT];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const uint32_t kb = ch * 4 + b;
-            wr[b] = load_w(wd, I, h0 + g, kb, t);
-            wr8[b] = load_w(wd, I, h0 + g + 8, kb, t);
+        for (int b = 0; b < 4; ++b)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = load_x(mid, T, I, nt * 8 + g, kb, t);
-        }
+            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = load_x(mid, T, I, nt * 8 + g, ch * 4 + b, t);
+        cp_wait<kStage - 1>();
+        __syncwarp();
+        const uint8_t *cw = ring + slot * kMatBytes;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
             float tmp[NT][4];
+            const uint32_t off = b * 16 + 4 * t;
+            const uint32_t wr = *reinterpret_cast<const uint32_t *>(cw + g * kRowPitch + off);
+            const uint32_t wr8 = *reinterpret_cast<const uint32_t *>(cw + (g + 8) * kRowPitch + off);
             const float s0 = e8m0((s4 >> (8 * b)) & 0xFFu), s8 = e8m0((s48 >> (8 * b)) & 0xFFu);
-            block_mma<NT>(wr[b], wr8[b], xv[b], tmp);
+            block_mma<NT>(wr, wr8, xv[b], tmp);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 acc[nt][0] = fmaf(tmp[nt][0], s0, acc[nt][0]);
@@ -199,7 +267,11 @@ __global__ void __launch_bounds__(kDownWarps * 32) down_kernel(const __half *__r
                 acc[nt][3] = fmaf(tmp[nt][3], s8, acc[nt][3]);
             }
         }
+        __syncwarp();
+        slot = (slot + 1) % kStage;
     }
+    cp_wait<0>();
+    __syncthreads();
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -217,17 +289,38 @@ __global__ void __launch_bounds__(kDownWarps * 32) down_kernel(const __half *__r
     }
 }
 
+constexpr uint32_t gate_smem(int NT)
+{
+    const uint32_t ring = kGateWarps * kStage * 2 * kMatBytes, part = kGateWarps * 2 * NT * 4 * 32 * 4;
+    return ring > part ? ring : part;
+}
+constexpr uint32_t down_smem(int NT)
+{
+    const uint32_t ring = kDownWarps * kStage * kMatBytes, part = kDownWarps * NT * 4 * 32 * 4;
+    return ring > part ? ring : part;
+}
+
+template <typename K>
+bool allow_smem(K kern, uint32_t bytes)
+{
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess;
+}
+
 template <bool SCALED, int EG, int NT>
 int launch_nt(const FusedLaunch &L, cudaStream_t st)
 {
-    gate_up_kernel<SCALED, EG, NT><<<L.I / 16, kGateWarps * 32, 0, st>>>(
+    static const bool ok = allow_smem(gate_up_kernel<SCALED, EG, NT>, gate_smem(NT)) &&
+                           allow_smem(down_kernel<SCALED, true, NT>, down_smem(NT)) &&
+                           allow_smem(down_kernel<SCALED, false, NT>, down_smem(NT));
+    if (!ok) return 2;
+    gate_up_kernel<SCALED, EG, NT><<<L.I / 16, kGateWarps * 32, gate_smem(NT), st>>>(
         static_cast<const __half *>(L.x), static_cast<const uint8_t *>(L.wg), static_cast<const uint8_t *>(L.wu), L.sg,
         L.su, static_cast<__half *>(L.mid), L.T, L.H, L.I);
     if (L.out_f16)
-        down_kernel<SCALED, true, NT><<<L.H / 16, kDownWarps * 32, 0, st>>>(
+        down_kernel<SCALED, true, NT><<<L.H / 16, kDownWarps * 32, down_smem(NT), st>>>(
             static_cast<const __half *>(L.mid), static_cast<const uint8_t *>(L.wd), L.sd, L.out, L.T, L.H, L.I);
     else
-        down_kernel<SCALED, false, NT><<<L.H / 16, kDownWarps * 32, 0, st>>>(
+        down_kernel<SCALED, false, NT><<<L.H / 16, kDownWarps * 32, down_smem(NT), st>>>(
             static_cast<const __half *>(L.mid), static_cast<const uint8_t *>(L.wd), L.sd, L.out, L.T, L.H, L.I);
     return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
