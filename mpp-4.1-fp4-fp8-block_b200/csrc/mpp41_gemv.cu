@@ -138,8 +138,25 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *
         cp_commit();
         issued += kGateWarps;
     }
+    // scales and activations are loaded into registers a chunk ahead (one token tile)
+    uint32_t nsg4 = 0, nsg48 = 0, nsu4 = 0, nsu48 = 0;
+    uint4 nxv[4][NT];
+    auto fetch = [&](uint32_t c) {
+        nsg4 = load_s4<SCALED>(sg, H, c0 + g, c);
+        nsg48 = load_s4<SCALED>(sg, H, c0 + g + 8, c);
+        nsu4 = load_s4<SCALED>(su, H, c0 + g, c);
+        nsu48 = load_s4<SCALED>(su, H, c0 + g + 8, c);
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) nxv[b][nt] = load_x(x, T, H, nt * 8 + g, c * 4 + b, t);
+    };
+    // one token tile: prefetch one chunk ahead; two tiles would need too many registers
+    constexpr bool kAhead = NT == 1;
+    if (kAhead && warp < chunks) fetch(warp);
     uint32_t slot = 0;
     for (uint32_t ch = warp; ch < chunks; ch += kGateWarps) {
+        if constexpr (!kAhead) fetch(ch);
         {   // keep kStage - 1 chunks in flight
             const uint32_t fill = (slot + kStage - 1) % kStage;
             if (issued < chunks) {
@@ -149,13 +166,13 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *
             cp_commit();
             issued += kGateWarps;
         }
-        const uint32_t sg4 = load_s4<SCALED>(sg, H, c0 + g, ch), sg48 = load_s4<SCALED>(sg, H, c0 + g + 8, ch);
-        const uint32_t su4 = load_s4<SCALED>(su, H, c0 + g, ch), su48 = load_s4<SCALED>(su, H, c0 + g + 8, ch);
+        const uint32_t sg4 = nsg4, sg48 = nsg48, su4 = nsu4, su48 = nsu48;
         uint4 xv[4][NT];
 #pragma unroll
         for (int b = 0; b < 4; ++b)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = load_x(x, T, H, nt * 8 + g, ch * 4 + b, t);
+            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = nxv[b][nt];
+        if (kAhead && ch + kGateWarps < chunks) fetch(ch + kGateWarps);
         cp_wait<kStage - 1>();
         __syncwarp();
         const uint8_t *cg = ring + slot * 2 * kMatBytes, *cu = cg + kMatBytes;
@@ -234,20 +251,35 @@ __global__ void __launch_bounds__(kDownWarps * 32) down_kernel(const __half *__r
         cp_commit();
         issued += kDownWarps;
     }
+    uint32_t ns4 = 0, ns48 = 0;
+    uint4 nxv[4][NT];
+    auto fetch = [&](uint32_t c) {
+        ns4 = load_s4<SCALED>(sd, I, h0 + g, c);
+        ns48 = load_s4<SCALED>(sd, I, h0 + g + 8, c);
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) nxv[b][nt] = load_x(mid, T, I, nt * 8 + g, c * 4 + b, t);
+    };
+    // one token tile: prefetch one chunk ahead; two tiles would need too many registers
+    constexpr bool kAhead = NT == 1;
+    if (kAhead && warp < chunks) fetch(warp);
     uint32_t slot = 0;
     for (uint32_t ch = warp; ch < chunks; ch += kDownWarps) {
+        if constexpr (!kAhead) fetch(ch);
         {
             const uint32_t fill = (slot + kStage - 1) % kStage;
             if (issued < chunks) stage_chunk(ring + fill * kMatBytes, wd, I, h0, issued, lane);
             cp_commit();
             issued += kDownWarps;
         }
-        const uint32_t s4 = load_s4<SCALED>(sd, I, h0 + g, ch), s48 = load_s4<SCALED>(sd, I, h0 + g + 8, ch);
+        const uint32_t s4 = ns4, s48 = ns48;
         uint4 xv[4][NT];
 #pragma unroll
         for (int b = 0; b < 4; ++b)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = load_x(mid, T, I, nt * 8 + g, ch * 4 + b, t);
+            for (int nt = 0; nt < NT; ++nt) xv[b][nt] = nxv[b][nt];
+        if (kAhead && ch + kDownWarps < chunks) fetch(ch + kDownWarps);
         cp_wait<kStage - 1>();
         __syncwarp();
         const uint8_t *cw = ring + slot * kMatBytes;
