@@ -303,7 +303,8 @@ mpp41_status mpp41_mlp_w4a4(mpp41_ctx *ctx, uint32_t tokens, uint32_t hidden, ui
  *      the FP4 tensor cores through kind::mxf4nvf4 (block16). Quantization
  *      (IEEE fp32, round to nearest even): g = amax(tensor) / 2688 (1 if
  *      zero); s = UE4M3((amax(block16) / 6) / g), saturating; element =
- *      E2M1(v / (decode(s) * g)); value = element * decode(s) * g.
+ *      E2M1(v * (1 / (decode(s) * g))) with one correctly rounded reciprocal
+ *      per block; value = element * decode(s) * g.
  *      - mpp41_quantize_nvfp4 (fp32 weights) / mpp41_quantize_act_nvfp4 (fp16
  *        activations): packed [rows][depth/2], scales [rows][depth/16],
  *        *tensor_scale (device float) = g.

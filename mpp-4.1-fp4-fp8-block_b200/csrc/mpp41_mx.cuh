@@ -55,7 +55,8 @@ __device__ __forceinline__ uint32_t mx_quant32(const float (&v)[32], uint4 &pack
 // Recipe (all steps IEEE fp32, round to nearest even):
 //   g = amax(tensor) / (6 * 448)            (1 for an all-zero tensor)
 //   s = E4M3((amax(block) / 6) / g)         (saturating; 0 when it underflows)
-//   q = E2M1(v / (decode(s) * g))           (0 when decode(s) == 0)
+//   q = E2M1(v * (1 / (decode(s) * g)))     (0 when decode(s) == 0; one
+//                                            correctly rounded reciprocal per block)
 // so value = q * decode(s) * g, and the largest block scale lands on 448.
 __host__ __device__ __forceinline__ float nvfp4_tensor_scale(float amax)
 {
@@ -85,16 +86,14 @@ __device__ __forceinline__ uint32_t nv_quant16(const float (&v)[16], float g, ui
     for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
     const uint32_t code = enc_ue4m3(__fdiv_rn(__fdiv_rn(amax, 6.0f), g));
     const float denom = __fmul_rn(dec_ue4m3(code), g);
+    const float inv = denom > 0.0f ? __frcp_rn(denom) : 0.0f;
     uint32_t out[2];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
         uint32_t word = 0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float a = denom > 0.0f ? __fdiv_rn(v[8 * q + 2 * i], denom) : 0.0f;
-            const float b = denom > 0.0f ? __fdiv_rn(v[8 * q + 2 * i + 1], denom) : 0.0f;
-            word |= enc_e2m1x2(a, b) << (8 * i);
-        }
+        for (int i = 0; i < 4; ++i)
+            word |= enc_e2m1x2(__fmul_rn(v[8 * q + 2 * i], inv), __fmul_rn(v[8 * q + 2 * i + 1], inv)) << (8 * i);
         out[q] = word;
     }
     packed = make_uint2(out[0], out[1]);

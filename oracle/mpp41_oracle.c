@@ -658,7 +658,8 @@ void orc_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *
  * Every step is an IEEE single-precision operation rounded to nearest even:
  *   g = amax(tensor) / 2688 (6 * 448), or 1 for an all-zero tensor;
  *   s = UE4M3((amax(block) / 6) / g), saturating at 448;
- *   element = E2M1(v / (decode(s) * g)), or 0 when decode(s) * g == 0. */
+ *   element = E2M1(v * (1 / (decode(s) * g))), one correctly rounded
+ *   reciprocal per block (0 when decode(s) * g == 0). */
 float orc_nvfp4_tensor_scale(const float *w, size_t n)
 {
     float amax = 0.0f;
@@ -681,13 +682,10 @@ void orc_quantize_nvfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *
             const uint8_t code = (uint8_t)(orc_e4m3_encode(s) & 0x7f);
             scales[(size_t)r * (depth / 16) + j] = code;
             volatile float denom = orc_e4m3_decode(code) * g;
+            volatile float inv = denom > 0.0f ? 1.0f / denom : 0.0f;
             for (int i = 0; i < 16; i += 2) {
-                float a = 0.0f, c = 0.0f;
-                if (denom > 0.0f) {
-                    volatile float qa = b[i] / denom, qc = b[i + 1] / denom;
-                    a = qa;
-                    c = qc;
-                }
+                volatile float qa = b[i] * inv, qc = b[i + 1] * inv;
+                const float a = qa, c = qc;
                 const uint8_t lo = orc_e2m1_encode(a), hi = orc_e2m1_encode(c);
                 packed[(size_t)r * (depth / 2) + (size_t)j * 8 + i / 2] = (uint8_t)(lo | (hi << 4));
             }
