@@ -277,6 +277,12 @@ mpp41_status mpp41_mlp_w8a8(mpp41_ctx *ctx, int wfmt, uint32_t tokens, uint32_t 
                             const void *x, const void *wg, const float *sg, const void *wu, const float *su,
                             const void *wd, const float *sd, void *out, void *scratch);
 
+/* ---- device-time measurement on the context's stream (CUDA events):
+ *      mpp41_timer_start records the start; mpp41_timer_stop records the end,
+ *      waits for it and returns the seconds in between. ---- */
+mpp41_status mpp41_timer_start(mpp41_ctx *ctx);
+mpp41_status mpp41_timer_stop(mpp41_ctx *ctx, double *seconds);
+
 /* ---- W4A4: activations as well as weights in MXFP4, multiplied on the FP4
  *      tensor cores with the E8M0 block scales applied inside the MMA (no
  *      reference counterpart: its FP4 rows keep fp16 activations; the weight

@@ -857,6 +857,26 @@ mpp41_status mpp41_quantize_act_s8(mpp41_ctx *ctx, const void *x, uint32_t token
     return MPP41_OK;
 }
 
+// ------------------------------------------------------------------ timer
+mpp41_status mpp41_timer_start(mpp41_ctx *ctx)
+{
+    NEED(ctx);
+    CK(cudaEventRecord(ctx->ev0, ctx->stream), "timer start");
+    return MPP41_OK;
+}
+
+mpp41_status mpp41_timer_stop(mpp41_ctx *ctx, double *seconds)
+{
+    NEED(ctx);
+    if (!seconds) return fail(MPP41_ERR_INVALID_ARGUMENT, "null seconds");
+    float ms = 0.0f;
+    CK(cudaEventRecord(ctx->ev1, ctx->stream), "timer stop");
+    CK(cudaEventSynchronize(ctx->ev1), "timer stop");
+    CK(cudaEventElapsedTime(&ms, ctx->ev0, ctx->ev1), "timer stop");
+    *seconds = ms * 1e-3;
+    return MPP41_OK;
+}
+
 // ------------------------------------------------------------------ W4A4
 static bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 static size_t up256(size_t n) { return (n + 255) & ~size_t(255); }

@@ -9,6 +9,15 @@
 //   --skip-tensor               accepted (the MTLTensor probe is Metal-only)
 //   --accum-probe               accepted (Apple accumulator probe, not applicable)
 //   --iterations N              timed iterations per row (default 20)
+//   --mode ref|baseline         MLP rows' inputs: the reference seeds (default) or, for the
+//                               MXFP4 rows, BASELINE mode B (x ~ N(0,1), weights N(0,0.02)
+//                               quantized OCP-MX on the GPU)
+//   --seed N                    seed of the mode-B and new rows' generators (default 0)
+//   --w4a4                      W4A4 and NVFP4 layer rows (config-0 shape)
+//   --moe                       mixture-of-experts row (T=512 H=7168 I=2048, 32 experts, top-8,
+//                               shared expert: one GPU's share of BASELINE config 4)
+//   --json                      benchmark rows as JSON lines instead of text
+//   --gpus N                    1 only (multi-GPU runs are one process per GPU)
 //
 // Buffers live in device memory (mpp41_alloc); inputs are generated on the host
 // and uploaded, outputs downloaded for the checksums.
@@ -26,6 +35,20 @@
 namespace {
 
 int g_iterations = 20;
+bool g_json = false;
+bool g_baseline = false;
+uint32_t g_seed = 0;
+
+// One timed benchmark row: text as the reference prints it, or a JSON line.
+void report(const char *name, double sec, double flops, const std::string &cks)
+{
+    const double ms = sec * 1e3 / g_iterations, tops = flops * g_iterations / sec / 1e12;
+    if (g_json)
+        printf("{\"row\": \"%s\", \"ms\": %.5f, \"tops\": %.3f, \"checksum\": \"%s\"}\n", name, ms, tops,
+               cks.c_str());
+    else
+        printf("  %s:\n    %.3f ms/MLP, %.3f effective TOPS\n    checksum: %s\n", name, ms, tops, cks.c_str());
+}
 
 [[noreturn]] void die(mpp41_status s, const char *what)
 {
@@ -66,6 +89,23 @@ std::vector<_Float16> half_values(size_t n, uint32_t seed, float scale = 0.25f)
         s = lcg(s, i);
         const int nib = (int)((s >> 28) & 0xF);
         v[i] = (_Float16)((float)((nib ^ 8) - 8) * scale);
+    }
+    return v;
+}
+
+// N(0, sigma) by Box-Muller over the same LCG (mode B inputs).
+std::vector<float> normal_values(size_t n, uint32_t seed, float sigma)
+{
+    std::vector<float> v(n);
+    uint32_t s = seed;
+    for (size_t i = 0; i < n; i += 2) {
+        s = lcg(s, i);
+        const double u1 = ((s >> 8) + 1.0) / 16777217.0;
+        s = lcg(s, i + 1);
+        const double u2 = (s >> 8) / 16777216.0;
+        const double r = std::sqrt(-2.0 * std::log(u1)), th = 6.283185307179586 * u2;
+        v[i] = (float)(r * std::cos(th) * sigma);
+        if (i + 1 < n) v[i + 1] = (float)(r * std::sin(th) * sigma);
     }
     return v;
 }
@@ -222,12 +262,117 @@ void run_big_matmul(mpp41_ctx *ctx)
     }
 }
 
+std::vector<_Float16> to_half(const std::vector<float> &v)
+{
+    std::vector<_Float16> h(v.size());
+    for (size_t i = 0; i < v.size(); ++i) h[i] = (_Float16)v[i];
+    return h;
+}
+
+// OCP-MX MXFP4 weights [rows][depth] quantized on the GPU from N(0, 0.02).
+struct MxWeights {
+    Dev q, s;
+    MxWeights(mpp41_ctx *ctx, uint32_t rows, uint32_t depth, uint32_t seed)
+        : q(ctx, (size_t)rows * depth / 2), s(ctx, (size_t)rows * depth / 32)
+    {
+        Dev w(ctx, normal_values((size_t)rows * depth, seed, 0.02f));
+        check(mpp41_quantize_mxfp4(ctx, (const float *)w.p, rows, depth, (uint8_t *)q.p, (uint8_t *)s.p), "quantize");
+        check(mpp41_synchronize(ctx), "quantize");
+    }
+};
+
+// NVFP4 weights (E2M1 + UE4M3 per 16 + fp32 tensor scale) quantized on the GPU from N(0, 0.02).
+struct NvWeights {
+    Dev q, s, t;
+    NvWeights(mpp41_ctx *ctx, uint32_t rows, uint32_t depth, uint32_t seed)
+        : q(ctx, (size_t)rows * depth / 2), s(ctx, (size_t)rows * depth / 16), t(ctx, 4)
+    {
+        Dev w(ctx, normal_values((size_t)rows * depth, seed, 0.02f));
+        check(mpp41_quantize_nvfp4(ctx, (const float *)w.p, rows, depth, (uint8_t *)q.p, (uint8_t *)s.p, (float *)t.p),
+              "quantize NVFP4");
+        check(mpp41_synchronize(ctx), "quantize NVFP4");
+    }
+};
+
+template <class F>
+double time_calls(mpp41_ctx *ctx, F call)
+{
+    for (int i = 0; i < 3; ++i) call();
+    check(mpp41_timer_start(ctx), "timer");
+    for (int i = 0; i < g_iterations; ++i) call();
+    double sec = 0;
+    check(mpp41_timer_stop(ctx, &sec), "timer");
+    check(mpp41_synchronize(ctx), "timed calls");
+    return sec;
+}
+
+// ---------------------------------------------------------------- W4A4 / NVFP4 rows (no reference counterpart)
+void run_w4a4(mpp41_ctx *ctx)
+{
+    const uint32_t T = 128, H = 1024, I = 4096;
+    if (!g_json) printf("\nW4A4 MLP rows (activations quantized too, FP4 tensor cores):\n  shape: tokens=%u, hidden=%u, intermediate=%u\n", T, H, I);
+    Dev x(ctx, to_half(normal_values((size_t)T * H, 0x5A5A0000u ^ g_seed, 1.0f)));
+    MxWeights g(ctx, I, H, 0x5A5A0001u ^ g_seed), u(ctx, I, H, 0x5A5A0002u ^ g_seed), d(ctx, H, I, 0x5A5A0003u ^ g_seed);
+    Dev out(ctx, (size_t)T * H * 2), scratch(ctx, mpp41_mlp_w4a4_scratch_bytes(T, H, I));
+    double sec = time_calls(ctx, [&] {
+        check(mpp41_mlp_w4a4(ctx, T, H, I, x.p, (const uint8_t *)g.q.p, (const uint8_t *)g.s.p, (const uint8_t *)u.q.p,
+                             (const uint8_t *)u.s.p, (const uint8_t *)d.q.p, (const uint8_t *)d.s.p, out.p, 1, scratch.p),
+              "mpp41_mlp_w4a4");
+    });
+    report("W4A4 MXFP4 MLP: x -> MXFP4, kind::mxf4 gate/up + SwiGLU -> MXFP4 mid, kind::mxf4 down", sec,
+           6.0 * T * H * (double)I, half_raw_checksum(out.get<uint16_t>().data(), (size_t)T * H));
+    // NVFP4: weights from the same fp32 values, quantized NVFP4 on the GPU
+    NvWeights ng(ctx, I, H, 0x5A5A0001u ^ g_seed), nu(ctx, I, H, 0x5A5A0002u ^ g_seed), nd(ctx, H, I, 0x5A5A0003u ^ g_seed);
+    Dev nscr(ctx, mpp41_mlp_nvfp4_scratch_bytes(T, H, I));
+    sec = time_calls(ctx, [&] {
+        check(mpp41_mlp_nvfp4(ctx, T, H, I, x.p, (const uint8_t *)ng.q.p, (const uint8_t *)ng.s.p, (const float *)ng.t.p,
+                              (const uint8_t *)nu.q.p, (const uint8_t *)nu.s.p, (const float *)nu.t.p, (const uint8_t *)nd.q.p,
+                              (const uint8_t *)nd.s.p, (const float *)nd.t.p, out.p, 1, nscr.p),
+              "mpp41_mlp_nvfp4");
+    });
+    report("W4A4 NVFP4 MLP: E2M1 + UE4M3/16 + fp32 tensor scales, kind::mxf4nvf4", sec, 6.0 * T * H * (double)I,
+           half_raw_checksum(out.get<uint16_t>().data(), (size_t)T * H));
+}
+
+// ---------------------------------------------------------------- MoE row (no reference counterpart)
+void run_moe(mpp41_ctx *ctx)
+{
+    const mpp41_moe_desc d = {512, 7168, 2048, 32, 8, 2048, 1};
+    if (!g_json)
+        printf("\nMixture-of-experts row (W4A4 experts):\n  shape: tokens=%u, hidden=%u, expert intermediate=%u, "
+               "experts=%u, top-%u, shared intermediate=%u\n", d.tokens, d.hidden, d.intermediate, d.experts, d.top_k,
+               d.shared_intermediate);
+    const size_t H = d.hidden, I = d.intermediate, E = d.experts, Is = d.shared_intermediate;
+    Dev x(ctx, to_half(normal_values((size_t)d.tokens * H, 0x3E3E0000u ^ g_seed, 1.0f)));
+    Dev logits(ctx, normal_values((size_t)d.tokens * E, 0x3E3E0001u ^ g_seed, 1.0f));
+    Dev wg(ctx, packed_bytes(E * I * H / 2, 0x3E3E0002u ^ g_seed)), wu(ctx, packed_bytes(E * I * H / 2, 0x3E3E0003u ^ g_seed));
+    Dev wd(ctx, packed_bytes(E * H * I / 2, 0x3E3E0004u ^ g_seed));
+    Dev sg(ctx, pattern_bytes(E * I * H / 32, 0x3E3E0005u, kScalePattern)), su(ctx, pattern_bytes(E * I * H / 32, 0x3E3E0006u, kScalePattern));
+    Dev sd(ctx, pattern_bytes(E * H * I / 32, 0x3E3E0007u, kScalePattern));
+    Dev swg(ctx, packed_bytes(Is * H / 2, 0x3E3E0008u)), swu(ctx, packed_bytes(Is * H / 2, 0x3E3E0009u));
+    Dev swd(ctx, packed_bytes(H * Is / 2, 0x3E3E000Au));
+    Dev ssg(ctx, pattern_bytes(Is * H / 32, 0x3E3E000Bu, kScalePattern)), ssu(ctx, pattern_bytes(Is * H / 32, 0x3E3E000Cu, kScalePattern));
+    Dev ssd(ctx, pattern_bytes(H * Is / 32, 0x3E3E000Du, kScalePattern));
+    Dev out(ctx, (size_t)d.tokens * H * 2), scratch(ctx, mpp41_moe_scratch_layout(&d, nullptr));
+    auto u8 = [](const Dev &b) { return (const uint8_t *)b.p; };
+    const double sec = time_calls(ctx, [&] {
+        check(mpp41_moe_w4a4(ctx, &d, x.p, (const float *)logits.p, u8(wg), u8(sg), u8(wu), u8(su), u8(wd), u8(sd), u8(swg),
+                             u8(ssg), u8(swu), u8(ssu), u8(swd), u8(ssd), out.p, scratch.p),
+              "mpp41_moe_w4a4");
+    });
+    report("MoE W4A4: route top-8, grouped kind::mxf4 experts, shared expert, combine", sec,
+           6.0 * d.tokens * H * (double)(d.top_k * I + Is), half_raw_checksum(out.get<uint16_t>().data(), (size_t)d.tokens * H));
+}
+
 // ---------------------------------------------------------------- MLP rows
 void run_mlp(mpp41_ctx *ctx)
 {
     const uint32_t T = 128, H = 1024, I = 4096;
-    printf("\nGated MLP benchmark:\n  op: down(silu(gate(x)) * up(x))\n");
-    printf("  shape: tokens=%u, hidden=%u, intermediate=%u\n  iterations: %d\n", T, H, I, g_iterations);
+    if (!g_json) {
+        printf("\nGated MLP benchmark:\n  op: down(silu(gate(x)) * up(x))\n");
+        printf("  shape: tokens=%u, hidden=%u, intermediate=%u\n  iterations: %d\n", T, H, I, g_iterations);
+        if (g_baseline) printf("  inputs: MXFP4 rows in BASELINE mode B (seed %u)\n", g_seed);
+    }
     const size_t gw = (size_t)I * H, dw = (size_t)H * I;
     Dev x_half(ctx, half_values((size_t)T * H, 0x11112222u, 0.125f));
     Dev x_int8(ctx, int8_values((size_t)T * H, 0x22223333u));
@@ -248,6 +393,9 @@ void run_mlp(mpp41_ctx *ctx)
     Dev sg(ctx, pattern_bytes((size_t)I * (H / 32), 0x7777ddddu, kScalePattern));
     Dev su(ctx, pattern_bytes((size_t)I * (H / 32), 0x8888eeeeu, kScalePattern));
     Dev sd(ctx, pattern_bytes((size_t)H * (I / 32), 0x9999ffffu, kScalePattern));
+    // mode B: x ~ N(0,1) fp16, weights N(0,0.02) quantized OCP-MX on the GPU
+    Dev xb(ctx, to_half(normal_values((size_t)T * H, 0x51ED0000u ^ g_seed, 1.0f)));
+    MxWeights bg(ctx, I, H, 0x51ED0001u ^ g_seed), bu(ctx, I, H, 0x51ED0002u ^ g_seed), bd(ctx, H, I, 0x51ED0003u ^ g_seed);
 
     struct Row { const char *name, *kernel; const Weights *w; bool mx; };
     const Row rows[] = {
@@ -275,19 +423,19 @@ void run_mlp(mpp41_ctx *ctx)
         check(mpp41_mlp_describe(r.kernel, T, H, I, &d), r.kernel);
         const size_t out_elem = d.out_dtype == MPP41_F16 ? 2 : 4;
         Dev out(ctx, (size_t)T * H * out_elem), scratch(ctx, mpp41_mlp_scratch_bytes(&d));
-        const void *x = d.afmt == MPP41_A_S8 ? x_int8.p : x_half.p;
+        const bool mode_b = g_baseline && r.mx;
+        const void *x = d.afmt == MPP41_A_S8 ? x_int8.p : (mode_b ? xb.p : x_half.p);
+        const void *wg = mode_b ? bg.q.p : r.w->g.p, *wu = mode_b ? bu.q.p : r.w->u.p, *wd = mode_b ? bd.q.p : r.w->d.p;
+        const uint8_t *s_g = r.mx ? (const uint8_t *)(mode_b ? bg.s.p : sg.p) : nullptr;
+        const uint8_t *s_u = r.mx ? (const uint8_t *)(mode_b ? bu.s.p : su.p) : nullptr;
+        const uint8_t *s_d = r.mx ? (const uint8_t *)(mode_b ? bd.s.p : sd.p) : nullptr;
         double sec = 0;
-        check(mpp41_mlp_benchmark(ctx, &d, x, r.w->g.p, r.w->u.p, r.w->d.p, r.mx ? (const uint8_t *)sg.p : nullptr,
-                                  r.mx ? (const uint8_t *)su.p : nullptr, r.mx ? (const uint8_t *)sd.p : nullptr,
-                                  scratch.p, out.p, g_iterations, &sec),
-              r.kernel);
-        const double tops = 2.0 * 3.0 * T * (double)H * I * g_iterations / sec / 1e12;
+        check(mpp41_mlp_benchmark(ctx, &d, x, wg, wu, wd, s_g, s_u, s_d, scratch.p, out.p, g_iterations, &sec), r.kernel);
         std::string cks;
         if (d.out_dtype == MPP41_S32) { const auto h = out.get<int32_t>(); cks = int_checksum(h.data(), h.size()); }
         else if (d.out_dtype == MPP41_F16) { const auto h = out.get<uint16_t>(); cks = half_raw_checksum(h.data(), h.size()); }
         else { const auto h = out.get<float>(); cks = float_checksum(h.data(), h.size()); }
-        printf("  %s:\n    %.3f ms/MLP, %.3f effective TOPS\n    checksum: %s\n", r.name, sec * 1e3 / g_iterations,
-               tops, cks.c_str());
+        report(r.name, sec, 2.0 * 3.0 * T * (double)H * I, cks);
     }
     delete halfw; delete i8w; delete i4w; delete i2w; delete f4w; delete e4w; delete e5w;
 }
@@ -296,14 +444,28 @@ void run_mlp(mpp41_ctx *ctx)
 
 int main(int argc, char **argv)
 {
-    bool bench = false, mlp = false, accum = false;
+    bool bench = false, mlp = false, accum = false, w4a4 = false, moe = false;
     for (int i = 1; i < argc; ++i) {
         if (!strcmp(argv[i], "--benchmark")) bench = true;
         else if (!strcmp(argv[i], "--mlp-benchmark")) mlp = true;
         else if (!strcmp(argv[i], "--accum-probe")) accum = true;
         else if (!strcmp(argv[i], "--skip-tensor")) {}
+        else if (!strcmp(argv[i], "--w4a4")) w4a4 = true;
+        else if (!strcmp(argv[i], "--moe")) moe = true;
+        else if (!strcmp(argv[i], "--json")) g_json = true;
         else if (!strcmp(argv[i], "--iterations") && i + 1 < argc) g_iterations = atoi(argv[++i]);
-        else { fprintf(stderr, "unknown argument %s\n", argv[i]); return 2; }
+        else if (!strcmp(argv[i], "--seed") && i + 1 < argc) g_seed = (uint32_t)strtoul(argv[++i], nullptr, 0);
+        else if (!strcmp(argv[i], "--mode") && i + 1 < argc) {
+            const char *m = argv[++i];
+            if (!strcmp(m, "baseline")) g_baseline = true;
+            else if (strcmp(m, "ref")) { fprintf(stderr, "--mode takes ref or baseline\n"); return 2; }
+        } else if (!strcmp(argv[i], "--gpus") && i + 1 < argc) {
+            if (atoi(argv[++i]) != 1) {
+                fprintf(stderr, "--gpus: this probe drives one GPU; multi-GPU layers run one process per GPU "
+                                "(mpp41_comm_init, mpp41_mlp_tp, mpp41_moe_ep)\n");
+                return 2;
+            }
+        } else { fprintf(stderr, "unknown argument %s\n", argv[i]); return 2; }
     }
     if (g_iterations < 1) g_iterations = 1;
     mpp41_ctx *ctx = nullptr;
@@ -315,6 +477,8 @@ int main(int argc, char **argv)
     printf("MTLTensor creation probe: not applicable (Metal host API).\n");
     if (bench) run_big_matmul(ctx);
     if (mlp) run_mlp(ctx);
+    if (w4a4) run_w4a4(ctx);
+    if (moe) run_moe(ctx);
     if (accum) printf("Accumulator precision probe: not applicable (Apple matmul2d semantics).\n");
     mpp41_destroy(ctx);
     if (!ok) {

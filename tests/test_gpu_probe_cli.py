@@ -30,3 +30,41 @@ def test_probe_mlp_rows_and_checksum():
     for name, value in rows:
         assert abs(float(value) - 403573.0) <= 1.0, (name, value)
     assert "W8A8" in r.stdout and "W2A8" in r.stdout
+
+
+def _json_rows(stdout):
+    import json
+    return [json.loads(l) for l in stdout.splitlines() if l.startswith("{")]
+
+
+def test_probe_new_rows_as_json():
+    """--w4a4 and --moe rows (no reference counterpart) print JSON lines with --json."""
+    r = subprocess.run([PROBE, "--w4a4", "--moe", "--json", "--iterations", "2", "--seed", "3"], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    rows = _json_rows(r.stdout)
+    names = [d["row"] for d in rows]
+    assert any(n.startswith("W4A4 MXFP4") for n in names) and any(n.startswith("W4A4 NVFP4") for n in names)
+    assert any(n.startswith("MoE W4A4") for n in names)
+    assert all(d["ms"] > 0 and d["tops"] > 0 for d in rows)
+
+
+def test_probe_mode_baseline_changes_only_the_mxfp4_rows():
+    base = subprocess.run([PROBE, "--mlp-benchmark", "--json", "--iterations", "2"], capture_output=True, text=True,
+                          timeout=300)
+    modeb = subprocess.run([PROBE, "--mlp-benchmark", "--json", "--iterations", "2", "--mode", "baseline"],
+                           capture_output=True, text=True, timeout=300)
+    assert base.returncode == 0 and modeb.returncode == 0, base.stderr + modeb.stderr
+    a = {d["row"]: d["checksum"] for d in _json_rows(base.stdout)}
+    b = {d["row"]: d["checksum"] for d in _json_rows(modeb.stdout)}
+    assert a.keys() == b.keys() and len(a) == 18
+    for name in a:
+        if name.startswith("MXFP4"):
+            assert a[name] != b[name], name          # mode B inputs
+        else:
+            assert a[name] == b[name], name          # reference seeds unchanged
+
+
+def test_probe_rejects_several_gpus():
+    r = subprocess.run([PROBE, "--gpus", "2"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 2 and "one process per GPU" in r.stderr
