@@ -121,6 +121,9 @@ std::vector<int8_t> int8_values(size_t n, uint32_t seed)
 const std::vector<uint8_t> kE4M3Pattern = {0x00, 0x20, 0x30, 0x38, 0x40, 0xb0, 0xb8, 0xc0, 0x58, 0xd8};
 const std::vector<uint8_t> kE5M2Pattern = {0x00, 0x34, 0x38, 0x3c, 0x40, 0xb4, 0xb8, 0xbc, 0xc0, 0x64};
 const std::vector<uint8_t> kScalePattern = {124, 125, 126, 127, 127, 128, 128, 129, 130};
+// MoE row: random E2M1 bytes with block scales 2^-9..2^-5, so that the
+// 7168-long gate/up sums and the 2048-long down sums stay well inside fp16
+const std::vector<uint8_t> kMoeScalePattern = {118, 119, 120, 121, 122};
 
 // ---------------------------------------------------------------- checksums
 // 32 samples at stride count/32 (main.swift:2844-2884)
@@ -347,12 +350,12 @@ void run_moe(mpp41_ctx *ctx)
     Dev logits(ctx, normal_values((size_t)d.tokens * E, 0x3E3E0001u ^ g_seed, 1.0f));
     Dev wg(ctx, packed_bytes(E * I * H / 2, 0x3E3E0002u ^ g_seed)), wu(ctx, packed_bytes(E * I * H / 2, 0x3E3E0003u ^ g_seed));
     Dev wd(ctx, packed_bytes(E * H * I / 2, 0x3E3E0004u ^ g_seed));
-    Dev sg(ctx, pattern_bytes(E * I * H / 32, 0x3E3E0005u, kScalePattern)), su(ctx, pattern_bytes(E * I * H / 32, 0x3E3E0006u, kScalePattern));
-    Dev sd(ctx, pattern_bytes(E * H * I / 32, 0x3E3E0007u, kScalePattern));
+    Dev sg(ctx, pattern_bytes(E * I * H / 32, 0x3E3E0005u, kMoeScalePattern)), su(ctx, pattern_bytes(E * I * H / 32, 0x3E3E0006u, kMoeScalePattern));
+    Dev sd(ctx, pattern_bytes(E * H * I / 32, 0x3E3E0007u, kMoeScalePattern));
     Dev swg(ctx, packed_bytes(Is * H / 2, 0x3E3E0008u)), swu(ctx, packed_bytes(Is * H / 2, 0x3E3E0009u));
     Dev swd(ctx, packed_bytes(H * Is / 2, 0x3E3E000Au));
-    Dev ssg(ctx, pattern_bytes(Is * H / 32, 0x3E3E000Bu, kScalePattern)), ssu(ctx, pattern_bytes(Is * H / 32, 0x3E3E000Cu, kScalePattern));
-    Dev ssd(ctx, pattern_bytes(H * Is / 32, 0x3E3E000Du, kScalePattern));
+    Dev ssg(ctx, pattern_bytes(Is * H / 32, 0x3E3E000Bu, kMoeScalePattern)), ssu(ctx, pattern_bytes(Is * H / 32, 0x3E3E000Cu, kMoeScalePattern));
+    Dev ssd(ctx, pattern_bytes(H * Is / 32, 0x3E3E000Du, kMoeScalePattern));
     Dev out(ctx, (size_t)d.tokens * H * 2), scratch(ctx, mpp41_moe_scratch_layout(&d, nullptr));
     auto u8 = [](const Dev &b) { return (const uint8_t *)b.p; };
     const double sec = time_calls(ctx, [&] {
