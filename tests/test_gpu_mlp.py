@@ -95,12 +95,12 @@ def test_mxfp4_token_counts(ctx, T):
     assert rel_fro(got, ref) <= TOL
 
 
-# T <= 16 with FP4 weights runs the weight-streaming GEMV kernels (mma.sync on
+# T <= 32 with FP4 weights runs the weight-streaming GEMV kernels (mma.sync on
 # registers, per-32-block scaling of the fp32 sums): 1..8 tokens use one N tile
-# of 8, 9..16 two; H and I cover several K chunks per warp and ragged CTA counts
+# of 8, 9..16 two, 17..32 four; H and I cover several K chunks per warp
 @pytest.mark.parametrize("gate_kernel", ["mxfp4_native_sp_h_f_n64", "mpp_mlp_h_fp4_f_n128"])
 @pytest.mark.parametrize("T,H,I", [(1, 1024, 4096), (5, 512, 1024), (8, 2048, 2048), (9, 1024, 1536),
-                                   (16, 4096, 14336)])
+                                   (16, 4096, 14336), (23, 1024, 2048), (32, 2048, 4096)])
 def test_gemv_decode_sizes(ctx, gate_kernel, T, H, I):
     got, ref, mid, mid_ref = run_mlp(ctx, gate_kernel, T, H, I)
     assert rel_fro(got, ref) <= TOL, gate_kernel
