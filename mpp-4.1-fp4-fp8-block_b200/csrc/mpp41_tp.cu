@@ -97,10 +97,17 @@ struct SymBuf {
     uint32_t epoch = 0;
 };
 
+// Large-T pipelining: the layer runs in token chunks on the context's stream
+// while each finished chunk's all-reduce runs on comm_stream.
+constexpr int kMaxTpChunks = 8;
+
 struct CommState {
     ncclComm_t comm = nullptr;
     int nranks = 0, rank = 0;
     SymBuf sym;
+    cudaStream_t comm_stream = nullptr;
+    cudaEvent_t chunk_ev[kMaxTpChunks] = {};
+    cudaEvent_t reduced_ev = nullptr;
 };
 
 namespace {
@@ -186,6 +193,33 @@ bool use_oneshot(const CommState *cs, const mpp41_mlp_desc *d, size_t n)
 }
 }  // namespace
 
+namespace {
+// Token chunks of the NCCL path: 4 from 1024 tokens (T divisible by 4), else
+// one; MPP41_TP_CHUNKS=N (1..8, dividing T) overrides.
+int tp_chunks(const mpp41_mlp_desc *d)
+{
+    int c = d->tokens >= 1024 && d->tokens % 4 == 0 ? 4 : 1;
+    if (const char *env = getenv("MPP41_TP_CHUNKS")) {
+        const int v = atoi(env);
+        if (v >= 1 && v <= kMaxTpChunks && d->tokens % (uint32_t)v == 0) c = v;
+    }
+    return c;
+}
+
+mpp41_status comm_stream_ready(CommState *cs)
+{
+    if (cs->comm_stream) return MPP41_OK;
+    if (cudaStreamCreateWithFlags(&cs->comm_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return err(MPP41_ERR_CUDA, "communication stream%s", nullptr);
+    for (cudaEvent_t &e : cs->chunk_ev)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+            return err(MPP41_ERR_CUDA, "chunk events%s", nullptr);
+    if (cudaEventCreateWithFlags(&cs->reduced_ev, cudaEventDisableTiming) != cudaSuccess)
+        return err(MPP41_ERR_CUDA, "chunk events%s", nullptr);
+    return MPP41_OK;
+}
+}  // namespace
+
 int comm_size(const mpp41_ctx *ctx) { return ctx && ctx->comm ? ctx->comm->nranks : 0; }
 int comm_rank(const mpp41_ctx *ctx) { return ctx && ctx->comm ? ctx->comm->rank : -1; }
 
@@ -225,6 +259,13 @@ void comm_release(mpp41_ctx *ctx)
 {
     if (!ctx || !ctx->comm) return;
     sym_release(ctx->comm);
+    if (ctx->comm->comm_stream) {
+        cudaStreamSynchronize(ctx->comm->comm_stream);
+        cudaStreamDestroy(ctx->comm->comm_stream);
+        for (cudaEvent_t &e : ctx->comm->chunk_ev)
+            if (e) cudaEventDestroy(e);
+        cudaEventDestroy(ctx->comm->reduced_ev);
+    }
     const NcclApi *a = nccl();
     if (a && ctx->comm->comm) a->comm_destroy(ctx->comm->comm);
     delete ctx->comm;
@@ -315,12 +356,38 @@ mpp41_status mpp41_mlp_tp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x
         return MPP41_OK;
     }
     void *partial = d->out_dtype == MPP41_F16 ? static_cast<uint8_t *>(scratch) + local_scratch : out;
-    mpp41_status s = mpp41_mlp(ctx, &l, x, wg, wu, wd, sg, su, sd, scratch, partial);
-    if (s) return s;
     const NcclApi *a = nccl();
     const ncclDataType_t dt = d->out_dtype == MPP41_S32 ? ncclInt32 : ncclFloat32;
-    const ncclResult_t r = a->all_reduce(partial, partial, n, dt, ncclSum, cs->comm, ctx->stream);
-    if (r != ncclSuccess) return err(MPP41_ERR_COMM, "ncclAllReduce: %s", a->error_string(r));
+    const int chunks = tp_chunks(d);
+    if (chunks > 1) {
+        // token chunks: chunk c's all-reduce (comm_stream) overlaps chunk c+1's layer (ctx stream)
+        mpp41_status s = comm_stream_ready(ctx->comm);
+        if (s) return s;
+        const uint32_t Tc = d->tokens / (uint32_t)chunks;
+        const size_t xb = d->afmt == MPP41_A_S8 ? 1 : 2;
+        for (int c = 0; c < chunks; ++c) {
+            mpp41_mlp_desc lc = l;
+            lc.tokens = Tc;
+            const size_t row0 = (size_t)c * Tc;
+            s = mpp41_mlp(ctx, &lc, static_cast<const uint8_t *>(x) + row0 * d->hidden * xb, wg, wu, wd, sg, su, sd,
+                          scratch, static_cast<uint8_t *>(partial) + row0 * d->hidden * 4);
+            if (s) return s;
+            if (cudaEventRecord(cs->chunk_ev[c], ctx->stream) != cudaSuccess ||
+                cudaStreamWaitEvent(cs->comm_stream, cs->chunk_ev[c], 0) != cudaSuccess)
+                return err(MPP41_ERR_CUDA, "chunk event%s", nullptr);
+            void *pc = static_cast<uint8_t *>(partial) + row0 * d->hidden * 4;
+            const ncclResult_t r = a->all_reduce(pc, pc, (size_t)Tc * d->hidden, dt, ncclSum, cs->comm, cs->comm_stream);
+            if (r != ncclSuccess) return err(MPP41_ERR_COMM, "ncclAllReduce: %s", a->error_string(r));
+        }
+        if (cudaEventRecord(cs->reduced_ev, cs->comm_stream) != cudaSuccess ||
+            cudaStreamWaitEvent(ctx->stream, cs->reduced_ev, 0) != cudaSuccess)
+            return err(MPP41_ERR_CUDA, "reduction event%s", nullptr);
+    } else {
+        mpp41_status s = mpp41_mlp(ctx, &l, x, wg, wu, wd, sg, su, sd, scratch, partial);
+        if (s) return s;
+        const ncclResult_t r = a->all_reduce(partial, partial, n, dt, ncclSum, cs->comm, ctx->stream);
+        if (r != ncclSuccess) return err(MPP41_ERR_COMM, "ncclAllReduce: %s", a->error_string(r));
+    }
     if (d->out_dtype == MPP41_F16) {
         const cudaError_t e = launch_f32_to_f16(static_cast<const float *>(partial), n, out, ctx->stream);
         if (e != cudaSuccess) return err(MPP41_ERR_CUDA, "fp16 conversion: %s", cudaGetErrorString(e));

@@ -91,7 +91,9 @@ def worker(rank, world, uid, shape, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("shape", [(128, 1024, 4096), (16, 4096, 14336), (1, 4096, 14336), (256, 4096, 14336)])
+# (1024, ...) runs in 4 token chunks whose all-reduces overlap the next chunk's layer
+@pytest.mark.parametrize("shape", [(128, 1024, 4096), (16, 4096, 14336), (1, 4096, 14336), (256, 4096, 14336),
+                                   (1024, 1024, 4096)])
 def test_tp2_matches_single_rank_oracle(shape):
     T, H, I = shape
     uid = mpp41.comm_unique_id()
