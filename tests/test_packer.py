@@ -51,3 +51,37 @@ def test_pack_and_run(ctx, tmp_path):
     got = from_dev(d_out, np.float16, (T, H))
     _, ref = O.mlp(0, O.W_MXFP4, 4, 1, T, H, I, x.view(np.uint16), L["wg"], L["wu"], L["wd"], L["sg"], L["su"], L["sd"])
     assert rel_fro(got, ref) <= 1e-3
+
+
+def test_shard_experts_partitions_the_stack():
+    rng = np.random.default_rng(2)
+    full = {k: rng.integers(0, 255, (8, 16, 4), dtype=np.uint8) for k in ("wg", "wu", "wd", "sg", "su", "sd")}
+    full["meta"] = {"format": packer.FORMAT}
+    parts = [packer.shard_experts(r, 4, full) for r in range(4)]
+    for k in ("wg", "wu", "wd", "sg", "su", "sd"):
+        assert np.array_equal(np.concatenate([p[k] for p in parts]), full[k])
+    assert parts[3]["meta"]["ep_rank"] == 3 and parts[3]["meta"]["experts_local"] == 2
+    with pytest.raises(ValueError):
+        packer.shard_experts(0, 3, full)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["nvfp4", "int8", "int4", "int2"])
+def test_pack_other_formats(ctx, tmp_path, fmt):
+    H, I = 256, 512
+    rng = np.random.default_rng(11)
+    w = {n: (rng.standard_normal(s) * 0.02).astype(np.float32) for n, s in (("g", (I, H)), ("u", (I, H)), ("d", (H, I)))}
+    L = packer.pack_layer(ctx, w["g"], w["u"], w["d"], fmt=fmt)[0]
+    for n in ("g", "u", "d"):
+        if fmt == "nvfp4":
+            pk, sc, ts = O.quantize_nvfp4(w[n])
+            assert L["t" + n] == np.float32(ts)
+        else:
+            pk, sc = O.quantize_int_rows(w[n], int(fmt[3:]))
+        assert np.array_equal(L["w" + n], pk) and np.array_equal(L["s" + n], sc)
+    p = os.path.join(tmp_path, "layer.npz")
+    packer.save(p, L)
+    back = packer.load(p)
+    assert back["meta"]["wfmt"] == fmt
+    for k in ("wg", "wu", "wd", "sg", "su", "sd"):
+        assert np.array_equal(back[k], L[k])
