@@ -195,7 +195,10 @@ mpp41_status mpp41_mlp_scalar(mpp41_ctx *ctx, const char *gate_kernel_name, cons
  *      (main.swift:2033-2135). Weights use the reference layouts ([n][k],
  *      scales [n][k/32]); sg/su/sd are only read for MXFP4. scratch must hold
  *      mpp41_mlp_scratch_bytes(desc) bytes: the fp16/fp32/int8 mid, then for
- *      fp16 output the split-K fp32 workspace and tile counters. ---- */
+ *      fp16 output the split-K fp32 workspace and tile counters. Kernels by
+ *      shape: up to 32 tokens with MXFP4/FP4 weights, two weight-streaming
+ *      GEMV kernels; otherwise one persistent tcgen05 kernel per layer
+ *      (token-major for 65..128 tokens of a small layer, weight-major else). ---- */
 size_t mpp41_mlp_scratch_bytes(const mpp41_mlp_desc *desc);
 mpp41_status mpp41_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const void *wg, const void *wu,
                        const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *scratch,
