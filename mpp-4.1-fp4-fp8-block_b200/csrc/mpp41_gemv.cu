@@ -1,5 +1,5 @@
-// Decode-sized MLP layer (T <= 32 tokens) with FP4 weights (MXFP4 or unscaled
-// FP4), the W4A16 math of the fused layer -- exact E2M1 x fp16 products, fp32
+// Decode-sized MLP layer (T <= 32 tokens) with 4-bit weights (MXFP4, unscaled
+// FP4 or INT4), the W4A16 math of the fused layer -- exact E2M1 x fp16 products, fp32
 // sums, SwiGLU on the fp32 gate/up sums, fp16 mid -- as two weight-streaming
 // kernels (gate/up + SwiGLU, then down). With so few tokens the layer is a
 // stream of 4-bit weights; decoding them into shared or tensor memory for
@@ -37,6 +37,22 @@ __device__ __forceinline__ uint32_t e2m1x2_to_h2(uint32_t byte)
     uint32_t h2;
     asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "r"(byte));
     return h2;
+}
+
+// Two packed 4-bit weights (one byte, low nibble = even k) -> half2, exactly:
+// E2M1 by the hardware conversion; INT4 (two's complement, the reference's
+// (n ^ 8) - 8) by placing n ^ 8 in the mantissa of 1024 and subtracting 1032.
+template <int W>
+__device__ __forceinline__ uint32_t dec2(uint32_t byte)
+{
+    if constexpr (W == W_I4) {
+        const uint32_t h = 0x64006400u | ((byte & 0xFu) ^ 8u) | ((((byte >> 4) & 0xFu) ^ 8u) << 16);
+        const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&h), __halves2half2(__ushort_as_half(0x6408),
+                                                                                        __ushort_as_half(0x6408)));
+        return *reinterpret_cast<const uint32_t *>(&r);
+    } else {
+        return e2m1x2_to_h2(byte);
+    }
 }
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -82,13 +98,13 @@ __device__ __forceinline__ void stage_chunk(uint8_t *dst, const uint8_t *w, uint
 // One 32-wide K block of one 16-row weight group against NT token tiles:
 // wg = this lane's 4 bytes of row g, wg8 = of row g + 8; x[nt] = the lane's 8
 // activations (k = 8t..8t+7) of token nt*8 + g; the block sums go to tmp.
-template <int NT>
+template <int W, int NT>
 __device__ __forceinline__ void block_mma(uint32_t wg, uint32_t wg8, const uint4 (&x)[NT], float (&tmp)[NT][4])
 {
-    const uint32_t a0s0 = e2m1x2_to_h2(wg & 0xFFu), a2s0 = e2m1x2_to_h2((wg >> 8) & 0xFFu);
-    const uint32_t a1s0 = e2m1x2_to_h2(wg8 & 0xFFu), a3s0 = e2m1x2_to_h2((wg8 >> 8) & 0xFFu);
-    const uint32_t a0s1 = e2m1x2_to_h2((wg >> 16) & 0xFFu), a2s1 = e2m1x2_to_h2(wg >> 24);
-    const uint32_t a1s1 = e2m1x2_to_h2((wg8 >> 16) & 0xFFu), a3s1 = e2m1x2_to_h2(wg8 >> 24);
+    const uint32_t a0s0 = dec2<W>(wg & 0xFFu), a2s0 = dec2<W>((wg >> 8) & 0xFFu);
+    const uint32_t a1s0 = dec2<W>(wg8 & 0xFFu), a3s0 = dec2<W>((wg8 >> 8) & 0xFFu);
+    const uint32_t a0s1 = dec2<W>((wg >> 16) & 0xFFu), a2s1 = dec2<W>(wg >> 24);
+    const uint32_t a1s1 = dec2<W>((wg8 >> 16) & 0xFFu), a3s1 = dec2<W>(wg8 >> 24);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.0f;
@@ -114,12 +130,13 @@ __device__ __forceinline__ uint32_t load_s4(const uint8_t *s, uint32_t K, uint32
 
 // ---------------------------------------------------------------- gate/up + SwiGLU
 // CTA: 16 channels [c0, c0+16) of gate and up, kGateWarps warps splitting K = H.
-template <bool SCALED, int EG, int NT>
+template <int W, int EG, int NT>
 __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *__restrict__ x, const uint8_t *__restrict__ wg,
                                                                   const uint8_t *__restrict__ wu, const uint8_t *__restrict__ sg,
                                                                   const uint8_t *__restrict__ su, __half *__restrict__ mid,
                                                                   uint32_t T, uint32_t H, uint32_t I)
 {
+    constexpr bool SCALED = W == W_MXFP4;
     extern __shared__ __align__(16) uint8_t wsm[];   // weight ring, then (aliased) the partial sums
     float(*part)[2][NT][4][32] = reinterpret_cast<float(*)[2][NT][4][32]>(wsm);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -185,7 +202,7 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *
             const uint32_t wur = *reinterpret_cast<const uint32_t *>(cu + g * kRowPitch + off);
             const uint32_t wur8 = *reinterpret_cast<const uint32_t *>(cu + (g + 8) * kRowPitch + off);
             const float s0 = e8m0((sg4 >> (8 * b)) & 0xFFu), s8 = e8m0((sg48 >> (8 * b)) & 0xFFu);
-            block_mma<NT>(wgr, wgr8, xv[b], tmp);
+            block_mma<W, NT>(wgr, wgr8, xv[b], tmp);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 ag[nt][0] = fmaf(tmp[nt][0], s0, ag[nt][0]);
@@ -194,7 +211,7 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *
                 ag[nt][3] = fmaf(tmp[nt][3], s8, ag[nt][3]);
             }
             const float u0 = e8m0((su4 >> (8 * b)) & 0xFFu), u8 = e8m0((su48 >> (8 * b)) & 0xFFu);
-            block_mma<NT>(wur, wur8, xv[b], tmp);
+            block_mma<W, NT>(wur, wur8, xv[b], tmp);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 au[nt][0] = fmaf(tmp[nt][0], u0, au[nt][0]);
@@ -232,11 +249,12 @@ __global__ void __launch_bounds__(kGateWarps * 32) gate_up_kernel(const __half *
 
 // ---------------------------------------------------------------- down
 // CTA: 16 output columns [h0, h0+16), kDownWarps warps splitting K = I.
-template <bool SCALED, bool OUT_F16, int NT>
+template <int W, bool OUT_F16, int NT>
 __global__ void __launch_bounds__(kDownWarps * 32) down_kernel(const __half *__restrict__ mid, const uint8_t *__restrict__ wd,
                                                                const uint8_t *__restrict__ sd, void *__restrict__ out,
                                                                uint32_t T, uint32_t H, uint32_t I)
 {
+    constexpr bool SCALED = W == W_MXFP4;
     extern __shared__ __align__(16) uint8_t wsm[];
     float(*part)[NT][4][32] = reinterpret_cast<float(*)[NT][4][32]>(wsm);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -290,7 +308,7 @@ __global__ void __launch_bounds__(kDownWarps * 32) down_kernel(const __half *__r
             const uint32_t wr = *reinterpret_cast<const uint32_t *>(cw + g * kRowPitch + off);
             const uint32_t wr8 = *reinterpret_cast<const uint32_t *>(cw + (g + 8) * kRowPitch + off);
             const float s0 = e8m0((s4 >> (8 * b)) & 0xFFu), s8 = e8m0((s48 >> (8 * b)) & 0xFFu);
-            block_mma<NT>(wr, wr8, xv[b], tmp);
+            block_mma<W, NT>(wr, wr8, xv[b], tmp);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 acc[nt][0] = fmaf(tmp[nt][0], s0, acc[nt][0]);
@@ -338,40 +356,40 @@ bool allow_smem(K kern, uint32_t bytes)
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess;
 }
 
-template <bool SCALED, int EG, int NT>
+template <int W, int EG, int NT>
 int launch_nt(const FusedLaunch &L, cudaStream_t st)
 {
-    static const bool ok = allow_smem(gate_up_kernel<SCALED, EG, NT>, gate_smem(NT)) &&
-                           allow_smem(down_kernel<SCALED, true, NT>, down_smem(NT)) &&
-                           allow_smem(down_kernel<SCALED, false, NT>, down_smem(NT));
+    static const bool ok = allow_smem(gate_up_kernel<W, EG, NT>, gate_smem(NT)) &&
+                           allow_smem(down_kernel<W, true, NT>, down_smem(NT)) &&
+                           allow_smem(down_kernel<W, false, NT>, down_smem(NT));
     if (!ok) return 2;
-    gate_up_kernel<SCALED, EG, NT><<<L.I / 16, kGateWarps * 32, gate_smem(NT), st>>>(
+    gate_up_kernel<W, EG, NT><<<L.I / 16, kGateWarps * 32, gate_smem(NT), st>>>(
         static_cast<const __half *>(L.x), static_cast<const uint8_t *>(L.wg), static_cast<const uint8_t *>(L.wu), L.sg,
         L.su, static_cast<__half *>(L.mid), L.T, L.H, L.I);
     if (L.out_f16)
-        down_kernel<SCALED, true, NT><<<L.H / 16, kDownWarps * 32, down_smem(NT), st>>>(
+        down_kernel<W, true, NT><<<L.H / 16, kDownWarps * 32, down_smem(NT), st>>>(
             static_cast<const __half *>(L.mid), static_cast<const uint8_t *>(L.wd), L.sd, L.out, L.T, L.H, L.I);
     else
-        down_kernel<SCALED, false, NT><<<L.H / 16, kDownWarps * 32, down_smem(NT), st>>>(
+        down_kernel<W, false, NT><<<L.H / 16, kDownWarps * 32, down_smem(NT), st>>>(
             static_cast<const __half *>(L.mid), static_cast<const uint8_t *>(L.wd), L.sd, L.out, L.T, L.H, L.I);
     return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
-template <bool SCALED, int EG>
+template <int W, int EG>
 int launch_eg(const FusedLaunch &L, cudaStream_t st)
 {
-    if (L.T <= 8) return launch_nt<SCALED, EG, 1>(L, st);
-    if (L.T <= 16) return launch_nt<SCALED, EG, 2>(L, st);
-    return launch_nt<SCALED, EG, 4>(L, st);
+    if (L.T <= 8) return launch_nt<W, EG, 1>(L, st);
+    if (L.T <= 16) return launch_nt<W, EG, 2>(L, st);
+    return launch_nt<W, EG, 4>(L, st);
 }
 
-template <bool SCALED>
+template <int W>
 int launch_s(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
     switch (L.gate_epi) {
-    case EPI_SWIGLU_PLAIN: return launch_eg<SCALED, EPI_SWIGLU_PLAIN>(L, st);
-    case EPI_SWIGLU_HALF: return launch_eg<SCALED, EPI_SWIGLU_HALF>(L, st);
-    case EPI_SWIGLU_HALF_H: return launch_eg<SCALED, EPI_SWIGLU_HALF_H>(L, st);
+    case EPI_SWIGLU_PLAIN: return launch_eg<W, EPI_SWIGLU_PLAIN>(L, st);
+    case EPI_SWIGLU_HALF: return launch_eg<W, EPI_SWIGLU_HALF>(L, st);
+    case EPI_SWIGLU_HALF_H: return launch_eg<W, EPI_SWIGLU_HALF_H>(L, st);
     default: *why = "SwiGLU variant"; return 1;
     }
 }
@@ -384,13 +402,16 @@ constexpr uint32_t kGemvMaxTokens = 32;
 
 bool gemv_covers(uint32_t T, uint32_t H, uint32_t I, int wfmt)
 {
-    return T >= 1 && T <= kGemvMaxTokens && (wfmt == W_MXFP4 || wfmt == W_FP4) && H % 128 == 0 && I % 128 == 0;
+    return T >= 1 && T <= kGemvMaxTokens && (wfmt == W_MXFP4 || wfmt == W_FP4 || wfmt == W_I4) && H % 128 == 0 &&
+           I % 128 == 0;
 }
 
 int launch_gemv_layer(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
     if (!gemv_covers(L.T, L.H, L.I, L.wfmt)) { *why = "shape or format"; return 1; }
-    const int rc = L.wfmt == W_MXFP4 ? gemv::launch_s<true>(L, st, why) : gemv::launch_s<false>(L, st, why);
+    const int rc = L.wfmt == W_MXFP4 ? gemv::launch_s<W_MXFP4>(L, st, why)
+                   : L.wfmt == W_FP4 ? gemv::launch_s<W_FP4>(L, st, why)
+                                     : gemv::launch_s<W_I4>(L, st, why);
     if (rc == 2) *why = cudaGetErrorString(cudaGetLastError());
     return rc;
 }

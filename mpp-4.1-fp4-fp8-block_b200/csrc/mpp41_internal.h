@@ -188,7 +188,7 @@ struct LayerPlan {
     size_t ws_bytes, sync_words;
 };
 LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16);
-// Decode-sized layers (T <= 32, MXFP4 or FP4 weights, H and I multiples of
+// Decode-sized layers (T <= 32, MXFP4 / FP4 / INT4 weights, H and I multiples of
 // 128) run as two weight-streaming kernels (mpp41_gemv.cu); launch_layer
 // routes them there. The mid goes to L.mid (fp16 [T][I]); no workspace.
 bool gemv_covers(uint32_t T, uint32_t H, uint32_t I, int wfmt);

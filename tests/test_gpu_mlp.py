@@ -95,10 +95,10 @@ def test_mxfp4_token_counts(ctx, T):
     assert rel_fro(got, ref) <= TOL
 
 
-# T <= 32 with FP4 weights runs the weight-streaming GEMV kernels (mma.sync on
+# T <= 32 with 4-bit weights (MXFP4, FP4, INT4) runs the weight-streaming GEMV kernels (mma.sync on
 # registers, per-32-block scaling of the fp32 sums): 1..8 tokens use one N tile
 # of 8, 9..16 two, 17..32 four; H and I cover several K chunks per warp
-@pytest.mark.parametrize("gate_kernel", ["mxfp4_native_sp_h_f_n64", "mpp_mlp_h_fp4_f_n128"])
+@pytest.mark.parametrize("gate_kernel", ["mxfp4_native_sp_h_f_n64", "mpp_mlp_h_fp4_f_n128", "mpp_mlp_h_i4_f_n128"])
 @pytest.mark.parametrize("T,H,I", [(1, 1024, 4096), (5, 512, 1024), (8, 2048, 2048), (9, 1024, 1536),
                                    (16, 4096, 14336), (23, 1024, 2048), (32, 2048, 4096)])
 def test_gemv_decode_sizes(ctx, gate_kernel, T, H, I):
