@@ -57,10 +57,13 @@ constexpr uint32_t kATile = kBM * 128;      // 16 KB
 constexpr uint32_t kSfRow = 16;
 constexpr uint32_t kSfaBytes = kBM * kSfRow;
 
-// Column tile BN = MMA N (rows of B per tile). 256: one CTA per SM, 4 stages,
-// all 512 tensor-memory columns. 128: two CTAs per SM (3 stages, 256 columns
-// each), so one CTA's pipeline fill and epilogue overlap the other's weight
-// stream -- the shape for weight-streaming launches (few rows per tile).
+// Column tile BN = MMA N (rows of B per tile). The library launches this
+// one-tile-per-CTA kernel with BN = 256 (one CTA per SM, 4 stages, all 512
+// tensor-memory columns) for M > 128; weight-streaming launches (grouped
+// experts, M <= 128) use the persistent 128 x 128 kernel of
+// mpp41_mxf4_persist.cuh instead. The BN = 128 configuration (two CTAs per
+// SM, 3 stages, 256 columns each) compiles but is not launched: it measured
+// no faster than BN = 256 on those shapes.
 template <int BN> struct Tile {
     static constexpr int kStages = BN == 256 ? 4 : 3;
     static constexpr int kCtasPerSm = BN == 256 ? 1 : 2;
