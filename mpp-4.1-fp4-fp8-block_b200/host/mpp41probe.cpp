@@ -34,20 +34,65 @@
 
 namespace {
 
-int g_iterations = 20;
+// Reference flags (main.swift:80-162, intArgument main.swift:2886-2892): boolean
+// switches, and --name=value integers that fall back to their default when
+// absent or not a number.
+std::vector<std::string> g_args;
 bool g_json = false;
 bool g_baseline = false;
 uint32_t g_seed = 0;
 
-// One timed benchmark row: text as the reference prints it, or a JSON line.
-void report(const char *name, double sec, double flops, const std::string &cks)
+bool has_flag(const char *name)
 {
-    const double ms = sec * 1e3 / g_iterations, tops = flops * g_iterations / sec / 1e12;
-    if (g_json)
-        printf("{\"row\": \"%s\", \"ms\": %.5f, \"tops\": %.3f, \"checksum\": \"%s\"}\n", name, ms, tops,
-               cks.c_str());
-    else
-        printf("  %s:\n    %.3f ms/MLP, %.3f effective TOPS\n    checksum: %s\n", name, ms, tops, cks.c_str());
+    for (const auto &a : g_args)
+        if (a == name) return true;
+    return false;
+}
+
+long int_arg(const char *name, long def)
+{
+    const std::string prefix = std::string(name) + "=";
+    for (const auto &a : g_args)
+        if (a.compare(0, prefix.size(), prefix) == 0) {
+            char *end = nullptr;
+            const char *v = a.c_str() + prefix.size();
+            const long r = strtol(v, &end, 10);
+            return (*v && end && !*end) ? r : def;
+        }
+    return def;
+}
+
+// One timed benchmark row.
+struct Result {
+    std::string name;
+    double seconds;   // for `iterations` calls
+    int iterations;
+    double flops;     // per call
+    std::string checksum;
+};
+
+// Rows as the reference prints them (printMatmulBenchmarkResult /
+// printMLPBenchmarkResult, main.swift:2754-2770) followed by its relative
+// slowdown table (main.swift:2772-2783), or one JSON line per row.
+void print_results(const std::vector<Result> &rs, const char *unit)
+{
+    if (rs.empty()) return;
+    size_t best = 0;
+    for (size_t i = 0; i < rs.size(); ++i) {
+        const Result &r = rs[i];
+        const double ms = r.seconds * 1e3 / r.iterations, tops = r.flops * r.iterations / r.seconds / 1e12;
+        if (g_json)
+            printf("{\"row\": \"%s\", \"ms\": %.5f, \"tops\": %.3f, \"checksum\": \"%s\"}\n", r.name.c_str(), ms,
+                   tops, r.checksum.c_str());
+        else
+            printf("  %s:\n    %.3f ms/%s, %.3f effective TOPS\n    checksum: %s\n", r.name.c_str(), ms, unit, tops,
+                   r.checksum.c_str());
+        if (r.seconds / r.iterations < rs[best].seconds / rs[best].iterations) best = i;
+    }
+    if (g_json) return;
+    const double b = rs[best].seconds / rs[best].iterations;
+    printf("  relative slowdown, best = %s:\n", rs[best].name.c_str());
+    for (const Result &r : rs) printf("    %s: %.2fx\n", r.name.c_str(), r.seconds / r.iterations / b);
 }
 
 [[noreturn]] void die(mpp41_status s, const char *what)
@@ -216,53 +261,68 @@ bool run_roundtrips(mpp41_ctx *ctx)
 }
 
 // ---------------------------------------------------------------- big matmul rows
+template <class F>
+double time_calls(mpp41_ctx *ctx, int iterations, F call)
+{
+    call();   // warm-up
+    check(mpp41_synchronize(ctx), "warm-up");
+    check(mpp41_timer_start(ctx), "timer");
+    for (int i = 0; i < iterations; ++i) call();
+    double sec = 0;
+    check(mpp41_timer_stop(ctx, &sec), "timer");
+    check(mpp41_synchronize(ctx), "timed calls");
+    return sec;
+}
+
 void run_big_matmul(mpp41_ctx *ctx)
 {
-    const uint32_t M = 2048, N = 2048, K = 2048;
-    printf("\nBig packed matmul benchmark:\n");
-    printf("  shape: A %ux%u, B %ux%u, C %ux%u\n", M, K, K, N, M, N);
-    printf("  iterations: %d\n", g_iterations);
+    const long size = int_arg("--matmul-size", 2048);
+    const uint32_t M = (uint32_t)int_arg("--m", size), N = (uint32_t)int_arg("--n", size), K = (uint32_t)int_arg("--k", size);
+    const int iters = (int)int_arg("--iterations", 3);
+    if ((long)M <= 0 || (long)N <= 0 || (long)K <= 0 || iters <= 0) {
+        fprintf(stderr, "error: Matmul sizes and iterations must be positive.\n");
+        exit(1);
+    }
+    const bool sweep = has_flag("--fp4-group-sweep");
+    if (!g_json) {
+        printf("\nBig packed matmul benchmark:\n");
+        printf("  shape: A %ux%u, B %ux%u, C %ux%u\n", M, K, K, N, M, N);
+        printf("  iterations: %d\n", iters);
+        if (sweep) printf("  FP4 unpack group sweep: 8 and 16 elements\n");
+    }
     const auto a_packed = packed_bytes((size_t)M * K / 2, 0x12345678u);
     const auto b_packed = packed_bytes((size_t)N * K / 2, 0x87654321u);
     const auto a_half = half_values((size_t)M * K, 0x2468ace0u);
     const auto a_int8 = int8_values((size_t)M * K, 0x13579bdfu);
     const auto b_half = half_values((size_t)N * K, 0xfdb97531u, 0.03125f);
     Dev dap(ctx, a_packed), dbp(ctx, b_packed), dah(ctx, a_half), dai(ctx, a_int8), dbh(ctx, b_half);
-    struct Row { const char *name, *kernel; const Dev *a, *b; int out; };   // out: 0 f32, 1 half, 2 i32
+    struct Row { const char *name, *kernel; const Dev *a, *b; int out; bool sweep_only; };   // out: 0 f32, 1 half, 2 i32
+    // the reference's order: FP4, the g8 sweep rows, then the others (main.swift:580)
     const Row rows[] = {
-        {"FP4 E2M1 g16 -> FP32 accumulate", "fp4_e2m1_matmul_benchmark", &dap, &dbp, 0},
-        {"half x FP4 E2M1 g16 -> half accumulate", "half_fp4_matmul_half_benchmark", &dah, &dbp, 1},
-        {"half x INT4 -> half accumulate", "half_int4_matmul_half_benchmark", &dah, &dbp, 1},
-        {"INT8 x half -> half accumulate", "int8_half_matmul_half_benchmark", &dai, &dbh, 1},
-        {"INT4 x INT4 -> INT32 accumulate", "int4_int8_matmul_benchmark", &dap, &dbp, 2},
+        {"FP4 E2M1 g16 -> FP32 accumulate", "fp4_e2m1_matmul_benchmark", &dap, &dbp, 0, false},
+        {"FP4 E2M1 g8 -> FP32 accumulate", "fp4_e2m1_matmul_g8_benchmark", &dap, &dbp, 0, true},
+        {"half x FP4 E2M1 g8 -> half accumulate", "half_fp4_matmul_half_g8_benchmark", &dah, &dbp, 1, true},
+        {"half x FP4 E2M1 g16 -> half accumulate", "half_fp4_matmul_half_benchmark", &dah, &dbp, 1, false},
+        {"half x INT4 -> half accumulate", "half_int4_matmul_half_benchmark", &dah, &dbp, 1, false},
+        {"INT8 x half -> half accumulate", "int8_half_matmul_half_benchmark", &dai, &dbh, 1, false},
+        {"INT4 x INT4 -> INT32 accumulate", "int4_int8_matmul_benchmark", &dap, &dbp, 2, false},
     };
     const mpp41_matmul_config cfg = {M, N, K, K / 2};
+    std::vector<Result> results;
     for (const Row &r : rows) {
+        if (r.sweep_only && !sweep) continue;
         Dev c(ctx, (size_t)M * N * (r.out == 1 ? 2 : 4));
         Dev ws(ctx, mpp41_matmul_workspace_bytes(r.kernel, &cfg));
-        check(mpp41_matmul(ctx, r.kernel, r.a->p, r.b->p, c.p, &cfg, ws.p), r.kernel);   // warm-up
-        check(mpp41_synchronize(ctx), "synchronize");
-        double t0 = 0, t1 = 0;
-        {
-            // time with the host clock around a synchronised batch (the C ABI
-            // exposes only synchronize; the MLP rows use mpp41_mlp_benchmark)
-            struct timespec a, b;
-            clock_gettime(CLOCK_MONOTONIC, &a);
-            for (int i = 0; i < g_iterations; ++i) check(mpp41_matmul(ctx, r.kernel, r.a->p, r.b->p, c.p, &cfg, ws.p), r.kernel);
-            check(mpp41_synchronize(ctx), "synchronize");
-            clock_gettime(CLOCK_MONOTONIC, &b);
-            t0 = a.tv_sec + a.tv_nsec * 1e-9;
-            t1 = b.tv_sec + b.tv_nsec * 1e-9;
-        }
-        const double sec = t1 - t0;
-        const double tops = 2.0 * M * N * (double)K * g_iterations / sec / 1e12;
+        const double sec = time_calls(ctx, iters, [&] {
+            check(mpp41_matmul(ctx, r.kernel, r.a->p, r.b->p, c.p, &cfg, ws.p), r.kernel);
+        });
         std::string cks;
         if (r.out == 0) { const auto h = c.get<float>(); cks = float_checksum(h.data(), h.size()); }
         else if (r.out == 1) { const auto h = c.get<uint16_t>(); cks = half_raw_checksum(h.data(), h.size()); }
         else { const auto h = c.get<int32_t>(); cks = int_checksum(h.data(), h.size()); }
-        printf("  %s:\n    %.3f ms/matmul, %.3f effective TOPS\n    checksum: %s\n", r.name,
-               sec * 1e3 / g_iterations, tops, cks.c_str());
+        results.push_back({r.name, sec, iters, 2.0 * M * N * (double)K, cks});
     }
+    print_results(results, "matmul");
 }
 
 std::vector<_Float16> to_half(const std::vector<float> &v)
@@ -297,18 +357,6 @@ struct NvWeights {
     }
 };
 
-template <class F>
-double time_calls(mpp41_ctx *ctx, F call)
-{
-    for (int i = 0; i < 3; ++i) call();
-    check(mpp41_timer_start(ctx), "timer");
-    for (int i = 0; i < g_iterations; ++i) call();
-    double sec = 0;
-    check(mpp41_timer_stop(ctx, &sec), "timer");
-    check(mpp41_synchronize(ctx), "timed calls");
-    return sec;
-}
-
 // ---------------------------------------------------------------- W4A4 / NVFP4 rows (no reference counterpart)
 void run_w4a4(mpp41_ctx *ctx)
 {
@@ -317,24 +365,27 @@ void run_w4a4(mpp41_ctx *ctx)
     Dev x(ctx, to_half(normal_values((size_t)T * H, 0x5A5A0000u ^ g_seed, 1.0f)));
     MxWeights g(ctx, I, H, 0x5A5A0001u ^ g_seed), u(ctx, I, H, 0x5A5A0002u ^ g_seed), d(ctx, H, I, 0x5A5A0003u ^ g_seed);
     Dev out(ctx, (size_t)T * H * 2), scratch(ctx, mpp41_mlp_w4a4_scratch_bytes(T, H, I));
-    double sec = time_calls(ctx, [&] {
+    const int iters = (int)int_arg("--mlp-iterations", 3);
+    std::vector<Result> results;
+    double sec = time_calls(ctx, iters, [&] {
         check(mpp41_mlp_w4a4(ctx, T, H, I, x.p, (const uint8_t *)g.q.p, (const uint8_t *)g.s.p, (const uint8_t *)u.q.p,
                              (const uint8_t *)u.s.p, (const uint8_t *)d.q.p, (const uint8_t *)d.s.p, out.p, 1, scratch.p),
               "mpp41_mlp_w4a4");
     });
-    report("W4A4 MXFP4 MLP: x -> MXFP4, kind::mxf4 gate/up + SwiGLU -> MXFP4 mid, kind::mxf4 down", sec,
-           6.0 * T * H * (double)I, half_raw_checksum(out.get<uint16_t>().data(), (size_t)T * H));
+    results.push_back({"W4A4 MXFP4 MLP: x -> MXFP4, kind::mxf4 gate/up + SwiGLU -> MXFP4 mid, kind::mxf4 down", sec, iters,
+                       6.0 * T * H * (double)I, half_raw_checksum(out.get<uint16_t>().data(), (size_t)T * H)});
     // NVFP4: weights from the same fp32 values, quantized NVFP4 on the GPU
     NvWeights ng(ctx, I, H, 0x5A5A0001u ^ g_seed), nu(ctx, I, H, 0x5A5A0002u ^ g_seed), nd(ctx, H, I, 0x5A5A0003u ^ g_seed);
     Dev nscr(ctx, mpp41_mlp_nvfp4_scratch_bytes(T, H, I));
-    sec = time_calls(ctx, [&] {
+    sec = time_calls(ctx, iters, [&] {
         check(mpp41_mlp_nvfp4(ctx, T, H, I, x.p, (const uint8_t *)ng.q.p, (const uint8_t *)ng.s.p, (const float *)ng.t.p,
                               (const uint8_t *)nu.q.p, (const uint8_t *)nu.s.p, (const float *)nu.t.p, (const uint8_t *)nd.q.p,
                               (const uint8_t *)nd.s.p, (const float *)nd.t.p, out.p, 1, nscr.p),
               "mpp41_mlp_nvfp4");
     });
-    report("W4A4 NVFP4 MLP: E2M1 + UE4M3/16 + fp32 tensor scales, kind::mxf4nvf4", sec, 6.0 * T * H * (double)I,
-           half_raw_checksum(out.get<uint16_t>().data(), (size_t)T * H));
+    results.push_back({"W4A4 NVFP4 MLP: E2M1 + UE4M3/16 + fp32 tensor scales, kind::mxf4nvf4", sec, iters,
+                       6.0 * T * H * (double)I, half_raw_checksum(out.get<uint16_t>().data(), (size_t)T * H)});
+    print_results(results, "MLP");
 }
 
 // ---------------------------------------------------------------- MoE row (no reference counterpart)
@@ -358,22 +409,33 @@ void run_moe(mpp41_ctx *ctx)
     Dev ssd(ctx, pattern_bytes(H * Is / 32, 0x3E3E000Du, kMoeScalePattern));
     Dev out(ctx, (size_t)d.tokens * H * 2), scratch(ctx, mpp41_moe_scratch_layout(&d, nullptr));
     auto u8 = [](const Dev &b) { return (const uint8_t *)b.p; };
-    const double sec = time_calls(ctx, [&] {
+    const int iters = (int)int_arg("--mlp-iterations", 3);
+    const double sec = time_calls(ctx, iters, [&] {
         check(mpp41_moe_w4a4(ctx, &d, x.p, (const float *)logits.p, u8(wg), u8(sg), u8(wu), u8(su), u8(wd), u8(sd), u8(swg),
                              u8(ssg), u8(swu), u8(ssu), u8(swd), u8(ssd), out.p, scratch.p),
               "mpp41_moe_w4a4");
     });
-    report("MoE W4A4: route top-8, grouped kind::mxf4 experts, shared expert, combine", sec,
-           6.0 * d.tokens * H * (double)(d.top_k * I + Is), half_raw_checksum(out.get<uint16_t>().data(), (size_t)d.tokens * H));
+    print_results({{"MoE W4A4: route top-8, grouped kind::mxf4 experts, shared expert, combine", sec, iters,
+                    6.0 * d.tokens * H * (double)(d.top_k * I + Is),
+                    half_raw_checksum(out.get<uint16_t>().data(), (size_t)d.tokens * H)}},
+                  "MLP");
 }
 
 // ---------------------------------------------------------------- MLP rows
 void run_mlp(mpp41_ctx *ctx)
 {
-    const uint32_t T = 128, H = 1024, I = 4096;
+    const long t_arg = int_arg("--mlp-tokens", 128), h_arg = int_arg("--mlp-hidden", 1024);
+    const long i_arg = int_arg("--mlp-intermediate", 4 * h_arg), it_arg = int_arg("--mlp-iterations", 3);
+    if (t_arg <= 0 || h_arg <= 0 || i_arg <= 0 || it_arg <= 0) {
+        fprintf(stderr, "error: MLP dimensions and iterations must be positive.\n");
+        exit(1);
+    }
+    const uint32_t T = (uint32_t)t_arg, H = (uint32_t)h_arg, I = (uint32_t)i_arg;
+    const int iters = (int)it_arg;
+    const bool sweep = has_flag("--fp4-group-sweep");
     if (!g_json) {
         printf("\nGated MLP benchmark:\n  op: down(silu(gate(x)) * up(x))\n");
-        printf("  shape: tokens=%u, hidden=%u, intermediate=%u\n  iterations: %d\n", T, H, I, g_iterations);
+        printf("  shape: tokens=%u, hidden=%u, intermediate=%u\n  iterations: %d\n", T, H, I, iters);
         if (g_baseline) printf("  inputs: MXFP4 rows in BASELINE mode B (seed %u)\n", g_seed);
     }
     const size_t gw = (size_t)I * H, dw = (size_t)H * I;
@@ -421,6 +483,19 @@ void run_mlp(mpp41_ctx *ctx)
         {"MPP/NAX W4A8 MLP: i8 x int4b -> i32", "mpp_mlp_i8_i4_i32_n128", i4w, false},
         {"MPP/NAX W2A8 MLP: i8 x int2b -> i32", "mpp_mlp_i8_i2_i32_n128", i2w, false},
     };
+    const double flops = 2.0 * 3.0 * T * (double)H * I;
+    std::vector<Result> results;
+    // scalar rows (encodeMLP, main.swift:2575-2634): half x, fp16 mid and out
+    Dev smid(ctx, (size_t)T * I * 2), sout(ctx, (size_t)T * H * 2);
+    const mpp41_mlp_config scfg = {T, H, I};
+    auto scalar_row = [&](const char *name, const char *gate, const char *down, const Weights *w) {
+        const double sec = time_calls(ctx, iters, [&] {
+            check(mpp41_mlp_scalar(ctx, gate, down, x_half.p, w->g.p, w->u.p, smid.p, w->d.p, sout.p, &scfg), gate);
+        });
+        const auto h = sout.get<uint16_t>();
+        results.push_back({name, sec, iters, flops, half_raw_checksum(h.data(), h.size())});
+    };
+    scalar_row("half MLP: half x half -> half", "half_mlp_gate_up_benchmark", "half_mlp_down_benchmark", halfw);
     for (const Row &r : rows) {
         mpp41_mlp_desc d;
         check(mpp41_mlp_describe(r.kernel, T, H, I, &d), r.kernel);
@@ -433,13 +508,25 @@ void run_mlp(mpp41_ctx *ctx)
         const uint8_t *s_u = r.mx ? (const uint8_t *)(mode_b ? bu.s.p : su.p) : nullptr;
         const uint8_t *s_d = r.mx ? (const uint8_t *)(mode_b ? bd.s.p : sd.p) : nullptr;
         double sec = 0;
-        check(mpp41_mlp_benchmark(ctx, &d, x, wg, wu, wd, s_g, s_u, s_d, scratch.p, out.p, g_iterations, &sec), r.kernel);
+        check(mpp41_mlp_benchmark(ctx, &d, x, wg, wu, wd, s_g, s_u, s_d, scratch.p, out.p, iters, &sec), r.kernel);
         std::string cks;
         if (d.out_dtype == MPP41_S32) { const auto h = out.get<int32_t>(); cks = int_checksum(h.data(), h.size()); }
         else if (d.out_dtype == MPP41_F16) { const auto h = out.get<uint16_t>(); cks = half_raw_checksum(h.data(), h.size()); }
         else { const auto h = out.get<float>(); cks = float_checksum(h.data(), h.size()); }
-        report(r.name, sec, 2.0 * 3.0 * T * (double)H * I, cks);
+        results.push_back({r.name, sec, iters, flops, cks});
     }
+    scalar_row("half MLP with INT8 weights: half x int8_t -> half", "half_int8_mlp_gate_up_benchmark",
+               "half_int8_mlp_down_benchmark", i8w);
+    scalar_row("half MLP with INT4 weights: half x int4b_format -> half", "half_int4_mlp_gate_up_benchmark",
+               "half_int4_mlp_down_benchmark", i4w);
+    scalar_row("half MLP with INT2 weights: half x int2b_format -> half", "half_int2_mlp_gate_up_benchmark",
+               "half_int2_mlp_down_benchmark", i2w);
+    scalar_row("half MLP with FP4 E2M1 g16 weights: half x FP4 -> half", "half_fp4_mlp_gate_up_benchmark",
+               "half_fp4_mlp_down_benchmark", f4w);
+    if (sweep)
+        scalar_row("half MLP with FP4 E2M1 g8 weights: half x FP4 -> half", "half_fp4_mlp_gate_up_g8_benchmark",
+                   "half_fp4_mlp_down_g8_benchmark", f4w);
+    print_results(results, "MLP");
     delete halfw; delete i8w; delete i4w; delete i2w; delete f4w; delete e4w; delete e5w;
 }
 
@@ -447,30 +534,49 @@ void run_mlp(mpp41_ctx *ctx)
 
 int main(int argc, char **argv)
 {
-    bool bench = false, mlp = false, accum = false, w4a4 = false, moe = false;
-    for (int i = 1; i < argc; ++i) {
-        if (!strcmp(argv[i], "--benchmark")) bench = true;
-        else if (!strcmp(argv[i], "--mlp-benchmark")) mlp = true;
-        else if (!strcmp(argv[i], "--accum-probe")) accum = true;
-        else if (!strcmp(argv[i], "--skip-tensor")) {}
-        else if (!strcmp(argv[i], "--w4a4")) w4a4 = true;
-        else if (!strcmp(argv[i], "--moe")) moe = true;
-        else if (!strcmp(argv[i], "--json")) g_json = true;
-        else if (!strcmp(argv[i], "--iterations") && i + 1 < argc) g_iterations = atoi(argv[++i]);
-        else if (!strcmp(argv[i], "--seed") && i + 1 < argc) g_seed = (uint32_t)strtoul(argv[++i], nullptr, 0);
-        else if (!strcmp(argv[i], "--mode") && i + 1 < argc) {
-            const char *m = argv[++i];
-            if (!strcmp(m, "baseline")) g_baseline = true;
-            else if (strcmp(m, "ref")) { fprintf(stderr, "--mode takes ref or baseline\n"); return 2; }
-        } else if (!strcmp(argv[i], "--gpus") && i + 1 < argc) {
-            if (atoi(argv[++i]) != 1) {
+    // Flags follow the reference command line (main.swift:80-162): booleans by
+    // name, integers as --name=value (intArgument, main.swift:2886-2892), and
+    // arguments it does not know are ignored. --json, --w4a4, --moe, --seed,
+    // --mode and --gpus are this probe's own.
+    for (int i = 1; i < argc; ++i) g_args.emplace_back(argv[i]);
+    auto value_of = [&](size_t &i, const char *name, std::string &out) {
+        const std::string &a = g_args[i];
+        const size_t n = strlen(name);
+        if (a == name && i + 1 < g_args.size()) { out = g_args[++i]; return true; }
+        if (a.compare(0, n, name) == 0 && a.size() > n && a[n] == '=') { out = a.substr(n + 1); return true; }
+        return false;
+    };
+    static const char *const known[] = {"--benchmark", "--mlp-benchmark", "--accum-probe", "--skip-tensor",
+                                        "--fp4-group-sweep", "--mxfp4-decompose", "--w4a4", "--moe", "--json"};
+    static const char *const known_int[] = {"--matmul-size", "--m", "--n", "--k", "--iterations", "--mlp-tokens",
+                                            "--mlp-hidden", "--mlp-intermediate", "--mlp-iterations"};
+    for (size_t i = 0; i < g_args.size(); ++i) {
+        std::string v;
+        if (value_of(i, "--seed", v)) { g_seed = (uint32_t)strtoul(v.c_str(), nullptr, 0); continue; }
+        if (value_of(i, "--mode", v)) {
+            if (v == "baseline") g_baseline = true;
+            else if (v != "ref") { fprintf(stderr, "--mode takes ref or baseline\n"); return 2; }
+            continue;
+        }
+        if (value_of(i, "--gpus", v)) {
+            if (atoi(v.c_str()) != 1) {
                 fprintf(stderr, "--gpus: this probe drives one GPU; multi-GPU layers run one process per GPU "
                                 "(mpp41_comm_init, mpp41_mlp_tp, mpp41_moe_ep)\n");
                 return 2;
             }
-        } else { fprintf(stderr, "unknown argument %s\n", argv[i]); return 2; }
+            continue;
+        }
+        bool ok = false;
+        for (const char *k : known) ok = ok || g_args[i] == k;
+        for (const char *k : known_int) {
+            const size_t n = strlen(k);
+            ok = ok || (g_args[i].compare(0, n, k) == 0 && g_args[i].size() > n && g_args[i][n] == '=');
+        }
+        if (!ok) fprintf(stderr, "warning: ignoring argument %s\n", g_args[i].c_str());
     }
-    if (g_iterations < 1) g_iterations = 1;
+    g_json = has_flag("--json");
+    const bool bench = has_flag("--benchmark"), mlp = has_flag("--mlp-benchmark"), accum = has_flag("--accum-probe");
+    const bool w4a4 = has_flag("--w4a4"), moe = has_flag("--moe");
     mpp41_ctx *ctx = nullptr;
     check(mpp41_create(0, &ctx), "mpp41_create");
     char name[256];
@@ -483,6 +589,8 @@ int main(int argc, char **argv)
     if (w4a4) run_w4a4(ctx);
     if (moe) run_moe(ctx);
     if (accum) printf("Accumulator precision probe: not applicable (Apple matmul2d semantics).\n");
+    if (has_flag("--mxfp4-decompose"))
+        printf("MXFP4 decomposition probe: not applicable (Metal kernel-variant timing).\n");
     mpp41_destroy(ctx);
     if (!ok) {
         fprintf(stderr, "error: One or more packed numeric checks failed.\n");

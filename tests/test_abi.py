@@ -76,5 +76,9 @@ def test_probe_cli_builds_and_fails_cleanly_without_a_device():
     import subprocess
     probe = os.path.join(os.path.dirname(mpp41.PKG) if False else mpp41.PKG, "bin", "mpp41probe")
     assert os.access(probe, os.X_OK)
+    # unknown flags are ignored, as the reference's command line does; with no
+    # device the probe exits 1 with the library's error
     r = subprocess.run([probe, "--no-such-flag"], capture_output=True, text=True, timeout=60)
-    assert r.returncode == 2 and "unknown argument" in r.stderr
+    assert r.returncode == 1 and "ignoring argument --no-such-flag" in r.stderr and "no device" in r.stderr
+    r = subprocess.run([probe, "--mode=fast"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 2 and "--mode takes ref or baseline" in r.stderr
