@@ -7,9 +7,9 @@ along K); fp32 accumulation, SiLU(gate)*up in fp32, fp16 output. A step is one
 layer. Dequantisation runs inside every step (the weights stay packed in HBM).
 
 Timed region: exactly K steps, captured as CUDA graphs and replayed, with 24
-distinct weight/activation sets rotated step by step (161 MB > the 126 MB L2),
+distinct weight/activation sets rotated step by step (173 MB > the 126 MB L2),
 bracketed by a barrier and cuda synchronize, CUDA events on the launching
-stream, max over ranks. N > 1 runs N independent replicas (the layer is
+stream, max over ranks; the region is timed 5 times and the median reported. N > 1 runs N independent replicas (the layer is
 single-GPU sized; weak scaling, no collective in the data path).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
@@ -42,9 +42,19 @@ BYTES_W = 3 * H * I // 2 + 3 * H * I // 32
 BYTES_LAYER = BYTES_W + T * H * 2 + T * H * 2
 ROTATE = 24
 METRIC = "MXFP4 fused-MLP µs/layer & TFLOP/s (% of roofline) at 1/2/4/8 B200"
-# DRAM bytes per launch of mlp_fused_kernel from one ncu capture of this
-# workload (profiles/mlp_fused_mxfp4_t128_h1024_i4096.md).
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# the layer kernel, from one ncu capture of this workload.
 NCU_TRAFFIC_LAYER = 7006720
+KERNEL = "mlp_small_kernel (gate/up + SwiGLU + down, one launch per layer)"
+REGIONS = 5          # timed regions of exactly K steps each; the median is reported
+
+
+def workload_config(world):
+    """The workload both arms time (identical keys in both JSON lines)."""
+    return {"workload": "mxfp4_mlp_t128_h1024_i4096 (BASELINE config 0)", "tokens": T, "hidden": H,
+            "intermediate": I, "weights": "MXFP4 (E2M1 + E8M0/32)", "activations": "fp16", "output": "fp16",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": f"rotating {ROTATE} weight/activation sets ({ROTATE * BYTES_LAYER / 1e6:.0f} MB) > 126 MB L2"}
 
 
 def load_peaks():
@@ -117,6 +127,7 @@ def reference_arm(args, rank):
     d = O.baseline_mlp_inputs(T, H, I)
     x = d["x"].view(np.uint16)
     run = lambda: O.mlp_mxfp4_cpu(T, H, I, x, d["wg"], d["wu"], d["wd"], d["sg"], d["su"], d["sd"], plain=True)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     for _ in range(args.warmup):
         run()
     t0 = time.perf_counter()
@@ -128,8 +139,8 @@ def reference_arm(args, rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
             "us_per_layer": dt * 1e6 / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "mxfp4_mlp_t128_h1024_i4096 (BASELINE config 0)", "tokens": T, "hidden": H,
-                       "intermediate": I},
+            "config": workload_config(world),
+            "compute": "fp32 CPU restatement of the layer (decode, fp32 sums, SwiGLU), OpenMP over all host threads",
             "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": nthr, "kind": "port",
                              "sample": f"{args.steps} full layers (T=128) on {nthr} threads"},
             "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -151,9 +162,17 @@ def cpu_baseline(host, seconds):
         _, nthr = O.mlp_mxfp4_cpu(*args, plain=True)
         n += 1
     dt = time.perf_counter() - t0
+    # the same restatement on one thread (a quarter of the sample time)
+    n1, t1 = 0, time.perf_counter()
+    while time.perf_counter() - t1 < seconds / 4 or n1 == 0:
+        O.mlp_mxfp4_cpu(*args, nthreads=1, plain=True)
+        n1 += 1
+    dt1 = time.perf_counter() - t1
     return {"value": FLOPS_PER_LAYER * n / dt / 1e12, "unit": "TFLOP/s", "cores": nthr, "kind": "port",
             "sample": f"{n} full layers (T=128, H=1024, I=4096) in {dt:.1f} s on {nthr} OpenMP threads, "
-                      f"oracle/cpu_baseline.c"}
+                      f"oracle/cpu_baseline.c",
+            "single_thread": {"value": FLOPS_PER_LAYER * n1 / dt1 / 1e12, "unit": "TFLOP/s", "cores": 1,
+                              "sample": f"{n1} full layers in {dt1:.1f} s on 1 thread"}}
 
 
 def main():
@@ -241,35 +260,45 @@ def main():
         layer(sets[i % ROTATE])
     torch.cuda.synchronize()
 
-    # ---- timed region: exactly K steps
+    # ---- timed regions: exactly K steps each, REGIONS times; the clock sampler
+    # runs from an untimed load phase (about 0.3 s of the same replays) through
+    # the last region, so its samples are taken under load
     sampler = ClockSampler(local)
     sampler.start()
-    time.sleep(0.2)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps // chunk):
-        g_full.replay()
-    if g_tail is not None:
-        g_tail.replay()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    t_load = time.perf_counter()
+    while time.perf_counter() - t_load < 0.3:
+        for _ in range(8):
+            g_full.replay()
+        torch.cuda.synchronize()
+    region_ms = []
+    for _ in range(REGIONS):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps // chunk):
+            g_full.replay()
+        if g_tail is not None:
+            g_tail.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        region_ms.append(ms)
     clocks = sampler.stop()
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = statistics.median(region_ms)
     us_layer = ms * 1e3 / args.steps
     value = world * FLOPS_PER_LAYER * args.steps / (ms * 1e-3) / 1e12
 
-    # ---- roofline of the one kernel per step (mlp_fused_kernel): its average
-    # launch duration is the timed region divided by the K launches
+    # ---- roofline of the one kernel per step: its average launch duration is
+    # the timed region divided by the K launches
     hbm, tflops_peak, peak_src = load_peaks()
     achieved = FLOPS_PER_LAYER / (us_layer * 1e-6) / 1e12
-    roofline = {"bound": "tensor", "kernel": "mlp_fused_kernel (gate/up + SwiGLU + down, one launch per layer)",
+    roofline = {"bound": "tensor", "kernel": KERNEL,
                 "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
                 "peak_source": f"bf16/f16 dense burst, {peak_src} (MEASURED_PEAKS.json)",
                 "traffic": NCU_TRAFFIC_LAYER,
@@ -345,12 +374,11 @@ def main():
                 "warmup": args.warmup, "ms_per_step": us_layer / 1e3, "us_per_layer": us_layer,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
                 "data": "synthetic (x ~ N(0,1), W ~ N(0,0.02) quantized OCP MXFP4 on the GPU)",
-                "config": {"workload": "mxfp4_mlp_t128_h1024_i4096 (BASELINE config 0)", "tokens": T,
-                           "hidden": H, "intermediate": I, "weights": "MXFP4 (E2M1 + E8M0/32)",
-                           "compute": "W4A16: in-CTA dequant to fp16, tcgen05 kind::f16, fp32 TMEM accum",
-                           "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                           "l2": f"rotating {ROTATE} weight/activation sets ({ROTATE * BYTES_LAYER / 1e6:.0f} MB)"
-                                 " > 126 MB L2"},
+                "config": workload_config(world),
+                "compute": "W4A16: packed weights decoded into tensor memory, tcgen05 kind::f16, fp32 TMEM "
+                           "accumulators, down-projection K splits reduced through L2",
+                "timing": f"median of {REGIONS} timed regions of exactly {args.steps} steps "
+                          f"(region ms: {', '.join(f'{m:.4f}' for m in region_ms)})",
                 "roofline": roofline, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
                 "oracle_rel_err": rel}
         if base is not None:

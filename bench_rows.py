@@ -2,11 +2,11 @@
 MXFP4 layer at other shapes, the W4A4 and NVFP4 layers,
 the plain block-scaled GEMMs and the MoE layer (config 4 per GPU).
 
-    python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row moe
-    python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row w4a4 --shape 4096,4096,14336
-    python mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row mxf4_gemm --shape 8192,8192,8192 --once
+    python bench_rows.py --row moe
+    python bench_rows.py --row w4a4 --shape 4096,4096,14336
+    python bench_rows.py --row mxf4_gemm --shape 8192,8192,8192 --once
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 --master-port 29511 \
-        mpp-4.1-fp4-fp8-block_b200/mpp41/bench_rows.py --row tp --shape 16,4096,14336
+        bench_rows.py --row tp --shape 16,4096,14336
 
 One JSON line per row: device time per call (CUDA events on the launching
 stream around a CUDA graph of back-to-back calls, median of 5 replays, after
@@ -28,9 +28,10 @@ import json
 import os
 import sys
 
-HERE = os.path.dirname(os.path.abspath(__file__))
-if os.path.dirname(HERE) not in sys.path:
-    sys.path.insert(0, os.path.dirname(HERE))
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "mpp-4.1-fp4-fp8-block_b200"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
 
 import torch  # noqa: E402
 
@@ -40,7 +41,7 @@ L2_BYTES = 126 << 20
 
 
 def peaks():
-    path = os.path.join(os.path.dirname(os.path.dirname(HERE)), "MEASURED_PEAKS.json")
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             d = json.load(f)

@@ -110,6 +110,13 @@ mpp41_status mpp41_set_stream(mpp41_ctx *ctx, void *cuda_stream);
 void *mpp41_get_stream(mpp41_ctx *ctx);
 /* Waits for the stream, then reports CUDA and device-side errors. */
 mpp41_status mpp41_synchronize(mpp41_ctx *ctx);
+/* Failure-path check of the bounded device waits (the counterpart of the
+ * reference's command-buffer error check, main.swift:251-256): enqueues one
+ * thread that waits, bounded by limit_ns (at most 10 s), until *flag >= target
+ * -- the wait the layer kernels use for their grid-wide counters. If nothing
+ * sets the flag in time the wait gives up, the kernel returns and the next
+ * mpp41_synchronize reports MPP41_ERR_TIMEOUT; the context stays usable. */
+mpp41_status mpp41_wait_probe(mpp41_ctx *ctx, const uint32_t *flag, uint32_t target, uint64_t limit_ns);
 /* Device address of the context's 32-bit device error word. */
 uint32_t *mpp41_device_error_word(mpp41_ctx *ctx);
 
@@ -196,9 +203,15 @@ mpp41_status mpp41_mlp_scalar(mpp41_ctx *ctx, const char *gate_kernel_name, cons
  *      scales [n][k/32]); sg/su/sd are only read for MXFP4. scratch must hold
  *      mpp41_mlp_scratch_bytes(desc) bytes: the fp16/fp32/int8 mid, then for
  *      fp16 output the split-K fp32 workspace and tile counters. Kernels by
- *      shape: up to 32 tokens with MXFP4/FP4 weights, two weight-streaming
- *      GEMV kernels; otherwise one persistent tcgen05 kernel per layer
- *      (token-major for 65..128 tokens of a small layer, weight-major else). ---- */
+ *      shape: up to 32 tokens with MXFP4/FP4/INT4 weights, two weight-
+ *      streaming GEMV kernels; 33..128 tokens of a small layer with 4-bit
+ *      weights (hidden <= 1024), the small-layer kernel
+ *      (one G and one D tile per CTA); otherwise one persistent tcgen05 kernel per layer
+ *      (token-major for 65..128 tokens of a small layer, weight-major else).
+ *      mpp41_mlp_last_kernel names the family the last mpp41_mlp call on the
+ *      context launched: "gemv", "small", "token_major", "weight_major",
+ *      "unfused" (two GEMM kernels) or "i8"; "" before the first call. ---- */
+const char *mpp41_mlp_last_kernel(const mpp41_ctx *ctx);
 size_t mpp41_mlp_scratch_bytes(const mpp41_mlp_desc *desc);
 mpp41_status mpp41_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const void *wg, const void *wu,
                        const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *scratch,
@@ -248,6 +261,14 @@ size_t mpp41_mlp_noalloc_scratch_bytes(const mpp41_mlp_desc *desc);
 mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *desc, const void *x, const void *wg, const void *wu,
                                const void *wd, const uint8_t *sg, const uint8_t *su, const uint8_t *sd, void *out,
                                void *cuda_stream);
+/* Device-side status of the no-alloc calls. The kernels record the first
+ * bounded wait that ran out (MPP41_ERR_TIMEOUT) or bounds check that tripped
+ * (MPP41_ERR_BOUNDS) in a static device word shared by all calls on the device;
+ * mpp41_mlp_noalloc returns MPP41_OK once it has launched. This call waits for
+ * `cuda_stream`, returns that recorded status (MPP41_OK when none) and clears
+ * it. Allocates nothing. The cached device addresses stay valid for the life
+ * of the CUDA context: do not use the no-alloc calls across cudaDeviceReset. */
+mpp41_status mpp41_mlp_noalloc_status(void *cuda_stream);
 
 /* ---- activation quantization (the epilogue after the layer, feeding the next
  *      layer's low-precision GEMM; no reference counterpart). fp16 x [tokens]

@@ -154,7 +154,7 @@ uint32_t down_splits(const mpp41_mlp_desc *d)
 
 LayerPlan desc_plan(const mpp41_mlp_desc *d)
 {
-    return plan_layer(d->tokens, d->hidden, d->intermediate, d->out_dtype == MPP41_F16);
+    return plan_layer(d->tokens, d->hidden, d->intermediate, d->out_dtype == MPP41_F16, d->wfmt);
 }
 
 // Scratch layout: [mid][fp32 workspace T x H][tile counters] for the
@@ -386,12 +386,14 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
         if (!s) s = enqueue_i8_gate_up(ctx, d, x, wg, wu, scratch, st);
         if (!s) s = enqueue_i8_gemm(ctx, d->wfmt, scratch, wd, out, d->tokens, d->hidden, d->intermediate, st,
                                     "int8 down GEMM");
+        if (!s) snprintf(ctx->last_mlp_kernel, sizeof(ctx->last_mlp_kernel), "i8");
         return s;
     }
     mpp41_status s = check_fp16_row(d);
     if (s) return s;
     if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su || !sd))
         return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate, up and down scales");
+    const char *declined = nullptr, *declined_kernel = "";
     if (!(d->flags & MPP41_MLP_UNFUSED) && d->wfmt != MPP41_W_F16 && d->epilogue != MPP41_SWIGLU_FLOAT &&
         desc_plan(d).sync_words <= ctx->sync_words) {
         const ScratchLayout SL = scratch_layout(d);
@@ -408,13 +410,28 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
         L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
         L.trace = ctx->trace;
         const char *why = "";
-        const int rc = launch_layer(desc_plan(d), L, st, &why);
-        if (rc == 0) return MPP41_OK;
+        const LayerPlan plan = desc_plan(d);
+        const int rc = launch_layer(plan, L, st, &why);
+        if (rc == 0) {
+            snprintf(ctx->last_mlp_kernel, sizeof(ctx->last_mlp_kernel), "%s",
+                     layer_kernel_name(plan, L.T, L.H, L.I, L.wfmt));
+            return MPP41_OK;
+        }
         if (rc == 2) return fail(MPP41_ERR_CUDA, "fused MLP kernel: %s", why);
+        declined = why;
+        declined_kernel = layer_kernel_name(plan, L.T, L.H, L.I, L.wfmt);
     }
     s = enqueue_gate_up(ctx, d, x, wg, wu, sg, su, scratch, out, st);
     if (s) return s;
-    return enqueue_down(ctx, d, scratch, wd, sd, out, true, st);
+    s = enqueue_down(ctx, d, scratch, wd, sd, out, true, st);
+    if (!s) {
+        if (declined)
+            snprintf(ctx->last_mlp_kernel, sizeof(ctx->last_mlp_kernel), "unfused (%s kernel declined: %s)",
+                     declined_kernel, declined);
+        else
+            snprintf(ctx->last_mlp_kernel, sizeof(ctx->last_mlp_kernel), "unfused");
+    }
+    return s;
 }
 
 }  // namespace
@@ -521,6 +538,18 @@ mpp41_status mpp41_set_trace(mpp41_ctx *ctx, unsigned long long *dev, size_t wor
     ctx->trace = dev;
     return MPP41_OK;
 }
+
+mpp41_status mpp41_wait_probe(mpp41_ctx *ctx, const uint32_t *flag, uint32_t target, uint64_t limit_ns)
+{
+    NEED(ctx);
+    if (!flag) return fail(MPP41_ERR_INVALID_ARGUMENT, "null flag");
+    if (limit_ns == 0 || limit_ns > 10000000000ull)
+        return fail(MPP41_ERR_INVALID_ARGUMENT, "limit must be in (0, 10 s]");
+    CK(launch_wait_probe(flag, target, limit_ns, ctx->err, ctx->stream), "wait probe launch");
+    return MPP41_OK;
+}
+
+const char *mpp41_mlp_last_kernel(const mpp41_ctx *ctx) { return ctx ? ctx->last_mlp_kernel : ""; }
 
 mpp41_status mpp41_synchronize(mpp41_ctx *ctx)
 {

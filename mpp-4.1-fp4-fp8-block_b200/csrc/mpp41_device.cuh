@@ -106,6 +106,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait until *p >= target (a counter other CTAs bump; read with
+// acquire semantics). Gives up after limit_ns, or early when another role of
+// the CTA has set *abort; a wait that runs out records MPP41_ERR_TIMEOUT plus
+// `site` in *err, sets *abort and returns false.
+__device__ __forceinline__ bool wait_flag_ge(const uint32_t *p, uint32_t target, uint64_t limit_ns,
+                                             volatile int *abort, uint32_t *err, uint32_t site)
+{
+    if (ld_acquire_gpu_u32(p) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        __nanosleep(32);
+        if (ld_acquire_gpu_u32(p) >= target) return true;
+        if (abort && *abort) return false;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            report_error(err, kErrTimeout, site);
+            if (abort) *abort = 1;
+            return false;
+        }
+    }
+}
+
 // Programmatic dependent launch: let the next kernel on the stream start its
 // prologue now / wait until the previous kernel finished and its writes are visible.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -180,19 +180,32 @@ uint32_t splits(uint32_t T, uint32_t H, uint32_t I, bool out_f16);
 int launch(const FusedLaunch &L, cudaStream_t st, const char **why);
 }  // namespace tok
 
+// Small-layer variant of the fused layer kernel (mpp41_mlp_small.cuh): T <= 128,
+// H <= 1024, 4-bit weights; one G and one D tile per CTA, the down projection's
+// 8 K splits reduced through a workspace of ws_bytes(T, H).
+namespace sl {
+bool covers(uint32_t T, uint32_t H, uint32_t I, int wfmt);
+size_t sync_words(uint32_t T, uint32_t H);
+size_t ws_bytes(uint32_t T, uint32_t H);
+int launch(const FusedLaunch &L, cudaStream_t st, const char **why);
+}  // namespace sl
+
 // Which fused kernel runs a layer, with its K splits and the workspace and
 // counter words it needs. Depends on the shape only.
 struct LayerPlan {
+    bool small;         // small-layer kernel (mpp41_mlp_small.cuh)
     bool token_major;
     uint32_t splits;
     size_t ws_bytes, sync_words;
 };
-LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16);
+LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16, int wfmt);
 // Decode-sized layers (T <= 32, MXFP4 / FP4 / INT4 weights, H and I multiples of
 // 128) run as two weight-streaming kernels (mpp41_gemv.cu); launch_layer
 // routes them there. The mid goes to L.mid (fp16 [T][I]); no workspace.
 bool gemv_covers(uint32_t T, uint32_t H, uint32_t I, int wfmt);
 int launch_gemv_layer(const FusedLaunch &L, cudaStream_t st, const char **why);
+// Name of the kernel family launch_layer uses for this plan and shape.
+const char *layer_kernel_name(const LayerPlan &plan, uint32_t T, uint32_t H, uint32_t I, int wfmt);
 // 0 = launched, 1 = shape/format not covered, 2 = CUDA error.
 int launch_layer(const LayerPlan &plan, FusedLaunch L, cudaStream_t st, const char **why);
 // 0 = launched, 1 = this shape/format is not covered by the fused kernel, 2 = CUDA error.
@@ -201,6 +214,8 @@ int launch_mlp_fused(const FusedLaunch &L, cudaStream_t st, const char **why);
 // Multi-GPU state of a context (mpp41_tp.cu); NULL until mpp41_comm_init.
 struct CommState;
 mpp41_status set_last_error(mpp41_status s, const char *msg);
+cudaError_t launch_wait_probe(const uint32_t *flag, uint32_t target, uint64_t limit_ns, uint32_t *err,
+                              cudaStream_t st);
 cudaError_t launch_f32_to_f16(const float *in, size_t n, void *out, cudaStream_t st);
 
 }  // namespace mpp41
@@ -217,6 +232,7 @@ struct mpp41_ctx {
     unsigned long long *trace;
     cudaEvent_t ev0, ev1;
     mpp41::CommState *comm = nullptr;
+    char last_mlp_kernel[192] = "";     // kernel family of the last enqueued mpp41_mlp layer (+ why a planned kernel declined)
 };
 
 namespace mpp41 {

@@ -55,10 +55,19 @@ uint32_t fused_splits(uint32_t T, uint32_t H, uint32_t I)
     return best;
 }
 
-LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16)
+LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16, int wfmt)
 {
     constexpr uint32_t kAssumedSMs = 148;
     LayerPlan pl{};
+    // Small layers with 4-bit weights: every CTA runs one
+    // G and one D tile; the down projection's 8 K splits reduce through L2.
+    if (T > 32 && sl::covers(T, H, I, wfmt)) {
+        pl.small = true;
+        pl.splits = 8;
+        pl.ws_bytes = sl::ws_bytes(T, H);
+        pl.sync_words = sl::sync_words(T, H);
+        return pl;
+    }
     // The weight-major kernel gives each CTA one tile: with fewer G tiles than
     // half the SMs (one 128-token tile of a small layer) each phase would
     // leave most SMs idle, so such layers use the token-major kernel, whose
@@ -76,11 +85,18 @@ LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16)
     return pl;
 }
 
+const char *layer_kernel_name(const LayerPlan &plan, uint32_t T, uint32_t H, uint32_t I, int wfmt)
+{
+    if (gemv_covers(T, H, I, wfmt)) return "gemv";
+    return plan.small ? "small" : plan.token_major ? "token_major" : "weight_major";
+}
+
 int launch_layer(const LayerPlan &plan, FusedLaunch L, cudaStream_t st, const char **why)
 {
     // decode-sized batches of FP4 weights: weight-streaming GEMV kernels
     if (!L.gemm_only && gemv_covers(L.T, L.H, L.I, L.wfmt)) return launch_gemv_layer(L, st, why);
     L.splits = plan.splits;
+    if (plan.small) return sl::launch(L, st, why);
     return plan.token_major ? tok::launch(L, st, why) : launch_mlp_fused(L, st, why);
 }
 

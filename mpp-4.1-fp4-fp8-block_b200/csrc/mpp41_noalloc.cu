@@ -85,7 +85,7 @@ mpp41_status setup(int dev, DevPtrs *out)
 // Same split rule as mpp41_mlp, so both entry points compute the same layer.
 mpp41::LayerPlan noalloc_plan(const mpp41_mlp_desc *d)
 {
-    return mpp41::plan_layer(d->tokens, d->hidden, d->intermediate, d->out_dtype == MPP41_F16);
+    return mpp41::plan_layer(d->tokens, d->hidden, d->intermediate, d->out_dtype == MPP41_F16, d->wfmt);
 }
 
 }  // namespace
@@ -131,11 +131,11 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
     mpp41_status s = setup(dev, &P);
     if (s) return s;
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    // Counters and error word must start at zero. The kernel leaves them zero,
-    // but a launch that gave up may not have; clearing them is a memset, not an
-    // allocation.
+    // The counters must start at zero. The kernel leaves them zero, but a
+    // launch that gave up may not have; clearing them is a memset, not an
+    // allocation. The error word is NOT cleared here: it keeps the first
+    // device-side error of any call until mpp41_mlp_noalloc_status reads it.
     e = cudaMemsetAsync(P.sync, 0, plan.sync_words * sizeof(uint32_t), st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(P.err, 0, sizeof(uint32_t), st);
     if (e != cudaSuccess) return err(MPP41_ERR_CUDA, "clear counters: %s", cudaGetErrorString(e));
 
     FusedLaunch L{};
@@ -155,4 +155,30 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
     if (rc == 1) return err(MPP41_ERR_UNSUPPORTED_SHAPE, "mpp41_mlp_noalloc: %s", why);
     if (rc == 2) return err(MPP41_ERR_CUDA, "mpp41_mlp_noalloc: %s", why);
     return MPP41_OK;
+}
+
+// Reads (and clears) the device error word the no-alloc kernels report into:
+// a bounded wait that ran out or a bounds check that tripped in any call since
+// the last read. Synchronizes `cuda_stream` first; the copies go through
+// pageable host memory (no allocation).
+extern "C" mpp41_status mpp41_mlp_noalloc_status(void *cuda_stream)
+{
+    using namespace mpp41;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) return err(MPP41_ERR_NO_DEVICE, "no current CUDA device");
+    DevPtrs P;
+    mpp41_status s = setup(dev, &P);
+    if (s) return s;
+    e = cudaStreamSynchronize(static_cast<cudaStream_t>(cuda_stream));
+    if (e != cudaSuccess) return err(MPP41_ERR_CUDA, "stream synchronize: %s", cudaGetErrorString(e));
+    uint32_t w = 0;
+    e = cudaMemcpy(&w, P.err, sizeof(w), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return err(MPP41_ERR_CUDA, "read device error word: %s", cudaGetErrorString(e));
+    if (!w) return MPP41_OK;
+    e = cudaMemset(P.err, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return err(MPP41_ERR_CUDA, "clear device error word: %s", cudaGetErrorString(e));
+    const uint32_t code = w & 0xFFFFu, site = w >> 16;
+    return err(code == 7 ? MPP41_ERR_TIMEOUT : code == 8 ? MPP41_ERR_BOUNDS : MPP41_ERR_CUDA,
+               "mpp41_mlp_noalloc: device-side error code %u at site 0x%x", code, site);
 }

@@ -677,4 +677,18 @@ cudaError_t launch_scalar_matmul(int kind, uint32_t M, uint32_t N, uint32_t K, c
     return cudaGetLastError();
 }
 
+// One thread waits, bounded by limit_ns, until *flag >= target: the same wait
+// the layer kernels use for their grid counters, so a flag that nothing sets
+// exercises the timeout path (error word -> MPP41_ERR_TIMEOUT) end to end.
+__global__ void wait_probe_kernel(const uint32_t *flag, uint32_t target, uint64_t limit_ns, uint32_t *err)
+{
+    if (threadIdx.x == 0) wait_flag_ge(flag, target, limit_ns, nullptr, err, 0xF01);
+}
+
+cudaError_t launch_wait_probe(const uint32_t *flag, uint32_t target, uint64_t limit_ns, uint32_t *err, cudaStream_t st)
+{
+    wait_probe_kernel<<<1, 32, 0, st>>>(flag, target, limit_ns, err);
+    return cudaGetLastError();
+}
+
 }  // namespace mpp41

@@ -133,6 +133,9 @@ def lib() -> C.CDLL:
         "mpp41_mlp_nvfp4": ([vp, u32, u32, u32] + [vp] * 11 + [C.c_int, vp], st),
         "mpp41_mlp_noalloc_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp_noalloc": ([C.POINTER(MLPDesc)] + [vp] * 9, st),
+        "mpp41_mlp_noalloc_status": ([vp], st),
+        "mpp41_mlp_last_kernel": ([vp], C.c_char_p),
+        "mpp41_wait_probe": ([vp, vp, C.c_uint32, C.c_uint64], st),
         "mpp41_mlp_describe": ([C.c_char_p, u32, u32, u32, C.POINTER(MLPDesc)], st),
         "mpp41_mlp_benchmark": ([vp, C.POINTER(MLPDesc)] + [vp] * 9 + [C.c_int, C.POINTER(C.c_double)], st),
         "mpp41_comm_unique_id": ([vp], st),
@@ -267,6 +270,12 @@ def mlp_noalloc(desc: MLPDesc, x, wg, wu, wd, sg, su, sd, out, stream_handle=Non
                                    _ptr(sd), _ptr(out), stream_handle))
 
 
+def mlp_noalloc_status(stream_handle=None):
+    """Waits for the stream, then raises MPP41Error if a no-alloc call recorded a
+    device-side error (bounded wait ran out, bounds check); clears it."""
+    _check(lib().mpp41_mlp_noalloc_status(stream_handle))
+
+
 def scratch_bytes(desc: MLPDesc) -> int:
     return lib().mpp41_mlp_scratch_bytes(C.byref(desc))
 
@@ -359,6 +368,14 @@ class Context:
     def mlp(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out):
         _check(lib().mpp41_mlp(self.h, C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(wd), _ptr(sg), _ptr(su),
                                _ptr(sd), _ptr(scratch), _ptr(out)))
+
+    def wait_probe(self, flag, target: int, limit_ns: int):
+        """Enqueue a bounded wait until *flag >= target (mpp41_wait_probe)."""
+        _check(lib().mpp41_wait_probe(self.h, _ptr(flag), target, limit_ns))
+
+    def mlp_last_kernel(self) -> str:
+        """Kernel family the last mlp() call launched ("cluster", "gemv", ...)."""
+        return lib().mpp41_mlp_last_kernel(self.h).decode()
 
     def mlp_gate_up(self, desc: MLPDesc, x, wg, wu, sg, su, scratch, out=None):
         _check(lib().mpp41_mlp_gate_up(self.h, C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(sg), _ptr(su),

@@ -44,8 +44,11 @@ def test_describe_matches_reference_pairings():
     assert (d.wfmt, d.epilogue, d.out_dtype) == (mpp41.W_E4M3, mpp41.SWIGLU_HALF_FROM_HALF, mpp41.F16)
     d = mpp41.describe("mpp_mlp_h_h_f_n128", 128, 1024, 4096)
     assert d.epilogue == mpp41.SWIGLU_FLOAT
-    # fp16 mid, then one fp32 T x H partial per down-projection K split (8 here)
+    # the small-layer kernel: fp16 mid, then its 8 K-split partial tiles (fp32 T x H each)
     assert mpp41.scratch_bytes(mpp41.describe("mpp_mlp_h_i4_f_n128", 128, 1024, 4096)) == 128 * 4096 * 2 + 8 * 128 * 1024 * 4
+    # the weight-major kernel: fp16 mid, then one fp32 T x H partial per K split (4 here)
+    d = mpp41.mlp_desc(256, 1024, 2048, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F32)
+    assert mpp41.scratch_bytes(d) == 256 * 2048 * 2 + 4 * 256 * 1024 * 4
     with pytest.raises(mpp41.MPP41Error) as e:
         mpp41.describe("not_a_kernel", 1, 64, 64)
     assert e.value.status == mpp41.ERR_MISSING_KERNEL

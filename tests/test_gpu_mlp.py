@@ -194,3 +194,21 @@ def test_fused_and_unfused_paths_agree(ctx, flags, out_dtype):
         ctx.mlp(desc, dv["x"], dv["wg"], dv["wu"], dv["wd"], dv["sg"], dv["su"], dv["sd"], d_scr, d_out)
         ctx.synchronize()
         assert rel_fro(from_dev(d_out, dt, (T, H)), ref) <= TOL
+
+
+@pytest.mark.parametrize("T,kernel", [(128, "small"), (64, "small"), (33, "small"), (16, "gemv"),
+                                      (129, "weight_major")])
+def test_config0_kernel_route(ctx, T, kernel):
+    """BASELINE config 0 (and its neighbours) take the planned kernel, not a
+    silent fallback to the two-kernel path."""
+    H, I = 1024, 4096
+    d = O.baseline_mlp_inputs(T, H, I, seed=3)
+    desc = mpp41.mlp_desc(T, H, I, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F16)
+    d_out, d_scr = empty_dev(T * H * 2), empty_dev(mpp41.scratch_bytes(desc))
+    dv = {k: to_dev(v) for k, v in d.items()}
+    ctx.mlp(desc, dv["x"], dv["wg"], dv["wu"], dv["wd"], dv["sg"], dv["su"], dv["sd"], d_scr, d_out)
+    ctx.synchronize()
+    assert ctx.mlp_last_kernel() == kernel
+    _, ref = O.mlp(0, O.W_MXFP4, 4, 1, T, H, I, d["x"].view(np.uint16), d["wg"], d["wu"], d["wd"],
+                   d["sg"], d["su"], d["sd"])
+    assert rel_fro(from_dev(d_out, np.float16, (T, H)), ref) <= TOL
