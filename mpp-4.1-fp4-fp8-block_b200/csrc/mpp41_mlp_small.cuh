@@ -32,14 +32,14 @@
 // finishes (programmatic dependent launch): only the x loads, the mid/out
 // stores and the counters wait for it. No TMA multicast is used.
 //
-// Warp roles (352 threads):
+// Warp roles (608 threads):
 //   warp 0       TMA producer of the activations (x slice, then mid split)
 //   warp 1       TMA producer of packed weights (16 KB stages of 256 K x 128
 //                rows, 4-slot shared-memory ring) and of all E8M0 scales
 //   warp 2       TMEM owner (512 columns) and single-thread MMA issuer
-//   warps 3..10  decode (lane quarter = warp % 4, K half = (warp-3)/4; 4 blocks
-//                of 32 weights of one row per stage) into a 3-slot TMEM ring,
-//                then the two epilogues
+//   warps 3..18  decode (lane quarter = warp % 4, K quarter = (warp-3)/4; 2
+//                blocks of 32 weights of one row per stage) into a 3-slot TMEM
+//                ring, then the two epilogues (token quarter = (warp-3)/4)
 // Every wait is bounded; pipeline barriers count one arrival per warp.
 #pragma once
 
@@ -55,7 +55,7 @@ namespace mpp41 {
 namespace sl {
 
 constexpr uint32_t kSplits = 8;      // K splits of the down projection
-constexpr int kXWarp = 0, kWWarp = 1, kMmaWarp = 2, kDec0 = 3, kDecWarps = 8;
+constexpr int kXWarp = 0, kWWarp = 1, kMmaWarp = 2, kDec0 = 3, kDecWarps = 16;
 constexpr int kThreads = (kDec0 + kDecWarps) * 32;
 constexpr int kEpi = kDecWarps * 32;
 constexpr uint32_t kNT = 64;         // tokens per tile (MMA N)
@@ -108,17 +108,20 @@ struct Params {
 enum TraceSlot : int {
     TR_START = 0, TR_W_LANDED = 1, TR_X_LANDED = 2, TR_G_DONE = 3, TR_G_PUB = 4, TR_CNT = 5, TR_D_DONE = 6,
     TR_RED = 7, TR_END = 8, TR_DEC_END = 9, TR_G_STORED = 10, TR_FENCED = 11, TR_D_STORED = 12, TR_D_ARRIVED = 13,
+    TR_END_NS = 14,     // %globaltimer at the CTA's end
+    TR_PDL_NS = 15,     // %globaltimer when griddepcontrol.wait returned (x producer)
+    TR_PREV_END_NS = 63,// the previous launch's TR_END_NS of this CTA index
     TR_MMA_GO = 16,     // [8] stage i: operands ready, MMAs issued
     TR_DEC_GO = 24,     // [8] stage i: decoder passed its waits
     TR_DEC_DONE = 32,   // [8] stage i: decoded operand stored in TMEM
     TR_MMA_X = 40,      // [8] stage i: activation operand landed (seen by the MMA issuer)
-    TR_MMA_ISSUED = 48, // [8] stage i: last MMA of the stage issued
+    TR_MMA_ISSUED = 48, // [8] stage i: last MMA of the stage issued (slots 48..55)
     kTraceSlots = 64
 };
 
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// Barrier over the 256 decode/epilogue threads that also ORs a predicate, so
+// Barrier over the 512 decode/epilogue threads that also ORs a predicate, so
 // every participant takes the same branch afterwards.
 __device__ __forceinline__ bool epi_bar_any(bool pred)
 {
@@ -126,12 +129,27 @@ __device__ __forceinline__ bool epi_bar_any(bool pred)
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.or.pred p, 1, 256, q;\n\t"
+        "bar.red.or.pred p, 1, 512, q;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(r)
         : "r"((uint32_t)pred)
         : "memory");
     return r != 0;
+}
+
+// Retiring a CTA: once its last counter wait has passed, one thread adds the
+// CTA to the finished count (retire_begin, whose result is not needed until
+// retire_end, so the round trip overlaps the CTA's remaining work); the last
+// CTA of the grid then resets every counter for the next launch on the stream.
+__device__ __forceinline__ uint32_t retire_begin(const Params &p) { return atomicAdd(p.sync, 1u); }
+
+__device__ __forceinline__ void retire_end(const Params &p, uint32_t ticket, uint32_t n_m)
+{
+    if (ticket == gridDim.x - 1) {
+        const uint32_t n = p.n_h * kSplits + p.n_h * n_m;
+        for (uint32_t i = 0; i < n; ++i) atomicExch(p.sync + 1 + i, 0u);
+        atomicExch(p.sync, 0u);
+    }
 }
 
 // D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16, A read from tensor memory.
@@ -157,6 +175,17 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[
 }
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns; thread i reads lane (base+i).
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
 
 template <int W, int EG, bool OUT_F16>
 __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_constant__ Params p)
@@ -197,6 +226,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
     uint32_t *g_cnt = p.sync + 1;                   // [n_h][8]
     uint32_t *d_cnt = p.sync + 1 + p.n_h * kSplits; // [n_h * n_m]
     unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceSlots : nullptr;
+    // trace: TR_START holds %globaltimer (ns), every other slot SM clock cycles
+    // since the start (clock64 is cheap; a %globaltimer read is not)
+    const long long clk0 = clock64();
     if (tr && threadIdx.x == 0) tr[TR_START] = globaltimer_ns();
 
     if (threadIdx.x == 0) {
@@ -240,26 +272,29 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
     const uint32_t tmem = *tmem_slot;
     pdl_launch_dependents();
 
+    // The three role warps run converged; each copy and MMA is issued by one
+    // elected lane, every wait is made by the whole warp.
     if (warp == kWWarp) {
         // ------------------------------------------------ packed weights and scales
-        if (lane == 0) {
-            if (W == W_MXFP4) {
-                mbar_arrive_expect_tx(sc_full, (has_g ? kRows * kScGRow : 0u) + (has_d ? kRows * kScDRow : 0u));
-                if (has_g) {
-                    tma_load_2d(smem + kOffScG, &p.tm_sg, 0, (int32_t)(gw * kGCh), sc_full);
-                    tma_load_2d(smem + kOffScG + kGCh * kScGRow, &p.tm_su, 0, (int32_t)(gw * kGCh), sc_full);
-                }
-                if (has_d)
-                    tma_load_2d(smem + kOffScD, &p.tm_sd, (int32_t)(ds * KS / 32), (int32_t)(dm * kRows), sc_full);
+        if (W == W_MXFP4 && elect_one_sync()) {
+            mbar_arrive_expect_tx(sc_full, (has_g ? kRows * kScGRow : 0u) + (has_d ? kRows * kScDRow : 0u));
+            if (has_g) {
+                tma_load_2d(smem + kOffScG, &p.tm_sg, 0, (int32_t)(gw * kGCh), sc_full);
+                tma_load_2d(smem + kOffScG + kGCh * kScGRow, &p.tm_su, 0, (int32_t)(gw * kGCh), sc_full);
             }
-            const uint32_t n = nG + nD;
-            bool ok = true;
-            for (uint32_t i = 0; i < n && ok; ++i) {
-                const uint32_t sl = i % kWSlots;
-                if (i >= kWSlots && !mbar_wait(&w_empty[sl], ((i / kWSlots) - 1u) & 1u, abort, p.err, 0xC01)) {
-                    ok = false;
-                    break;
-                }
+            if (has_d)
+                tma_load_2d(smem + kOffScD, &p.tm_sd, (int32_t)(ds * KS / 32), (int32_t)(dm * kRows), sc_full);
+        }
+        __syncwarp();
+        const uint32_t n = nG + nD;
+        bool ok = true;
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t sl = i % kWSlots;
+            if (i >= kWSlots && !mbar_wait(&w_empty[sl], ((i / kWSlots) - 1u) & 1u, abort, p.err, 0xC01)) {
+                ok = false;
+                break;
+            }
+            if (elect_one_sync()) {
                 mbar_arrive_expect_tx(&w_full[sl], kWStage);
                 uint8_t *dst = sW + sl * kWStage;
                 if (i < nG) {
@@ -271,50 +306,59 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
                     tma_load_2d(dst, &p.tm_wd, kx, (int32_t)(dm * kRows), &w_full[sl]);
                 }
             }
-            // no copies in flight when the CTA exits
-            if (ok)
-                for (uint32_t i = (n > kWSlots ? n - kWSlots : 0); i < n; ++i)
-                    mbar_wait(&w_full[i % kWSlots], (i / kWSlots) & 1u, nullptr, p.err, 0xC02);
-            if (W == W_MXFP4) mbar_wait(sc_full, 0, nullptr, p.err, 0xC03);
+            __syncwarp();
         }
+        // no copies in flight when the CTA exits
+        if (ok)
+            for (uint32_t i = (n > kWSlots ? n - kWSlots : 0); i < n; ++i)
+                mbar_wait(&w_full[i % kWSlots], (i / kWSlots) & 1u, nullptr, p.err, 0xC02);
+        if (W == W_MXFP4) mbar_wait(sc_full, 0, nullptr, p.err, 0xC03);
     } else if (warp == kXWarp) {
         // ------------------------------------------------ activations
-        if (lane == 0) {
-            pdl_wait_prior();   // x and the counters come from / are reset by the previous kernel
+        pdl_wait_prior();   // x and the counters come from / are reset by the previous kernel
+        if (tr && lane == 0) {
+            tr[TR_PREV_END_NS] = tr[TR_END_NS];
+            tr[TR_PDL_NS] = globaltimer_ns();
+        }
+        if (elect_one_sync()) {
             for (uint32_t s = 0; s < nG; ++s) {
                 mbar_arrive_expect_tx(&x_full[s], kActStage);
                 tma_load_3d(sX + s * kActStage, &p.tm_x, 0, (int32_t)(gh * kNT), (int32_t)(s * kSK / 64), &x_full[s]);
             }
-            bool ok = has_d;
-            // mid goes where x was: wait until the G MMAs have read it
-            if (ok && has_g) ok = mbar_wait(g_done, 0, abort, p.err, 0xC11);
-            if (ok) ok = wait_flag_ge(g_cnt + dh * kSplits + ds, p.g_per_split, kWaitLimitNs, abort, p.err, 0xC12);
-            if (tr) tr[TR_CNT] = globaltimer_ns();
-            if (ok) {
-                fence_proxy_async_global();   // the G tiles' generic mid stores before our TMA reads
+        }
+        __syncwarp();
+        bool ok = has_d;
+        // mid goes where x was: wait until the G MMAs have read it
+        if (ok && has_g) ok = mbar_wait(g_done, 0, abort, p.err, 0xC11);
+        if (ok) ok = wait_flag_ge(g_cnt + dh * kSplits + ds, p.g_per_split, kWaitLimitNs, abort, p.err, 0xC12);
+        if (tr && lane == 0) tr[TR_CNT] = (unsigned long long)(clock64() - clk0);
+        if (ok) {
+            fence_proxy_async_global();   // the G tiles' generic mid stores before our TMA reads
+            if (elect_one_sync()) {
                 for (uint32_t s = 0; s < nD; ++s) {
                     mbar_arrive_expect_tx(&m_full[s], kActStage);
                     tma_load_3d(sX + s * kActStage, &p.tm_mid, 0, (int32_t)(dh * kNT),
                                 (int32_t)((ds * KS + s * kSK) / 64), &m_full[s]);
                 }
-                for (uint32_t s = 0; s < nD; ++s) mbar_wait(&m_full[s], 0, nullptr, p.err, 0xC13);
             }
-            for (uint32_t s = 0; s < nG; ++s) mbar_wait(&x_full[s], 0, nullptr, p.err, 0xC14);
+            __syncwarp();
+            for (uint32_t s = 0; s < nD; ++s) mbar_wait(&m_full[s], 0, nullptr, p.err, 0xC13);
         }
+        for (uint32_t s = 0; s < nG; ++s) mbar_wait(&x_full[s], 0, nullptr, p.err, 0xC14);
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16_f32(kRows, kNT);
-            bool ok = true;
-            for (uint32_t i = 0; i < nG + nD && ok; ++i) {
-                const bool g = i < nG;
-                const uint32_t s = g ? i : i - nG, sl = i % kASlots;
-                if (!mbar_wait(g ? &x_full[s] : &m_full[s], 0, abort, p.err, 0xC21)) { ok = false; break; }
-                if (tr && i < 8) tr[TR_MMA_X + i] = globaltimer_ns();
-                if (!mbar_wait(&a_full[sl], (i / kASlots) & 1u, abort, p.err, 0xC22)) { ok = false; break; }
-                if (tr && i == 0) tr[TR_X_LANDED] = globaltimer_ns();
-                if (tr && i < 8) tr[TR_MMA_GO + i] = globaltimer_ns();
-                tc_fence_after();
+        const uint32_t idesc = idesc_f16_f32(kRows, kNT);
+        bool ok = true;
+        for (uint32_t i = 0; i < nG + nD; ++i) {
+            const bool g = i < nG;
+            const uint32_t s = g ? i : i - nG, sl = i % kASlots;
+            if (!mbar_wait(g ? &x_full[s] : &m_full[s], 0, abort, p.err, 0xC21)) { ok = false; break; }
+            if (tr && lane == 0 && i < 8) tr[TR_MMA_X + i] = (unsigned long long)(clock64() - clk0);
+            if (!mbar_wait(&a_full[sl], (i / kASlots) & 1u, abort, p.err, 0xC22)) { ok = false; break; }
+            if (tr && lane == 0 && i == 0) tr[TR_X_LANDED] = (unsigned long long)(clock64() - clk0);
+            if (tr && lane == 0 && i < 8) tr[TR_MMA_GO + i] = (unsigned long long)(clock64() - clk0);
+            tc_fence_after();
+            if (elect_one_sync()) {
                 const uint32_t d_tmem = tmem + (g ? kGAcc : kDAcc);
                 const uint32_t a0 = tmem + kACol0 + sl * kASlotCols;
                 const uint64_t b0 = smem_desc_sw128(sX + s * kActStage);
@@ -322,24 +366,26 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
                 for (uint32_t k = 0; k < kSK / 16; ++k)
                     mma_f16_ts(d_tmem, a0 + k * 8, b0 + (k / 4) * (kAtom >> 4) + 2 * (k % 4), idesc, (s | k) != 0u);
                 mma_commit(&a_empty[sl]);
-                if (tr && i < 8) tr[TR_MMA_ISSUED + i] = globaltimer_ns();
                 if (g && i + 1 == nG) mma_commit(g_done);
             }
-            if (ok) mma_commit(d_done);
+            __syncwarp();
+            if (tr && lane == 0 && i < 8) tr[TR_MMA_ISSUED + i] = (unsigned long long)(clock64() - clk0);
         }
+        if (ok && elect_one_sync()) mma_commit(d_done);
+        __syncwarp();
     } else {
         // ------------------------------------------------ decode, then epilogues
-        const uint32_t te = threadIdx.x - kDec0 * 32;   // 0..255
+        const uint32_t te = threadIdx.x - kDec0 * 32;   // 0..511
         const uint32_t q = warp & 3;                    // TMEM lanes 32q..32q+31
-        const uint32_t kq = (warp - kDec0) >> 2;        // decode: K half of the stage; epilogue: token half
+        const uint32_t kq = (warp - kDec0) >> 2;        // decode: K quarter of the stage; epilogue: token quarter
         const uint32_t r = q * 32 + lane;               // TMEM lane = weight row of the tile
         const uint32_t lane_base = (q * 32u) << 16;
         bool ok = true;
         if (W == W_MXFP4) ok = mbar_wait(sc_full, 0, abort, p.err, 0xC31);
         // ---------------------------------------------- G epilogue: SwiGLU -> fp16 mid
-        // Runs once, inside the decode loop just before the first stage whose
-        // TMEM slot waits on a D MMA (the D MMAs need the mid of other CTAs'
-        // G epilogues), or after the loop.
+        // Runs once, inside the decode loop before the first D stage: the D
+        // weights are decoded while other CTAs' G tiles finish (the D MMAs wait
+        // for their mid anyway), so the mid of this tile is published first.
         bool g_epi_done = !has_g;
         auto g_epilogue = [&]() {
             g_epi_done = true;
@@ -347,21 +393,21 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
             const bool gok = ok && mbar_wait(g_done, 0, abort, p.err, 0xC41);
             if (!epi_bar_any(!gok || *abort)) {
                 tc_fence_after();
-                if (tr && te == 0) tr[TR_G_DONE] = globaltimer_ns();
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem + lane_base + kGAcc + kq * 32, v);
+                if (tr && te == 0) tr[TR_G_DONE] = (unsigned long long)(clock64() - clk0);
+                uint32_t v[16];
+                tmem_ld_x16(tmem + lane_base + kGAcc + kq * 16, v);
                 tmem_ld_wait();
                 // lane pair (2j, 2j+1) = (gate, up) of channel j: the even lane
-                // finishes tokens 0..15 of this warp's 32, the odd lane 16..31
+                // finishes tokens 0..7 of this warp's 16, the odd lane 8..15
                 const uint32_t j = r >> 1, is_up = lane & 1u;
 #pragma unroll
-                for (uint32_t t = 0; t < 16; ++t) {
-                    const uint32_t mine = is_up ? v[16 + t] : v[t];
-                    const uint32_t send = is_up ? v[t] : v[16 + t];
+                for (uint32_t t = 0; t < 8; ++t) {
+                    const uint32_t mine = is_up ? v[8 + t] : v[t];
+                    const uint32_t send = is_up ? v[t] : v[8 + t];
                     const uint32_t other = __shfl_xor_sync(0xffffffffu, send, 1);
                     const float gv = __uint_as_float(is_up ? other : mine);
                     const float uv = __uint_as_float(is_up ? mine : other);
-                    sMid[(kq * 32 + is_up * 16 + t) * kGCh + j] = __float2half_rn(swiglu<EG>(gv, uv));
+                    sMid[(kq * 16 + is_up * 8 + t) * kGCh + j] = __float2half_rn(swiglu<EG>(gv, uv));
                 }
                 epi_bar_any(false);
                 // 64 tokens x 128 bytes to mid[gh*64 + t][gw*64 ..)
@@ -371,38 +417,38 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
                         *reinterpret_cast<uint4 *>(p.mid + (size_t)tok * p.I + gw * kGCh + c8 * 8) =
                             *reinterpret_cast<const uint4 *>(sMid + tl * kGCh + c8 * 8);
                 }
-                if (tr && te == 0) tr[TR_G_STORED] = globaltimer_ns();
+                if (tr && te == 0) tr[TR_G_STORED] = (unsigned long long)(clock64() - clk0);
                 // publish: generic stores ordered before other CTAs' TMA (async proxy)
                 // reads, one release by one thread after the barrier
                 fence_proxy_async_global();
                 epi_bar_any(false);
                 if (te == 0) {
                     __threadfence();
-                    if (tr) tr[TR_FENCED] = globaltimer_ns();
+                    if (tr) tr[TR_FENCED] = (unsigned long long)(clock64() - clk0);
                     atomicAdd(g_cnt + gh * kSplits + gw / p.g_per_split, 1u);
-                    if (tr) tr[TR_G_PUB] = globaltimer_ns();
+                    if (tr) tr[TR_G_PUB] = (unsigned long long)(clock64() - clk0);
                 }
             }
         };
         for (uint32_t i = 0; i < nG + nD && ok; ++i) {
-            if (!g_epi_done && i == nG + kASlots - 1) g_epilogue();
+            if (!g_epi_done && i == nG) g_epilogue();
             const bool g = i < nG;
             const uint32_t s = g ? i : i - nG, wsl = i % kWSlots, asl = i % kASlots;
             if (!mbar_wait(&w_full[wsl], (i / kWSlots) & 1u, abort, p.err, 0xC32)) { ok = false; break; }
-            if (tr && i == 0 && te == 0) tr[TR_W_LANDED] = globaltimer_ns();
+            if (tr && i == 0 && te == 0) tr[TR_W_LANDED] = (unsigned long long)(clock64() - clk0);
             if (i >= kASlots) {   // MMAs of stage i-3 (same TMEM slot) completed
                 if (!mbar_wait(&a_empty[asl], ((i / kASlots) - 1u) & 1u, abort, p.err, 0xC33)) { ok = false; break; }
                 tc_fence_after();
             }
-            if (tr && te == 0 && i < 8) tr[TR_DEC_GO + i] = globaltimer_ns();
+            if (tr && te == 0 && i < 8) tr[TR_DEC_GO + i] = (unsigned long long)(clock64() - clk0);
             // packed row of the slot: G rows interleave gate (even lanes) and up (odd lanes)
             const uint32_t rr = g ? ((r & 1u) ? kGCh + (r >> 1) : (r >> 1)) : r;
             const uint8_t *rowp = sW + wsl * kWStage + rr * 128;
             const uint8_t *scp = g ? sScG + rr * kScGRow + s * (kSK / 32) : sScD + rr * kScDRow + s * (kSK / 32);
-            const uint32_t col = tmem + lane_base + kACol0 + asl * kASlotCols + kq * 64;
+            const uint32_t col = tmem + lane_base + kACol0 + asl * kASlotCols + kq * 32;
 #pragma unroll
-            for (uint32_t b = 0; b < 4; ++b) {
-                const uint32_t c16 = kq * 4 + b;   // 16-byte chunk of the 128-byte row (32 weights)
+            for (uint32_t b = 0; b < 2; ++b) {
+                const uint32_t c16 = kq * 2 + b;   // 16-byte chunk of the 128-byte row (32 weights)
                 const uint4 v = *reinterpret_cast<const uint4 *>(rowp + ((c16 ^ (rr & 7u)) << 4));
                 const uint32_t wr[8] = {v.x, v.y, v.z, v.w, 0u, 0u, 0u, 0u};
                 const uint32_t sb = (W == W_MXFP4) ? scp[c16] : 127u;
@@ -417,60 +463,61 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
                 mbar_arrive(&a_full[asl]);
                 mbar_arrive(&w_empty[wsl]);
             }
-            if (tr && te == 0 && i < 8) tr[TR_DEC_DONE + i] = globaltimer_ns();
+            if (tr && te == 0 && i < 8) tr[TR_DEC_DONE + i] = (unsigned long long)(clock64() - clk0);
         }
-        if (tr && te == 0) tr[TR_DEC_END] = globaltimer_ns();
+        if (tr && te == 0) tr[TR_DEC_END] = (unsigned long long)(clock64() - clk0);
         if (!g_epi_done) g_epilogue();
         pdl_wait_prior();   // before the first write of the workspace / out
 
         // ---------------------------------------------- D epilogue: split-K reduction through L2
         const bool dok = has_d && ok && mbar_wait(d_done, 0, abort, p.err, 0xC42);
-        if (!epi_bar_any(!dok || *abort)) {
+        const bool dskip = epi_bar_any(!dok || *abort);
+        uint32_t ticket = ~0u;                       // thread te == 0 only
+        if (dskip && te == 0) ticket = retire_begin(p);   // no counter waits ahead
+        if (!dskip) {
             tc_fence_after();
-            if (tr && te == 0) tr[TR_D_DONE] = globaltimer_ns();
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + kDAcc + kq * 32, v);
+            if (tr && te == 0) tr[TR_D_DONE] = (unsigned long long)(clock64() - clk0);
+            uint32_t v[16];
+            tmem_ld_x16(tmem + lane_base + kDAcc + kq * 16, v);
             tmem_ld_wait();
             // partial tile, token-major: ws[dt][ds][token][row]; a warp stores
             // 128 contiguous bytes (32 rows) per token
             float *part = p.ws + ((size_t)dt * kSplits + ds) * (kNT * kRows);
 #pragma unroll
-            for (uint32_t t = 0; t < 32; ++t) __stcg(part + (kq * 32 + t) * kRows + r, __uint_as_float(v[t]));
-            if (tr && te == 0) tr[TR_D_STORED] = globaltimer_ns();
+            for (uint32_t t = 0; t < 16; ++t) __stcg(part + (kq * 16 + t) * kRows + r, __uint_as_float(v[t]));
+            if (tr && te == 0) tr[TR_D_STORED] = (unsigned long long)(clock64() - clk0);
             epi_bar_any(false);
             bool aok = true;
             if (te == 0) {
                 __threadfence();
                 atomicAdd(d_cnt + dt, 1u);
-                if (tr) tr[TR_D_ARRIVED] = globaltimer_ns();
+                if (tr) tr[TR_D_ARRIVED] = (unsigned long long)(clock64() - clk0);
                 // all 8 splits of the tile are co-resident: waiting cannot deadlock
                 aok = wait_flag_ge(d_cnt + dt, kSplits, kWaitLimitNs, abort, p.err, 0xC43);
+                ticket = retire_begin(p);
             }
             if (!epi_bar_any(!aok)) {
-                if (tr && te == 0) tr[TR_RED] = globaltimer_ns();
+                if (tr && te == 0) tr[TR_RED] = (unsigned long long)(clock64() - clk0);
                 // this split sums rows ds*16 .. +16 of the tile over the 8 partials
-                const uint32_t tok = te >> 2, r4 = ds * kBand + (te & 3u) * 4;
-                const float *src = p.ws + (size_t)dt * kSplits * (kNT * kRows) + tok * kRows + r4;
-                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                const uint32_t tok = te >> 3, r2 = ds * kBand + (te & 7u) * 2;
+                const float *src = p.ws + (size_t)dt * kSplits * (kNT * kRows) + tok * kRows + r2;
+                float2 a = make_float2(0.f, 0.f);
 #pragma unroll
                 for (uint32_t sp = 0; sp < kSplits; ++sp) {
-                    const float4 b = __ldcg(reinterpret_cast<const float4 *>(src + sp * (kNT * kRows)));
-                    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+                    const float2 b = __ldcg(reinterpret_cast<const float2 *>(src + sp * (kNT * kRows)));
+                    a.x += b.x; a.y += b.y;
                 }
-                const uint32_t gtok = dh * kNT + tok, hcol = dm * kRows + r4;
+                const uint32_t gtok = dh * kNT + tok, hcol = dm * kRows + r2;
                 if (gtok < p.T) {
-                    if constexpr (OUT_F16) {
-                        const __half2 h01 = __floats2half2_rn(a.x, a.y), h23 = __floats2half2_rn(a.z, a.w);
-                        uint2 u;
-                        u.x = *reinterpret_cast<const uint32_t *>(&h01);
-                        u.y = *reinterpret_cast<const uint32_t *>(&h23);
-                        *reinterpret_cast<uint2 *>(static_cast<__half *>(p.out) + (size_t)gtok * p.H + hcol) = u;
-                    } else {
-                        *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + (size_t)gtok * p.H + hcol) = a;
-                    }
+                    if constexpr (OUT_F16)
+                        *reinterpret_cast<__half2 *>(static_cast<__half *>(p.out) + (size_t)gtok * p.H + hcol) =
+                            __floats2half2_rn(a.x, a.y);
+                    else
+                        *reinterpret_cast<float2 *>(static_cast<float *>(p.out) + (size_t)gtok * p.H + hcol) = a;
                 }
             }
         }
+        if (te == 0) retire_end(p, ticket, n_m);
     }
 
     // ---------------------------------------------------- teardown
@@ -480,13 +527,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
-    if (tr && threadIdx.x == 0) tr[TR_END] = globaltimer_ns();
-    // this CTA no longer touches the counters: count it; the last CTA of the
-    // grid resets them for the next launch on the stream
-    if (threadIdx.x == 0 && atomicAdd(p.sync, 1u) == gridDim.x - 1) {
-        const uint32_t n = p.n_h * kSplits + p.n_h * (p.H / kRows);
-        for (uint32_t i = 0; i < n; ++i) atomicExch(p.sync + 1 + i, 0u);
-        atomicExch(p.sync, 0u);
+    if (tr && threadIdx.x == 0) {
+        tr[TR_END] = (unsigned long long)(clock64() - clk0);
+        tr[TR_END_NS] = globaltimer_ns();
     }
 }
 
