@@ -44,7 +44,7 @@ ROTATE = 24
 METRIC = "MXFP4 fused-MLP µs/layer & TFLOP/s (% of roofline) at 1/2/4/8 B200"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the layer kernel, from one ncu capture of this workload.
-NCU_TRAFFIC_LAYER = 7006720
+NCU_TRAFFIC_LAYER = 6993664
 KERNEL = "mlp_small_kernel (gate/up + SwiGLU + down, one launch per layer)"
 REGIONS = 5          # timed regions of exactly K steps each; the median is reported
 

@@ -121,6 +121,14 @@ enum TraceSlot : int {
 
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
+// Release increment at GPU scope: the writes that happen before it (this
+// thread's, and through the preceding CTA barrier the other threads') are
+// visible to whoever acquires the new count.
+__device__ __forceinline__ void red_release_add(uint32_t *p, uint32_t v)
+{
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Barrier over the 512 decode/epilogue threads that also ORs a predicate, so
 // every participant takes the same branch afterwards.
 __device__ __forceinline__ bool epi_bar_any(bool pred)
@@ -423,9 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
                 fence_proxy_async_global();
                 epi_bar_any(false);
                 if (te == 0) {
-                    __threadfence();
+                    red_release_add(g_cnt + gh * kSplits + gw / p.g_per_split, 1u);
                     if (tr) tr[TR_FENCED] = (unsigned long long)(clock64() - clk0);
-                    atomicAdd(g_cnt + gh * kSplits + gw / p.g_per_split, 1u);
                     if (tr) tr[TR_G_PUB] = (unsigned long long)(clock64() - clk0);
                 }
             }
@@ -489,8 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
             epi_bar_any(false);
             bool aok = true;
             if (te == 0) {
-                __threadfence();
-                atomicAdd(d_cnt + dt, 1u);
+                red_release_add(d_cnt + dt, 1u);
                 if (tr) tr[TR_D_ARRIVED] = (unsigned long long)(clock64() - clk0);
                 // all 8 splits of the tile are co-resident: waiting cannot deadlock
                 aok = wait_flag_ge(d_cnt + dt, kSplits, kWaitLimitNs, abort, p.err, 0xC43);
