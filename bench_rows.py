@@ -10,10 +10,11 @@ the plain block-scaled GEMMs and the MoE layer (config 4 per GPU).
 
 One JSON line per row: device time per call (CUDA events on the launching
 stream around a CUDA graph of back-to-back calls, median of 5 replays, after
-3 warm-up calls), TFLOP/s, and the fraction of a peak: the FP4 rows against
-4x the measured dense bf16 peak (MEASURED_PEAKS.json; kind::mxf4 issues 4x the
-kind::f16 rate), the weight-streaming rows against the measured HBM copy
-bandwidth for their algorithmic bytes. Weights are random packed bytes (every
+3 warm-up calls), TFLOP/s, and fractions of peaks: every row against the
+measured kind::mxf4 issue-rate peak (9.53 PFLOP/s at 1965 MHz on 148 SMs,
+measured with host/mpp41_mma_peaks.cu) and against the measured dense f16
+peak (MEASURED_PEAKS.json), the weight-streaming rows also against the measured
+HBM copy bandwidth for their algorithmic bytes. Weights are random packed bytes (every
 E2M1 code) with block scales near 1; inputs larger than L2 are used as they
 are, smaller weight sets are rotated through copies that together exceed L2.
 `--once` runs 2 warm-up calls and one call, for profilers. `--row tp` (under
@@ -38,6 +39,7 @@ import torch  # noqa: E402
 import mpp41  # noqa: E402
 
 L2_BYTES = 126 << 20
+MXF4_PEAK_TFLOPS = 9530.0   # kind::mxf4.block_scale 128x256x64, 128.1 cycles per MMA, 1965 MHz, 148 SMs
 
 
 def peaks():
@@ -92,7 +94,6 @@ def main():
     if args.row == "tp":
         return tp_row(args)
     hbm, bf16, src = peaks()
-    fp4_peak = 4 * bf16
     st = torch.cuda.Stream()
     torch.cuda.set_stream(st)
     ctx = mpp41.Context(0)
@@ -193,8 +194,11 @@ def main():
     tflops = flops / us / 1e6
     gbs = abytes / us / 1e3
     line.update(us=round(us, 2), tflops=round(tflops, 1), algorithmic_bytes=int(abytes), gbs=round(gbs, 1),
-                frac_fp4_peak=round(tflops / fp4_peak, 3), frac_hbm=round(gbs / hbm, 3),
-                peaks={"fp4_tflops": fp4_peak, "hbm_gbs": hbm, "source": src + " (fp4 = 4 x bf16)"})
+                frac_fp4_peak=round(tflops / MXF4_PEAK_TFLOPS, 3), frac_f16_peak=round(tflops / bf16, 3),
+                frac_hbm=round(gbs / hbm, 3),
+                peaks={"fp4_tflops": MXF4_PEAK_TFLOPS, "f16_tflops": bf16, "hbm_gbs": hbm,
+                       "source": "fp4: measured kind::mxf4 issue rate (host/mpp41_mma_peaks.cu); f16 and HBM: "
+                                 + src + " (MEASURED_PEAKS.json)"})
     print(json.dumps(line))
 
 

@@ -150,6 +150,15 @@ __device__ __forceinline__ bool elect_one_sync()
     return p != 0;
 }
 
+// mbar_wait made by all 32 lanes of a converged warp, with one outcome for
+// the warp (a wait that gave up in any lane counts as given up in all), so
+// the warp stays converged for the elect.sync that follows.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *err,
+                                          uint32_t site)
+{
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, err, site));
+}
+
 // Programmatic dependent launch: let the next kernel on the stream start its
 // prologue now / wait until the previous kernel finished and its writes are visible.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

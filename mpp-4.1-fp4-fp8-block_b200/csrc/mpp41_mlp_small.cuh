@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
         bool ok = true;
         for (uint32_t i = 0; i < n; ++i) {
             const uint32_t sl = i % kWSlots;
-            if (i >= kWSlots && !mbar_wait(&w_empty[sl], ((i / kWSlots) - 1u) & 1u, abort, p.err, 0xC01)) {
+            if (i >= kWSlots && !warp_wait(&w_empty[sl], ((i / kWSlots) - 1u) & 1u, abort, p.err, 0xC01)) {
                 ok = false;
                 break;
             }
@@ -337,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
         __syncwarp();
         bool ok = has_d;
         // mid goes where x was: wait until the G MMAs have read it
-        if (ok && has_g) ok = mbar_wait(g_done, 0, abort, p.err, 0xC11);
-        if (ok) ok = wait_flag_ge(g_cnt + dh * kSplits + ds, p.g_per_split, kWaitLimitNs, abort, p.err, 0xC12);
+        if (ok && has_g) ok = warp_wait(g_done, 0, abort, p.err, 0xC11);
+        if (ok) ok = __all_sync(0xffffffffu, wait_flag_ge(g_cnt + dh * kSplits + ds, p.g_per_split, kWaitLimitNs, abort, p.err, 0xC12));
         if (tr && lane == 0) tr[TR_CNT] = (unsigned long long)(clock64() - clk0);
         if (ok) {
             fence_proxy_async_global();   // the G tiles' generic mid stores before our TMA reads
@@ -360,9 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
         for (uint32_t i = 0; i < nG + nD; ++i) {
             const bool g = i < nG;
             const uint32_t s = g ? i : i - nG, sl = i % kASlots;
-            if (!mbar_wait(g ? &x_full[s] : &m_full[s], 0, abort, p.err, 0xC21)) { ok = false; break; }
+            if (!warp_wait(g ? &x_full[s] : &m_full[s], 0, abort, p.err, 0xC21)) { ok = false; break; }
             if (tr && lane == 0 && i < 8) tr[TR_MMA_X + i] = (unsigned long long)(clock64() - clk0);
-            if (!mbar_wait(&a_full[sl], (i / kASlots) & 1u, abort, p.err, 0xC22)) { ok = false; break; }
+            if (!warp_wait(&a_full[sl], (i / kASlots) & 1u, abort, p.err, 0xC22)) { ok = false; break; }
             if (tr && lane == 0 && i == 0) tr[TR_X_LANDED] = (unsigned long long)(clock64() - clk0);
             if (tr && lane == 0 && i < 8) tr[TR_MMA_GO + i] = (unsigned long long)(clock64() - clk0);
             tc_fence_after();

@@ -211,15 +211,17 @@ __global__ void __launch_bounds__(kThreads, Tile<BN>::kCtasPerSm) mxf4_gemm_kern
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // The producer and MMA warps run converged: every wait is made by the whole
+    // warp, every copy / MMA issued by one elected lane.
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
-        if (lane == 0) {
-            const int32_t rb0 = (int32_t)(b_off + p.b0_row0 + blockIdx.x * p.b_row_step);
-            const int32_t rb1 = (int32_t)(b_off + p.b1_row0 + blockIdx.x * p.b_row_step);
-            uint32_t s = 0;
-            for (; s < nk; ++s) {
-                const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
-                if (!mbar_wait(&empty[st], ph ^ 1u, abort, p.err, 0xC01)) break;
+        const int32_t rb0 = (int32_t)(b_off + p.b0_row0 + blockIdx.x * p.b_row_step);
+        const int32_t rb1 = (int32_t)(b_off + p.b1_row0 + blockIdx.x * p.b_row_step);
+        uint32_t s = 0;
+        for (; s < nk; ++s) {
+            const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
+            if (!warp_wait(&empty[st], ph ^ 1u, abort, p.err, 0xC01)) break;
+            if (elect_one_sync()) {
                 mbar_arrive_expect_tx(&full[st], kATile + Tl::kBTile + kSfaBytes + Tl::kSfbBytes);
                 const int32_t kb = (int32_t)(s * (kBK / 2));
                 const int32_t ks = (int32_t)((NV ? s : (s >> 1)) * kSfRow);
@@ -230,17 +232,18 @@ __global__ void __launch_bounds__(kThreads, Tile<BN>::kCtasPerSm) mxf4_gemm_kern
                 tma_load_2d(sSb + st * Tl::kSfbBytes, &p.tm_sb0, ks, rb0, &full[st]);
                 tma_load_2d(sSb + st * Tl::kSfbBytes + Tl::kHalfRows * kSfRow, &p.tm_sb1, ks, rb1, &full[st]);
             }
-            // drain: no copy may still be landing when the CTA exits
-            for (uint32_t t = (s > kStages ? s - kStages : 0); t < s; ++t)
-                mbar_wait(&full[t % kStages], (t / kStages) & 1u, nullptr, p.err, 0xC02);
+            __syncwarp();
         }
+        // drain: no copy may still be landing when the CTA exits
+        for (uint32_t t = (s > kStages ? s - kStages : 0); t < s; ++t)
+            mbar_wait(&full[t % kStages], (t / kStages) & 1u, nullptr, p.err, 0xC02);
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            for (uint32_t s = 0; s < nk; ++s) {
-                const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
-                if (!mbar_wait(&sf_ready[st], ph, abort, p.err, 0xC03)) break;
-                tc_fence_after();
+        for (uint32_t s = 0; s < nk; ++s) {
+            const uint32_t st = s % kStages, ph = (s / kStages) & 1u;
+            if (!warp_wait(&sf_ready[st], ph, abort, p.err, 0xC03)) break;
+            tc_fence_after();
+            if (elect_one_sync()) {
                 const uint64_t ad = smem_desc_sw128(sA + st * kATile);
                 const uint64_t bd = smem_desc_sw128(sB + st * Tl::kBTile);
                 const uint32_t sfa0 = tmem + kSfCol0 + st * (kSfaCols + kSfbCols);
@@ -259,8 +262,10 @@ __global__ void __launch_bounds__(kThreads, Tile<BN>::kCtasPerSm) mxf4_gemm_kern
                 }
                 mma_commit(&empty[st]);
             }
-            mma_commit(done);
+            __syncwarp();
         }
+        if (elect_one_sync()) mma_commit(done);
+        __syncwarp();
     } else {
         // ------------------------------------------------ scales into tensor memory
         const uint32_t quarter = warp & 3;

@@ -105,17 +105,19 @@ __global__ void __launch_bounds__(kPThreads, 1) mxf4_persist_kernel(const __grid
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // The producer and MMA warps run converged: every wait is made by the whole
+    // warp, every copy / MMA issued by one elected lane.
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
-        if (lane == 0) {
-            uint32_t g = 0;
-            bool alive = true;
-            for (uint32_t t = blockIdx.x; t < total && alive; t += gridDim.x) {
-                PTile tl;
-                ptile(p, t, tl);
-                for (uint32_t kk = 0; kk < nk; ++kk, ++g) {
-                    const uint32_t st = g % S, ph = (g / S) & 1u;
-                    if (!mbar_wait(&empty[st], ph ^ 1u, abort, p.err, 0xD01)) { alive = false; break; }
+        uint32_t g = 0;
+        bool alive = true;
+        for (uint32_t t = blockIdx.x; t < total && alive; t += gridDim.x) {
+            PTile tl;
+            ptile(p, t, tl);
+            for (uint32_t kk = 0; kk < nk; ++kk, ++g) {
+                const uint32_t st = g % S, ph = (g / S) & 1u;
+                if (!warp_wait(&empty[st], ph ^ 1u, abort, p.err, 0xD01)) { alive = false; break; }
+                if (elect_one_sync()) {
                     mbar_arrive_expect_tx(&full[st], kATile + kPBTile + kSfaBytes + kPSfbBytes);
                     const int32_t kb = (int32_t)(kk * (kBK / 2));
                     const int32_t ks = (int32_t)((NV ? kk : (kk >> 1)) * kSfRow);
@@ -126,25 +128,26 @@ __global__ void __launch_bounds__(kPThreads, 1) mxf4_persist_kernel(const __grid
                     tma_load_2d(sSb + st * kPSfbBytes, &p.tm_sb0, ks, tl.rb0, &full[st]);
                     tma_load_2d(sSb + st * kPSfbBytes + 64 * kSfRow, &p.tm_sb1, ks, tl.rb1, &full[st]);
                 }
+                __syncwarp();
             }
-            // drain: no copy may still be landing when the CTA exits
-            for (uint32_t q = (g > (uint32_t)S ? g - S : 0); q < g; ++q)
-                mbar_wait(&full[q % S], (q / S) & 1u, nullptr, p.err, 0xD02);
         }
+        // drain: no copy may still be landing when the CTA exits
+        for (uint32_t q = (g > (uint32_t)S ? g - S : 0); q < g; ++q)
+            mbar_wait(&full[q % S], (q / S) & 1u, nullptr, p.err, 0xD02);
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            uint32_t g = 0, j = 0;
-            bool alive = true;
-            for (uint32_t t = blockIdx.x; t < total && alive; t += gridDim.x, ++j) {
-                const uint32_t b = j & 1u, use = j >> 1;
-                if (!mbar_wait(&acc_empty[b], (use & 1u) ^ 1u, abort, p.err, 0xD03)) break;
+        uint32_t g = 0, j = 0;
+        bool alive = true;
+        for (uint32_t t = blockIdx.x; t < total && alive; t += gridDim.x, ++j) {
+            const uint32_t b = j & 1u, use = j >> 1;
+            if (!warp_wait(&acc_empty[b], (use & 1u) ^ 1u, abort, p.err, 0xD03)) break;
+            tc_fence_after();
+            const uint32_t acc = tmem + b * kPBN;
+            for (uint32_t kk = 0; kk < nk; ++kk, ++g) {
+                const uint32_t st = g % S, ph = (g / S) & 1u;
+                if (!warp_wait(&sf_ready[st], ph, abort, p.err, 0xD04)) { alive = false; break; }
                 tc_fence_after();
-                const uint32_t acc = tmem + b * kPBN;
-                for (uint32_t kk = 0; kk < nk; ++kk, ++g) {
-                    const uint32_t st = g % S, ph = (g / S) & 1u;
-                    if (!mbar_wait(&sf_ready[st], ph, abort, p.err, 0xD04)) { alive = false; break; }
-                    tc_fence_after();
+                if (elect_one_sync()) {
                     const uint64_t ad = smem_desc_sw128(sA + st * kATile);
                     const uint64_t bd = smem_desc_sw128(sB + st * kPBTile);
                     const uint32_t sfa0 = tmem + kRing0 + st * (kSfaCols + kSfbCols);
@@ -163,10 +166,13 @@ __global__ void __launch_bounds__(kPThreads, 1) mxf4_persist_kernel(const __grid
                     }
                     mma_commit(&empty[st]);
                 }
-                if (alive) mma_commit(&acc_full[b]);
+                __syncwarp();
             }
-            mma_commit(drain);
+            if (alive && elect_one_sync()) mma_commit(&acc_full[b]);
+            __syncwarp();
         }
+        if (elect_one_sync()) mma_commit(drain);
+        __syncwarp();
     } else if (warp < 6) {
         // ------------------------------------------------ scales into tensor memory
         const uint32_t lane_base = ((uint32_t)(warp & 3) * 32u) << 16;
