@@ -50,7 +50,11 @@ typedef enum mpp41_wfmt {
     MPP41_W_FP4 = 4,    /* E2M1 [n][k/2], unscaled */
     MPP41_W_E4M3 = 5,   /* FP8 E4M3 [n][k] */
     MPP41_W_E5M2 = 6,   /* FP8 E5M2 [n][k] */
-    MPP41_W_MXFP4 = 7   /* E2M1 [n][k/2] + E8M0 scales [n][k/32] */
+    MPP41_W_MXFP4 = 7,  /* E2M1 [n][k/2] + E8M0 scales [n][k/32] */
+    MPP41_W_E4M3_MX = 8,/* FP8 E4M3 [n][k] + E8M0 scales [n][k/32] (MXFP8, BASELINE config 2; the
+                           reference has unscaled FP8 rows only): each weight is
+                           half(value * 2^(scale - 127)) */
+    MPP41_W_E5M2_MX = 9 /* FP8 E5M2 [n][k] + E8M0 scales [n][k/32], as MPP41_W_E4M3_MX */
 } mpp41_wfmt;
 
 /* Activation (A operand) formats. */
@@ -92,6 +96,13 @@ typedef struct mpp41_mlp_desc {
  * kernel, down GEMM) instead of the fused path; scratch then also holds
  * gate and up. */
 #define MPP41_MLP_UNFUSED 0x1u
+/* Per-output-channel fp16 scales (no reference counterpart):
+ * with INT8 / INT4 / INT2 weights, sg, su and sd point to fp16 scales of the
+ * gate rows [intermediate], up rows [intermediate] and down rows [hidden]; each
+ * fp32 gate / up / down sum is multiplied by its row's scale before the SwiGLU
+ * (gate, up) or the output (down). Runs on the fused kernels for fp16
+ * activations and fp16-mid SwiGLU variants. */
+#define MPP41_MLP_ROW_SCALES 0x2u
 
 typedef struct mpp41_ctx mpp41_ctx;
 

@@ -191,7 +191,7 @@ mpp41_status check_mlp_desc(const mpp41_mlp_desc *d)
     if (d->hidden % 64 || d->intermediate % 64)
         return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "hidden and intermediate must be multiples of 64 (got %u, %u)",
                     d->hidden, d->intermediate);
-    if (d->wfmt < 0 || d->wfmt > 7) return fail(MPP41_ERR_INVALID_ARGUMENT, "bad weight format %d", d->wfmt);
+    if (d->wfmt < 0 || d->wfmt > MPP41_W_E5M2_MX) return fail(MPP41_ERR_INVALID_ARGUMENT, "bad weight format %d", d->wfmt);
     return MPP41_OK;
 }
 
@@ -273,6 +273,34 @@ mpp41_status enqueue_f32_gemm(mpp41_ctx *ctx, int wfmt, const void *a, const voi
 // mpp_mlp_swiglu_i8 (int8 mid in scratch), the down GEMM writes int32.
 bool is_i8_row(const mpp41_mlp_desc *d) { return d->afmt == MPP41_A_S8; }
 
+// MXFP8 weights or per-output-channel scales: only the
+// small-layer kernel computes them.
+bool is_scaled_row(const mpp41_mlp_desc *d)
+{
+    return d->wfmt == MPP41_W_E4M3_MX || d->wfmt == MPP41_W_E5M2_MX || (d->flags & MPP41_MLP_ROW_SCALES);
+}
+
+mpp41_status check_scaled_row(const mpp41_mlp_desc *d, const void *sg, const void *su, const void *sd)
+{
+    if (!is_scaled_row(d)) return MPP41_OK;
+    if (d->flags & MPP41_MLP_ROW_SCALES) {
+        if (d->wfmt != MPP41_W_I8 && d->wfmt != MPP41_W_I4 && d->wfmt != MPP41_W_I2)
+            return fail(MPP41_ERR_INVALID_ARGUMENT, "MPP41_MLP_ROW_SCALES needs INT8, INT4 or INT2 weights");
+    }
+    if (!sg || !su || !sd) return fail(MPP41_ERR_INVALID_ARGUMENT, "scaled weights need gate, up and down scales");
+    if (d->afmt != MPP41_A_F16 || d->epilogue == MPP41_SWIGLU_FLOAT || d->epilogue == MPP41_SWIGLU_I8 ||
+        (d->flags & MPP41_MLP_UNFUSED))
+        return fail(MPP41_ERR_MISSING_KERNEL,
+                    "MXFP8 weights and per-row scales run on the fused small-layer kernel only (fp16 "
+                    "activations, an fp16-mid SwiGLU)");
+    if (d->tokens <= 32 || !sl::covers(d->tokens, d->hidden, d->intermediate, d->wfmt))
+        return fail(MPP41_ERR_UNSUPPORTED_SHAPE,
+                    "MXFP8 weights and per-row scales run on the small-layer kernel: 33..128 tokens, hidden <= 1024 "
+                    "(a multiple of the stage K), intermediate a multiple of 8 stages (MXFP8: hidden 1024, "
+                    "intermediate 4096); got %u x %u x %u", d->tokens, d->hidden, d->intermediate);
+    return MPP41_OK;
+}
+
 mpp41_status check_i8_row(const mpp41_mlp_desc *d)
 {
     if (d->epilogue != MPP41_SWIGLU_I8 || d->out_dtype != MPP41_S32)
@@ -309,6 +337,8 @@ mpp41_status enqueue_gate_up(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void
     }
     mpp41_status s = check_fp16_row(d);
     if (s) return s;
+    if (is_scaled_row(d))
+        return fail(MPP41_ERR_MISSING_KERNEL, "MXFP8 weights and per-row scales run through mpp41_mlp only");
     if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su))
         return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate and up scales");
     const ScratchLayout SL = scratch_layout(d);
@@ -348,6 +378,8 @@ mpp41_status enqueue_down(mpp41_ctx *ctx, const mpp41_mlp_desc *d, void *scratch
     if (d->epilogue == MPP41_SWIGLU_FLOAT)   // fp32 mid: mpp_mlp_f_h_f_n128 / mpp_mlp_f_i8_f_n128
         return enqueue_f32_gemm(ctx, d->wfmt, scratch, wd, out, d->tokens, d->hidden, d->intermediate, st,
                                 "fp32-mid down GEMM");
+    if (is_scaled_row(d))
+        return fail(MPP41_ERR_MISSING_KERNEL, "MXFP8 weights and per-row scales run through mpp41_mlp only");
     if (d->wfmt == MPP41_W_MXFP4 && !sd) return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs down scales");
     const ScratchLayout SL = scratch_layout(d);
     WqLaunch dn{};
@@ -393,6 +425,9 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
     if (s) return s;
     if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su || !sd))
         return fail(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate, up and down scales");
+    s = check_scaled_row(d, sg, su, sd);
+    if (s) return s;
+    const bool scaled = is_scaled_row(d);
     const char *declined = nullptr, *declined_kernel = "";
     if (!(d->flags & MPP41_MLP_UNFUSED) && d->wfmt != MPP41_W_F16 && d->epilogue != MPP41_SWIGLU_FLOAT &&
         desc_plan(d).sync_words <= ctx->sync_words) {
@@ -409,6 +444,7 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
         L.err = ctx->err;
         L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
         L.trace = ctx->trace;
+        L.row_scales = (d->flags & MPP41_MLP_ROW_SCALES) != 0;
         const char *why = "";
         const LayerPlan plan = desc_plan(d);
         const int rc = launch_layer(plan, L, st, &why);
@@ -418,6 +454,7 @@ mpp41_status enqueue_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x,
             return MPP41_OK;
         }
         if (rc == 2) return fail(MPP41_ERR_CUDA, "fused MLP kernel: %s", why);
+        if (scaled) return fail(MPP41_ERR_UNSUPPORTED_SHAPE, "small-layer kernel declined: %s", why);
         declined = why;
         declined_kernel = layer_kernel_name(plan, L.T, L.H, L.I, L.wfmt);
     }

@@ -11,7 +11,13 @@
 namespace mpp41 {
 
 // Weight formats; values match enum mpp41_wfmt of include/mpp41.h.
-enum WFmt : int { W_F16 = 0, W_I8 = 1, W_I4 = 2, W_I2 = 3, W_FP4 = 4, W_E4M3 = 5, W_E5M2 = 6, W_MXFP4 = 7 };
+enum WFmt : int {
+    W_F16 = 0, W_I8 = 1, W_I4 = 2, W_I2 = 3, W_FP4 = 4, W_E4M3 = 5, W_E5M2 = 6, W_MXFP4 = 7,
+    W_E4M3_MX = 8, W_E5M2_MX = 9    // FP8 with an E8M0 scale per 32 weights along K (MXFP8)
+};
+
+// Formats that carry an E8M0 scale per 32 weights ([rows][k/32]).
+__host__ __device__ constexpr bool wfmt_mx(int w) { return w == W_MXFP4 || w == W_E4M3_MX || w == W_E5M2_MX; }
 
 // Bits per packed weight.
 __host__ __device__ constexpr int wfmt_bits(int w)
@@ -158,6 +164,8 @@ struct FusedLaunch {
     uint32_t *err;
     uint32_t T, H, I, splits;
     unsigned long long *trace;   // optional per-CTA phase/wait counters (profiling)
+    // sg / su / sd are fp16 per-output-row scales (INT weights; small-layer kernel only)
+    bool row_scales = false;
     // GEMM only: out[T][H] = mid[T][I] x wd[H][I]^T (down tiles, no split, no
     // gate/up phase); x / wg / wu / sg / su are not read
     bool gemm_only = false;

@@ -13,16 +13,33 @@
 namespace mpp41 {
 namespace sl {
 
+template <int W>
+static bool covers_t(uint32_t T, uint32_t H, uint32_t I)
+{
+    using F = Fmt<W>;
+    if (T == 0 || T > 2 * kNT) return false;
+    if (H % F::kSK || (uint64_t)kNT * H * 2 > kXBytes) return false;
+    const uint32_t ks = I / kSplits;
+    if (I % (kSplits * F::kSK) || ks / F::kSK > kMaxMSt || H / F::kSK > kMaxXSt) return false;
+    // the E8M0 rows staged per tile are exactly H/32 and I/8/32 bytes
+    if (F::kMx && (H / 32 != kScGRow || ks / 32 != kScDRow)) return false;
+    return true;
+}
+
 bool covers(uint32_t T, uint32_t H, uint32_t I, int wfmt)
 {
-    if (wfmt != W_MXFP4 && wfmt != W_FP4 && wfmt != W_I4) return false;
-    if (T == 0 || T > 2 * kNT) return false;
-    if (H % kSK || H > kMaxXSt * kSK) return false;
-    const uint32_t ks = I / kSplits;
-    if (I % (kSplits * kSK) || ks > kMaxMSt * kSK) return false;
-    // the E8M0 rows staged per tile are exactly H/32 and I/8/32 bytes
-    if (wfmt == W_MXFP4 && (H / 32 != kScGRow || ks / 32 != kScDRow)) return false;
-    return true;
+    switch (wfmt) {
+    case W_MXFP4: return covers_t<W_MXFP4>(T, H, I);
+    case W_FP4: return covers_t<W_FP4>(T, H, I);
+    case W_I4: return covers_t<W_I4>(T, H, I);
+    case W_I8: return covers_t<W_I8>(T, H, I);
+    case W_I2: return covers_t<W_I2>(T, H, I);
+    case W_E4M3: return covers_t<W_E4M3>(T, H, I);
+    case W_E5M2: return covers_t<W_E5M2>(T, H, I);
+    case W_E4M3_MX: return covers_t<W_E4M3_MX>(T, H, I);
+    case W_E5M2_MX: return covers_t<W_E5M2_MX>(T, H, I);
+    default: return false;   // fp16 weights are not packed
+    }
 }
 
 size_t sync_words(uint32_t T, uint32_t H)
@@ -50,16 +67,25 @@ static int launch_t(const FusedLaunch &L, cudaStream_t st, const char **why)
     // at most one G tile and one D tile per CTA
     const uint32_t grid = p.n_g > p.n_d ? p.n_g : p.n_d;
     if (!L.ws) { *why = "workspace"; return 1; }
-    const uint64_t rawH = (uint64_t)L.H / 2, rawI = (uint64_t)L.I / 2;
-    bool ok = make_map_kblocks(&p.tm_x, L.x, L.H, L.T, kNT, kSK / 64) &&
-              make_map_kblocks(&p.tm_mid, L.mid, L.I, L.T, kNT, kSK / 64) &&
-              make_map(&p.tm_wg, L.wg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, 128, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
-              make_map(&p.tm_wu, L.wu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, 128, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
-              make_map(&p.tm_wd, L.wd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawI, L.H, 128, kRows, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (ok && W == W_MXFP4)
+    using F = Fmt<W>;
+    const uint64_t rawH = (uint64_t)L.H * F::kBits / 8, rawI = (uint64_t)L.I * F::kBits / 8;
+    const CUtensorMapSwizzle wsw = F::kSw ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    bool ok = make_map_kblocks(&p.tm_x, L.x, L.H, L.T, kNT, F::kSK / 64) &&
+              make_map_kblocks(&p.tm_mid, L.mid, L.I, L.T, kNT, F::kSK / 64) &&
+              make_map(&p.tm_wg, L.wg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, F::kRowB, kGCh, wsw) &&
+              make_map(&p.tm_wu, L.wu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawH, L.I, F::kRowB, kGCh, wsw) &&
+              make_map(&p.tm_wd, L.wd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawI, L.H, F::kRowB, kRows, wsw);
+    if (ok && F::kMx)
         ok = make_map(&p.tm_sg, L.sg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, kScGRow, kGCh, CU_TENSOR_MAP_SWIZZLE_NONE) &&
              make_map(&p.tm_su, L.su, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.H / 32, L.I, kScGRow, kGCh, CU_TENSOR_MAP_SWIZZLE_NONE) &&
              make_map(&p.tm_sd, L.sd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, L.I / 32, L.H, kScDRow, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (L.row_scales) {
+        if (W != W_I8 && W != W_I4 && W != W_I2) { *why = "per-row scales need INT8/INT4/INT2 weights"; return 1; }
+        if (!L.sg || !L.su || !L.sd) { *why = "per-row scales need gate, up and down scale vectors"; return 1; }
+        p.rs_g = reinterpret_cast<const __half *>(L.sg);
+        p.rs_u = reinterpret_cast<const __half *>(L.su);
+        p.rs_d = reinterpret_cast<const __half *>(L.sd);
+    }
     if (!ok) { *why = "tensor maps (16-byte aligned bases and row pitches needed)"; return 1; }
     p.mid = static_cast<__half *>(L.mid);
     p.out = L.out;
@@ -137,6 +163,12 @@ int launch(const FusedLaunch &L, cudaStream_t st, const char **why)
     case W_FP4: return launch_w<W_FP4>(L, st, why);
     case W_I4: return launch_w<W_I4>(L, st, why);
     case W_MXFP4: return launch_w<W_MXFP4>(L, st, why);
+    case W_I8: return launch_w<W_I8>(L, st, why);
+    case W_I2: return launch_w<W_I2>(L, st, why);
+    case W_E4M3: return launch_w<W_E4M3>(L, st, why);
+    case W_E5M2: return launch_w<W_E5M2>(L, st, why);
+    case W_E4M3_MX: return launch_w<W_E4M3_MX>(L, st, why);
+    case W_E5M2_MX: return launch_w<W_E5M2_MX>(L, st, why);
     default: *why = "weight format not covered by the small-layer kernel"; return 1;
     }
 }

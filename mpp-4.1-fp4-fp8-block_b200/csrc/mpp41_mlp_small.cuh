@@ -61,37 +61,55 @@ constexpr int kEpi = kDecWarps * 32;
 constexpr uint32_t kNT = 64;         // tokens per tile (MMA N)
 constexpr uint32_t kRows = 128;      // weight rows per tile (MMA M)
 constexpr uint32_t kGCh = 64;        // channels per G tile
-constexpr uint32_t kSK = 256;        // K per stage
-constexpr uint32_t kWSlots = 4;      // packed-weight ring (shared memory)
-constexpr uint32_t kASlots = 3;      // decoded-operand ring (tensor memory)
-constexpr uint32_t kMaxXSt = 4;      // x stages (H <= 1024)
-constexpr uint32_t kMaxMSt = 2;      // mid stages (I / 8 <= 512)
-constexpr uint32_t kActStage = kNT * 2 * kSK;            // 32 KB: 4 swizzle atoms of 64 rows x 128 B
-constexpr uint32_t kAtom = kNT * 128;                    // 8 KB
-constexpr uint32_t kWStage = kRows * 128;                // 16 KB of packed 4-bit weights
+constexpr uint32_t kXBytes = 128u << 10;   // activation region: the x slice (64 tokens x H <= 1024), later mid
+constexpr uint32_t kWBytes = 64u << 10;    // packed-weight ring
+constexpr uint32_t kMaxXSt = 8, kMaxMSt = 4, kMaxWSlots = 8, kMaxASlots = 6;   // barrier array sizes
+constexpr uint32_t kAtom = kNT * 128;                    // 8 KB: 64 rows x 64 fp16 (one 128-byte swizzle atom)
 constexpr uint32_t kScGRow = 32, kScDRow = 16;           // E8M0 bytes per row (H/32, I/8/32)
 constexpr uint32_t kBand = kRows / kSplits;              // output rows each split sums (16)
 // TMEM columns: G accumulator, D accumulator, then the operand ring
-constexpr uint32_t kTmemCols = 512, kGAcc = 0, kDAcc = 64, kACol0 = 128, kASlotCols = kSK / 2;
+constexpr uint32_t kTmemCols = 512, kGAcc = 0, kDAcc = 64, kACol0 = 128;
+
+// Per-format stage geometry. A stage covers the K whose packed bytes fill one
+// 128-byte row (64 bytes for 2-bit weights): 256 K for 4-bit, 128 K for 8-bit
+// and 256 K for 2-bit formats.
+template <int W>
+struct Fmt {
+    static constexpr int kBits = wfmt_bits(W);
+    static constexpr bool kMx = wfmt_mx(W);
+    static constexpr uint32_t kRowB = kBits == 2 ? 64u : 128u;            // packed bytes per row per stage
+    static constexpr uint32_t kSK = kRowB * 8u / (uint32_t)kBits;         // K per stage
+    static constexpr bool kSw = kRowB == 128u;                            // 128-byte swizzled weight rows
+    static constexpr uint32_t kWStage = kRows * kRowB;
+    static constexpr uint32_t kWSlots = kWBytes / kWStage;
+    static constexpr uint32_t kASlotCols = kSK / 2;                       // fp16 pairs per TMEM column
+    static constexpr uint32_t kASlots =
+        (kTmemCols - kACol0) / kASlotCols > kMaxASlots ? kMaxASlots : (kTmemCols - kACol0) / kASlotCols;
+    static constexpr uint32_t kActStage = kNT * 2 * kSK;                  // x / mid bytes per stage
+    static constexpr uint32_t kBlk = kSK / 128;                           // 32-weight blocks per decode thread
+    static constexpr uint32_t kBlkB = 32u * (uint32_t)kBits / 8u;         // packed bytes per block
+    static_assert(kWSlots <= kMaxWSlots && kASlots >= 2 && kBlk >= 1, "stage geometry");
+};
+
 // shared memory (offsets from a 1024-aligned base)
 constexpr uint32_t kOffX = 0;
-constexpr uint32_t kOffW = kOffX + kMaxXSt * kActStage;
-constexpr uint32_t kOffScG = kOffW + kWSlots * kWStage;
+constexpr uint32_t kOffW = kOffX + kXBytes;
+constexpr uint32_t kOffScG = kOffW + kWBytes;
 constexpr uint32_t kOffScD = kOffScG + kRows * kScGRow;
 constexpr uint32_t kOffMid = kOffScD + kRows * kScDRow;
 constexpr uint32_t kOffBar = kOffMid + kNT * kGCh * 2;
 constexpr uint32_t kSmem = 1024 + kOffBar + 256;
 static_assert(kSmem <= 227u * 1024u, "shared memory");
-static_assert(kASlots * kASlotCols + kACol0 <= kTmemCols, "tensor memory");
 
 struct Params {
-    CUtensorMap tm_x;           // x [T][H] fp16 as [H/64][T][64], box {64, 64, 4}, SW128
-    CUtensorMap tm_mid;         // mid [T][I] fp16 as [I/64][T][64], box {64, 64, 4}, SW128
-    CUtensorMap tm_wg, tm_wu;   // packed [I][H/2], box {128, 64}, SW128
-    CUtensorMap tm_wd;          // packed [H][I/2], box {128, 128}, SW128
+    CUtensorMap tm_x;           // x [T][H] fp16 as [H/64][T][64], box {64, 64, kSK/64}, SW128
+    CUtensorMap tm_mid;         // mid [T][I] fp16 as [I/64][T][64], box {64, 64, kSK/64}, SW128
+    CUtensorMap tm_wg, tm_wu;   // packed [I][H*bits/8], box {kRowB, 64} (SW128 when kRowB = 128)
+    CUtensorMap tm_wd;          // packed [H][I*bits/8], box {kRowB, 128}
     CUtensorMap tm_sg, tm_su;   // E8M0 [I][H/32], box {32, 64}
     CUtensorMap tm_sd;          // E8M0 [H][I/32], box {16, 128}
     __half *mid;
+    const __half *rs_g, *rs_u, *rs_d;   // per-output-channel scales (row-scaled INT weights) or null
     void *out;                  // fp32 or fp16 [T][H]
     float *ws;                  // fp32 partials [n_h * H/128 tiles][8 splits][64 tokens][128 rows]
     uint32_t *sync;             // [0] finished CTAs, [1 + h*8 + s] finished G tiles,
@@ -198,7 +216,9 @@ __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16])
 template <int W, int EG, bool OUT_F16>
 __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_constant__ Params p)
 {
-    static_assert(wfmt_bits(W) == 4, "4-bit weight formats only");
+    using F = Fmt<W>;
+    constexpr uint32_t kSK = F::kSK, kWSlots = F::kWSlots, kASlots = F::kASlots, kActStage = F::kActStage;
+    constexpr uint32_t kWStage = F::kWStage, kASlotCols = F::kASlotCols, kRowB = F::kRowB;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sX = smem + kOffX;
@@ -210,10 +230,10 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
     uint64_t *x_full = bars;                        // [kMaxXSt]
     uint64_t *m_full = x_full + kMaxXSt;            // [kMaxMSt]
     uint64_t *w_full = m_full + kMaxMSt;            // [kWSlots]
-    uint64_t *w_empty = w_full + kWSlots;           // [kWSlots] decode warps done with a slot
-    uint64_t *a_full = w_empty + kWSlots;           // [kASlots] decoded operand in TMEM
-    uint64_t *a_empty = a_full + kASlots;           // [kASlots] MMAs reading it completed
-    uint64_t *sc_full = a_empty + kASlots;
+    uint64_t *w_empty = w_full + kMaxWSlots;        // [kWSlots] decode warps done with a slot
+    uint64_t *a_full = w_empty + kMaxWSlots;        // [kASlots] decoded operand in TMEM
+    uint64_t *a_empty = a_full + kMaxASlots;        // [kASlots] MMAs reading it completed
+    uint64_t *sc_full = a_empty + kMaxASlots;
     uint64_t *g_done = sc_full + 1;                 // G accumulator complete (x no longer read)
     uint64_t *d_done = g_done + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(d_done + 1);
@@ -260,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
         tma_prefetch_desc(&p.tm_wg);
         tma_prefetch_desc(&p.tm_wu);
         tma_prefetch_desc(&p.tm_wd);
-        if (W == W_MXFP4) {
+        if (F::kMx) {
             tma_prefetch_desc(&p.tm_sg);
             tma_prefetch_desc(&p.tm_su);
             tma_prefetch_desc(&p.tm_sd);
@@ -284,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
     // elected lane, every wait is made by the whole warp.
     if (warp == kWWarp) {
         // ------------------------------------------------ packed weights and scales
-        if (W == W_MXFP4 && elect_one_sync()) {
+        if (F::kMx && elect_one_sync()) {
             mbar_arrive_expect_tx(sc_full, (has_g ? kRows * kScGRow : 0u) + (has_d ? kRows * kScDRow : 0u));
             if (has_g) {
                 tma_load_2d(smem + kOffScG, &p.tm_sg, 0, (int32_t)(gw * kGCh), sc_full);
@@ -306,11 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
                 mbar_arrive_expect_tx(&w_full[sl], kWStage);
                 uint8_t *dst = sW + sl * kWStage;
                 if (i < nG) {
-                    const int32_t kx = (int32_t)(i * kSK / 2);
+                    const int32_t kx = (int32_t)(i * kRowB);
                     tma_load_2d(dst, &p.tm_wg, kx, (int32_t)(gw * kGCh), &w_full[sl]);
-                    tma_load_2d(dst + kGCh * 128, &p.tm_wu, kx, (int32_t)(gw * kGCh), &w_full[sl]);
+                    tma_load_2d(dst + kGCh * kRowB, &p.tm_wu, kx, (int32_t)(gw * kGCh), &w_full[sl]);
                 } else {
-                    const int32_t kx = (int32_t)((ds * KS + (i - nG) * kSK) / 2);
+                    const int32_t kx = (int32_t)((ds * KS + (i - nG) * kSK) * F::kBits / 8);
                     tma_load_2d(dst, &p.tm_wd, kx, (int32_t)(dm * kRows), &w_full[sl]);
                 }
             }
@@ -320,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
         if (ok)
             for (uint32_t i = (n > kWSlots ? n - kWSlots : 0); i < n; ++i)
                 mbar_wait(&w_full[i % kWSlots], (i / kWSlots) & 1u, nullptr, p.err, 0xC02);
-        if (W == W_MXFP4) mbar_wait(sc_full, 0, nullptr, p.err, 0xC03);
+        if (F::kMx) mbar_wait(sc_full, 0, nullptr, p.err, 0xC03);
     } else if (warp == kXWarp) {
         // ------------------------------------------------ activations
         pdl_wait_prior();   // x and the counters come from / are reset by the previous kernel
@@ -389,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
         const uint32_t r = q * 32 + lane;               // TMEM lane = weight row of the tile
         const uint32_t lane_base = (q * 32u) << 16;
         bool ok = true;
-        if (W == W_MXFP4) ok = mbar_wait(sc_full, 0, abort, p.err, 0xC31);
+        if (F::kMx) ok = mbar_wait(sc_full, 0, abort, p.err, 0xC31);
         // ---------------------------------------------- G epilogue: SwiGLU -> fp16 mid
         // Runs once, inside the decode loop before the first D stage: the D
         // weights are decoded while other CTAs' G tiles finish (the D MMAs wait
@@ -405,6 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
                 uint32_t v[16];
                 tmem_ld_x16(tmem + lane_base + kGAcc + kq * 16, v);
                 tmem_ld_wait();
+                if (p.rs_g) {   // per-output-channel scale of this lane's gate / up row
+                    const float sc = __half2float(((r & 1u) ? p.rs_u : p.rs_g)[gw * kGCh + (r >> 1)]);
+#pragma unroll
+                    for (uint32_t t = 0; t < 16; ++t) v[t] = __float_as_uint(__uint_as_float(v[t]) * sc);
+                }
                 // lane pair (2j, 2j+1) = (gate, up) of channel j: the even lane
                 // finishes tokens 0..7 of this warp's 16, the odd lane 8..15
                 const uint32_t j = r >> 1, is_up = lane & 1u;
@@ -450,18 +475,28 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
             if (tr && te == 0 && i < 8) tr[TR_DEC_GO + i] = (unsigned long long)(clock64() - clk0);
             // packed row of the slot: G rows interleave gate (even lanes) and up (odd lanes)
             const uint32_t rr = g ? ((r & 1u) ? kGCh + (r >> 1) : (r >> 1)) : r;
-            const uint8_t *rowp = sW + wsl * kWStage + rr * 128;
+            const uint8_t *rowp = sW + wsl * kWStage + rr * kRowB;
             const uint8_t *scp = g ? sScG + rr * kScGRow + s * (kSK / 32) : sScD + rr * kScDRow + s * (kSK / 32);
-            const uint32_t col = tmem + lane_base + kACol0 + asl * kASlotCols + kq * 32;
+            const uint32_t col = tmem + lane_base + kACol0 + asl * kASlotCols;
 #pragma unroll
-            for (uint32_t b = 0; b < 2; ++b) {
-                const uint32_t c16 = kq * 2 + b;   // 16-byte chunk of the 128-byte row (32 weights)
-                const uint4 v = *reinterpret_cast<const uint4 *>(rowp + ((c16 ^ (rr & 7u)) << 4));
-                const uint32_t wr[8] = {v.x, v.y, v.z, v.w, 0u, 0u, 0u, 0u};
-                const uint32_t sb = (W == W_MXFP4) ? scp[c16] : 127u;
+            for (uint32_t b = 0; b < F::kBlk; ++b) {
+                const uint32_t blk = kq * F::kBlk + b;   // 32-weight block of the stage
+                uint32_t wr[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+                if constexpr (F::kBits == 2) {
+                    const uint2 v = *reinterpret_cast<const uint2 *>(rowp + blk * F::kBlkB);
+                    wr[0] = v.x; wr[1] = v.y;
+                } else {
+#pragma unroll
+                    for (uint32_t c = 0; c < F::kBlkB / 16; ++c) {
+                        const uint32_t c16 = blk * (F::kBlkB / 16) + c;   // 16-byte chunk of the 128-byte row
+                        const uint4 v = *reinterpret_cast<const uint4 *>(rowp + ((c16 ^ (rr & 7u)) << 4));
+                        wr[4 * c] = v.x; wr[4 * c + 1] = v.y; wr[4 * c + 2] = v.z; wr[4 * c + 3] = v.w;
+                    }
+                }
+                const uint32_t sb = F::kMx ? scp[blk] : 127u;
                 uint32_t o[16];
                 decode_words<W>(wr, sb, o);
-                tmem_st_x16(col + b * 16, o);
+                tmem_st_x16(col + blk * 16, o);
             }
             tmem_st_wait();
             tc_fence_before();
@@ -514,6 +549,10 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_small_kernel(const __grid_con
                     a.x += b.x; a.y += b.y;
                 }
                 const uint32_t gtok = dh * kNT + tok, hcol = dm * kRows + r2;
+                if (p.rs_d) {
+                    a.x *= __half2float(p.rs_d[hcol]);
+                    a.y *= __half2float(p.rs_d[hcol + 1]);
+                }
                 if (gtok < p.T) {
                     if constexpr (OUT_F16)
                         *reinterpret_cast<__half2 *>(static_cast<__half *>(p.out) + (size_t)gtok * p.H + hcol) =

@@ -105,15 +105,16 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
     if (!d) return err(MPP41_ERR_INVALID_ARGUMENT, "null descriptor");
     if (!x || !wg || !wu || !wd || !out) return err(MPP41_ERR_INVALID_ARGUMENT, "null buffer");
     if (!d->tokens || !d->hidden || !d->intermediate) return err(MPP41_ERR_INVALID_ARGUMENT, "sizes must be positive");
-    if (d->afmt != MPP41_A_F16 || d->wfmt == MPP41_W_F16 || d->wfmt < 0 || d->wfmt > MPP41_W_MXFP4)
+    if (d->afmt != MPP41_A_F16 || d->wfmt == MPP41_W_F16 || d->wfmt < 0 || d->wfmt > MPP41_W_E5M2_MX)
         return err(MPP41_ERR_MISSING_KERNEL, "mpp41_mlp_noalloc covers fp16 activations with packed weights only");
     if (d->epilogue != MPP41_SWIGLU_HALF && d->epilogue != MPP41_SWIGLU_HALF_FROM_HALF &&
         d->epilogue != MPP41_SWIGLU_FP32)
         return err(MPP41_ERR_MISSING_KERNEL, "mpp41_mlp_noalloc needs an fp16-mid SwiGLU variant");
     if (d->out_dtype != MPP41_F32 && d->out_dtype != MPP41_F16)
         return err(MPP41_ERR_INVALID_ARGUMENT, "output dtype must be F32 or F16");
-    if (d->wfmt == MPP41_W_MXFP4 && (!sg || !su || !sd))
-        return err(MPP41_ERR_INVALID_ARGUMENT, "MXFP4 needs gate, up and down scales");
+    const bool scaled = d->wfmt == MPP41_W_E4M3_MX || d->wfmt == MPP41_W_E5M2_MX || (d->flags & MPP41_MLP_ROW_SCALES);
+    if ((d->wfmt == MPP41_W_MXFP4 || scaled) && (!sg || !su || !sd))
+        return err(MPP41_ERR_INVALID_ARGUMENT, "scaled weights need gate, up and down scales");
     const size_t need = mpp41_mlp_noalloc_scratch_bytes(d);
     if (need > MPP41_NOALLOC_SCRATCH_BYTES)
         return err(MPP41_ERR_UNSUPPORTED_SHAPE,
@@ -122,6 +123,9 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
                    "caller-allocated buffer",
                    need, (unsigned)MPP41_NOALLOC_SCRATCH_BYTES);
     const LayerPlan plan = noalloc_plan(d);
+    if (scaled && !plan.small)
+        return err(MPP41_ERR_UNSUPPORTED_SHAPE,
+                   "MXFP8 weights and per-row scales run on the small-layer kernel (33..128 tokens, hidden <= 1024)");
     if (plan.sync_words > kSyncWords)
         return err(MPP41_ERR_UNSUPPORTED_SHAPE, "too many output tiles for the static counters");
     int dev = 0;
@@ -150,6 +154,7 @@ extern "C" mpp41_status mpp41_mlp_noalloc(const mpp41_mlp_desc *d, const void *x
     L.sync = P.sync;
     L.err = P.err;
     L.T = d->tokens; L.H = d->hidden; L.I = d->intermediate;
+    L.row_scales = (d->flags & MPP41_MLP_ROW_SCALES) != 0;
     const char *why = "";
     const int rc = launch_layer(plan, L, st, &why);
     if (rc == 1) return err(MPP41_ERR_UNSUPPORTED_SHAPE, "mpp41_mlp_noalloc: %s", why);

@@ -169,6 +169,27 @@ __device__ __forceinline__ void decode_words(const uint32_t (&wr)[8], uint32_t s
                 o[8 * q + 2 * i + 1] = hsub2_bits(b, 0x64806480u);
             }
         }
+    } else if constexpr (W == W_E4M3_MX || W == W_E5M2_MX) {
+        // FP8 bytes decoded exactly (as below), then value * 2^(s-127) rounded
+        // once to fp16: one fp16 multiply by an exactly representable power of
+        // two (both operands exact, so RN(product) = half(value * scale)), else
+        // fp32 math and a single rounding -- the rule of mxfp4_dequant_*_half.
+        decode_words<W == W_E4M3_MX ? W_E4M3 : W_E5M2>(wr, 127u, o);
+        const uint32_t s = scale_byte;
+        if (s >= 113u && s <= 142u) {
+            if (s != 127u) {
+                const uint32_t f = ((s - 112u) << 10) * 0x10001u;   // 2^(s-127) as fp16x2
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] = hmul2_bits(o[i], f);
+            }
+        } else {
+            const float sf = e8m0_to_float(s);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                __half2 h = *reinterpret_cast<__half2 *>(&o[i]);
+                o[i] = half2_bits(__low2float(h) * sf, __high2float(h) * sf);
+            }
+        }
     } else if constexpr (W == W_E4M3) {
 #pragma unroll
         for (int q = 0; q < 2; ++q) {

@@ -25,11 +25,12 @@ HEADER = os.path.join(ROOT, "include", "mpp41.h")
 
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED_SHAPE, ERR_NO_DEVICE, ERR_MISSING_KERNEL, ERR_OUT_OF_MEMORY, \
     ERR_CUDA, ERR_TIMEOUT, ERR_BOUNDS, ERR_COMM = range(10)
-W_F16, W_I8, W_I4, W_I2, W_FP4, W_E4M3, W_E5M2, W_MXFP4 = range(8)
+W_F16, W_I8, W_I4, W_I2, W_FP4, W_E4M3, W_E5M2, W_MXFP4, W_E4M3_MX, W_E5M2_MX = range(10)
 A_F16, A_S8 = 0, 1
 SWIGLU_FLOAT, SWIGLU_HALF, SWIGLU_HALF_FROM_HALF, SWIGLU_I8, SWIGLU_FP32 = range(5)
 F32, F16, S32, S8 = range(4)
 MLP_UNFUSED = 0x1
+MLP_ROW_SCALES = 0x2
 FMT_E2M1, FMT_E4M3, FMT_E5M2 = 0, 1, 2
 
 

@@ -279,6 +279,14 @@ void orc_decode_weights(int wfmt, const void *w, const uint8_t *scales,
                 v = e * s;
                 break;
             }
+            case ORC_W_E4M3_MX:
+            case ORC_W_E5M2_MX: {
+                const uint8_t c = b[(size_t)r * depth + k];
+                const float e = wfmt == ORC_W_E4M3_MX ? orc_e4m3_decode(c) : orc_e5m2_decode(c);
+                const float s = orc_e8m0_decode(scales[(size_t)r * (depth / 32) + k / 32]);
+                v = orc_half_to_float(orc_float_to_half(e * s));   /* e * 2^n is exact in fp32 */
+                break;
+            }
             default: v = 0.0;
             }
             o[k] = v;
@@ -365,11 +373,45 @@ int8_t orc_swiglu_i8(int32_t g, int32_t u)
 /* Whole MLP row: gate GEMM, up GEMM, swiglu, down GEMM                 */
 /* (encodeMPPMLP main.swift:2636-2722, encodeMXFP4FusedMLP 2033-2135).  */
 /* ------------------------------------------------------------------ */
+static void mlp_impl(int act, int wfmt, int epi, int out_kind,
+                     uint32_t T, uint32_t H, uint32_t I,
+                     const void *x, const void *wg, const void *wu, const void *wd,
+                     const uint8_t *sg, const uint8_t *su, const uint8_t *sd,
+                     const uint16_t *rsg, const uint16_t *rsu, const uint16_t *rsd,
+                     void *mid_out, void *out);
+
 void orc_mlp(int act, int wfmt, int epi, int out_kind,
              uint32_t T, uint32_t H, uint32_t I,
              const void *x, const void *wg, const void *wu, const void *wd,
              const uint8_t *sg, const uint8_t *su, const uint8_t *sd,
              void *mid_out, void *out)
+{
+    mlp_impl(act, wfmt, epi, out_kind, T, H, I, x, wg, wu, wd, sg, su, sd, NULL, NULL, NULL, mid_out, out);
+}
+
+void orc_mlp_row_scaled(int wfmt, int epi, int out_kind,
+                        uint32_t T, uint32_t H, uint32_t I,
+                        const void *x, const void *wg, const void *wu, const void *wd,
+                        const uint16_t *sg, const uint16_t *su, const uint16_t *sd,
+                        void *mid_out, void *out)
+{
+    mlp_impl(0, wfmt, epi, out_kind, T, H, I, x, wg, wu, wd, NULL, NULL, NULL, sg, su, sd, mid_out, out);
+}
+
+/* Per-output-channel scale (fp16) of column c applied to an exact sum. */
+static void scale_columns(double *m, uint32_t rows, uint32_t cols, const uint16_t *scale)
+{
+    if (!scale) return;
+    for (uint32_t r = 0; r < rows; ++r)
+        for (uint32_t c = 0; c < cols; ++c) m[(size_t)r * cols + c] *= orc_half_to_float(scale[c]);
+}
+
+static void mlp_impl(int act, int wfmt, int epi, int out_kind,
+                     uint32_t T, uint32_t H, uint32_t I,
+                     const void *x, const void *wg, const void *wu, const void *wd,
+                     const uint8_t *sg, const uint8_t *su, const uint8_t *sd,
+                     const uint16_t *rsg, const uint16_t *rsu, const uint16_t *rsd,
+                     void *mid_out, void *out)
 {
     double *xd = malloc(sizeof(double) * (size_t)T * H);
     double *w = malloc(sizeof(double) * (size_t)I * H);
@@ -385,6 +427,8 @@ void orc_mlp(int act, int wfmt, int epi, int out_kind,
     orc_gemm_f64(xd, w, gate, T, I, H);
     orc_decode_weights(wfmt, wu, su, I, H, w);
     orc_gemm_f64(xd, w, up, T, I, H);
+    scale_columns(gate, T, I, rsg);
+    scale_columns(up, T, I, rsu);
 
     for (size_t i = 0; i < (size_t)T * I; ++i) {
         switch (epi) {
@@ -424,6 +468,7 @@ void orc_mlp(int act, int wfmt, int epi, int out_kind,
 
     orc_decode_weights(wfmt, wd, sd, H, I, w);
     orc_gemm_f64(mid, w, o, T, H, I);
+    scale_columns(o, T, H, rsd);
     for (size_t i = 0; i < (size_t)T * H; ++i) {
         if (out_kind == 0) ((float *)out)[i] = (float)o[i];
         else if (out_kind == 1) ((uint16_t *)out)[i] = dbl_to_half(o[i]);

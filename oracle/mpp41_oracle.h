@@ -50,10 +50,15 @@ void orc_unpack(int fmt, const uint8_t *packed, size_t n, float *out);
 /* ---- weight formats (shared with include/mpp41.h) ---- */
 enum {
     ORC_W_F16 = 0, ORC_W_I8 = 1, ORC_W_I4 = 2, ORC_W_I2 = 3,
-    ORC_W_FP4 = 4, ORC_W_E4M3 = 5, ORC_W_E5M2 = 6, ORC_W_MXFP4 = 7
+    ORC_W_FP4 = 4, ORC_W_E4M3 = 5, ORC_W_E5M2 = 6, ORC_W_MXFP4 = 7,
+    ORC_W_E4M3_MX = 8, ORC_W_E5M2_MX = 9
 };
 /* Decode a weight matrix stored [rows][depth] (depth = K, contiguous) into
- * doubles. scales is [rows][depth/32] E8M0 and only read for ORC_W_MXFP4. */
+ * doubles. scales is [rows][depth/32] E8M0 and only read for ORC_W_MXFP4 and
+ * the MXFP8 formats ORC_W_E4M3_MX / ORC_W_E5M2_MX, whose weights are
+ * half(value * 2^(scale - 127)) (the fp16 dequantization rule of
+ * mxfp4_dequant_*_half, MXFP4Kernels.metal:509-564, applied to FP8 elements;
+ * the reference has unscaled FP8 rows only). */
 void orc_decode_weights(int wfmt, const void *w, const uint8_t *scales,
                         uint32_t rows, uint32_t depth, double *out);
 
@@ -86,6 +91,15 @@ void orc_mlp(int act, int wfmt, int epi, int out_kind,
              const void *x, const void *wg, const void *wu, const void *wd,
              const uint8_t *sg, const uint8_t *su, const uint8_t *sd,
              void *mid_out, void *out);
+/* As orc_mlp with per-output-channel fp16 scales (INT
+ * weights; no reference counterpart): sg / su / sd are fp16 [intermediate],
+ * [intermediate], [hidden]; gate[t][c] = sg[c] * sum_k x[t][k] Wg[c][k] (and
+ * up, down alike), each exact sum scaled before its rounding / SwiGLU. */
+void orc_mlp_row_scaled(int wfmt, int epi, int out_kind,
+                        uint32_t tokens, uint32_t hidden, uint32_t intermediate,
+                        const void *x, const void *wg, const void *wu, const void *wd,
+                        const uint16_t *sg, const uint16_t *su, const uint16_t *sd,
+                        void *mid_out, void *out);
 
 /* OCP-MX fp32 -> MXFP4 quantizer (E2M1 [rows][depth/2], E8M0 [rows][depth/32]). */
 void orc_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales);

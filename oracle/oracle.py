@@ -17,7 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 
 # weight formats (match include/mpp41.h enum mpp41_wfmt)
-W_F16, W_I8, W_I4, W_I2, W_FP4, W_E4M3, W_E5M2, W_MXFP4 = range(8)
+W_F16, W_I8, W_I4, W_I2, W_FP4, W_E4M3, W_E5M2, W_MXFP4, W_E4M3_MX, W_E5M2_MX = range(10)
 
 # reference seeds, main.swift:611-638 (MLP) and 409-413 (big matmul)
 MLP_SEEDS = {
@@ -62,6 +62,7 @@ def lib() -> C.CDLL:
         L.orc_mxfp4_dequant_half.argtypes = [vp, vp, vp, u32, u32]
         L.orc_gemm_f64.argtypes = [vp, vp, vp, u32, u32, u32]
         L.orc_mlp.argtypes = [C.c_int] * 4 + [u32] * 3 + [vp] * 9
+        L.orc_mlp_row_scaled.argtypes = [C.c_int] * 3 + [u32] * 3 + [vp] * 9
         L.orc_mlp_mxfp4_cpu.argtypes = [u32] * 3 + [vp] * 8 + [C.c_int, u32, u32, C.c_int]
         L.orc_quantize_mxfp4.argtypes = [vp, u32, u32, vp, vp]
         L.orc_quantize_nvfp4.argtypes = [vp, u32, u32, vp, vp, vp]
@@ -149,17 +150,60 @@ def mxfp4_dequant_half(packed, scales, rows, depth) -> np.ndarray:
     return out.view(np.float16)
 
 
-def mlp(act, wfmt, epi, out_kind, T, H, I, x, wg, wu, wd, sg=None, su=None, sd=None):
-    """Returns (mid, out) of one MLP row, fp64-exact GEMMs (see mpp41_oracle.h)."""
+def mlp(act, wfmt, epi, out_kind, T, H, I, x, wg, wu, wd, sg=None, su=None, sd=None, row_scales=False):
+    """Returns (mid, out) of one MLP row, fp64-exact GEMMs (see mpp41_oracle.h).
+    row_scales: sg / su / sd are fp16 per-output-channel scales (INT weights)."""
     mid_dt = {0: np.float32, 1: np.float16, 2: np.float16, 3: np.int8, 4: np.float16}[epi]
     out_dt = {0: np.float32, 1: np.float16, 2: np.int32}[out_kind]
     mid = np.empty((T, I), mid_dt)
     out = np.empty((T, H), out_dt)
     ps = [(_p(np.ascontiguousarray(a)) if a is not None else None) for a in (sg, su, sd)]
-    lib().orc_mlp(act, wfmt, epi, out_kind, T, H, I, _p(np.ascontiguousarray(x)),
-                  _p(np.ascontiguousarray(wg)), _p(np.ascontiguousarray(wu)),
-                  _p(np.ascontiguousarray(wd)), *ps, _p(mid), _p(out))
+    args = (T, H, I, _p(np.ascontiguousarray(x)), _p(np.ascontiguousarray(wg)), _p(np.ascontiguousarray(wu)),
+            _p(np.ascontiguousarray(wd)), *ps, _p(mid), _p(out))
+    if row_scales:
+        lib().orc_mlp_row_scaled(wfmt, epi, out_kind, *args)
+    else:
+        lib().orc_mlp(act, wfmt, epi, out_kind, *args)
     return mid, out
+
+
+INT_QMAX = {W_I8: 127, W_I4: 7, W_I2: 1}
+
+
+def quantize_int_rowscale(w: np.ndarray, wfmt: int):
+    """Per-output-row symmetric integer weights with an fp16 scale (BASELINE
+    config 2's INT rows): s = half(amax / qmax) (1 for an all-zero row),
+    q = clip(rint(w / s), -qmax - 1, qmax), packed in the reference layouts
+    (INT8 bytes; INT4 low nibble = even k; INT2 LSB pair first). Returns
+    (packed, fp16 scales)."""
+    w = np.asarray(w, np.float32)
+    qmax = INT_QMAX[wfmt]
+    s = (np.abs(w).max(axis=1) / qmax).astype(np.float16)
+    s[s == 0] = np.float16(1.0)
+    q = np.clip(np.rint(w / s.astype(np.float32)[:, None]), -qmax - 1, qmax).astype(np.int32)
+    if wfmt == W_I8:
+        return q.astype(np.int8), s
+    if wfmt == W_I4:
+        n = (q & 0xF).astype(np.uint8)
+        return (n[:, 0::2] | (n[:, 1::2] << 4)).astype(np.uint8), s
+    n = (q & 0x3).astype(np.uint8)
+    return (n[:, 0::4] | (n[:, 1::4] << 2) | (n[:, 2::4] << 4) | (n[:, 3::4] << 6)).astype(np.uint8), s
+
+
+def quantize_mxfp8(w: np.ndarray, e5m2: bool = False):
+    """OCP-MX style FP8 with an E8M0 scale per 32 along K (BASELINE config 2's
+    FP8 rows): e = floor(log2(block amax)) - emax (8 for E4M3, 15 for E5M2),
+    elements = RNE-saturated encode(w / 2^e). Returns (bytes [rows][depth],
+    scales [rows][depth/32])."""
+    w = np.asarray(w, np.float32)
+    rows, depth = w.shape
+    blk = w.reshape(rows, depth // 32, 32)
+    amax = np.abs(blk).max(axis=2)
+    e = np.where(amax > 0, np.floor(np.log2(np.where(amax > 0, amax, 1.0))) - (15 if e5m2 else 8), -127)
+    e = np.clip(e, -127, 127).astype(np.int32)
+    scaled = (blk / np.exp2(e.astype(np.float64))[:, :, None]).astype(np.float32).reshape(-1)
+    packed = pack(2 if e5m2 else 1, scaled).reshape(rows, depth)
+    return packed, (e + 127).astype(np.uint8)
 
 
 def swiglu(kind: int, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
