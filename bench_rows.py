@@ -85,14 +85,99 @@ def timed(ctx, st, run, once):
     return sorted(ts)[2]
 
 
+# BASELINE config 2's weight-type sweep: (name, wfmt, flags, bits per weight, scale bytes per weight, per-row)
+CONFIG2_ROWS = [
+    ("fp16", 0, 0, 16, 0.0, False), ("int8_rowscale", 1, 2, 8, 0.0, True), ("int4_rowscale", 2, 2, 4, 0.0, True),
+    ("int2_rowscale", 3, 2, 2, 0.0, True), ("e4m3_mx", 8, 0, 8, 1 / 32, False), ("e5m2_mx", 9, 0, 8, 1 / 32, False),
+    ("mxfp4", 7, 0, 4, 1 / 32, False), ("w8a8", 1, -1, 8, 0.0, True), ("w4a8", 2, -1, 4, 0.0, True),
+    ("w2a8", 3, -1, 2, 0.0, True),
+]
+
+
+def config2_rows(args):
+    """One line per weight format at T=128, H=1024, I=4096:
+    the fp16-activation rows through mpp41_mlp (per-row fp16 scales for INT,
+    E8M0 per 32 for MXFP8 / MXFP4) and the int8-activation rows through
+    mpp41_mlp_w8a8. Weight sets rotated past L2; random weight bytes (timing
+    does not depend on the values)."""
+    T, H, I = (int(v) for v in (args.shape or "128,1024,4096").split(","))
+    hbm, bf16, src = peaks()
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    ctx = mpp41.Context(0)
+    ctx.set_stream(st.cuda_stream)
+    for name, wfmt, flags, bits, sbytes, per_row in CONFIG2_ROWS:
+        wbytes = 3 * H * I * (bits / 8 + sbytes) + (2 * I + H) * (4 if flags < 0 else 2) * per_row
+        cp = max(1, int(-(-L2_BYTES // wbytes))) if wbytes < L2_BYTES else 1
+        def mats(rows, k):
+            w = torch.randint(0, 256, (cp, rows * k * bits // 8), dtype=torch.uint8, device="cuda")
+            if wfmt == 0:   # fp16 weights: small values, no inf/nan
+                w = (torch.randn(cp, rows * k, device="cuda") * 0.02).half().view(torch.uint8).reshape(cp, -1)
+            if per_row:
+                s = (torch.rand(cp, rows, device="cuda") * 0.01 + 0.001)
+                s = s if flags < 0 else s.half()
+            elif sbytes:
+                s = torch.full((cp, rows * k // 32), 120, dtype=torch.uint8, device="cuda")
+            else:
+                s = None
+            return w, s
+        (wg, sg), (wu, su), (wd, sd) = mats(I, H), mats(I, H), mats(H, I)
+        if wfmt in (8, 9):   # finite FP8 bytes: clear the exponent's top bit
+            for w in (wg, wu, wd):
+                w &= 0xB7
+        x = torch.randn(T * H, device="cuda").half()
+        out = torch.empty(T * H, dtype=torch.float16, device="cuda")
+        it = [0]
+        if flags < 0:
+            scr = torch.empty(lib_w8a8_scratch(T, H, I), dtype=torch.uint8, device="cuda")
+
+            def run():
+                i = it[0] % cp
+                it[0] += 1
+                ctx.mlp_w8a8(wfmt, T, H, I, x, wg[i], sg[i], wu[i], su[i], wd[i], sd[i], out, scr)
+        else:
+            desc = mpp41.mlp_desc(T, H, I, wfmt, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F16, flags)
+            scr = torch.empty(mpp41.scratch_bytes(desc), dtype=torch.uint8, device="cuda")
+
+            def run():
+                i = it[0] % cp
+                it[0] += 1
+                ctx.mlp(desc, x, wg[i], wu[i], wd[i], None if sg is None else sg[i], None if su is None else su[i],
+                        None if sd is None else sd[i], scr, out)
+        us = timed(ctx, st, run, args.once)
+        kernel = ctx.mlp_last_kernel() if flags >= 0 else "w8a8"
+        if us is None:
+            print(json.dumps({"row": "config2", "format": name, "once": True}))
+            continue
+        flops = 6.0 * T * H * I
+        abytes = wbytes + T * H * 2 * 2
+        print(json.dumps({"row": "config2", "format": name, "kernel": kernel,
+                          "config": {"T": T, "H": H, "I": I}, "weight_copies": cp, "us": round(us, 2),
+                          "tflops": round(flops / us / 1e6, 1), "algorithmic_bytes": int(abytes),
+                          "gbs": round(abytes / us / 1e3, 1), "frac_hbm": round(abytes / us / 1e3 / hbm, 3),
+                          "frac_f16_peak": round(flops / us / 1e6 / bf16, 3),
+                          "peaks": {"hbm_gbs": hbm, "f16_tflops": bf16, "source": src + " (MEASURED_PEAKS.json)"}}),
+              flush=True)
+        del wg, wu, wd, sg, su, sd, scr
+        gc.collect()
+        torch.cuda.empty_cache()
+
+
+def lib_w8a8_scratch(T, H, I):
+    return mpp41.lib().mpp41_mlp_w8a8_scratch_bytes(T, H, I)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--row", required=True, choices=["w4a16", "w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe", "tp"])
+    ap.add_argument("--row", required=True,
+                    choices=["w4a16", "w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe", "tp", "config2"])
     ap.add_argument("--shape", default=None, help="T,H,I (layers), M,N,K (GEMMs), T,H,I,E,k,shared_I (moe)")
     ap.add_argument("--once", action="store_true")
     args = ap.parse_args()
     if args.row == "tp":
         return tp_row(args)
+    if args.row == "config2":
+        return config2_rows(args)
     hbm, bf16, src = peaks()
     st = torch.cuda.Stream()
     torch.cuda.set_stream(st)
