@@ -9,8 +9,12 @@ layer. Dequantisation runs inside every step (the weights stay packed in HBM).
 Timed region: exactly K steps, captured as CUDA graphs and replayed, with 24
 distinct weight/activation sets rotated step by step (173 MB > the 126 MB L2),
 bracketed by a barrier and cuda synchronize, CUDA events on the launching
-stream, max over ranks; the region is timed 5 times and the median reported. N > 1 runs N independent replicas (the layer is
-single-GPU sized; weak scaling, no collective in the data path).
+stream, max over ranks; the region is timed 5 times and the median reported.
+N > 1 runs N independent replicas of that layer (it is single-GPU sized;
+weak scaling, no collective in its data path) for `value`, and adds a `tp`
+object: the Llama-3-8B MLP tensor-parallel over the N GPUs
+(mpp41_mlp_tp, NCCL all-reduce) at 128 and 4096 tokens against the same layer
+on one GPU, with the local layer and the all-reduce timed apart.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -173,6 +177,91 @@ def cpu_baseline(host, seconds):
                       f"oracle/cpu_baseline.c",
             "single_thread": {"value": FLOPS_PER_LAYER * n1 / dt1 / 1e12, "unit": "TFLOP/s", "cores": 1,
                               "sample": f"{n1} full layers in {dt1:.1f} s on 1 thread"}}
+
+
+TP_H, TP_I = 4096, 14336          # Llama-3-8B MLP
+TP_TOKENS = (128, 4096)
+TP_REPS = 10
+
+
+def tp_measurement(ctx, rank, world, dist, stream):
+    """BASELINE config 3 tensor-parallel over the job's GPUs (mpp41_mlp_tp: rank r
+    owns intermediate slice r, NCCL all-reduce of the fp32 partial output): the
+    device time per layer (CUDA events on the launching stream around a CUDA
+    graph of TP_REPS layers, max over ranks) at each token count, next to the
+    same layer on one GPU (mpp41_mlp, every rank times it on its own GPU, max
+    over ranks), the rank's local layer alone (mpp41_mlp on its shard) and the
+    all-reduce alone, so the limiting step is named. Random MXFP4 weight bytes
+    with block scales near 2^-7 (timing does not depend on the values)."""
+    import numpy as np
+    import torch
+
+    import mpp41
+    idt = torch.zeros(mpp41.COMM_ID_BYTES, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        idt.copy_(torch.from_numpy(np.frombuffer(mpp41.comm_unique_id(), np.uint8).copy()))
+    dist.broadcast(idt, 0)
+    ctx.comm_init(world, rank, bytes(idt.cpu().numpy().tobytes()))
+    H, I, Ip = TP_H, TP_I, TP_I // world
+    rb = lambda *shape: torch.randint(0, 256, shape, dtype=torch.uint8, device="cuda")
+    sc = lambda *shape: torch.full(shape, 120, dtype=torch.uint8, device="cuda")
+    shard = (rb(Ip, H // 2), rb(Ip, H // 2), rb(H, Ip // 2), sc(Ip, H // 32), sc(Ip, H // 32), sc(H, Ip // 32))
+    full = (rb(I, H // 2), rb(I, H // 2), rb(H, I // 2), sc(I, H // 32), sc(I, H // 32), sc(H, I // 32))
+
+    def timed(fn, graph=True):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        g = None
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(TP_REPS):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        if g is not None:
+            g.replay()
+        else:
+            for _ in range(TP_REPS):
+                fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) * 1e3 / TP_REPS], device="cuda")
+        del g   # a graph holding NCCL kernels goes before the communicator does
+        torch.cuda.synchronize()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    rows = []
+    for T in TP_TOKENS:
+        x = torch.randn(T * H, device="cuda").half()
+        out = torch.empty(T * H, dtype=torch.float16, device="cuda")
+        part = torch.empty(T * H, dtype=torch.float32, device="cuda")
+        d = mpp41.mlp_desc(T, H, I, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F16)
+        dl = mpp41.mlp_desc(T, H, Ip, mpp41.W_MXFP4, mpp41.A_F16, mpp41.SWIGLU_FP32, mpp41.F16)
+        scr_tp = torch.empty(mpp41.tp_scratch_bytes(d, world), dtype=torch.uint8, device="cuda")
+        scr_l = torch.empty(mpp41.scratch_bytes(dl), dtype=torch.uint8, device="cuda")
+        scr_1 = torch.empty(mpp41.scratch_bytes(d), dtype=torch.uint8, device="cuda")
+        t_tp = timed(lambda: ctx.mlp_tp(d, x, *shard, scr_tp, out))
+        t_local = timed(lambda: ctx.mlp(dl, x, *shard, scr_l, out))
+        t_ar = timed(lambda: dist.all_reduce(part), graph=False)   # torch's NCCL group, eager launches
+        t_1 = timed(lambda: ctx.mlp(d, x, *full, scr_1, out))
+        flops = 6.0 * T * H * I
+        rows.append({"tokens": T, "us_per_layer": round(t_tp, 2), "us_per_layer_1gpu": round(t_1, 2),
+                     "speedup": round(t_1 / t_tp, 3), "efficiency": round(t_1 / (world * t_tp), 3),
+                     "tflops": round(flops / t_tp / 1e6, 1), "us_local_layer": round(t_local, 2),
+                     "us_allreduce_fp32": round(t_ar, 2),
+                     "limited_by": "all-reduce" if t_ar > t_local else "local layer"})
+        del scr_tp, scr_l, scr_1, x, out, part
+    ctx.comm_destroy()
+    return {"model": "Llama-3-8B MLP (H=4096, I=14336), MXFP4 weights, fp16 out (BASELINE config 3)",
+            "ranks": world, "split": "gate/up rows and down columns by intermediate slice, NCCL all-reduce of "
+            "the fp32 partial output", "timing": f"CUDA graph of {TP_REPS} layers, CUDA events, max over ranks",
+            "rows": rows}
 
 
 def main():
@@ -368,6 +457,8 @@ def main():
            "us_per_layer": e2e_ms * 1e3 / e2e_steps, "steps": e2e_steps,
            "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2}
 
+    tp = tp_measurement(ctx, rank, world, dist, stream) if dist is not None else None
+
     if rank == 0:
         base = cpu_baseline(host, args.cpu_seconds) if world == 1 else None
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -383,6 +474,8 @@ def main():
                 "oracle_rel_err": rel}
         if base is not None:
             line["cpu_baseline"] = base
+        if tp is not None:
+            line["tp"] = tp
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import numpy as np
 
-BITS = {0: 16, 1: 8, 2: 4, 3: 2, 4: 4, 5: 8, 6: 8, 7: 4}   # enum mpp41_wfmt
+BITS = {0: 16, 1: 8, 2: 4, 3: 2, 4: 4, 5: 8, 6: 8, 7: 4, 8: 8, 9: 8}   # enum mpp41_wfmt
 
 
 def shard(wfmt: int, rank: int, nranks: int, H: int, I: int, wg, wu, wd, sg=None, su=None, sd=None):
