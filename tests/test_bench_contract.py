@@ -4,6 +4,7 @@ GPU arm, `impl: reference`, a cpu_baseline describing the run and an e2e
 block with zero host<->device bytes."""
 import json
 import os
+import socket
 import subprocess
 import sys
 
@@ -27,11 +28,17 @@ def test_reference_arm_json_line():
     assert "workload" in d["config"]
 
 
+def free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def test_reference_arm_under_torchrun_prints_once():
     """Launched like the driver's N=2 run: rank 0 alone times and prints, the
     other rank exits 0 without output."""
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
-           "--master-addr", "127.0.0.1", "--master-port", "29613", os.path.join(ROOT, "bench.py"),
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), os.path.join(ROOT, "bench.py"),
            "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "1"]
     out = subprocess.run(cmd, capture_output=True, text=True, timeout=600, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]

@@ -118,3 +118,38 @@ def test_fp32_activation_rows(ctx, kernel, wfmt, m, n, k):
     got = from_dev(d_c, np.float32, (m, n))
     ref = a.astype(np.float64) @ O.decode_weights(wfmt, w, None, n, k).T
     assert rel_fro(got, ref) <= 1e-5, kernel
+
+
+# README.md:342-352 accumulator semantics, as device tests: constant fills so
+# every output element has the same exact integer value.
+def _ones_gemm(ctx, kernel, wfmt_byte, k, zeros, out_dt):
+    m = n = 128
+    a = np.ones((m, k), np.float16)
+    if wfmt_byte == "fp4":
+        w = np.full((n, k // 2), 0x22, np.uint8)          # E2M1 nibble 0x2 = 1.0
+        if zeros:
+            w[:, :zeros // 2] = 0
+    else:
+        w = np.full((n, k), 0x38, np.uint8)               # E4M3 0x38 = 1.0
+        w[:, :zeros] = 0
+    d_c = empty_dev(m * n * np.dtype(out_dt).itemsize)
+    ctx.gemm(kernel, to_dev(a), to_dev(w), d_c, m, n, k)
+    return from_dev(d_c, out_dt, (m, n))
+
+
+@pytest.mark.parametrize("kernel,fmt", [("mpp_mlp_h_fp8e4m3_f_n128", "e4m3"), ("mpp_mlp_h_fp4_f_n128", "fp4")])
+def test_sum_of_ones_exact_through_131072_float_destination(ctx, kernel, fmt):
+    got = _ones_gemm(ctx, kernel, fmt, 131072, 0, np.float32)
+    assert np.all(got == 131072.0)
+
+
+def test_sum_of_ones_exact_to_65504_half_destination(ctx):
+    # K = 65536 with 32 zero weights: exact sum 65504, the largest finite half
+    got = _ones_gemm(ctx, "mpp_mlp_h_fp8e4m3_h_n128", "e4m3", 65536, 32, np.float16)
+    assert np.all(got.astype(np.float64) == 65504.0)
+
+
+def test_half_destination_rounds_once_65448_to_65440(ctx):
+    # K = 65472 with 24 zero weights: exact sum 65448, one rounding to half -> 65440
+    got = _ones_gemm(ctx, "mpp_mlp_h_fp8e4m3_h_n128", "e4m3", 65472, 24, np.float16)
+    assert np.all(got.astype(np.float64) == 65440.0)

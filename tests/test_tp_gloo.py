@@ -4,6 +4,7 @@ partials with all_reduce and must reproduce the single-rank oracle layer. This
 checks the shard layout mpp41_mlp_tp relies on (gate/up rows, down columns and
 their E8M0 scale blocks) without a GPU."""
 import os
+import socket
 import sys
 
 import numpy as np
@@ -54,7 +55,9 @@ def worker(rank, world, port, wfmt, q):
 def test_two_rank_shards_sum_to_the_layer(wfmt):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + wfmt * 7 + os.getpid() % 500
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as sk:   # a free port, chosen now
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
     procs = [ctx.Process(target=worker, args=(r, 2, port, wfmt, q)) for r in range(2)]
     for p in procs:
         p.start()
