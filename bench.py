@@ -51,6 +51,8 @@ METRIC = "MXFP4 fused-MLP µs/layer & TFLOP/s (% of roofline) at 1/2/4/8 B200"
 NCU_TRAFFIC_LAYER = 6993664
 KERNEL = "mlp_small_kernel (gate/up + SwiGLU + down, one launch per layer)"
 REGIONS = 5          # timed regions of exactly K steps each; the median is reported
+E2E_CHUNK = 8        # steps per copy chunk in the end-to-end loop
+E2E_PASS = 96        # steps per captured end-to-end pass (the 24 sets, 4 times)
 
 
 def workload_config(world):
@@ -397,39 +399,46 @@ def main():
                                    "tensor_f16": FLOPS_PER_LAYER / (tflops_peak * 1e12) * 1e6}}
 
     # ---- end to end through the C ABI with host buffers (pinned). Every step
-    # copies its x host->device, runs the layer and copies its output back; the
-    # copies run on two copy streams (one per direction), double-buffered, so
-    # step i's copies overlap the layers of steps i-1 / i+1 as in a serving
-    # loop. One pass over the 24 rotating sets is captured as a CUDA graph (the
-    # copies, the events and the mpp41_mlp launches), replayed back to back.
-    e2e_steps = max(ROTATE, min(args.steps, 2000) // ROTATE * ROTATE)
-    x_host = [sets[i]["x"].cpu().pin_memory() for i in range(ROTATE)]
-    out_host = [torch.empty(T, H, dtype=torch.float16).pin_memory() for _ in range(ROTATE)]
-    xd = [torch.empty(T, H, dtype=torch.float16, device="cuda") for _ in range(2)]
-    od = [torch.empty(T, H, dtype=torch.float16, device="cuda") for _ in range(2)]
+    # copies its own x host->device, runs the layer and copies its own output
+    # back, all inside the timed region. The copies run on two copy streams (one
+    # per direction), one copy per chunk of E2E_CHUNK steps (the chunk's steps
+    # are contiguous in the pinned host arrays), double-buffered per chunk:
+    # chunk c's inputs are copied while chunk c-1 computes, its outputs are
+    # copied out while chunk c+1 computes, and the layers of a chunk launch back
+    # to back on the compute stream (one cross-stream wait per chunk, so the
+    # layers keep their programmatic-dependent-launch overlap). One pass of
+    # E2E_PASS steps (the 24 rotating sets, 4 times) is captured as a CUDA graph
+    # (the copies, the events and the mpp41_mlp launches), replayed back to back.
+    e2e_steps = max(E2E_PASS, min(args.steps, 2000) // E2E_PASS * E2E_PASS)
+    # host buffers: one pinned array per direction, the steps of a chunk contiguous
+    x_host = torch.stack([sets[i % ROTATE]["x"].cpu() for i in range(E2E_PASS)]).pin_memory()
+    out_host = torch.empty(E2E_PASS, T, H, dtype=torch.float16).pin_memory()
+    xd = torch.empty(2, E2E_CHUNK, T, H, dtype=torch.float16, device="cuda")
+    od = torch.empty(2, E2E_CHUNK, T, H, dtype=torch.float16, device="cuda")
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
     ev = lambda: torch.cuda.Event()
-    x_ready, layer_done, out_free = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    x_ready, chunk_done, out_free = ([ev(), ev()] for _ in range(3))
 
     def e2e_pass():
         h2d.wait_stream(stream)
         d2h.wait_stream(stream)
-        for i in range(ROTATE):
-            k = i & 1
-            if i >= 2:
-                h2d.wait_event(layer_done[k])       # xd[k] no longer read by the layer of step i-2
-            with torch.cuda.stream(h2d):
-                xd[k].copy_(x_host[i], non_blocking=True)
-            x_ready[k].record(h2d)
-            stream.wait_event(x_ready[k])
-            if i >= 2:
-                stream.wait_event(out_free[k])      # od[k] copied out by step i-2
-            layer(dict(sets[i], x=xd[k], out=od[k]))
-            layer_done[k].record(stream)
-            d2h.wait_event(layer_done[k])
-            with torch.cuda.stream(d2h):
-                out_host[i].copy_(od[k], non_blocking=True)
-            out_free[k].record(d2h)
+        for c in range(E2E_PASS // E2E_CHUNK):
+            b, c0 = c & 1, c * E2E_CHUNK
+            if c >= 2:
+                h2d.wait_event(chunk_done[b])     # chunk c-2 no longer reads these x buffers
+            with torch.cuda.stream(h2d):          # the chunk's inputs in one copy
+                xd[b].copy_(x_host[c0:c0 + E2E_CHUNK], non_blocking=True)
+            x_ready[b].record(h2d)
+            stream.wait_event(x_ready[b])
+            if c >= 2:
+                stream.wait_event(out_free[b])    # chunk c-2's outputs are copied out
+            for j in range(E2E_CHUNK):
+                layer(dict(sets[(c0 + j) % ROTATE], x=xd[b, j], out=od[b, j]))
+            chunk_done[b].record(stream)
+            d2h.wait_event(chunk_done[b])
+            with torch.cuda.stream(d2h):          # the chunk's outputs in one copy
+                out_host[c0:c0 + E2E_CHUNK].copy_(od[b], non_blocking=True)
+            out_free[b].record(d2h)
         stream.wait_stream(h2d)
         stream.wait_stream(d2h)
 
@@ -444,7 +453,7 @@ def main():
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for _ in range(e2e_steps // ROTATE):
+    for _ in range(e2e_steps // E2E_PASS):
         g_e2e.replay()
     b.record(stream)
     torch.cuda.synchronize()

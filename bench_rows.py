@@ -163,6 +163,85 @@ def config2_rows(args):
         torch.cuda.empty_cache()
 
 
+# BASELINE config 1's big-matmul rows (2048^3): kernel name, A bytes/elem, B bytes/elem, C bytes/elem
+CONFIG1_MATMULS = [
+    ("fp4_e2m1_matmul_benchmark", 0.5, 0.5, 4), ("half_fp4_matmul_half_benchmark", 2, 0.5, 2),
+    ("half_int4_matmul_half_benchmark", 2, 0.5, 2), ("int8_half_matmul_half_benchmark", 1, 2, 2),
+    ("int4_int8_matmul_benchmark", 0.5, 0.5, 4),
+]
+
+
+def config1_rows(args):
+    """bulk pack / unpack of 2^24 values (E2M1, E4M3, E5M2)
+    against the HBM roofline of their algorithmic bytes, and the five 2048^3
+    tensor-core matmul rows (mpp41_matmul) against their byte floor and the
+    measured f16 rate. Inputs larger than L2 are used as they are; the 2048^3
+    operands (<= 25 MB) are rotated through copies that exceed L2."""
+    hbm, bf16, src = peaks()
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    ctx = mpp41.Context(0)
+    ctx.set_stream(st.cuda_stream)
+    n = 1 << 24
+    vals = (torch.rand(4, n, device="cuda") * 1200 - 600)       # 4 x 64 MB fp32 > L2
+    packed = torch.empty(4, n, dtype=torch.uint8, device="cuda")
+    outs = torch.empty(4, n, dtype=torch.float32, device="cuda")
+    for fmt, name in ((0, "e2m1"), (1, "e4m3"), (2, "e5m2")):
+        pb = n // 2 if fmt == 0 else n
+        for op in ("pack", "unpack"):
+            it = [0]
+
+            def run():
+                i = it[0] % 4
+                it[0] += 1
+                if op == "pack":
+                    ctx.pack(fmt, vals[i], n, packed[i])
+                else:
+                    ctx.unpack(fmt, packed[i], n, outs[i])
+            us = timed(ctx, st, run, args.once)
+            if us is None:
+                continue
+            abytes = n * 4 + pb
+            print(json.dumps({"row": "config1", "op": f"{op}_{name}", "elements": n, "us": round(us, 2),
+                              "algorithmic_bytes": abytes, "gbs": round(abytes / us / 1e3, 1),
+                              "frac_hbm": round(abytes / us / 1e3 / hbm, 3),
+                              "peaks": {"hbm_gbs": hbm, "source": src + " (MEASURED_PEAKS.json)"}}), flush=True)
+    del vals, packed, outs
+    torch.cuda.empty_cache()
+    M = N = K = 2048
+    for kernel, ab, bb, cb in CONFIG1_MATMULS:
+        abytes = M * K * ab + N * K * bb + M * N * cb
+        cp = max(1, int(-(-L2_BYTES // abytes)))
+        a = torch.randint(0, 256, (cp, int(M * K * ab)), dtype=torch.uint8, device="cuda")
+        b = torch.randint(0, 256, (cp, int(N * K * bb)), dtype=torch.uint8, device="cuda")
+        if ab == 2:   # fp16 A: finite values
+            a = (torch.randn(cp, M * K, device="cuda") * 0.25).half().view(torch.uint8).reshape(cp, -1)
+        if bb == 2:
+            b = (torch.randn(cp, N * K, device="cuda") * 0.25).half().view(torch.uint8).reshape(cp, -1)
+        c = torch.empty(cp, int(M * N * cb), dtype=torch.uint8, device="cuda")
+        wsb = mpp41.Context.matmul_workspace_bytes(kernel, M, N, K)
+        ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device="cuda") if wsb else None
+        it = [0]
+
+        def run():
+            i = it[0] % cp
+            it[0] += 1
+            ctx.matmul(kernel, a[i], b[i], c[i], M, N, K, ws)
+        us = timed(ctx, st, run, args.once)
+        if us is None:
+            continue
+        flops = 2.0 * M * N * K
+        print(json.dumps({"row": "config1", "op": kernel, "shape": [M, N, K], "copies": cp, "us": round(us, 2),
+                          "tflops": round(flops / us / 1e6, 1), "algorithmic_bytes": int(abytes),
+                          "gbs": round(abytes / us / 1e3, 1), "frac_f16_peak": round(flops / us / 1e6 / bf16, 3),
+                          "byte_floor_us": round(abytes / hbm / 1e3, 2),
+                          "peaks": {"hbm_gbs": hbm, "f16_tflops": bf16, "source": src + " (MEASURED_PEAKS.json)"}}),
+              flush=True)
+        del a, b, c, ws
+        gc.collect()
+        torch.cuda.empty_cache()
+
+
 def lib_w8a8_scratch(T, H, I):
     return mpp41.lib().mpp41_mlp_w8a8_scratch_bytes(T, H, I)
 
@@ -170,7 +249,7 @@ def lib_w8a8_scratch(T, H, I):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--row", required=True,
-                    choices=["w4a16", "w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe", "tp", "config2"])
+                    choices=["w4a16", "w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe", "tp", "config2", "config1"])
     ap.add_argument("--shape", default=None, help="T,H,I (layers), M,N,K (GEMMs), T,H,I,E,k,shared_I (moe)")
     ap.add_argument("--once", action="store_true")
     args = ap.parse_args()
@@ -178,6 +257,8 @@ def main():
         return tp_row(args)
     if args.row == "config2":
         return config2_rows(args)
+    if args.row == "config1":
+        return config1_rows(args)
     hbm, bf16, src = peaks()
     st = torch.cuda.Stream()
     torch.cuda.set_stream(st)
