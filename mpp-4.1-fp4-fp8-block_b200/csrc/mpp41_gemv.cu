@@ -25,6 +25,9 @@
 #include "mpp41_device.cuh"
 #include "mpp41_internal.h"
 #include "mpp41_wq_gemm.cuh"
+#include "mpp41_gemv.cuh"
+
+#include <cstring>
 
 namespace mpp41 {
 namespace gemv {
@@ -395,6 +398,171 @@ int launch_s(const FusedLaunch &L, cudaStream_t st, const char **why)
 }
 
 }  // namespace gemv
+
+
+// ---------------------------------------------------------------- persistent streaming kernel
+namespace gv {
+
+bool covers(uint32_t T, uint32_t H, uint32_t I, int wfmt)
+{
+    return T >= 1 && T <= kMaxTokens && (wfmt == W_MXFP4 || wfmt == W_FP4 || wfmt == W_I4) && H % 256 == 0 &&
+           I % 256 == 0 && I <= kMaxChunks * kUnitK;
+}
+
+size_t ws_bytes() { return (size_t)kMaxGrid * kSlotFloats * sizeof(float); }
+
+// retire ticket, one count per 1024-channel mid chunk, one per down group
+size_t sync_words(uint32_t H, uint32_t I) { return 1 + (size_t)(I + kUnitK - 1) / kUnitK + (size_t)H / 32; }
+
+// Down-unit starts per CTA: gate/up groups go round-robin (CTA b has
+// nk_g * ceil((n_gg - b) / grid) units), and the down ranges are cut so that
+// every CTA's gate/up + down total is as even as the round-robin allows
+// (ds[b] = ideal cumulative total minus gate/up cumulative, kept monotone).
+static void down_starts(uint32_t n_gg, uint32_t nk_g, uint32_t u_d, uint32_t grid, uint32_t *ds)
+{
+    const uint64_t W = (uint64_t)n_gg * nk_g + u_d;
+    uint64_t cg = 0;
+    ds[0] = 0;
+    for (uint32_t b = 1; b < grid; ++b) {
+        cg += (uint64_t)nk_g * (n_gg > b - 1 ? (n_gg - (b - 1) + grid - 1) / grid : 0);
+        const int64_t ideal = (int64_t)((uint64_t)b * W / grid) - (int64_t)cg;
+        int64_t v = ideal < (int64_t)ds[b - 1] ? (int64_t)ds[b - 1] : ideal;
+        if (v > (int64_t)u_d) v = u_d;
+        ds[b] = (uint32_t)v;
+    }
+    ds[grid] = u_d;
+}
+
+// Most partials of other CTAs that one down group's finishing CTA adds (the CTA
+// holding a group's last units finishes it from the earlier parts).
+static uint32_t max_other_parts(const uint32_t *ds, uint32_t grid, uint32_t nk)
+{
+    uint32_t most = 0;
+    for (uint32_t b = 0; b < grid; ++b) {
+        const uint32_t d0 = ds[b], d1 = ds[b + 1];
+        if (d0 >= d1) continue;
+        const uint32_t g0u = (d0 / nk) * nk;
+        if (!(g0u < d0 && g0u + nk <= d1)) continue;   // not finishing a group that began earlier
+        uint32_t n = 0;
+        for (uint32_t c = b; c-- > 0 && ds[c + 1] > g0u;) n += ds[c + 1] > ds[c];
+        if (n > most) most = n;
+    }
+    return most;
+}
+
+template <int W, int EG, bool F16, int NT, bool T1, int CW>
+static int launch_t(const FusedLaunch &L, cudaStream_t st, const char **why)
+{
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.T = L.T; p.H = L.H; p.I = L.I;
+    p.n_gg = L.I / 16;
+    p.n_dg = L.H / 32;
+    p.nk_g = (L.H + kUnitK - 1) / kUnitK;
+    p.nk_d = (L.I + kUnitK - 1) / kUnitK;
+    p.u_d = p.n_dg * p.nk_d;
+    p.n_chunks = p.nk_d;
+    p.x_bytes = L.T * 2048;
+    const uint32_t fixed = smem_plan(0, 0, NT, CW).total + 1024;   // + base alignment
+    uint32_t stages = (kSmemLimit - fixed) / (kWStage + kSStage + p.x_bytes);
+    if (stages > kMaxStages) stages = kMaxStages;
+    if (stages < 2) { *why = "ring of fewer than 2 stages"; return 1; }
+    p.stages = stages;
+    const uint32_t smem = smem_plan(stages, p.x_bytes, NT, CW).total + 1024;
+    if (!L.ws || !L.sync) { *why = "workspace"; return 1; }
+    bool ok = make_map_rows128(&p.tm_wg, L.wg, L.H / 2, L.I, 16, 4) &&
+              make_map_rows128(&p.tm_wu, L.wu, L.H / 2, L.I, 16, 4) &&
+              make_map_rows128(&p.tm_wd, L.wd, L.I / 2, L.H, 16, 4) &&
+              make_map_kblocks(&p.tm_x, L.x, L.H, L.T, L.T, 16) &&
+              make_map_kblocks(&p.tm_mid, L.mid, L.I, L.T, L.T, 16);
+    if (!ok) { *why = "tensor maps (16-byte aligned bases needed)"; return 1; }
+    if (W == W_MXFP4) {
+        if (!L.sg || !L.su || !L.sd) { *why = "MXFP4 scales"; return 1; }
+        const uintptr_t a = reinterpret_cast<uintptr_t>(L.sg) | reinterpret_cast<uintptr_t>(L.su) |
+                            reinterpret_cast<uintptr_t>(L.sd);
+        if (a & 3u) { *why = "scale planes need 4-byte aligned bases"; return 1; }
+        p.sc16 = (a & 15u) == 0 && (L.H / 32) % 16 == 0 && (L.I / 32) % 16 == 0;
+        p.sg = L.sg; p.su = L.su; p.sd = L.sd;
+    }
+    p.mid = static_cast<__half *>(L.mid);
+    p.out = L.out;
+    p.ws = L.ws;
+    p.sync = L.sync;
+    p.err = L.err;
+    p.trace = L.trace;
+
+    auto kern = gemv_layer_kernel<W, EG, F16, NT, T1, CW>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) { cudaGetLastError(); *why = cudaGetErrorString(e); return 2; }
+    // every CTA must be resident at once (down units wait for gate/up groups of
+    // other CTAs): one CTA per SM, at most one per SM of the device
+    static thread_local int checked_dev = -1, sms = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (checked_dev != dev) {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        checked_dev = dev;
+    }
+    uint32_t grid = (uint32_t)sms < kMaxGrid ? (uint32_t)sms : kMaxGrid;
+    const uint32_t work = p.n_gg > p.u_d ? p.n_gg : p.u_d;
+    if (grid > work) grid = work;
+    // a finishing CTA holds at most kMaxParts other partials in shared memory
+    for (;; --grid) {
+        down_starts(p.n_gg, p.nk_g, p.u_d, grid, p.d_start);
+        if (grid == 1 || max_other_parts(p.d_start, grid, p.nk_d) <= kMaxParts) break;
+    }
+
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(Roles<CW>::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    // programmatic stream serialization: the weight stream starts while the
+    // previous kernel finishes; activations and scratch wait for it
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) { cudaGetLastError(); *why = cudaGetErrorString(e); return 2; }
+    return 0;
+}
+
+template <int W, int EG, bool F16>
+static int launch_nt(const FusedLaunch &L, cudaStream_t st, const char **why)
+{
+    if (L.T == 1) return launch_t<W, EG, F16, 1, true, 8>(L, st, why);
+    return L.T <= 8 ? launch_t<W, EG, F16, 1, false, 8>(L, st, why) : launch_t<W, EG, F16, 2, false, 8>(L, st, why);
+}
+
+template <int W>
+static int launch_w(const FusedLaunch &L, cudaStream_t st, const char **why)
+{
+    switch (L.gate_epi) {
+    case EPI_SWIGLU_PLAIN:
+        return L.out_f16 ? launch_nt<W, EPI_SWIGLU_PLAIN, true>(L, st, why) : launch_nt<W, EPI_SWIGLU_PLAIN, false>(L, st, why);
+    case EPI_SWIGLU_HALF:
+        return L.out_f16 ? launch_nt<W, EPI_SWIGLU_HALF, true>(L, st, why) : launch_nt<W, EPI_SWIGLU_HALF, false>(L, st, why);
+    case EPI_SWIGLU_HALF_H:
+        return L.out_f16 ? launch_nt<W, EPI_SWIGLU_HALF_H, true>(L, st, why)
+                         : launch_nt<W, EPI_SWIGLU_HALF_H, false>(L, st, why);
+    default: *why = "SwiGLU variant"; return 1;
+    }
+}
+
+int launch(const FusedLaunch &L, cudaStream_t st, const char **why)
+{
+    if (!covers(L.T, L.H, L.I, L.wfmt)) { *why = "shape or format"; return 1; }
+    switch (L.wfmt) {
+    case W_MXFP4: return launch_w<W_MXFP4>(L, st, why);
+    case W_FP4: return launch_w<W_FP4>(L, st, why);
+    default: return launch_w<W_I4>(L, st, why);
+    }
+}
+
+}  // namespace gv
 
 // four token tiles of 8; on the Llama-3-8B layer T = 17..32 run 80-89 us here
 // against about 100 us on the weight-major tcgen05 kernel

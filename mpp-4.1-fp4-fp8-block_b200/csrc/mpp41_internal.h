@@ -129,6 +129,11 @@ bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t
 // fp16 [rows][cols] viewed as [cols/64][rows][64]: one copy of box {64, br, nblk}
 // lands nblk consecutive 128-byte-swizzled K atoms of br rows each.
 bool make_map_kblocks(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint32_t br, uint32_t nblk);
+// Packed byte rows [rows][row_bytes] viewed as [row_bytes/128][rows][128 B]: one
+// copy of box {128, box_rows, box_chunks} lands box_chunks 128-byte-swizzled
+// column chunks of box_rows rows each.
+bool make_map_rows128(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows,
+                      uint32_t box_chunks);
 
 // OCP-MX quantization of fp32 [rows][depth] to E2M1 [rows][depth/2] + E8M0 [rows][depth/32].
 cudaError_t launch_quantize_mxfp4(const float *w, uint32_t rows, uint32_t depth, uint8_t *packed, uint8_t *scales,
@@ -201,15 +206,24 @@ int launch(const FusedLaunch &L, cudaStream_t st, const char **why);
 // Which fused kernel runs a layer, with its K splits and the workspace and
 // counter words it needs. Depends on the shape only.
 struct LayerPlan {
+    bool gemv;          // decode-sized weight-streaming kernel (mpp41_gemv.cuh)
     bool small;         // small-layer kernel (mpp41_mlp_small.cuh)
     bool token_major;
     uint32_t splits;
     size_t ws_bytes, sync_words;
 };
 LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16, int wfmt);
-// Decode-sized layers (T <= 32, MXFP4 / FP4 / INT4 weights, H and I multiples of
-// 128) run as two weight-streaming kernels (mpp41_gemv.cu); launch_layer
-// routes them there. The mid goes to L.mid (fp16 [T][I]); no workspace.
+// Decode-sized layers, 4-bit weights (MXFP4 / FP4 / INT4). T <= 16 with H and
+// I multiples of 256: one persistent weight-streaming kernel (mpp41_gemv.cuh)
+// with gv::ws_bytes() of workspace and gv::sync_words(H, I) counters.
+namespace gv {
+bool covers(uint32_t T, uint32_t H, uint32_t I, int wfmt);
+size_t ws_bytes();
+size_t sync_words(uint32_t H, uint32_t I);
+int launch(const FusedLaunch &L, cudaStream_t st, const char **why);
+}  // namespace gv
+// T <= 32 otherwise (H and I multiples of 128): two register-fed kernels
+// (gate/up + SwiGLU, then down; mpp41_gemv.cu). The mid goes to L.mid; no workspace.
 bool gemv_covers(uint32_t T, uint32_t H, uint32_t I, int wfmt);
 int launch_gemv_layer(const FusedLaunch &L, cudaStream_t st, const char **why);
 // Name of the kernel family launch_layer uses for this plan and shape.

@@ -59,6 +59,14 @@ LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16, int wfmt)
 {
     constexpr uint32_t kAssumedSMs = 148;
     LayerPlan pl{};
+    // Decode-sized layers with 4-bit weights: one persistent weight-streaming kernel.
+    if (gv::covers(T, H, I, wfmt)) {
+        pl.gemv = true;
+        pl.splits = 1;
+        pl.ws_bytes = gv::ws_bytes();
+        pl.sync_words = gv::sync_words(H, I);
+        return pl;
+    }
     // Small layers with 4-bit weights: every CTA runs one
     // G and one D tile; the down projection's 8 K splits reduce through L2.
     if (T > 32 && sl::covers(T, H, I, wfmt)) {
@@ -87,13 +95,15 @@ LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16, int wfmt)
 
 const char *layer_kernel_name(const LayerPlan &plan, uint32_t T, uint32_t H, uint32_t I, int wfmt)
 {
-    if (gemv_covers(T, H, I, wfmt)) return "gemv";
+    if (plan.gemv) return "gemv";
+    if (gemv_covers(T, H, I, wfmt)) return "gemv_regs";
     return plan.small ? "small" : plan.token_major ? "token_major" : "weight_major";
 }
 
 int launch_layer(const LayerPlan &plan, FusedLaunch L, cudaStream_t st, const char **why)
 {
-    // decode-sized batches of FP4 weights: weight-streaming GEMV kernels
+    // decode-sized batches of 4-bit weights: weight-streaming GEMV kernels
+    if (!L.gemm_only && plan.gemv) return gv::launch(L, st, why);
     if (!L.gemm_only && gemv_covers(L.T, L.H, L.I, L.wfmt)) return launch_gemv_layer(L, st, why);
     L.splits = plan.splits;
     if (plan.small) return sl::launch(L, st, why);

@@ -59,6 +59,21 @@ bool make_map_kblocks(CUtensorMap *m, const void *base, uint64_t cols, uint64_t 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_rows128(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows,
+                      uint32_t box_chunks)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || row_bytes % 128 != 0) return false;
+    const cuuint64_t dims[3] = {128, rows, row_bytes / 128};
+    const cuuint64_t strides[2] = {row_bytes, 128};
+    const cuuint32_t box[3] = {128, box_rows, box_chunks};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int W, int BN, int E>
 static int launch_t(const WqLaunch &L, cudaStream_t st, const char **why)
 {
