@@ -450,7 +450,7 @@ static uint32_t max_other_parts(const uint32_t *ds, uint32_t grid, uint32_t nk)
     return most;
 }
 
-template <int W, int EG, bool F16, int NT, bool T1, int CW>
+template <int W, int EG, bool F16, int NT, bool T1, int CW, int TEAMS>
 static int launch_t(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
     Params p;
@@ -491,7 +491,7 @@ static int launch_t(const FusedLaunch &L, cudaStream_t st, const char **why)
     p.err = L.err;
     p.trace = L.trace;
 
-    auto kern = gemv_layer_kernel<W, EG, F16, NT, T1, CW>;
+    auto kern = gemv_layer_kernel<W, EG, F16, NT, T1, CW, TEAMS>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) { cudaGetLastError(); *why = cudaGetErrorString(e); return 2; }
     // every CTA must be resident at once (down units wait for gate/up groups of
@@ -515,7 +515,7 @@ static int launch_t(const FusedLaunch &L, cudaStream_t st, const char **why)
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(Roles<CW>::kThreads);
+    cfg.blockDim = dim3(Roles<CW, TEAMS>::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     // programmatic stream serialization: the weight stream starts while the
@@ -533,8 +533,8 @@ static int launch_t(const FusedLaunch &L, cudaStream_t st, const char **why)
 template <int W, int EG, bool F16>
 static int launch_nt(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
-    if (L.T == 1) return launch_t<W, EG, F16, 1, true, 8>(L, st, why);
-    return L.T <= 8 ? launch_t<W, EG, F16, 1, false, 8>(L, st, why) : launch_t<W, EG, F16, 2, false, 8>(L, st, why);
+    if (L.T == 1) return launch_t<W, EG, F16, 1, true, 8, 2>(L, st, why);
+    return L.T <= 8 ? launch_t<W, EG, F16, 1, false, 8, 2>(L, st, why) : launch_t<W, EG, F16, 2, false, 8, 1>(L, st, why);
 }
 
 template <int W>

@@ -56,14 +56,17 @@
 namespace mpp41 {
 namespace gv {
 
-// Warp roles for CW math warps.
-template <int CW>
+// Warp roles for CW math warps in TEAMS teams. Team q takes the units n with
+// n % TEAMS == q, so while one team waits for its next stage and loads it, the
+// other keeps the tensor pipes busy (one team member per scheduler).
+template <int CW, int TEAMS>
 struct Roles {
     static constexpr int kPW = CW;             // weight producer warp
     static constexpr int kXW = CW + 1;         // activation producer warp
     static constexpr int kSW = CW + 2;         // sync warp: cross-CTA counts and partials
     static constexpr int kThreads = (CW + 3) * 32;
-    static constexpr int kBPW = 32 / CW;       // K blocks (of 32) per warp per unit
+    static constexpr int kTW = CW / TEAMS;     // warps per team (each unit's consumers)
+    static constexpr int kBPW = 32 / kTW;      // K blocks (of 32) per warp per unit
 };
 
 constexpr uint32_t kUnitK = 1024;         // K per unit
@@ -259,7 +262,7 @@ template <int NT, int BPW>
 struct UnitRegs {
     uint4 xv[BPW][NT];
     uint32_t wr[2][BPW][2];
-    uint32_t sc[2][2];   // E8M0 bytes of the warp's blocks, rows g and g + 8 (byte b: block b)
+    uint32_t sc[2][2][(BPW + 3) / 4];   // E8M0 bytes of the warp's blocks, rows g, g + 8 (byte b%4 of word b/4)
 };
 
 // Shared memory -> registers (plain loads, ordered after the stage's mbarrier
@@ -280,12 +283,15 @@ __device__ __forceinline__ void load_unit(UnitRegs<NT, BPW> &r, const uint8_t *w
             r.wr[bx][b][0] = *reinterpret_cast<const uint32_t *>(wst + bx * kBox + o.w[b]);
             r.wr[bx][b][1] = *reinterpret_cast<const uint32_t *>(wst + bx * kBox + o.w[b] + 1024);
         }
-        if constexpr (W == W_MXFP4 && BPW == 4) {
-            r.sc[bx][0] = *reinterpret_cast<const uint32_t *>(sst + bx * 512 + o.s);
-            r.sc[bx][1] = *reinterpret_cast<const uint32_t *>(sst + bx * 512 + o.s + 256);
+        if constexpr (W == W_MXFP4 && BPW >= 4) {
+#pragma unroll
+            for (int q = 0; q < BPW / 4; ++q) {
+                r.sc[bx][0][q] = *reinterpret_cast<const uint32_t *>(sst + bx * 512 + o.s + 4 * q);
+                r.sc[bx][1][q] = *reinterpret_cast<const uint32_t *>(sst + bx * 512 + o.s + 256 + 4 * q);
+            }
         } else if constexpr (W == W_MXFP4) {
-            r.sc[bx][0] = *reinterpret_cast<const uint16_t *>(sst + bx * 512 + o.s);
-            r.sc[bx][1] = *reinterpret_cast<const uint16_t *>(sst + bx * 512 + o.s + 256);
+            r.sc[bx][0][0] = *reinterpret_cast<const uint16_t *>(sst + bx * 512 + o.s);
+            r.sc[bx][1][0] = *reinterpret_cast<const uint16_t *>(sst + bx * 512 + o.s + 256);
         }
     }
 }
@@ -306,8 +312,8 @@ __device__ __forceinline__ void compute_unit(const UnitRegs<NT, BPW> &r, float (
             const uint32_t a1s0 = dh[0], a3s0 = dh[1], a1s1 = dh[2], a3s1 = dh[3];
             if constexpr (W == W_MXFP4) {
                 // E8M0 byte b -> float bits byte << 23 (byte select, then an integer multiply)
-                const float sl = __uint_as_float(__byte_perm(r.sc[bx][0], 0u, 0x4440u | b) * (1u << 23));
-                const float sh = __uint_as_float(__byte_perm(r.sc[bx][1], 0u, 0x4440u | b) * (1u << 23));
+                const float sl = __uint_as_float(__byte_perm(r.sc[bx][0][b / 4], 0u, 0x4440u | (b % 4)) * (1u << 23));
+                const float sh = __uint_as_float(__byte_perm(r.sc[bx][1][b / 4], 0u, 0x4440u | (b % 4)) * (1u << 23));
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     float tmp[4];
@@ -401,10 +407,10 @@ __device__ __forceinline__ uint32_t down_owner_below(const Params &p, uint32_t u
 // Workspace slot of CTA c's down partial: [box][token][row] fp32.
 __device__ __forceinline__ float *ws_slot(const Params &p, uint32_t c) { return p.ws + (size_t)c * kSlotFloats; }
 
-template <int W, int EG, bool OUT_F16, int NT, bool T1, int CW>
-__global__ void __launch_bounds__(Roles<CW>::kThreads, 1) gemv_layer_kernel(const __grid_constant__ Params p)
+template <int W, int EG, bool OUT_F16, int NT, bool T1, int CW, int TEAMS>
+__global__ void __launch_bounds__(Roles<CW, TEAMS>::kThreads, 1) gemv_layer_kernel(const __grid_constant__ Params p)
 {
-    using R = Roles<CW>;
+    using R = Roles<CW, TEAMS>;
     constexpr int kBPW = R::kBPW;
     constexpr bool SCALED = W == W_MXFP4;
     extern __shared__ uint8_t smem_raw[];
@@ -435,7 +441,7 @@ __global__ void __launch_bounds__(Roles<CW>::kThreads, 1) gemv_layer_kernel(cons
         for (uint32_t i = 0; i < S; ++i) {
             mbar_init(wfull + i, SCALED ? 33u : 1u);
             mbar_init(xfull + i, 1u);
-            mbar_init(empty + i, CW);
+            mbar_init(empty + i, R::kTW);
         }
         mbar_init(partsbar, 32u);
         mbar_init(headbar, 1u);
@@ -667,7 +673,8 @@ __global__ void __launch_bounds__(Roles<CW>::kThreads, 1) gemv_layer_kernel(cons
         pdl_wait_prior();
         const uint32_t g = lane >> 2, t = lane & 3u;
         const uint32_t ctid = threadIdx.x;   // 0 .. CW*32-1
-        const LaneOff<NT, kBPW> lo = lane_offsets<NT, kBPW>(warp, g, t, p.T);
+        const uint32_t team = warp / R::kTW, wt = warp % R::kTW;   // team, warp within the team
+        const LaneOff<NT, kBPW> lo = lane_offsets<NT, kBPW>(wt, g, t, p.T);
         // element e = ctid < NT*128 of a group's sums: tile nt = e >> 7, fragment i, lane l;
         // row (l>>2) + 8*(i>>1), token nt*8 + 2*(l&3) + (i&1)
         const bool mine = ctid < (uint32_t)NT * 128;
@@ -682,15 +689,22 @@ __global__ void __launch_bounds__(Roles<CW>::kThreads, 1) gemv_layer_kernel(cons
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
         };
-        // one unit: wait for its stage, load it into registers, multiply, release the stage
+        // one unit: wait for its stage, load it into registers, multiply, release the
+        // stage (units of the other team only advance the stage counter)
+        uint32_t n_at = 0;
         auto unit = [&](uint32_t kc, uint32_t K) {
+            const bool my = (n_at++ % TEAMS) == team;
+            if (!my) {
+                if (++s == S) { s = 0; par ^= 1u; }
+                return;
+            }
             const long long tw = clock64();
             bool ok = !*abort;
             ok = ok && warp_wait(wfull + s, par, abort, p.err, 0xE06);
             ok = ok && warp_wait(xfull + s, par, abort, p.err, 0xE07);
             const long long tc = clock64();
             cwait += tc - tw;
-            if (ok && kc * kUnitK + warp * kBPW * 32 < K) {
+            if (ok && kc * kUnitK + wt * kBPW * 32 < K) {
                 UnitRegs<NT, kBPW> r;
                 load_unit<W, NT, kBPW>(r, gbase + L.w + s * kWStage, gbase + L.x + s * p.x_bytes,
                                        gbase + L.s + s * kSStage, reinterpret_cast<const uint8_t *>(zero16), lo);
