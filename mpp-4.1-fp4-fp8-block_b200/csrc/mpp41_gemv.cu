@@ -405,8 +405,11 @@ namespace gv {
 
 bool covers(uint32_t T, uint32_t H, uint32_t I, int wfmt)
 {
+    // below 8M weights per matrix the launch's fixed costs (ring fill, one grid-wide
+    // hand-off) outweigh the streaming: such layers keep the register-fed kernels
+    // (BASELINE config 0 at T=1, 1024 x 4096: 7.1 us there, 12.1 us here)
     return T >= 1 && T <= kMaxTokens && (wfmt == W_MXFP4 || wfmt == W_FP4 || wfmt == W_I4) && H % 256 == 0 &&
-           I % 256 == 0 && I <= kMaxChunks * kUnitK;
+           I % 256 == 0 && I <= kMaxChunks * kUnitK && (uint64_t)H * I >= (8ull << 20);
 }
 
 size_t ws_bytes() { return (size_t)kMaxGrid * kSlotFloats * sizeof(float); }

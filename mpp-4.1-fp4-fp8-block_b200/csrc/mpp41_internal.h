@@ -214,7 +214,7 @@ struct LayerPlan {
 };
 LayerPlan plan_layer(uint32_t T, uint32_t H, uint32_t I, bool out_f16, int wfmt);
 // Decode-sized layers, 4-bit weights (MXFP4 / FP4 / INT4). T <= 16 with H and
-// I multiples of 256: one persistent weight-streaming kernel (mpp41_gemv.cuh)
+// I multiples of 256 and H * I >= 8M: one persistent weight-streaming kernel (mpp41_gemv.cuh)
 // with gv::ws_bytes() of workspace and gv::sync_words(H, I) counters.
 namespace gv {
 bool covers(uint32_t T, uint32_t H, uint32_t I, int wfmt);

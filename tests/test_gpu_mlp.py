@@ -108,6 +108,42 @@ def test_gemv_decode_sizes(ctx, gate_kernel, T, H, I):
     assert diff.mean() < 1e-3
 
 
+# Decode sizes with at least 8M weights per matrix run the persistent
+# weight-streaming kernel (one launch: TMA ring, round-robin gate/up groups,
+# per-chunk mid readiness, down groups split across CTAs and summed in CTA
+# order). Shapes cover one and two token tiles, K chunks cut short (2304 = 2.25
+# chunks of 1024, 3840 = 3.75) and the Llama-3-8B layer.
+@pytest.mark.parametrize("gate_kernel", ["mxfp4_native_sp_h_f_n64", "mpp_mlp_h_fp4_f_n128", "mpp_mlp_h_i4_f_n128"])
+@pytest.mark.parametrize("T,H,I", [(1, 4096, 14336), (3, 2048, 4096), (8, 2304, 3840), (11, 4096, 2048),
+                                   (16, 2048, 8192)])
+def test_gemv_stream_sizes(ctx, gate_kernel, T, H, I):
+    got, ref, mid, mid_ref = run_mlp(ctx, gate_kernel, T, H, I)
+    assert ctx.mlp_last_kernel() == "gemv"
+    assert rel_fro(got, ref) <= TOL, gate_kernel
+    diff = mid.astype(np.float64) != mid_ref.astype(np.float64)
+    assert diff.mean() < 1e-3
+
+
+def test_gemv_stream_repeat_deterministic(ctx):
+    """Counters reset themselves between launches and the split down groups add
+    their parts in a fixed order: two launches give the same bits."""
+    T, H, I = 2, 4096, 8192
+    desc = mpp41.describe("mxfp4_native_sp_h_f_n64", T, H, I)
+    x = activations(T, H)
+    wg, sg = weights(desc.wfmt, I, H, 11, False)
+    wu, su = weights(desc.wfmt, I, H, 12, False)
+    wd, sd = weights(desc.wfmt, H, I, 13, False)
+    dv = [to_dev(a) for a in (x, wg, wu, wd, sg, su, sd)]
+    outs = []
+    for _ in range(3):
+        d_out, d_scr = empty_dev(T * H * 4), empty_dev(mpp41.scratch_bytes(desc))
+        ctx.mlp(desc, *dv, d_scr, d_out)
+        ctx.synchronize()
+        assert ctx.mlp_last_kernel() == "gemv"
+        outs.append(from_dev(d_out, np.float32, (T, H)))
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
 def test_gemv_wide_scales(ctx):
     got, ref, _, _ = run_mlp(ctx, "mxfp4_native_sp_h_f_n64", 3, 512, 1024, wide=True)
     fin = np.isfinite(ref)
@@ -196,7 +232,7 @@ def test_fused_and_unfused_paths_agree(ctx, flags, out_dtype):
         assert rel_fro(from_dev(d_out, dt, (T, H)), ref) <= TOL
 
 
-@pytest.mark.parametrize("T,kernel", [(128, "small"), (64, "small"), (33, "small"), (16, "gemv"),
+@pytest.mark.parametrize("T,kernel", [(128, "small"), (64, "small"), (33, "small"), (16, "gemv_regs"),
                                       (129, "weight_major")])
 def test_config0_kernel_route(ctx, T, kernel):
     """BASELINE config 0 (and its neighbours) take the planned kernel, not a
