@@ -214,13 +214,15 @@ mpp41_status mpp41_mlp_scalar(mpp41_ctx *ctx, const char *gate_kernel_name, cons
  *      scales [n][k/32]); sg/su/sd are only read for MXFP4. scratch must hold
  *      mpp41_mlp_scratch_bytes(desc) bytes: the fp16/fp32/int8 mid, then for
  *      fp16 output the split-K fp32 workspace and tile counters. Kernels by
- *      shape: up to 32 tokens with MXFP4/FP4/INT4 weights, two weight-
- *      streaming GEMV kernels; 33..128 tokens of a small layer with 4-bit
+ *      shape: up to 16 tokens with MXFP4/FP4/INT4 weights, hidden and
+ *      intermediate multiples of 256 and at least 8M weights per matrix, one
+ *      persistent weight-streaming kernel ("gemv"); other layers up to 32 tokens
+ *      with those weights, two register-fed GEMV kernels ("gemv_regs"); 33..128 tokens of a small layer with 4-bit
  *      weights (hidden <= 1024), the small-layer kernel
  *      (one G and one D tile per CTA); otherwise one persistent tcgen05 kernel per layer
  *      (token-major for 65..128 tokens of a small layer, weight-major else).
  *      mpp41_mlp_last_kernel names the family the last mpp41_mlp call on the
- *      context launched: "gemv", "small", "token_major", "weight_major",
+ *      context launched: "gemv", "gemv_regs", "small", "token_major", "weight_major",
  *      "unfused" (two GEMM kernels) or "i8"; "" before the first call. ---- */
 const char *mpp41_mlp_last_kernel(const mpp41_ctx *ctx);
 size_t mpp41_mlp_scratch_bytes(const mpp41_mlp_desc *desc);
