@@ -174,6 +174,32 @@ mpp41_status mpp41_dequant(mpp41_ctx *ctx, const char *kernel_name, const uint8_
 mpp41_status mpp41_gemm(mpp41_ctx *ctx, const char *kernel_name, const void *a, const void *b, void *c, uint32_t m,
                         uint32_t n, uint32_t k, const uint8_t *scales);
 
+/* ---- Weight handles: replace the host-built multi-plane MTLTensor over a
+ *      weight's packed values and scale plane (main.swift:2172-2212 builds it,
+ *      2254-2262 binds it; MXFP4Kernels.metal:180-226 reads through it, the
+ *      mxfp4_native_sph_* rows). A handle names the planes once -- format
+ *      (mpp41_wfmt), packed data [n][k], scales (E8M0 [n][k/32] for block-scaled
+ *      formats, fp16 [n] for MPP41_MLP_ROW_SCALES layers, else NULL) -- and keeps
+ *      the TMA descriptors the kernels encode for them: a kernel's first launch
+ *      through the handle encodes its box, later launches reuse it. The caller
+ *      keeps ownership of the planes and must not free them before the handle;
+ *      a handle belongs to the context's device. Calls through the same handle
+ *      from several host threads are safe. ---- */
+typedef struct mpp41_weight mpp41_weight;
+mpp41_status mpp41_weight_create(mpp41_ctx *ctx, int32_t wfmt, const void *data, const uint8_t *scales, uint32_t k,
+                                 uint32_t n, mpp41_weight **out);
+void mpp41_weight_destroy(mpp41_weight *w);
+/* Descriptors encoded for this handle so far, and launches that reused one. */
+mpp41_status mpp41_weight_map_counts(const mpp41_weight *w, uint64_t *encoded, uint64_t *reused);
+/* mpp41_gemm through a handle: c[m][n] = a[m][k] * w^T, kernel_name as for
+ * mpp41_gemm (its weight format must be the handle's). */
+mpp41_status mpp41_gemm_weight(mpp41_ctx *ctx, const char *kernel_name, const void *a, const mpp41_weight *w, void *c,
+                               uint32_t m);
+/* mpp41_mlp through handles: gate and up [intermediate][hidden], down
+ * [hidden][intermediate], all of desc->wfmt; same kernels, results and scratch. */
+mpp41_status mpp41_mlp_weights(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const mpp41_weight *wg,
+                               const mpp41_weight *wu, const mpp41_weight *wd, void *scratch, void *out);
+
 /* ---- OCP-MX quantizer (no reference counterpart: the reference draws random
  *      packed bytes, main.swift:2785-2793): fp32 w [rows][depth] ->
  *      E2M1 packed [rows][depth/2] + E8M0 scales [rows][depth/32], shared

@@ -1515,4 +1515,10 @@ mpp41_status mpp41_mlp_benchmark(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const 
 // Lets other translation units of the library report through mpp41_last_error().
 namespace mpp41 {
 mpp41_status set_last_error(mpp41_status s, const char *msg) { return fail(s, "%s", msg); }
+
+int gemm_kernel_wfmt(const char *name)
+{
+    const KernelInfo *k = find_kernel(name);
+    return k && k->kind == K_GEMM && k->afmt == 0 ? k->arg0 : -1;
+}
 }  // namespace mpp41

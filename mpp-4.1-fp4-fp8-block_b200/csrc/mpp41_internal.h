@@ -236,6 +236,15 @@ int launch_mlp_fused(const FusedLaunch &L, cudaStream_t st, const char **why);
 // Multi-GPU state of a context (mpp41_tp.cu); NULL until mpp41_comm_init.
 struct CommState;
 mpp41_status set_last_error(mpp41_status s, const char *msg);
+// Weight format of a GEMM kernel name with fp16 activations, or -1.
+int gemm_kernel_wfmt(const char *name);
+// Weight handles (mpp41_weight.cu): the map cache of the handle, active on this
+// host thread, that owns `base` (nullptr when none); lookups and inserts of
+// encoded tensor maps keyed by every encoding argument.
+struct WeightMapCache;
+WeightMapCache *active_cache_for(const void *base);
+bool cache_find(WeightMapCache *c, const uint64_t (&key)[8], CUtensorMap *m);
+void cache_put(WeightMapCache *c, const uint64_t (&key)[8], const CUtensorMap &m);
 cudaError_t launch_wait_probe(const uint32_t *flag, uint32_t target, uint64_t limit_ns, uint32_t *err,
                               cudaStream_t st);
 cudaError_t launch_f32_to_f16(const float *in, size_t n, void *out, cudaStream_t st);

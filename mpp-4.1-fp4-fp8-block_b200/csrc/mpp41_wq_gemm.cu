@@ -29,9 +29,25 @@ static EncodeTiledFn encode_fn()
     return fn;
 }
 
+static bool make_map_encode(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols,
+                            uint64_t rows, uint32_t bc, uint32_t br, CUtensorMapSwizzle sw);
+
 // 2D row-major tensor [rows][cols] of `elem`-byte elements, tile box {bc, br}.
 bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols,
                      uint64_t rows, uint32_t bc, uint32_t br, CUtensorMapSwizzle sw)
+{
+    // a plane of an active weight handle: its map is encoded once and reused
+    WeightMapCache *cache = active_cache_for(base);
+    const uint64_t key[8] = {1, reinterpret_cast<uintptr_t>(base), (uint64_t)dt, elem, cols, rows,
+                             (uint64_t)bc | ((uint64_t)br << 32), (uint64_t)sw};
+    if (cache && cache_find(cache, key, m)) return true;
+    const bool ok = make_map_encode(m, base, dt, elem, cols, rows, bc, br, sw);
+    if (ok && cache) cache_put(cache, key, *m);
+    return ok;
+}
+
+static bool make_map_encode(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint32_t elem, uint64_t cols,
+                            uint64_t rows, uint32_t bc, uint32_t br, CUtensorMapSwizzle sw)
 {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
@@ -62,6 +78,9 @@ bool make_map_kblocks(CUtensorMap *m, const void *base, uint64_t cols, uint64_t 
 bool make_map_rows128(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows,
                       uint32_t box_chunks)
 {
+    WeightMapCache *cache = active_cache_for(base);
+    const uint64_t key[8] = {2, reinterpret_cast<uintptr_t>(base), row_bytes, rows, box_rows, box_chunks, 0, 0};
+    if (cache && cache_find(cache, key, m)) return true;
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || row_bytes % 128 != 0) return false;
@@ -69,9 +88,11 @@ bool make_map_rows128(CUtensorMap *m, const void *base, uint64_t row_bytes, uint
     const cuuint64_t strides[2] = {row_bytes, 128};
     const cuuint32_t box[3] = {128, box_rows, box_chunks};
     const cuuint32_t es[3] = {1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    const bool ok = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (ok && cache) cache_put(cache, key, *m);
+    return ok;
 }
 
 template <int W, int BN, int E>

@@ -111,6 +111,11 @@ def lib() -> C.CDLL:
         "mpp41_mlp_scalar": ([vp, C.c_char_p, C.c_char_p, vp, vp, vp, vp, vp, vp, C.POINTER(MLPConfig)], st),
         "mpp41_mlp_scratch_bytes": ([C.POINTER(MLPDesc)], sz),
         "mpp41_mlp": ([vp, C.POINTER(MLPDesc)] + [vp] * 9, st),
+        "mpp41_weight_create": ([vp, C.c_int32, vp, vp, u32, u32, C.POINTER(vp)], st),
+        "mpp41_weight_destroy": ([vp], None),
+        "mpp41_weight_map_counts": ([vp, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)], st),
+        "mpp41_gemm_weight": ([vp, C.c_char_p, vp, vp, vp, u32], st),
+        "mpp41_mlp_weights": ([vp, C.POINTER(MLPDesc), vp, vp, vp, vp, vp, vp], st),
         "mpp41_mlp_gate_up": ([vp, C.POINTER(MLPDesc)] + [vp] * 7, st),
         "mpp41_mlp_down": ([vp, C.POINTER(MLPDesc), vp, vp, vp, vp, C.c_int], st),
         "mpp41_quantize_mxfp4": ([vp, vp, u32, u32, vp, vp], st),
@@ -281,6 +286,32 @@ def scratch_bytes(desc: MLPDesc) -> int:
     return lib().mpp41_mlp_scratch_bytes(C.byref(desc))
 
 
+class Weight:
+    """Handle over a weight's device planes (mpp41_weight); keeps the planes
+    referenced while it lives."""
+
+    def __init__(self, h, planes):
+        self.h = h
+        self._planes = planes
+
+    def map_counts(self):
+        """(descriptors encoded, launches that reused one)."""
+        e, r = C.c_uint64(), C.c_uint64()
+        _check(lib().mpp41_weight_map_counts(self.h, C.byref(e), C.byref(r)))
+        return e.value, r.value
+
+    def close(self):
+        if self.h:
+            lib().mpp41_weight_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Context:
     """One libmpp41 context (device + stream + device error word)."""
 
@@ -369,6 +400,19 @@ class Context:
     def mlp(self, desc: MLPDesc, x, wg, wu, wd, sg, su, sd, scratch, out):
         _check(lib().mpp41_mlp(self.h, C.byref(desc), _ptr(x), _ptr(wg), _ptr(wu), _ptr(wd), _ptr(sg), _ptr(su),
                                _ptr(sd), _ptr(scratch), _ptr(out)))
+
+    def weight(self, wfmt: int, data, scales, k: int, n: int) -> "Weight":
+        """A weight handle (mpp41_weight_create) over device planes data [n][k]
+        and scales; the planes must outlive it."""
+        h = C.c_void_p()
+        _check(lib().mpp41_weight_create(self.h, wfmt, _ptr(data), _ptr(scales), k, n, C.byref(h)))
+        return Weight(h, (data, scales))
+
+    def gemm_weight(self, kernel: str, a, w: "Weight", c, m: int):
+        _check(lib().mpp41_gemm_weight(self.h, kernel.encode(), _ptr(a), w.h, _ptr(c), m))
+
+    def mlp_weights(self, desc: MLPDesc, x, wg: "Weight", wu: "Weight", wd: "Weight", scratch, out):
+        _check(lib().mpp41_mlp_weights(self.h, C.byref(desc), _ptr(x), wg.h, wu.h, wd.h, _ptr(scratch), _ptr(out)))
 
     def wait_probe(self, flag, target: int, limit_ns: int):
         """Enqueue a bounded wait until *flag >= target (mpp41_wait_probe)."""
