@@ -400,18 +400,30 @@ def tp_row(args):
     x = torch.randn(T * H, device="cuda").half()
     out = torch.empty(T * H, dtype=torch.float16, device="cuda")
     res = {}
-    for path in ("oneshot", "nccl"):
+    # one-shot peer-memory all-reduce where its 2 MB buffer holds the partial; NCCL
+    # (chunked overlap for T >= 1024); NCCL with one chunk (no overlap) for the gain
+    paths = (["oneshot"] if T * H * 4 <= (2 << 20) else []) + ["nccl"] + (["nccl_one_chunk"] if T >= 1024 else [])
+    # the unsharded layer on one GPU (this rank's device), same timing
+    full = [to(a) for a in (wg, wu, wd, sg, su, sd)]
+    scr1 = torch.empty(mpp41.scratch_bytes(desc), dtype=torch.uint8, device="cuda")
+    for path in paths + ["one_gpu"]:
+        os.environ.pop("MPP41_TP_ALLREDUCE", None)
+        os.environ.pop("MPP41_TP_CHUNKS", None)
         if path == "oneshot":
             os.environ["MPP41_TP_ALLREDUCE"] = "oneshot"
+        if path == "nccl_one_chunk":
+            os.environ["MPP41_TP_CHUNKS"] = "1"
+        if path == "one_gpu":
+            call = lambda: ctx.mlp(desc, x, *full[:3], *full[3:], scr1, out)
         else:
-            os.environ.pop("MPP41_TP_ALLREDUCE", None)
+            call = lambda: ctx.mlp_tp(desc, x, *w, scr, out)
         for _ in range(5):
-            ctx.mlp_tp(desc, x, *w, scr, out)
+            call()
         ctx.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=st):
             for _ in range(20):
-                ctx.mlp_tp(desc, x, *w, scr, out)
+                call()
         ctx.synchronize()
         dist.barrier()
         g.replay()
@@ -430,10 +442,13 @@ def tp_row(args):
         dist.all_reduce(us, op=dist.ReduceOp.MAX)
         res[path] = round(float(us[0]), 2)
     os.environ.pop("MPP41_TP_ALLREDUCE", None)
+    os.environ.pop("MPP41_TP_CHUNKS", None)
     dist.barrier()
     if rank == 0:
+        best = min(res[p] for p in paths)
         print(json.dumps({"row": "tp", "config": {"T": T, "H": H, "I": I, "ranks": world},
-                          "us_per_layer": res, "tflops_oneshot": round(6.0 * T * H * I / res["oneshot"] / 1e6, 1)}))
+                          "us_per_layer": res, "tflops_best_tp": round(6.0 * T * H * I / best / 1e6, 1),
+                          "efficiency": round(res["one_gpu"] / (world * best), 3)}))
     ctx.comm_destroy()
     dist.destroy_process_group()
 

@@ -74,6 +74,8 @@ def test_tp2_oneshot_matches_nccl(shape):
 def worker(rank, world, uid, shape, q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     T, H, I = shape
+    if T >= 1024:   # the chunked path: token chunks whose all-reduces overlap the next chunk
+        os.environ["MPP41_TP_CHUNKS"] = "4"
     d = O.baseline_mlp_inputs(T, H, I, seed=3)
     ctx = mpp41.Context(rank)
     ctx.comm_init(world, rank, uid)
@@ -91,7 +93,7 @@ def worker(rank, world, uid, shape, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-# (1024, ...) runs in 4 token chunks whose all-reduces overlap the next chunk's layer
+# (1024, ...) asks for 4 token chunks whose all-reduces overlap the next chunk's layer
 @pytest.mark.parametrize("shape", [(128, 1024, 4096), (16, 4096, 14336), (1, 4096, 14336), (256, 4096, 14336),
                                    (1024, 1024, 4096)])
 def test_tp2_matches_single_rank_oracle(shape):
