@@ -73,7 +73,9 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 // outputs up to 2 MiB of fp32 partial (T * H * 4; e.g. T <= 128 at H = 4096),
 // at most kMaxPeers ranks. On 2 B200s it measured no faster than NCCL for the
 // Llama-3-8B layer (89 vs 85 us per layer at T = 1, both dominated by the
-// local layer), so NCCL stays the default.
+// local layer), so NCCL stays the default. Allowed up to 256 MiB it also lost at
+// large T (T = 4096: 1171 us against NCCL's 1115): the partial makes one more
+// round trip through the shared buffer than NCCL's reduction.
 constexpr size_t kOneShotMaxBytes = 2u << 20;
 
 // The layer one rank computes: same shape with the intermediate slice, fp32
