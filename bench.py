@@ -52,7 +52,7 @@ NCU_TRAFFIC_LAYER = 6993664
 KERNEL = "mlp_small_kernel (gate/up + SwiGLU + down, one launch per layer)"
 REGIONS = 5          # timed regions of exactly K steps each; the median is reported
 E2E_CHUNK = 8        # steps per copy chunk in the end-to-end loop
-E2E_PASS = 96        # steps per captured end-to-end pass (the 24 sets, 4 times)
+E2E_PASS = 384       # steps per captured end-to-end pass (the 24 sets, 16 times)
 
 
 def workload_config(world):
@@ -407,8 +407,11 @@ def main():
     # copied out while chunk c+1 computes, and the layers of a chunk launch back
     # to back on the compute stream (one cross-stream wait per chunk, so the
     # layers keep their programmatic-dependent-launch overlap). One pass of
-    # E2E_PASS steps (the 24 rotating sets, 4 times) is captured as a CUDA graph
-    # (the copies, the events and the mpp41_mlp launches), replayed back to back.
+    # E2E_PASS steps (the 24 rotating sets, 16 times) is captured as a CUDA graph
+    # (the copies, the events and the mpp41_mlp launches), replayed back to back;
+    # each pass starts with its first chunk's input copy and ends with its last
+    # chunk's output copy, which nothing overlaps, so a longer pass spreads that
+    # fill and drain over more steps, as a serving loop does.
     e2e_steps = max(E2E_PASS, min(args.steps, 2000) // E2E_PASS * E2E_PASS)
     # host buffers: one pinned array per direction, the steps of a chunk contiguous
     x_host = torch.stack([sets[i % ROTATE]["x"].cpu() for i in range(E2E_PASS)]).pin_memory()
