@@ -204,7 +204,9 @@ def tp_measurement(ctx, rank, world, dist, stream):
         idt.copy_(torch.from_numpy(np.frombuffer(mpp41.comm_unique_id(), np.uint8).copy()))
     dist.broadcast(idt, 0)
     ctx.comm_init(world, rank, bytes(idt.cpu().numpy().tobytes()))
-    H, I, Ip = TP_H, TP_I, TP_I // world
+    from mpp41 import tp as tp_layout
+    i0, i1 = tp_layout.slice_bounds(TP_I, world, rank)
+    H, I, Ip = TP_H, TP_I, i1 - i0
     rb = lambda *shape: torch.randint(0, 256, shape, dtype=torch.uint8, device="cuda")
     sc = lambda *shape: torch.full(shape, 120, dtype=torch.uint8, device="cuda")
     shard = (rb(Ip, H // 2), rb(Ip, H // 2), rb(H, Ip // 2), sc(Ip, H // 32), sc(Ip, H // 32), sc(H, Ip // 32))

@@ -457,9 +457,14 @@ mpp41_status mpp41_moe_ep(mpp41_ctx *ctx, const mpp41_moe_desc *desc, uint32_t c
                           const uint8_t *shared_wd, const uint8_t *shared_sd, void *out, void *scratch);
 
 /* ---- tensor parallelism (no counterpart in the
- *      single-GPU reference). Rank r of P holds rows [r*I/P, (r+1)*I/P) of the
- *      gate and up weights (and their scale rows) and the same columns of the
- *      down weights, repacked contiguous [H][I/P] (scales [H][I/(32P)]). Each
+ *      single-GPU reference). Rank r of P holds rows [i0, i1) of the gate and
+ *      up weights (and their scale rows) and the same columns of the down
+ *      weights, repacked contiguous [H][i1-i0] (scales [H][(i1-i0)/32]). The
+ *      slices: when I is a multiple of 512 with at least P units of 512, the
+ *      units are dealt in order, the first I/512 mod P ranks taking one more
+ *      (rank r starts at 512*(r*floor(I/512/P) + min(r, I/512 mod P))), so every
+ *      slice keeps the 16-byte-aligned scale rows the fused kernels need;
+ *      otherwise [r*I/P, (r+1)*I/P), which needs I a multiple of 32*P. Each
  *      rank computes its partial output with the fused layer kernel in fp32,
  *      then the partials are summed across ranks (NCCL all-reduce on the
  *      context's stream) into `out` on every rank. NCCL is loaded at run time

@@ -80,10 +80,33 @@ constexpr size_t kOneShotMaxBytes = 2u << 20;
 
 // The layer one rank computes: same shape with the intermediate slice, fp32
 // (or int32) output so the partial sums add exactly before the final rounding.
-mpp41_mlp_desc local_desc(const mpp41_mlp_desc *d, int nranks)
+// Intermediate slice [i0, i1) of rank r of P: 512-channel units dealt in order
+// (the first I/512 mod P ranks take one more) when I is a multiple of 512 with
+// at least P units -- every slice then keeps scale rows of a multiple of 16
+// bytes (the fused kernels' TMA needs them; I = 14336 over 8 ranks is 4 x 2048 +
+// 4 x 1536 rather than 8 x 1792); otherwise even slices of I/P.
+void tp_slice(uint32_t I, int P, int r, uint32_t *i0, uint32_t *i1)
+{
+    const uint32_t u = I / 512;
+    if (I % 512 == 0 && u >= (uint32_t)P) {
+        const uint32_t base = u / (uint32_t)P, extra = u % (uint32_t)P;
+        auto start = [&](uint32_t q) { return 512u * (q * base + (q < extra ? q : extra)); };
+        *i0 = start((uint32_t)r);
+        *i1 = start((uint32_t)r + 1);
+    } else {
+        *i0 = (uint32_t)r * I / (uint32_t)P;
+        *i1 = (uint32_t)(r + 1) * I / (uint32_t)P;
+    }
+}
+
+bool tp_even_slices(uint32_t I, int P) { return !(I % 512 == 0 && I / 512 >= (uint32_t)P); }
+
+mpp41_mlp_desc local_desc(const mpp41_mlp_desc *d, int nranks, int rank)
 {
     mpp41_mlp_desc l = *d;
-    l.intermediate = d->intermediate / (uint32_t)nranks;
+    uint32_t i0, i1;
+    tp_slice(d->intermediate, nranks, rank, &i0, &i1);
+    l.intermediate = i1 - i0;
     if (l.out_dtype == MPP41_F16) l.out_dtype = MPP41_F32;
     return l;
 }
@@ -321,8 +344,9 @@ void mpp41_comm_destroy(mpp41_ctx *ctx) { comm_release(ctx); }
 
 size_t mpp41_mlp_tp_scratch_bytes(const mpp41_mlp_desc *d, int nranks)
 {
-    if (!d || nranks < 1 || d->intermediate % (uint32_t)nranks) return 0;
-    const mpp41_mlp_desc l = local_desc(d, nranks);
+    if (!d || nranks < 1) return 0;
+    if (tp_even_slices(d->intermediate, nranks) && d->intermediate % (uint32_t)nranks) return 0;
+    const mpp41_mlp_desc l = local_desc(d, nranks, 0);   // rank 0 holds the largest slice
     size_t b = align256(mpp41_mlp_scratch_bytes(&l));
     if (d->out_dtype == MPP41_F16) b += (size_t)d->tokens * d->hidden * 4;   // fp32 partial
     return b;
@@ -335,12 +359,14 @@ mpp41_status mpp41_mlp_tp(mpp41_ctx *ctx, const mpp41_mlp_desc *d, const void *x
     if (!ctx || !d) return err(MPP41_ERR_INVALID_ARGUMENT, "null context or descriptor%s", nullptr);
     if (!ctx->comm) return err(MPP41_ERR_COMM, "mpp41_comm_init has not been called on this context%s", nullptr);
     const CommState *cs = ctx->comm;
-    if (d->intermediate % (uint32_t)(32 * cs->nranks))
+    if (tp_even_slices(d->intermediate, cs->nranks) && d->intermediate % (uint32_t)(32 * cs->nranks))
         return err(MPP41_ERR_UNSUPPORTED_SHAPE, "intermediate must split into 32-aligned slices per rank%s", nullptr);
     if (d->out_dtype != MPP41_F32 && d->out_dtype != MPP41_F16 && d->out_dtype != MPP41_S32)
         return err(MPP41_ERR_INVALID_ARGUMENT, "tensor-parallel output must be F32, F16 or S32%s", nullptr);
-    const mpp41_mlp_desc l = local_desc(d, cs->nranks);
-    const size_t local_scratch = align256(mpp41_mlp_scratch_bytes(&l));
+    const mpp41_mlp_desc l = local_desc(d, cs->nranks, cs->rank);
+    // the partial follows the largest slice's scratch, as mpp41_mlp_tp_scratch_bytes lays it out
+    const mpp41_mlp_desc l0 = local_desc(d, cs->nranks, 0);
+    const size_t local_scratch = align256(mpp41_mlp_scratch_bytes(&l0));
     const size_t n = (size_t)d->tokens * d->hidden;
     if (use_oneshot(cs, d, n)) {
         // partial straight into this rank's peer-mapped buffer, then the one-shot reduction
