@@ -402,15 +402,18 @@ def tp_row(args):
     res = {}
     # one-shot peer-memory all-reduce where its 2 MB buffer holds the partial; NCCL
     # (chunked overlap for T >= 1024); NCCL with one chunk (no overlap) for the gain
-    paths = (["oneshot"] if T * H * 4 <= (2 << 20) else []) + ["nccl"] + (["nccl_one_chunk"] if T >= 1024 else [])
+    paths = (["oneshot"] if T * H * 4 <= (2 << 20) else []) + ["nccl", "nccl_allreduce"] + (["nccl_one_chunk"] if T >= 1024 else [])
     # the unsharded layer on one GPU (this rank's device), same timing
     full = [to(a) for a in (wg, wu, wd, sg, su, sd)]
     scr1 = torch.empty(mpp41.scratch_bytes(desc), dtype=torch.uint8, device="cuda")
     for path in paths + ["one_gpu"]:
         os.environ.pop("MPP41_TP_ALLREDUCE", None)
         os.environ.pop("MPP41_TP_CHUNKS", None)
+        os.environ.pop("MPP41_TP_REDUCE", None)
         if path == "oneshot":
             os.environ["MPP41_TP_ALLREDUCE"] = "oneshot"
+        if path == "nccl_allreduce":     # fp32 all-reduce, then fp16 conversion
+            os.environ["MPP41_TP_REDUCE"] = "allreduce"
         if path == "nccl_one_chunk":
             os.environ["MPP41_TP_CHUNKS"] = "1"
         if path == "one_gpu":
@@ -443,6 +446,7 @@ def tp_row(args):
         res[path] = round(float(us[0]), 2)
     os.environ.pop("MPP41_TP_ALLREDUCE", None)
     os.environ.pop("MPP41_TP_CHUNKS", None)
+    os.environ.pop("MPP41_TP_REDUCE", None)
     dist.barrier()
     if rank == 0:
         best = min(res[p] for p in paths)
