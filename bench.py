@@ -188,12 +188,12 @@ TP_REPS = 10
 
 def tp_measurement(ctx, rank, world, dist, stream):
     """BASELINE config 3 tensor-parallel over the job's GPUs (mpp41_mlp_tp: rank r
-    owns intermediate slice r, NCCL all-reduce of the fp32 partial output): the
+    owns intermediate slice r, NCCL sum of the fp32 partial outputs): the
     device time per layer (CUDA events on the launching stream around a CUDA
     graph of TP_REPS layers, max over ranks) at each token count, next to the
     same layer on one GPU (mpp41_mlp, every rank times it on its own GPU, max
     over ranks), the rank's local layer alone (mpp41_mlp on its shard) and the
-    all-reduce alone, so the limiting step is named. Random MXFP4 weight bytes
+    sum of the partials alone, so the limiting step is named. Random MXFP4 weight bytes
     with block scales near 2^-7 (timing does not depend on the values)."""
     import numpy as np
     import torch
@@ -253,18 +253,34 @@ def tp_measurement(ctx, rank, world, dist, stream):
         t_tp = timed(lambda: ctx.mlp_tp(d, x, *shard, scr_tp, out))
         t_local = timed(lambda: ctx.mlp(dl, x, *shard, scr_l, out))
         t_ar = timed(lambda: dist.all_reduce(part), graph=False)   # torch's NCCL group, eager launches
+        # the sum mpp41_mlp_tp runs for fp16 output of 2^20 elements and up: reduce-scatter
+        # of the fp32 partial, this rank's share to fp16, all-gather of the fp16 shares
+        split_sum = T * H >= (1 << 20) and (T * H) % (8 * world) == 0
+        if split_sum:
+            share = T * H // world
+            mine = part[rank * share:(rank + 1) * share]
+            mine16 = out[rank * share:(rank + 1) * share]
+
+            def rs_ag():
+                dist.reduce_scatter_tensor(mine, part)
+                mine16.copy_(mine)
+                dist.all_gather_into_tensor(out, mine16)
+            t_sum = timed(rs_ag, graph=False)
+        else:
+            t_sum = t_ar
         t_1 = timed(lambda: ctx.mlp(d, x, *full, scr_1, out))
         flops = 6.0 * T * H * I
         rows.append({"tokens": T, "us_per_layer": round(t_tp, 2), "us_per_layer_1gpu": round(t_1, 2),
                      "speedup": round(t_1 / t_tp, 3), "efficiency": round(t_1 / (world * t_tp), 3),
                      "tflops": round(flops / t_tp / 1e6, 1), "us_local_layer": round(t_local, 2),
-                     "us_allreduce_fp32": round(t_ar, 2),
-                     "limited_by": "all-reduce" if t_ar > t_local else "local layer"})
+                     "us_allreduce_fp32": round(t_ar, 2), "us_sum": round(t_sum, 2),
+                     "sum": "reduce-scatter fp32 + all-gather fp16" if split_sum else "all-reduce fp32",
+                     "limited_by": "sum of partials" if t_sum > t_local else "local layer"})
         del scr_tp, scr_l, scr_1, x, out, part
     ctx.comm_destroy()
     return {"model": "Llama-3-8B MLP (H=4096, I=14336), MXFP4 weights, fp16 out (BASELINE config 3)",
-            "ranks": world, "split": "gate/up rows and down columns by intermediate slice, NCCL all-reduce of "
-            "the fp32 partial output", "timing": f"CUDA graph of {TP_REPS} layers, CUDA events, max over ranks",
+            "ranks": world, "split": "gate/up rows and down columns by intermediate slice; the fp32 partial "
+            "outputs summed by NCCL (reduce-scatter + fp16 all-gather from 2^20 outputs, else all-reduce)", "timing": f"CUDA graph of {TP_REPS} layers, CUDA events, max over ranks",
             "rows": rows}
 
 

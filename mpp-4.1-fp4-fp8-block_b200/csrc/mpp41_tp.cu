@@ -235,11 +235,12 @@ int tp_chunks(const mpp41_mlp_desc *d)
     return c;
 }
 
-// fp16 output of at least 2 MB of fp32 partials goes through reduce-scatter +
+// fp16 output of at least 4 MB of fp32 partials goes through reduce-scatter +
 // fp16 all-gather; MPP41_TP_REDUCE=allreduce asks for the fp32 all-reduce. On 2
 // B200s, Llama-3-8B layer: T=4096 1084 us against 1101, T=256 134 against 140;
-// at T=16 the two collectives' latency loses (50.7 us against 42.0).
-constexpr size_t kGatherMinElems = (size_t)1 << 19;
+// below that the two collectives' latency loses (T=128: 100.5 us against 92.4,
+// T=16: 50.7 against 42.0).
+constexpr size_t kGatherMinElems = (size_t)1 << 20;
 
 bool use_gather_f16(const CommState *cs, const mpp41_mlp_desc *d, size_t n)
 {
