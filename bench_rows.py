@@ -252,6 +252,8 @@ def main():
                     choices=["w4a16", "w4a4", "nvfp4", "mxf4_gemm", "nvf4_gemm", "moe", "tp", "config2", "config1"])
     ap.add_argument("--shape", default=None, help="T,H,I (layers), M,N,K (GEMMs), T,H,I,E,k,shared_I (moe)")
     ap.add_argument("--once", action="store_true")
+    ap.add_argument("--trace", action="store_true",
+                    help="w4a16 on the weight-major kernel: also print one call's per-CTA phase trace")
     args = ap.parse_args()
     if args.row == "tp":
         return tp_row(args)
@@ -366,6 +368,38 @@ def main():
                        "source": "fp4: measured kind::mxf4 issue rate (host/mpp41_mma_peaks.cu); f16 and HBM: "
                                  + src + " (MEASURED_PEAKS.json)"})
     print(json.dumps(line))
+    if args.trace and args.row == "w4a16" and ctx.mlp_last_kernel() == "weight_major":
+        print(json.dumps(weight_major_trace(ctx, run)))
+
+
+# Trace slots of mpp41::mlp_fused_kernel (csrc/mpp41_mlp_fused.cuh, enum TraceSlot):
+# cycle totals per role, and per-stage stamps of the CTA's first 32 stages
+WM_TOTALS = {"mma_wait_stage": 11, "mma_wait_acc": 13, "dec_wait_raw": 14, "dec_wait_slot": 15, "dec_work": 16,
+             "dec_wait_acc": 18, "dec_wait_scales": 58, "raw_producer_wait": 8, "act_producer_wait": 9,
+             "epilogue_g": 17, "epilogue_d": 19}
+WM_STAMPS = {"act_issued": 96, "dec_raw_ready": 128, "dec_start": 160, "dec_done": 64, "mma_ready": 224}
+
+
+def weight_major_trace(ctx, run):
+    """One traced call of the weight-major layer kernel: per role, the median over
+    CTAs of the cycles spent waiting and working (converted to us at the CTA's
+    own clock), and for CTA 0 the time of stages 4..11 at each step of the
+    pipeline (activation copy issued, packed weights ready for the decoders,
+    decode start / done, stage ready for the MMA)."""
+    import numpy as np
+    tr = torch.zeros(256 * 148, dtype=torch.int64, device="cuda")
+    ctx.set_trace(tr)
+    run()
+    torch.cuda.synchronize()
+    ctx.set_trace(None)
+    a = tr.cpu().numpy().reshape(148, 256).astype(np.int64)
+    a = a[a[:, 0] > 0]
+    mhz = a[:, 20] / np.maximum(a[:, 2] - a[:, 0], 1) * 1e3
+    f = float(np.median(mhz))
+    out = {"row": "w4a16_trace", "ctas": int(len(a)), "sm_mhz": round(f), "kernel_us": round(float(np.median(a[:, 20])) / f, 1)}
+    out["median_us"] = {k: round(float(np.median(a[:, i])) / f, 1) for k, i in WM_TOTALS.items()}
+    out["cta0_stage_us"] = {k: [round(float(v) / f, 2) for v in a[0, i + 4:i + 12]] for k, i in WM_STAMPS.items()}
+    return out
 
 
 def tp_row(args):

@@ -103,7 +103,7 @@ enum TraceSlot : int {
     TR_DEC_WAIT_ACC = 18, TR_EPI_D = 19, TR_CYCLES = 20, TR_MMA_ISSUE = 21, TR_DEC_FIRST_RAW = 22,
     TR_DEC_FIRST_SC = 23, TR_MMA_FIRST_A = 24, TR_D_FENCED = 25, TR_D_COUNTED = 26, TR_D_CONVERTED = 27,
     TR_D_LAST = 28, TR_G_ACC = 29, TR_G_STORED = 30, TR_G_PUBLISHED = 31, TR_MMA_STAGE = 32, TR_D_STORED = 56,
-    TR_D_ACC_WAITED = 57, TR_DEC_STAGE = 64, TR_AP_STAGE = 96, TR_DEC_RAW_READY = 128,
+    TR_D_ACC_WAITED = 57, TR_DEC_WAIT_SC = 58, TR_DEC_STAGE = 64, TR_AP_STAGE = 96, TR_DEC_RAW_READY = 128,
     TR_DEC_START = 160, TR_MMA_WAIT_START = 192, TR_MMA_READY = 224, TR_WARP_DONE = 240,
     kTraceSlots = 256
 };
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
     const uint32_t NT = p.NT;
     unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceSlots : nullptr;
     const long long clk0 = p.trace ? clock64() : 0;
-    unsigned long long tw0 = 0, tw1 = 0, tw2 = 0, tw3 = 0;   // per-role accumulators (trace only)
+    unsigned long long tw0 = 0, tw1 = 0, tw2 = 0, tw3 = 0, tw4 = 0;   // per-role accumulators (trace only)
     if (tr && threadIdx.x == 0) {
         tr[TR_START] = globaltimer_ns();
         uint32_t smid;
@@ -465,17 +465,21 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         for (uint32_t t = blockIdx.x; t < ntiles && !__any_sync(0xffffffffu, *abort != 0); t += gridDim.x, ++ti_n) {
             const TileInfo ti = tile_info(p, t);
             const uint32_t acc = ti_n & 1u;
+            const long long cwa = clk_if(tr);
             if (!warp_wait(&acc_empty[acc], ((ti_n >> 1) & 1u) ^ 1u, abort, p.err, 0x801)) break;
+            if (tr) tw2 += (unsigned long long)(clock64() - cwa);
             tc_fence_after();
             const uint32_t d_tmem = tmem + acc * kAccCols;
             bool ok = true;
             for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
                 const uint32_t sl = gs & (kFStages - 1);
                 if (tr && lane == 0 && gs < 32) tr[TR_MMA_WAIT_START + gs] = (unsigned long long)(clock64() - clk0);
+                const long long cws = clk_if(tr);
                 if (!warp_wait(&st_full[sl], (gs / kFStages) & 1u, abort, p.err, 0x802)) {
                     ok = false;
                     break;
                 }
+                if (tr) tw0 += (unsigned long long)(clock64() - cws);
                 if (tr && lane == 0 && gs == 0) tr[TR_MMA_FIRST_A] = (unsigned long long)(clock64() - clk0);
                 if (tr && lane == 0 && gs < 16) tr[TR_MMA_READY + gs] = (unsigned long long)(clock64() - clk0);
                 tc_fence_after();
@@ -525,7 +529,10 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 }
                 if (W == W_MXFP4 && s % SPS == 0) {
                     scs = gsc % kScChunks;
-                    if (!mbar_wait(&sc_full[scs], (gsc / kScChunks) & 1u, abort, p.err, 0x901)) { ok = false; break; }
+                    if (!mbar_wait_t(&sc_full[scs], (gsc / kScChunks) & 1u, abort, p.err, 0x901, tw4, tr != nullptr)) {
+                        ok = false;
+                        break;
+                    }
                 }
                 if (gs >= kFStages) {   // MMA of stage gs-4 (same TMEM slot) completed
                     if (!mbar_wait_t(&st_empty[sl], ((gs / kFStages) - 1u) & 1u, abort, p.err, 0x903, tw1,
@@ -752,6 +759,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         if (warp == kMmaWarp && lane == 0) { tr[TR_MMA_WAIT_A] = tw0; tr[TR_MMA_WAIT_ACC] = tw2; tr[TR_MMA_ISSUE] = tw3; }
         if (threadIdx.x == kDec0 * 32) {
             tr[TR_DEC_WAIT_RAW] = tw0; tr[TR_DEC_WAIT_SLOT] = tw1; tr[TR_DEC_WORK] = tw2; tr[TR_DEC_WAIT_ACC] = tw3;
+            tr[TR_DEC_WAIT_SC] = tw4;
             tr[TR_D_EPI_END] = globaltimer_ns();
         }
         if (threadIdx.x == 0) { tr[TR_END] = globaltimer_ns(); tr[TR_CYCLES] = (unsigned long long)(clock64() - clk0); }
