@@ -110,7 +110,7 @@ int launch_layer(const LayerPlan &plan, FusedLaunch L, cudaStream_t st, const ch
     return plan.token_major ? tok::launch(L, st, why) : launch_mlp_fused(L, st, why);
 }
 
-template <int W, int EG, bool F16>
+template <int W, int EG, bool F16, bool PAIR = false>
 static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
     FusedParams p;
@@ -132,8 +132,13 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
         *why = "MXFP4 scale rows need hidden, intermediate and the K split to be multiples of 512";
         return 1;
     }
-    p.n_gtiles = L.gemm_only ? 0 : (L.I / kGCh) * mt;
-    p.n_dtiles = (L.H / kWRows) * L.splits * mt;
+    if (PAIR && (L.gemm_only || p.NT != (uint32_t)kMaxNT || L.H % (2 * kWRows) || L.I % (2 * kGCh))) {
+        *why = "CTA pairs need full 128-token tiles, hidden a multiple of 256 and intermediate of 128";
+        return 1;
+    }
+    // pairs: tile counts are pair tiles (G 128 channels, D 256 outputs)
+    p.n_gtiles = L.gemm_only ? 0 : (L.I / (PAIR ? 2 * kGCh : kGCh)) * mt;
+    p.n_dtiles = (L.H / (PAIR ? 2 * kWRows : kWRows)) * L.splits * mt;
     p.g_per_slice = L.gemm_only ? 0 : L.I / L.splits / kGCh;
     if (L.splits > 1 && !L.ws) { *why = "workspace"; return 1; }
     // GEMM mode has no gate/up phase: its G maps are built over the down
@@ -141,7 +146,8 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     const void *gx = L.gemm_only ? L.mid : L.x, *gg = L.gemm_only ? L.wd : L.wg, *gu = L.gemm_only ? L.wd : L.wu;
     const uint64_t grow = L.gemm_only ? rawI : rawH;
     const uint32_t gk = L.gemm_only ? L.I : L.H, gn = L.gemm_only ? L.H : L.I;
-    bool ok = make_map_kblocks(&p.tm_x, gx, gk, L.T, p.NT, 2) && make_map_kblocks(&p.tm_mid, L.mid, L.I, L.T, p.NT, 2) &&
+    const uint32_t nt_box = PAIR ? p.NT / 2 : p.NT;   // tokens each CTA loads per stage
+    bool ok = make_map_kblocks(&p.tm_x, gx, gk, L.T, nt_box, 2) && make_map_kblocks(&p.tm_mid, L.mid, L.I, L.T, nt_box, 2) &&
               make_map(&p.tm_wg, gg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, grow, gn, kChunkRow, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
               make_map(&p.tm_wu, gu, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, grow, gn, kChunkRow, kGCh, CU_TENSOR_MAP_SWIZZLE_128B) &&
               make_map(&p.tm_wd, L.wd, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rawI, L.H, kChunkRow, kWRows, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -159,7 +165,7 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     p.err = L.err;
     p.trace = L.trace;
 
-    auto kern = mlp_fused_kernel<W, EG, F16>;
+    auto kern = mlp_fused_kernel<W, EG, F16, PAIR>;
     const uint32_t smem = kFusedSmem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) { cudaGetLastError(); *why = cudaGetErrorString(e); return 2; }
@@ -169,36 +175,72 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFThreads, smem);
     if (e != cudaSuccess || per_sm < 1) { cudaGetLastError(); *why = "occupancy"; return 2; }
     const uint32_t ntiles = p.n_gtiles + p.n_dtiles;
-    uint32_t grid = (uint32_t)sms;   // one CTA per SM: each holds all 512 TMEM columns
-    if (grid > ntiles) grid = ntiles;
-    // tiles go to CTAs round-robin, down tiles last: with no more down tiles
-    // than CTAs each CTA holds at most one and it is its final tile
-    p.d_spin = p.n_dtiles <= grid ? 1u : 0u;
-
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kFThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    uint32_t grid = (uint32_t)sms;   // one CTA per SM: each holds all 512 TMEM columns
+    if (PAIR) {
+        // every CTA must be resident (grid-wide waits): as many pairs as fit at once
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.attrs = attr + 1;
+        cfg.numAttrs = 1;
+        cfg.gridDim = dim3(2);
+        int clusters = 0;
+        e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+        if (e != cudaSuccess || clusters < 1) { cudaGetLastError(); *why = "cluster occupancy"; return 2; }
+        grid = 2u * (uint32_t)clusters;
+        if (grid > (uint32_t)sms) grid = (uint32_t)sms & ~1u;
+        if (grid > 2 * ntiles) grid = 2 * ntiles;
+    } else if (grid > ntiles) {
+        grid = ntiles;
+    }
+    // tiles go to CTAs (pairs) round-robin, down tiles last: with no more down
+    // tiles than CTAs (pairs) each holds at most one and it is its final tile
+    p.d_spin = p.n_dtiles <= (PAIR ? grid / 2 : grid) ? 1u : 0u;
+    cfg.gridDim = dim3(grid);
     // Programmatic stream serialization: this grid may launch while the previous
     // kernel on the stream finishes (it only prefetches and decodes weights until
     // griddepcontrol.wait). Every grid-wide wait of this kernel comes after that
     // wait, when the previous grid has exited and all of this grid's CTAs (at
     // most one per SM) can be resident.
-    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = PAIR ? 2 : 1;
     e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess) { cudaGetLastError(); *why = cudaGetErrorString(e); return 2; }
     return 0;
 }
 
+// CTA pairs for MXFP4 layers with full token tiles, unless MPP41_FUSED_PAIR=0.
+static bool want_pair(const FusedLaunch &L)
+{
+    const char *e = getenv("MPP41_FUSED_PAIR");
+    if (!e || strcmp(e, "1") != 0) return false;
+    return !L.gemm_only && L.T >= (uint32_t)kMaxNT && L.H % (2 * kWRows) == 0 && L.I % (2 * kGCh) == 0;
+}
+
 template <int W>
 static int launch_fw(const FusedLaunch &L, cudaStream_t st, const char **why)
 {
+    if constexpr (W == W_MXFP4) {
+        if (want_pair(L)) {
+            switch (L.gate_epi * 2 + (L.out_f16 ? 1 : 0)) {
+            case EPI_SWIGLU_HALF * 2 + 1: return launch_ft<W, EPI_SWIGLU_HALF, true, true>(L, st, why);
+            case EPI_SWIGLU_HALF_H * 2 + 1: return launch_ft<W, EPI_SWIGLU_HALF_H, true, true>(L, st, why);
+            case EPI_SWIGLU_PLAIN * 2 + 1: return launch_ft<W, EPI_SWIGLU_PLAIN, true, true>(L, st, why);
+            case EPI_SWIGLU_HALF * 2: return launch_ft<W, EPI_SWIGLU_HALF, false, true>(L, st, why);
+            case EPI_SWIGLU_HALF_H * 2: return launch_ft<W, EPI_SWIGLU_HALF_H, false, true>(L, st, why);
+            case EPI_SWIGLU_PLAIN * 2: return launch_ft<W, EPI_SWIGLU_PLAIN, false, true>(L, st, why);
+            }
+        }
+    }
     if (L.out_f16) {
         switch (L.gate_epi) {
         case EPI_SWIGLU_HALF: return launch_ft<W, EPI_SWIGLU_HALF, true>(L, st, why);

@@ -225,6 +225,124 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---- CTA pairs (tcgen05 cta_group::2): two CTAs of a 2-CTA cluster run one
+// M = 256 MMA; each holds 128 weight rows in its tensor memory and half of the
+// token tile in its shared memory, and the even CTA issues the MMAs. The
+// barriers the MMA issuer waits on live in the even CTA; the odd CTA arrives on
+// them through shared::cluster addresses.
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void *local, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cl(uint32_t caddr)
+{
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx_cl(uint32_t caddr, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(caddr),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t addr, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait with cluster-scope acquire (arrivals from the peer CTA), bounded the same way.
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *err,
+                                             uint32_t site)
+{
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait_cl(addr, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_cl(addr, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (abort && *abort) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                report_error(err, kErrTimeout, site);
+                if (abort) *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// 3-D tiled load into this CTA's shared memory whose completion is counted on
+// an mbarrier of either CTA of the pair (no multicast).
+__device__ __forceinline__ void tma_load_3d_pair(void *dst, const void *tmap, int32_t c0, int32_t c1, int32_t c2,
+                                                 uint32_t bar_caddr)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_u32(dst)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(bar_caddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on the mbarrier at `caddr` (either CTA of the pair) once all MMAs this
+// thread issued before it complete.
+__device__ __forceinline__ void mma_commit_pair(uint32_t caddr)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(caddr)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 struct TileInfo {
     bool is_g;
     uint32_t m0;      // first token
@@ -236,21 +354,26 @@ struct TileInfo {
     __device__ __forceinline__ uint32_t kstage(uint32_t s) const { return s + rot < nk ? s + rot : s + rot - nk; }
 };
 
-__device__ __forceinline__ TileInfo tile_info(const FusedParams &p, uint32_t t)
+// Tile t of the list. With CTA pairs t indexes pair tiles (G: 128 channels,
+// D: 256 outputs) and `half` (the CTA's rank in the pair) picks this CTA's
+// 64 channels / 128 outputs; both CTAs of a pair walk the same K stages.
+template <bool PAIR = false>
+__device__ __forceinline__ TileInfo tile_info(const FusedParams &p, uint32_t t, uint32_t half = 0)
 {
     TileInfo ti;
+    constexpr uint32_t kGW = PAIR ? 2 * kGCh : kGCh, kDW = PAIR ? 2 * kWRows : kWRows;
     if (t < p.n_gtiles) {
-        const uint32_t gch = p.I / kGCh;
+        const uint32_t gch = p.I / kGW;
         ti.is_g = true;
-        ti.c0 = (t % gch) * kGCh;
+        ti.c0 = (t % gch) * kGW + half * kGCh;
         ti.m0 = (t / gch) * p.NT;
         ti.kb = 0;
         ti.k0 = 0;
         ti.nk = p.H / kFBK;
     } else {
-        const uint32_t d = t - p.n_gtiles, nh = p.H / kWRows, ks = p.I / p.splits;
+        const uint32_t d = t - p.n_gtiles, nh = p.H / kDW, ks = p.I / p.splits;
         ti.is_g = false;
-        ti.c0 = (d % nh) * kWRows;
+        ti.c0 = (d % nh) * kDW + half * kWRows;
         ti.kb = (d / nh) % p.splits;
         ti.m0 = (d / (nh * p.splits)) * p.NT;
         ti.k0 = ti.kb * ks;
@@ -270,7 +393,7 @@ __device__ __forceinline__ uint32_t *slice_counter(const FusedParams &p, uint32_
     return p.sync + 2 + (p.H / kWRows) * n_mt + mt * p.splits + kb;
 }
 
-template <int W, int EG, bool OUT_F16>
+template <int W, int EG, bool OUT_F16, bool PAIR = false>
 __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_constant__ FusedParams p)
 {
     constexpr uint32_t RB = kFBK * wfmt_bits(W) / 8;   // packed bytes per row per stage
@@ -303,6 +426,10 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ntiles = p.n_gtiles + p.n_dtiles;
     const uint32_t NT = p.NT;
+    // pairs: tile list walked per cluster; `half` is this CTA's rank in the pair
+    const uint32_t half = PAIR ? cluster_rank() : 0u;
+    const uint32_t t_first = PAIR ? blockIdx.x >> 1 : blockIdx.x, t_step = PAIR ? gridDim.x >> 1 : gridDim.x;
+    const uint32_t NTc = PAIR ? NT / 2 : NT;   // tokens of the tile this CTA loads
     unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceSlots : nullptr;
     const long long clk0 = p.trace ? clock64() : 0;
     unsigned long long tw0 = 0, tw1 = 0, tw2 = 0, tw3 = 0, tw4 = 0;   // per-role accumulators (trace only)
@@ -322,13 +449,15 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
             mbar_init(&sc_full[s], 1);
             mbar_init(&sc_empty[s], kDecWarps);
         }
+        // pairs: the even CTA's st_full / acc_empty also count the odd CTA's arrivals
+        constexpr uint32_t kSides = PAIR ? 2 : 1;
         for (int s = 0; s < kFStages; ++s) {
-            mbar_init(&st_full[s], 1 + kDecWarps);
+            mbar_init(&st_full[s], kSides * (1 + kDecWarps));
             mbar_init(&st_empty[s], 1);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], kDecWarps);
+            mbar_init(&acc_empty[s], kSides * kDecWarps);
         }
         *abort = 0;
         fence_mbar_init();
@@ -348,11 +477,17 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         tma_prefetch_desc(&p.tm_mid);
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(tmem_slot, kTmemCols);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync_all();   // the peer's barriers are initialised before any remote arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (tr && threadIdx.x == 0) tr[TR_PROLOGUE] = globaltimer_ns();
@@ -367,8 +502,8 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         if (lane == 0) {
             uint32_t gc = 0, gsc = 0;
             bool ok = true;
-            for (uint32_t t = blockIdx.x; t < ntiles && ok && !*abort; t += gridDim.x) {
-                const TileInfo ti = tile_info(p, t);
+            for (uint32_t t = t_first; t < ntiles && ok && !*abort; t += t_step) {
+                const TileInfo ti = tile_info<PAIR>(p, t, half);
                 const int32_t row0 = (int32_t)ti.c0;
                 for (uint32_t s = 0; s < ti.nk; ++s) {
                     if (W == W_MXFP4 && s % SPS == 0) {
@@ -416,9 +551,9 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
             pdl_wait_prior();   // activations and counters may come from the previous kernel
             uint32_t gs = 0, last[2] = {0, 0}, waited_t = ~0u;
             bool ok = true, any[2] = {false, false};
-            const uint32_t atom = NT * 128;
-            for (uint32_t t = blockIdx.x; t < ntiles && ok && !*abort; t += gridDim.x) {
-                const TileInfo ti = tile_info(p, t);
+            const uint32_t atom = NTc * 128;
+            for (uint32_t t = t_first; t < ntiles && ok && !*abort; t += t_step) {
+                const TileInfo ti = tile_info<PAIR>(p, t, half);
                 const CUtensorMap *tm = ti.is_g ? &p.tm_x : &p.tm_mid;
                 for (uint32_t s = 0; s < ti.nk; ++s, ++gs) {
                     if ((gs & 1u) != (uint32_t)warp) continue;
@@ -442,31 +577,59 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                         break;
                     }
                     if (tr && gs < 32) tr[TR_AP_STAGE + gs] = (unsigned long long)(clock64() - clk0);
-                    mbar_arrive_expect_tx(&st_full[sl], 2 * atom);
                     uint8_t *dst = sB + sl * kStageBytes;
                     const int32_t kx = (int32_t)(ti.k0 + ti.kstage(s) * kFBK);
-                    tma_load_3d(dst, tm, 0, (int32_t)ti.m0, kx / 64, &st_full[sl]);
+                    if constexpr (PAIR) {
+                        // this CTA's half of the token tile; completion counted in the even CTA
+                        const uint32_t bar = cluster_addr(&st_full[sl], 0);
+                        mbar_arrive_expect_tx_cl(bar, 2 * atom);
+                        tma_load_3d_pair(dst, tm, 0, (int32_t)(ti.m0 + half * NTc), kx / 64, bar);
+                    } else {
+                        mbar_arrive_expect_tx(&st_full[sl], 2 * atom);
+                        tma_load_3d(dst, tm, 0, (int32_t)ti.m0, kx / 64, &st_full[sl]);
+                    }
                     last[sl >> 1] = gs;
                     any[sl >> 1] = true;
                 }
             }
             // no copies left in flight when the CTA exits: the last use of each slot
+            // (pairs: the MMAs that read it completed, which the issuer reports to both CTAs)
             for (int i = 0; i < 2; ++i)
-                if (any[i]) mbar_wait(&st_full[last[i] & (kFStages - 1)], (last[i] / kFStages) & 1u, nullptr, p.err, 0x703);
+                if (any[i]) {
+                    if constexpr (PAIR)
+                        mbar_wait(&st_empty[last[i] & (kFStages - 1)], (last[i] / kFStages) & 1u, nullptr, p.err, 0x703);
+                    else
+                        mbar_wait(&st_full[last[i] & (kFStages - 1)], (last[i] / kFStages) & 1u, nullptr, p.err, 0x703);
+                }
         }
     } else if (warp == kMmaWarp) {
+      if (!(PAIR && half != 0)) {   // pairs: the odd CTA's MMA warp only holds its TMEM allocation
         // ------------------------------------------------ MMA issuer
         // The whole warp runs the loop and makes every wait; one elected lane
         // issues (measured: ~70 vs 43 cycles per small-N MMA when one divergent
         // lane runs a loop with waits while its warp-mates wait elsewhere).
-        const uint32_t idesc = idesc_f16_f32(kWRows, (int)NT);
-        const uint32_t atom = NT * 128;
+        // Pairs: the even CTA issues M = 256 MMAs over both CTAs' weight rows and
+        // token halves, and reports completions to the barriers of both.
+        const uint32_t idesc = idesc_f16_f32(PAIR ? 2 * kWRows : kWRows, (int)NT);
+        const uint32_t atom = NTc * 128;
+        auto wait_in = [&](uint64_t *bar, uint32_t parity, uint32_t site) -> bool {
+            if constexpr (PAIR) return __all_sync(0xffffffffu, mbar_wait_cl(bar, parity, abort, p.err, site));
+            else return warp_wait(bar, parity, abort, p.err, site);
+        };
+        auto commit = [&](uint64_t *bar) {
+            if constexpr (PAIR) {
+                mma_commit_pair(cluster_addr(bar, 0));
+                mma_commit_pair(cluster_addr(bar, 1));
+            } else {
+                mma_commit(bar);
+            }
+        };
         uint32_t gs = 0, ti_n = 0;
-        for (uint32_t t = blockIdx.x; t < ntiles && !__any_sync(0xffffffffu, *abort != 0); t += gridDim.x, ++ti_n) {
-            const TileInfo ti = tile_info(p, t);
+        for (uint32_t t = t_first; t < ntiles && !__any_sync(0xffffffffu, *abort != 0); t += t_step, ++ti_n) {
+            const TileInfo ti = tile_info<PAIR>(p, t, half);
             const uint32_t acc = ti_n & 1u;
             const long long cwa = clk_if(tr);
-            if (!warp_wait(&acc_empty[acc], ((ti_n >> 1) & 1u) ^ 1u, abort, p.err, 0x801)) break;
+            if (!wait_in(&acc_empty[acc], ((ti_n >> 1) & 1u) ^ 1u, 0x801)) break;
             if (tr) tw2 += (unsigned long long)(clock64() - cwa);
             tc_fence_after();
             const uint32_t d_tmem = tmem + acc * kAccCols;
@@ -475,7 +638,7 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 const uint32_t sl = gs & (kFStages - 1);
                 if (tr && lane == 0 && gs < 32) tr[TR_MMA_WAIT_START + gs] = (unsigned long long)(clock64() - clk0);
                 const long long cws = clk_if(tr);
-                if (!warp_wait(&st_full[sl], (gs / kFStages) & 1u, abort, p.err, 0x802)) {
+                if (!wait_in(&st_full[sl], (gs / kFStages) & 1u, 0x802)) {
                     ok = false;
                     break;
                 }
@@ -489,18 +652,23 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                     for (uint32_t j = 0; j < 2; ++j) {
                         const uint64_t bd = smem_desc_sw128(sB + sl * kStageBytes + j * atom);
 #pragma unroll
-                        for (uint32_t k = 0; k < 4; ++k)
-                            mma_f16_ts(d_tmem, a0 + j * 32 + k * 8, bd + 2 * k, idesc, (s | j | k) != 0u);
+                        for (uint32_t k = 0; k < 4; ++k) {
+                            if constexpr (PAIR)
+                                mma_f16_ts_pair(d_tmem, a0 + j * 32 + k * 8, bd + 2 * k, idesc, (s | j | k) != 0u);
+                            else
+                                mma_f16_ts(d_tmem, a0 + j * 32 + k * 8, bd + 2 * k, idesc, (s | j | k) != 0u);
+                        }
                     }
-                    mma_commit(&st_empty[sl]);
+                    commit(&st_empty[sl]);
                 }
                 __syncwarp();
                 if (tr && lane == 0 && gs < 24) tr[TR_MMA_STAGE + gs] = (unsigned long long)(clock64() - clk0);
             }
             if (!ok) break;
-            if (elect_one_sync()) mma_commit(&acc_full[acc]);
+            if (elect_one_sync()) commit(&acc_full[acc]);
             __syncwarp();
         }
+      }
     } else {
         // ------------------------------------------------ decode + epilogue
         const uint32_t te = threadIdx.x - kDec0 * 32;   // 0..511
@@ -509,8 +677,8 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
         const uint32_t r = quarter * 32 + lane;        // weight row of the tile = TMEM lane
         const uint32_t lane_base = (quarter * 32u) << 16;
         uint32_t gs = 0, gc = 0, gsc = 0, ti_n = 0;
-        for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti_n) {
-            const TileInfo ti = tile_info(p, t);
+        for (uint32_t t = t_first; t < ntiles; t += t_step, ++ti_n) {
+            const TileInfo ti = tile_info<PAIR>(p, t, half);
             // packed row in the chunk: G rows interleave gate and up channels
             const uint32_t rr = ti.is_g ? ((r & 1u) ? kGCh + (r >> 1) : (r >> 1)) : r;
             bool ok = true;
@@ -563,7 +731,10 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&st_full[sl]);
+                if (lane == 0) {
+                    if (PAIR && half != 0) mbar_arrive_cl(cluster_addr(&st_full[sl], 0));
+                    else mbar_arrive(&st_full[sl]);
+                }
                 if (tr) tw2 += (unsigned long long)(clock64() - cdec);
                 if (tr && te == 0 && gs < 32) tr[TR_DEC_STAGE + gs] = (unsigned long long)(clock64() - clk0);
                 if (tr && lane == 0 && gs == 2) tr[TR_WARP_DONE + (warp - kDec0)] = (unsigned long long)(clock64() - clk0);
@@ -606,7 +777,10 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
                 if (cb + 32 >= ncol) {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                    if (lane == 0) {
+                        if (PAIR && half != 0) mbar_arrive_cl(cluster_addr(&acc_empty[acc], 0));
+                        else mbar_arrive(&acc_empty[acc]);
+                    }
                 }
                 if (ti.is_g) {
                     // lane pair (2j, 2j+1) = (gate, up) of channel j: the even lane
@@ -749,9 +923,13 @@ __global__ void __launch_bounds__(kFThreads, 1) mlp_fused_kernel(const __grid_co
     // ---------------------------------------------------- teardown
     tc_fence_before();
     __syncthreads();
+    // pairs: neither CTA leaves while the other may still arrive on its barriers
+    // or (the even CTA's MMAs) read its shared and tensor memory
+    if constexpr (PAIR) cluster_sync_all();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem, kTmemCols);
+        else tmem_dealloc(tmem, kTmemCols);
     }
     if (tr) {
         if (warp == kRawWarp && lane == 0) tr[TR_RAWP_WAIT_EMPTY] = tw0;
