@@ -249,7 +249,10 @@ mpp41_status mpp41_mlp_scalar(mpp41_ctx *ctx, const char *gate_kernel_name, cons
  *      (token-major for 65..128 tokens of a small layer, weight-major else).
  *      mpp41_mlp_last_kernel names the family the last mpp41_mlp call on the
  *      context launched: "gemv", "gemv_regs", "small", "token_major", "weight_major",
- *      "unfused" (two GEMM kernels) or "i8"; "" before the first call. ---- */
+ *      "unfused" (two GEMM kernels) or "i8"; "" before the first call.
+ *      MPP41_FUSED_PAIR=1 (read at each call) runs MXFP4 weight-major layers
+ *      with full 128-token tiles as CTA pairs (tcgen05 cta_group::2, M = 256):
+ *      same results within fp32 summation order, no faster on B200 so far. ---- */
 const char *mpp41_mlp_last_kernel(const mpp41_ctx *ctx);
 size_t mpp41_mlp_scratch_bytes(const mpp41_mlp_desc *desc);
 mpp41_status mpp41_mlp(mpp41_ctx *ctx, const mpp41_mlp_desc *desc, const void *x, const void *wg, const void *wu,
