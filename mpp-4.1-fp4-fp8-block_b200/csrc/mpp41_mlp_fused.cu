@@ -191,9 +191,14 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
         cfg.attrs = attr + 1;
         cfg.numAttrs = 1;
         cfg.gridDim = dim3(2);
-        int clusters = 0;
-        e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
-        if (e != cudaSuccess || clusters < 1) { cudaGetLastError(); *why = "cluster occupancy"; return 2; }
+        // co-resident pairs of this kernel, per device (the query costs a driver call)
+        static int cached[64] = {0};
+        int clusters = dev < 64 ? cached[dev] : 0;
+        if (clusters < 1) {
+            e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+            if (e != cudaSuccess || clusters < 1) { cudaGetLastError(); *why = "cluster occupancy"; return 2; }
+            if (dev < 64) cached[dev] = clusters;
+        }
         grid = 2u * (uint32_t)clusters;
         if (grid > (uint32_t)sms) grid = (uint32_t)sms & ~1u;
         if (grid > 2 * ntiles) grid = 2 * ntiles;
