@@ -469,8 +469,11 @@ mpp41_status mpp41_moe_ep(mpp41_ctx *ctx, const mpp41_moe_desc *desc, uint32_t c
  *      slice keeps the 16-byte-aligned scale rows the fused kernels need;
  *      otherwise [r*I/P, (r+1)*I/P), which needs I a multiple of 32*P. Each
  *      rank computes its partial output with the fused layer kernel in fp32,
- *      then the partials are summed across ranks (NCCL all-reduce on the
- *      context's stream) into `out` on every rank. NCCL is loaded at run time
+ *      then the partials are summed across ranks on the context's stream
+ *      into `out` on every rank: for fp16 output of at least 2^20 elements an
+ *      NCCL reduce-scatter of the fp32 partials, each rank's share rounded to
+ *      fp16 and an fp16 all-gather (MPP41_TP_REDUCE=allreduce asks for the
+ *      other form), otherwise an NCCL all-reduce. NCCL is loaded at run time
  *      (libnccl.so.2); without it mpp41_comm_init fails with MPP41_ERR_COMM. ---- */
 #define MPP41_COMM_ID_BYTES 128
 /* Rank 0 creates the id and shares it with the other ranks (any channel). */
