@@ -223,7 +223,8 @@ static int launch_ft(const FusedLaunch &L, cudaStream_t st, const char **why)
     return 0;
 }
 
-// CTA pairs for MXFP4 layers with full token tiles, unless MPP41_FUSED_PAIR=0.
+// CTA pairs for MXFP4 layers with full token tiles when MPP41_FUSED_PAIR=1 (opt-in:
+// on B200 the pair form measured on par with the single-CTA form).
 static bool want_pair(const FusedLaunch &L)
 {
     const char *e = getenv("MPP41_FUSED_PAIR");
